@@ -1,0 +1,199 @@
+// Row argmax over logits, the greedy pick of cli::detail::select_argmax_token_id (src/cli/cli_app.cpp:72-94) applied
+// to every row of a [rows, cols] bf16/f32 matrix (the reference scans the last row of [seq, vocab] logits).
+//
+// Semantics of the reference's scan (best = x[0]; for i >= 1: if (x[i] > best) take i):
+//  - the largest value wins, ties go to the lowest index (strict '>'), +0 and -0 compare equal;
+//  - NaN never wins, except that a NaN at index 0 is never replaced, so the result is 0.
+// These are reproduced exactly with an order-independent key: key(i) = (orderable(x[i]) << 32) | (2^32 - 1 - i),
+// where orderable() maps floats to unsigned integers monotonically (after folding -0 into +0) and NaN to 0 ("no
+// candidate"). max(key) is the reference's answer whenever x[0] is not NaN.
+//
+// Layout: a row is split across a thread-block cluster of up to 8 CTAs, each CTA scanning a contiguous column range
+// with 16-byte vector loads, 4 in flight per thread. CTA partials are combined through distributed shared memory
+// (cluster rank 0 reads the other CTAs' shared slots), so no global scratch and no second launch are needed.
+//
+// Roofline: HBM-bound. Algorithmic bytes per row: cols * size read + 8 bytes written.
+#include <cooperative_groups.h>
+
+#include "common.cuh"
+#include "runtime.h"
+
+namespace cg = cooperative_groups;
+
+namespace cppinf::device {
+namespace {
+
+constexpr int kThreads = 256;
+constexpr int kWarps = kThreads / 32;
+constexpr int kUnroll = 4;
+constexpr int kMaxCluster = 8;
+
+__device__ __forceinline__ unsigned long long argmax_key(float v, uint32_t index) {
+    uint32_t u = __float_as_uint(v);
+    if ((u & 0x7fffffffu) > 0x7f800000u) {
+        return 0ull;  // NaN: never a candidate
+    }
+    if ((u & 0x7fffffffu) == 0u) {
+        u = 0u;  // -0 == +0
+    }
+    const uint32_t ord = (u & 0x80000000u) ? ~u : (u | 0x80000000u);
+    return (static_cast<unsigned long long>(ord) << 32) | static_cast<unsigned long long>(0xffffffffu - index);
+}
+
+__device__ __forceinline__ unsigned long long umax64(unsigned long long a, unsigned long long b) {
+    return a > b ? a : b;
+}
+
+template <typename T>
+__device__ __forceinline__ unsigned long long scan_vector(uint4 raw, uint32_t first, unsigned long long best) {
+    using V = Vec16<T>;
+    float f[V::kVec];
+    V::unpack(raw, f);
+#pragma unroll
+    for (int j = 0; j < V::kVec; ++j) {
+        best = umax64(best, argmax_key(f[j], first + j));
+    }
+    return best;
+}
+
+template <typename T>
+__global__ void __launch_bounds__(kThreads) row_argmax_kernel(const void* __restrict__ x, int64_t cols,
+                                                              int64_t row_stride, int64_t* __restrict__ out,
+                                                              bool vector_ok) {
+    using V = Vec16<T>;
+    constexpr int kVec = V::kVec;
+    __shared__ unsigned long long warp_best[kWarps];
+    __shared__ unsigned long long cta_best;
+
+    cg::cluster_group cluster = cg::this_cluster();
+    const unsigned rank = cluster.block_rank();
+    const unsigned csize = cluster.num_blocks();
+    const int64_t row = blockIdx.x / csize;
+    const char* xr = static_cast<const char*>(x) + row * row_stride * static_cast<int64_t>(sizeof(T));
+
+    // Column range of this CTA, cut at 16-byte vector boundaries.
+    const int64_t per_cta = ((cols + csize - 1) / csize + kVec - 1) / kVec * kVec;
+    const int64_t lo = per_cta * rank;
+    const int64_t hi = lo + per_cta < cols ? lo + per_cta : cols;
+
+    unsigned long long best = 0ull;
+    if (lo < hi) {
+        if (vector_ok) {
+            const int64_t nvec = (hi - lo) / kVec;
+            const char* base = xr + lo * static_cast<int64_t>(sizeof(T));
+            int64_t v = threadIdx.x;
+            for (; v + (kUnroll - 1) * kThreads < nvec; v += kUnroll * kThreads) {
+                uint4 raw[kUnroll];
+#pragma unroll
+                for (int u = 0; u < kUnroll; ++u) {
+                    raw[u] = ld_stream(base + (v + u * kThreads) * 16);
+                }
+#pragma unroll
+                for (int u = 0; u < kUnroll; ++u) {
+                    best = scan_vector<T>(raw[u], static_cast<uint32_t>(lo + (v + u * kThreads) * kVec), best);
+                }
+            }
+            for (; v < nvec; v += kThreads) {
+                best = scan_vector<T>(ld_stream(base + v * 16), static_cast<uint32_t>(lo + v * kVec), best);
+            }
+            for (int64_t e = lo + nvec * kVec + threadIdx.x; e < hi; e += kThreads) {
+                best = umax64(best, argmax_key(V::load1(xr, e), static_cast<uint32_t>(e)));
+            }
+        } else {
+            for (int64_t e = lo + threadIdx.x; e < hi; e += kThreads) {
+                best = umax64(best, argmax_key(V::load1(xr, e), static_cast<uint32_t>(e)));
+            }
+        }
+    }
+
+#pragma unroll
+    for (int offset = 16; offset > 0; offset >>= 1) {
+        best = umax64(best, __shfl_xor_sync(0xffffffffu, best, offset));
+    }
+    const int warp = threadIdx.x / 32;
+    if ((threadIdx.x & 31) == 0) {
+        warp_best[warp] = best;
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        unsigned long long b = warp_best[0];
+#pragma unroll
+        for (int w = 1; w < kWarps; ++w) {
+            b = umax64(b, warp_best[w]);
+        }
+        cta_best = b;
+    }
+    // Make every CTA's cta_best visible to the cluster, then let rank 0 combine them over DSMEM.
+    cluster.sync();
+    if (rank == 0 && threadIdx.x == 0) {
+        unsigned long long b = cta_best;
+        for (unsigned r = 1; r < csize; ++r) {
+            b = umax64(b, *cluster.map_shared_rank(&cta_best, r));
+        }
+        const float first = V::load1(xr, 0);
+        int64_t index = 0;
+        if (first == first && b != 0ull) {
+            index = static_cast<int64_t>(0xffffffffu - static_cast<uint32_t>(b & 0xffffffffull));
+        }
+        out[row] = index;
+    }
+    // Keep every CTA (and its shared memory) alive until rank 0 has read it.
+    cluster.sync();
+}
+
+}  // namespace
+}  // namespace cppinf::device
+
+using namespace cppinf::device;
+namespace rt = cppinf::runtime;
+
+extern "C" {
+
+int cppinf_row_argmax(cppinf_dtype dtype, const void* x, int64_t rows, int64_t cols, int64_t row_stride,
+                      int64_t* out, void* stream) {
+    CPPINF_REQUIRE(rt::valid_dtype(dtype), CPPINF_ERR_INVALID_ARGUMENT, "row_argmax received an unsupported dtype.");
+    CPPINF_REQUIRE(rows >= 0, CPPINF_ERR_INVALID_ARGUMENT, "logits sequence length must be non-negative.");
+    CPPINF_REQUIRE(cols > 0, CPPINF_ERR_INVALID_ARGUMENT, "logits vocab size must be non-zero.");
+    CPPINF_REQUIRE(cols < (int64_t{1} << 31), CPPINF_ERR_OVERFLOW, "row_argmax supports fewer than 2^31 columns.");
+    CPPINF_REQUIRE(rows <= 1 || row_stride >= cols, CPPINF_ERR_INVALID_ARGUMENT,
+                   "row_argmax requires a row stride of at least the column count.");
+    if (rows == 0) {
+        return rt::ok();
+    }
+    CPPINF_REQUIRE(x && out, CPPINF_ERR_INVALID_ARGUMENT, "row_argmax received a null pointer.");
+    CPPINF_REQUIRE(rows <= (int64_t{1} << 27), CPPINF_ERR_UNSUPPORTED, "row_argmax supports at most 2^27 rows.");
+    const int vec = dtype == CPPINF_DTYPE_BF16 ? 8 : 4;
+    const bool vector_ok = rt::aligned16(x) && (rows <= 1 || row_stride % vec == 0);
+
+    // Enough CTAs to cover the SMs a few times, but no CTA with fewer than ~2K columns.
+    const int64_t target_ctas = static_cast<int64_t>(rt::sm_count()) * 4;
+    int64_t cluster = 1;
+    while (cluster < kMaxCluster && rows * cluster < target_ctas && cols / (cluster * 2) >= 2048) {
+        cluster *= 2;
+    }
+
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(static_cast<unsigned>(rows * cluster), 1, 1);
+    cfg.blockDim = dim3(kThreads, 1, 1);
+    cfg.dynamicSmemBytes = 0;
+    cfg.stream = rt::as_stream(stream);
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = static_cast<unsigned>(cluster);
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    cudaError_t err;
+    if (dtype == CPPINF_DTYPE_BF16) {
+        err = cudaLaunchKernelEx(&cfg, row_argmax_kernel<bf16>, x, cols, row_stride, out, vector_ok);
+    } else {
+        err = cudaLaunchKernelEx(&cfg, row_argmax_kernel<float>, x, cols, row_stride, out, vector_ok);
+    }
+    if (err != cudaSuccess) {
+        return rt::cuda_fail(err, "cudaLaunchKernelEx(row_argmax)");
+    }
+    return rt::after_launch("row_argmax");
+}
+
+}  // extern "C"

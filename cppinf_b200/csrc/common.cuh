@@ -1,0 +1,149 @@
+// Shared device-side helpers for the cppinf_b200 kernels: 128-bit global loads/stores, bf16 <-> f32 conversion,
+// warp reductions and the launch bookkeeping every entry point uses.
+//
+// Numerics: every kernel in this library is compiled with --fmad=false, so each f32 multiply and add is rounded
+// separately, the same as the reference's x86-64 SSE code (built without -mfma). f32 -> bf16 conversion is IEEE
+// round-to-nearest-even (cvt.rn.bf16x2.f32), which equals the reference's `bits + 0x7fff + lsb` rounding
+// (src/tensors/bfloat16.cpp:8-15) for every non-NaN value. NaN stays NaN (the reference helper's payload-dependent
+// NaN handling is not reproduced).
+#pragma once
+
+#include <cuda_bf16.h>
+#include <cuda_runtime.h>
+
+#include <cstdint>
+
+namespace cppinf::device {
+
+using bf16 = __nv_bfloat16;
+
+// ---- 128-bit memory access -------------------------------------------------------------------------------------
+
+// Read-only, streaming load: bypasses L1 allocation (the data is touched once) and asks L2 for 256-byte sectors so
+// neighbouring warps' requests share DRAM bursts.
+__device__ __forceinline__ uint4 ld_stream(const void* ptr) {
+    uint4 r;
+    asm volatile("ld.global.nc.L1::no_allocate.L2::256B.v4.u32 {%0, %1, %2, %3}, [%4];"
+                 : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w)
+                 : "l"(ptr));
+    return r;
+}
+
+// Read-only load that is expected to hit in L1/L2 (norm weights, RoPE table rows).
+__device__ __forceinline__ uint4 ld_cached(const void* ptr) {
+    return __ldg(reinterpret_cast<const uint4*>(ptr));
+}
+
+__device__ __forceinline__ float4 ld_cached_f4(const float* ptr) {
+    return __ldg(reinterpret_cast<const float4*>(ptr));
+}
+
+// Plain 128-bit store.
+__device__ __forceinline__ void st_v4(void* ptr, uint4 v) {
+    asm volatile("st.global.v4.u32 [%0], {%1, %2, %3, %4};" ::"l"(ptr), "r"(v.x), "r"(v.y), "r"(v.z), "r"(v.w)
+                 : "memory");
+}
+
+// Streaming (evict-first) 128-bit store for outputs that are not read again by this kernel.
+__device__ __forceinline__ void st_stream(void* ptr, uint4 v) {
+    asm volatile("st.global.cs.v4.u32 [%0], {%1, %2, %3, %4};" ::"l"(ptr), "r"(v.x), "r"(v.y), "r"(v.z), "r"(v.w)
+                 : "memory");
+}
+
+// ---- bf16 / f32 packing ------------------------------------------------------------------------------------------
+
+__device__ __forceinline__ float bf16_lo(uint32_t packed) {
+    return __uint_as_float(packed << 16);
+}
+
+__device__ __forceinline__ float bf16_hi(uint32_t packed) {
+    return __uint_as_float(packed & 0xffff0000u);
+}
+
+// Packs two f32 values into a bf16x2 word (lo in the low half), round-to-nearest-even.
+__device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
+    uint32_t r;
+    asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(r) : "f"(hi), "f"(lo));
+    return r;
+}
+
+__device__ __forceinline__ float round_to_bf16(float v) {
+    return bf16_lo(pack_bf16x2(v, 0.0f));
+}
+
+// Element traits: a 16-byte vector holds kVec elements of T, read or written as f32.
+template <typename T>
+struct Vec16;
+
+template <>
+struct Vec16<bf16> {
+    static constexpr int kVec = 8;
+    __device__ __forceinline__ static void unpack(uint4 v, float (&f)[8]) {
+        f[0] = bf16_lo(v.x);
+        f[1] = bf16_hi(v.x);
+        f[2] = bf16_lo(v.y);
+        f[3] = bf16_hi(v.y);
+        f[4] = bf16_lo(v.z);
+        f[5] = bf16_hi(v.z);
+        f[6] = bf16_lo(v.w);
+        f[7] = bf16_hi(v.w);
+    }
+    __device__ __forceinline__ static uint4 pack(const float (&f)[8]) {
+        return make_uint4(pack_bf16x2(f[0], f[1]), pack_bf16x2(f[2], f[3]), pack_bf16x2(f[4], f[5]),
+                          pack_bf16x2(f[6], f[7]));
+    }
+    // Value as stored: rounds f32 to bf16 and back.
+    __device__ __forceinline__ static float quantize(float v) { return round_to_bf16(v); }
+    __device__ __forceinline__ static float load1(const void* base, int64_t i) {
+        const uint16_t bits = __ldg(reinterpret_cast<const unsigned short*>(base) + i);
+        return __uint_as_float(static_cast<uint32_t>(bits) << 16);
+    }
+    __device__ __forceinline__ static void store1(void* base, int64_t i, float v) {
+        reinterpret_cast<unsigned short*>(base)[i] = static_cast<unsigned short>(pack_bf16x2(v, 0.0f) & 0xffffu);
+    }
+};
+
+template <>
+struct Vec16<float> {
+    static constexpr int kVec = 4;
+    __device__ __forceinline__ static void unpack(uint4 v, float (&f)[4]) {
+        f[0] = __uint_as_float(v.x);
+        f[1] = __uint_as_float(v.y);
+        f[2] = __uint_as_float(v.z);
+        f[3] = __uint_as_float(v.w);
+    }
+    __device__ __forceinline__ static uint4 pack(const float (&f)[4]) {
+        return make_uint4(__float_as_uint(f[0]), __float_as_uint(f[1]), __float_as_uint(f[2]), __float_as_uint(f[3]));
+    }
+    __device__ __forceinline__ static float quantize(float v) { return v; }
+    __device__ __forceinline__ static float load1(const void* base, int64_t i) {
+        return __ldg(reinterpret_cast<const float*>(base) + i);
+    }
+    __device__ __forceinline__ static void store1(void* base, int64_t i, float v) {
+        reinterpret_cast<float*>(base)[i] = v;
+    }
+};
+
+// ---- warp reductions ---------------------------------------------------------------------------------------------
+
+// Butterfly sum over groups of `kLanes` consecutive lanes (a power of two <= 32). Every lane of a group ends with
+// the same bits: step s adds the partner's partial, and f32 addition is commutative, so partners agree.
+template <int kLanes>
+__device__ __forceinline__ float group_sum(float v) {
+#pragma unroll
+    for (int offset = kLanes / 2; offset > 0; offset >>= 1) {
+        v = v + __shfl_xor_sync(0xffffffffu, v, offset);
+    }
+    return v;
+}
+
+template <int kLanes>
+__device__ __forceinline__ float group_max(float v) {
+#pragma unroll
+    for (int offset = kLanes / 2; offset > 0; offset >>= 1) {
+        v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, offset));
+    }
+    return v;
+}
+
+}  // namespace cppinf::device

@@ -1,0 +1,325 @@
+// Split-half RoPE, nn::apply_rope (src/nn/rope.cpp:73-124), and the fused per-head q/k RMSNorm + RoPE that the
+// attention block runs (src/nn/qwen_attention.cpp:383-390: ops::rms_norm on [B, T, H, D] head views, result rounded
+// to the model dtype, then apply_rope_batched at position cache_length + t).
+//
+// Angles: the reference evaluates powf/cosf/sinf on the host for every (head, token, pair). Here the host builds the
+// same values once into a [positions][D] f32 table (cos in [0, D/2), sin in [D/2, D)) with the same libm calls, and
+// the kernels read the row of the token's position. Device results therefore equal the reference's bit for bit: the
+// rotation first*cos - second*sin / second*cos + first*sin is evaluated with separately rounded f32 products and
+// sums (the library is built with --fmad=false).
+//
+// Fused kernel layout: q [T, Hq, D] and k [T, Hk, D] dense; one head vector (D elements) is held by D/kVec lanes,
+// one 16-byte vector each, so a warp covers 32*kVec/D head vectors. The RMSNorm reduction is a butterfly inside the
+// head's lane group (the library's canonical order: lane l owns chunk l). The split-half partner of chunk l is
+// chunk l ^ (lanes/2), fetched with one shuffle per element.
+//
+// Roofline: HBM-bound. Algorithmic bytes per token: (Hq + Hk) * D * size read + the same written; the table row
+// (D * 4 bytes per position) and the two weight vectors are shared by all heads and come from L1/L2.
+#include <cmath>
+#include <vector>
+
+#include "common.cuh"
+#include "runtime.h"
+
+namespace cppinf::device {
+namespace {
+
+constexpr int kThreads = 256;
+constexpr int kWarps = kThreads / 32;
+
+struct QkParams {
+    const void* q;
+    const void* k;
+    const void* qw;
+    const void* kw;
+    void* q_out;
+    void* k_out;
+    const float* table;
+    int64_t tokens;
+    int64_t position_offset;
+    int q_heads;
+    int k_heads;
+    float eps;
+};
+
+template <typename T, int kLanes>
+__global__ void __launch_bounds__(kThreads) qk_norm_rope_kernel(QkParams p) {
+    using V = Vec16<T>;
+    constexpr int kVec = V::kVec;
+    constexpr int kDim = kLanes * kVec;
+    constexpr int kHalf = kDim / 2;
+    constexpr int kHeadsPerWarp = 32 / kLanes;
+    const int lane = threadIdx.x & 31;
+    const int hl = lane % kLanes;        // lane within the head group
+    const int group = lane / kLanes;     // head slot within the warp
+    const int heads = p.q_heads + p.k_heads;
+    const int64_t total = p.tokens * heads;
+    const int64_t warp_global = static_cast<int64_t>(blockIdx.x) * kWarps + threadIdx.x / 32;
+    const int64_t hv = warp_global * kHeadsPerWarp + group;
+    const bool active = hv < total;
+
+    int64_t t = 0;
+    const char* src = nullptr;
+    char* dst = nullptr;
+    const char* wsrc = nullptr;
+    if (active) {
+        t = hv / heads;
+        const int h = static_cast<int>(hv - t * heads);
+        if (h < p.q_heads) {
+            const int64_t off = (t * p.q_heads + h) * kDim * static_cast<int64_t>(sizeof(T));
+            src = static_cast<const char*>(p.q) + off;
+            dst = static_cast<char*>(p.q_out) + off;
+            wsrc = static_cast<const char*>(p.qw);
+        } else {
+            const int64_t off = (t * p.k_heads + (h - p.q_heads)) * kDim * static_cast<int64_t>(sizeof(T));
+            src = static_cast<const char*>(p.k) + off;
+            dst = static_cast<char*>(p.k_out) + off;
+            wsrc = static_cast<const char*>(p.kw);
+        }
+    }
+
+    float x[kVec];
+    float ss = 0.0f;
+    if (active) {
+        V::unpack(ld_stream(src + hl * 16), x);
+#pragma unroll
+        for (int j = 0; j < kVec; ++j) {
+            ss = ss + x[j] * x[j];
+        }
+    } else {
+#pragma unroll
+        for (int j = 0; j < kVec; ++j) {
+            x[j] = 0.0f;
+        }
+    }
+    // All 32 lanes take part in the shuffles; groups never exchange data because every offset is < kLanes.
+    ss = group_sum<kLanes>(ss);
+    const float mean = ss / static_cast<float>(kDim);
+    const float rms = sqrtf(mean + p.eps);
+    const float inv = 1.0f / rms;
+
+    float n[kVec];
+    if (active) {
+        float w[kVec];
+        V::unpack(ld_cached(wsrc + hl * 16), w);
+#pragma unroll
+        for (int j = 0; j < kVec; ++j) {
+            // The reference's rms_norm returns a tensor of the model dtype; RoPE reads those rounded values.
+            n[j] = V::quantize((x[j] * inv) * w[j]);
+        }
+    } else {
+#pragma unroll
+        for (int j = 0; j < kVec; ++j) {
+            n[j] = 0.0f;
+        }
+    }
+
+    float partner[kVec];
+#pragma unroll
+    for (int j = 0; j < kVec; ++j) {
+        partner[j] = __shfl_xor_sync(0xffffffffu, n[j], kLanes / 2);
+    }
+
+    if (active) {
+        const bool first_half = hl < kLanes / 2;
+        const int pair0 = (first_half ? hl : hl - kLanes / 2) * kVec;
+        const float* row = p.table + (p.position_offset + t) * kDim;
+        float c[kVec];
+        float s[kVec];
+#pragma unroll
+        for (int j = 0; j < kVec; j += 4) {
+            const float4 cv = ld_cached_f4(row + pair0 + j);
+            const float4 sv = ld_cached_f4(row + kHalf + pair0 + j);
+            c[j] = cv.x;
+            c[j + 1] = cv.y;
+            c[j + 2] = cv.z;
+            c[j + 3] = cv.w;
+            s[j] = sv.x;
+            s[j + 1] = sv.y;
+            s[j + 2] = sv.z;
+            s[j + 3] = sv.w;
+        }
+        float out[kVec];
+#pragma unroll
+        for (int j = 0; j < kVec; ++j) {
+            // first  = first * cos - second * sin   (src/nn/rope.cpp:115-116)
+            // second = second * cos + first * sin   (src/nn/rope.cpp:117-118)
+            out[j] = first_half ? (n[j] * c[j] - partner[j] * s[j]) : (n[j] * c[j] + partner[j] * s[j]);
+        }
+        st_stream(dst + hl * 16, V::pack(out));
+    }
+}
+
+struct RopeParams {
+    const void* x;
+    void* y;
+    const float* table;
+    int64_t dim0, dim1;
+    int64_t s0, s1, s2;
+    int64_t position_offset;
+    int head_dim;
+    int seq_dim;
+};
+
+// Standalone apply_rope on a strided rank-3 view: one thread per (dim0, dim1, pair).
+template <typename T>
+__global__ void __launch_bounds__(kThreads) rope_kernel(RopeParams p, int64_t total_pairs) {
+    using V = Vec16<T>;
+    const int half = p.head_dim / 2;
+    const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
+    for (int64_t idx = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; idx < total_pairs;
+         idx += stride) {
+        const int pair = static_cast<int>(idx % half);
+        const int64_t r = idx / half;
+        const int64_t i1 = r % p.dim1;
+        const int64_t i0 = r / p.dim1;
+        const int64_t seq = p.seq_dim == 0 ? i0 : i1;
+        const float* row = p.table + (p.position_offset + seq) * p.head_dim;
+        const float c = __ldg(row + pair);
+        const float s = __ldg(row + half + pair);
+        const int64_t base = i0 * p.s0 + i1 * p.s1;
+        const float first = V::load1(p.x, base + pair * p.s2);
+        const float second = V::load1(p.x, base + (pair + half) * p.s2);
+        const int64_t out_base = r * p.head_dim;
+        V::store1(p.y, out_base + pair, first * c - second * s);
+        V::store1(p.y, out_base + pair + half, second * c + first * s);
+    }
+}
+
+template <typename T, int kLanes>
+void launch_qk(const QkParams& p, cudaStream_t s) {
+    constexpr int kHeadsPerBlock = kWarps * (32 / kLanes);
+    const int64_t total = p.tokens * (p.q_heads + p.k_heads);
+    const auto blocks = static_cast<unsigned>(runtime::ceil_div(total, kHeadsPerBlock));
+    qk_norm_rope_kernel<T, kLanes><<<blocks, kThreads, 0, s>>>(p);
+}
+
+template <typename T>
+bool dispatch_qk(const QkParams& p, int lanes, cudaStream_t s) {
+    switch (lanes) {
+    case 2:
+        launch_qk<T, 2>(p, s);
+        return true;
+    case 4:
+        launch_qk<T, 4>(p, s);
+        return true;
+    case 8:
+        launch_qk<T, 8>(p, s);
+        return true;
+    case 16:
+        launch_qk<T, 16>(p, s);
+        return true;
+    case 32:
+        launch_qk<T, 32>(p, s);
+        return true;
+    default:
+        return false;
+    }
+}
+
+}  // namespace
+}  // namespace cppinf::device
+
+using namespace cppinf::device;
+namespace rt = cppinf::runtime;
+
+extern "C" {
+
+int cppinf_rope_table(float base, int64_t head_dim, int64_t positions, float* table) {
+    CPPINF_REQUIRE(std::isfinite(base) && base > 0.0f, CPPINF_ERR_INVALID_ARGUMENT,
+                   "apply_rope requires a positive finite rope base.");
+    CPPINF_REQUIRE(head_dim > 0, CPPINF_ERR_INVALID_ARGUMENT, "rope head size must be non-zero.");
+    CPPINF_REQUIRE(head_dim % 2 == 0, CPPINF_ERR_INVALID_ARGUMENT, "apply_rope requires an even head size.");
+    CPPINF_REQUIRE(positions >= 0, CPPINF_ERR_INVALID_ARGUMENT, "rope table positions must be non-negative.");
+    CPPINF_REQUIRE(positions == 0 || table, CPPINF_ERR_INVALID_ARGUMENT, "rope table received a null pointer.");
+    const int64_t half = head_dim / 2;
+    // One inverse frequency per feature pair, as src/nn/rope.cpp:85-90 computes it.
+    std::vector<float> inverse_frequencies(static_cast<std::size_t>(half));
+    for (int64_t i = 0; i < half; ++i) {
+        inverse_frequencies[static_cast<std::size_t>(i)] =
+            std::pow(base, -static_cast<float>(i) / static_cast<float>(half));
+    }
+    for (int64_t pos = 0; pos < positions; ++pos) {
+        const auto position = static_cast<float>(pos);
+        float* row = table + pos * head_dim;
+        for (int64_t i = 0; i < half; ++i) {
+            const float angle = position * inverse_frequencies[static_cast<std::size_t>(i)];
+            row[i] = std::cos(angle);
+            row[half + i] = std::sin(angle);
+        }
+    }
+    return rt::ok();
+}
+
+int cppinf_rope(cppinf_dtype dtype, const void* x, int64_t dim0, int64_t dim1, int64_t head_dim, int64_t s0,
+                int64_t s1, int64_t s2, int64_t seq_dim, int64_t position_offset, const float* table,
+                int64_t table_positions, void* y, void* stream) {
+    CPPINF_REQUIRE(rt::valid_dtype(dtype), CPPINF_ERR_INVALID_ARGUMENT, "apply_rope received an unsupported dtype.");
+    CPPINF_REQUIRE(seq_dim == 0 || seq_dim == 1, CPPINF_ERR_INVALID_ARGUMENT,
+                   "apply_rope requires the sequence dimension to be 0 or 1.");
+    CPPINF_REQUIRE(dim0 > 0, CPPINF_ERR_INVALID_ARGUMENT, "rope dim 0 must be non-zero.");
+    CPPINF_REQUIRE(dim1 > 0, CPPINF_ERR_INVALID_ARGUMENT, "rope dim 1 must be non-zero.");
+    CPPINF_REQUIRE(head_dim > 0, CPPINF_ERR_INVALID_ARGUMENT, "rope head size must be non-zero.");
+    CPPINF_REQUIRE(head_dim % 2 == 0, CPPINF_ERR_INVALID_ARGUMENT, "apply_rope requires an even head size.");
+    CPPINF_REQUIRE(head_dim <= (int64_t{1} << 30), CPPINF_ERR_UNSUPPORTED, "apply_rope head size is too large.");
+    CPPINF_REQUIRE(s0 >= 0 && s1 >= 0 && s2 >= 0, CPPINF_ERR_INVALID_ARGUMENT,
+                   "apply_rope strides must be non-negative.");
+    CPPINF_REQUIRE(position_offset >= 0, CPPINF_ERR_INVALID_ARGUMENT, "apply_rope position offset must be >= 0.");
+    const int64_t seq_len = seq_dim == 0 ? dim0 : dim1;
+    CPPINF_REQUIRE(position_offset + seq_len <= table_positions, CPPINF_ERR_OUT_OF_RANGE,
+                   "apply_rope positions exceed the rope table.");
+    CPPINF_REQUIRE(x && y && table, CPPINF_ERR_INVALID_ARGUMENT, "apply_rope received a null pointer.");
+    RopeParams p{x, y, table, dim0, dim1, s0, s1, s2, position_offset, static_cast<int>(head_dim),
+                 static_cast<int>(seq_dim)};
+    const int64_t total_pairs = dim0 * dim1 * (head_dim / 2);
+    const int64_t per_sm = rt::max_threads_per_sm() / kThreads;
+    const int64_t wave = static_cast<int64_t>(rt::sm_count()) * (per_sm > 0 ? per_sm : 1);
+    const int64_t needed = rt::ceil_div(total_pairs, kThreads);
+    const auto blocks = static_cast<unsigned>(needed < wave ? needed : wave);
+    if (dtype == CPPINF_DTYPE_BF16) {
+        rope_kernel<bf16><<<blocks, kThreads, 0, rt::as_stream(stream)>>>(p, total_pairs);
+    } else {
+        rope_kernel<float><<<blocks, kThreads, 0, rt::as_stream(stream)>>>(p, total_pairs);
+    }
+    return rt::after_launch("rope");
+}
+
+int cppinf_qk_norm_rope(cppinf_dtype dtype, const void* q, const void* k, const void* q_weight,
+                        const void* k_weight, void* q_out, void* k_out, int64_t tokens, int64_t q_heads,
+                        int64_t k_heads, int64_t head_dim, int64_t position_offset, float eps, const float* table,
+                        int64_t table_positions, void* stream) {
+    CPPINF_REQUIRE(rt::valid_dtype(dtype), CPPINF_ERR_INVALID_ARGUMENT, "qk_norm_rope received an unsupported dtype.");
+    CPPINF_REQUIRE(tokens >= 0 && q_heads >= 0 && k_heads >= 0, CPPINF_ERR_INVALID_ARGUMENT,
+                   "qk_norm_rope requires non-negative sizes.");
+    CPPINF_REQUIRE(q_heads + k_heads <= (int64_t{1} << 20), CPPINF_ERR_UNSUPPORTED,
+                   "qk_norm_rope supports at most 2^20 heads.");
+    CPPINF_REQUIRE(head_dim > 0, CPPINF_ERR_INVALID_ARGUMENT, "rms_norm requires a non-empty last dimension.");
+    CPPINF_REQUIRE(head_dim % 2 == 0, CPPINF_ERR_INVALID_ARGUMENT, "apply_rope requires an even head size.");
+    CPPINF_REQUIRE(eps >= 0.0f, CPPINF_ERR_INVALID_ARGUMENT, "rms_norm requires a non-negative epsilon.");
+    CPPINF_REQUIRE(position_offset >= 0, CPPINF_ERR_INVALID_ARGUMENT, "qk_norm_rope position offset must be >= 0.");
+    CPPINF_REQUIRE(position_offset + tokens <= table_positions, CPPINF_ERR_OUT_OF_RANGE,
+                   "qk_norm_rope positions exceed the rope table.");
+    const int vec = dtype == CPPINF_DTYPE_BF16 ? 8 : 4;
+    const int64_t lanes = head_dim / vec;
+    CPPINF_REQUIRE(head_dim % (2 * vec) == 0 && lanes >= 2 && lanes <= 32 && (lanes & (lanes - 1)) == 0,
+                   CPPINF_ERR_UNSUPPORTED,
+                   "qk_norm_rope needs head_dim / (16 / element size) to be a power of two between 2 and 32.");
+    if (tokens == 0 || q_heads + k_heads == 0) {
+        return rt::ok();
+    }
+    CPPINF_REQUIRE(table && (q_heads == 0 || (q && q_weight && q_out)) && (k_heads == 0 || (k && k_weight && k_out)),
+                   CPPINF_ERR_INVALID_ARGUMENT, "qk_norm_rope received a null pointer.");
+    CPPINF_REQUIRE(rt::aligned16(table) && (q_heads == 0 || (rt::aligned16(q) && rt::aligned16(q_weight) &&
+                                                             rt::aligned16(q_out))) &&
+                       (k_heads == 0 || (rt::aligned16(k) && rt::aligned16(k_weight) && rt::aligned16(k_out))),
+                   CPPINF_ERR_UNSUPPORTED, "qk_norm_rope requires 16-byte aligned operands.");
+    QkParams p{q,      k,        q_weight,        k_weight, q_out, k_out, table, tokens, position_offset,
+               static_cast<int>(q_heads), static_cast<int>(k_heads), eps};
+    const auto s = rt::as_stream(stream);
+    const bool launched = dtype == CPPINF_DTYPE_BF16 ? dispatch_qk<bf16>(p, static_cast<int>(lanes), s)
+                                                     : dispatch_qk<float>(p, static_cast<int>(lanes), s);
+    CPPINF_REQUIRE(launched, CPPINF_ERR_UNSUPPORTED, "qk_norm_rope has no kernel for this head size.");
+    return rt::after_launch("qk_norm_rope");
+}
+
+}  // extern "C"

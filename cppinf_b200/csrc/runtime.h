@@ -1,0 +1,69 @@
+// Host-side bookkeeping shared by the C ABI entry points: thread-local error messages, status propagation, launch
+// accounting and cached device properties.
+#pragma once
+
+#include <cuda_runtime.h>
+
+#include <atomic>
+#include <cstdint>
+#include <string>
+
+#include "cppinf_b200.h"
+
+namespace cppinf::runtime {
+
+// Records `message` as the calling thread's last error and returns `status`.
+int fail(int status, const std::string& message);
+
+// Clears the calling thread's last error and returns CPPINF_OK.
+int ok();
+
+// Converts a failed CUDA call into CPPINF_ERR_CUDA with the call site in the message.
+int cuda_fail(cudaError_t err, const char* what);
+
+// Checks the launch that was just enqueued and counts it.
+int after_launch(const char* kernel_name);
+
+// Number of SMs of the current device (cached per device).
+int sm_count();
+
+// Largest number of threads per SM of the current device (cached per device).
+int max_threads_per_sm();
+
+inline bool aligned16(const void* p) {
+    return (reinterpret_cast<std::uintptr_t>(p) & 15u) == 0;
+}
+
+inline cudaStream_t as_stream(void* stream) {
+    return static_cast<cudaStream_t>(stream);
+}
+
+inline int64_t ceil_div(int64_t a, int64_t b) {
+    return (a + b - 1) / b;
+}
+
+inline std::size_t dtype_size(cppinf_dtype dtype) {
+    return dtype == CPPINF_DTYPE_BF16 ? 2 : 4;
+}
+
+inline bool valid_dtype(cppinf_dtype dtype) {
+    return dtype == CPPINF_DTYPE_BF16 || dtype == CPPINF_DTYPE_F32;
+}
+
+}  // namespace cppinf::runtime
+
+// Early-return helpers for entry points.
+#define CPPINF_REQUIRE(cond, status, msg)                  \
+    do {                                                   \
+        if (!(cond)) {                                     \
+            return ::cppinf::runtime::fail((status), (msg)); \
+        }                                                  \
+    } while (0)
+
+#define CPPINF_CUDA_TRY(call)                                            \
+    do {                                                                 \
+        const cudaError_t cppinf_err_ = (call);                          \
+        if (cppinf_err_ != cudaSuccess) {                                \
+            return ::cppinf::runtime::cuda_fail(cppinf_err_, #call);     \
+        }                                                                \
+    } while (0)

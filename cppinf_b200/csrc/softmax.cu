@@ -1,0 +1,284 @@
+// Row softmax kernels:
+//  - ops::softmax_last_dim (src/ops/nn_ops.cpp:74-99, oneDNN softmax_accurate), bf16 or f32 in and out;
+//  - ops::scaled_causal_softmax_last_dim (src/ops/nn_ops.cpp:101-162), f32 [matrices, Q, K] with Q == K;
+//  - the position-aware variant of attention, scaled_position_causal_softmax_last_dim
+//    (src/nn/qwen_attention.cpp:164-235), f32 [batch, heads, Qcap, Kcap] with per-batch offsets and lengths.
+//
+// One warp owns one row. Only the visible prefix of a row is read (16-byte vectors into registers); the whole row is
+// written, masked columns included. Per row, following the reference: m = max over visible k of (x*scale),
+// e_k = exp(x_k*scale - m) for visible k and 0 otherwise, sum = sum of e, out_k = e_k / sum. Masked columns hold
+// 0 / sum, which is 0 unless the sum is NaN, as in the reference's division loop. The position-aware variant writes
+// 0 everywhere when the sum is 0 (a row with no visible key, or a query row past the query length).
+//
+// The sum is a per-lane partial followed by a butterfly, so it differs from the reference's left-to-right f32 sum
+// only by rounding (f32 results agree to about 1e-6 relative). exp is CUDA's expf (max 2 ulp), the reference's
+// std::exp is glibc expf.
+//
+// Roofline: HBM-bound. Algorithmic bytes per row: visible elements read + the full row written.
+#include <cmath>
+
+#include "common.cuh"
+#include "runtime.h"
+
+namespace cppinf::device {
+namespace {
+
+constexpr int kThreads = 256;
+constexpr int kWarps = kThreads / 32;
+constexpr int kMaxBatch = 64;
+
+// Visibility rules: visible(row) is the number of leading visible columns, zero_row(row) says whether the row is
+// written as zeros regardless of the sum.
+struct FullRows {
+    int64_t width;
+    __device__ __forceinline__ int64_t visible(int64_t) const { return width; }
+    static constexpr bool kZeroOnEmpty = false;
+};
+
+struct SquareCausalRows {
+    int64_t query_len;
+    __device__ __forceinline__ int64_t visible(int64_t row) const { return row % query_len + 1; }
+    static constexpr bool kZeroOnEmpty = false;
+};
+
+struct PositionCausalRows {
+    int64_t query_cap;
+    int64_t key_cap;
+    int64_t heads;
+    int64_t query_offsets[kMaxBatch];
+    int64_t query_lengths[kMaxBatch];
+    int64_t key_lengths[kMaxBatch];
+    __device__ __forceinline__ int64_t visible(int64_t row) const {
+        const int64_t q = row % query_cap;
+        const int64_t b = row / query_cap / heads;
+        if (q >= query_lengths[b]) {
+            return 0;
+        }
+        const int64_t causal = query_offsets[b] + q + 1;
+        const int64_t keys = key_lengths[b];
+        return causal < keys ? causal : keys;
+    }
+    static constexpr bool kZeroOnEmpty = true;
+};
+
+template <typename T, int kChunks, typename Rows>
+__global__ void __launch_bounds__(kThreads) softmax_regs_kernel(const void* __restrict__ x, void* __restrict__ y,
+                                                                int64_t rows, int64_t width, float scale, Rows rule) {
+    using V = Vec16<T>;
+    constexpr int kVec = V::kVec;
+    const int lane = threadIdx.x & 31;
+    const int64_t warp_stride = static_cast<int64_t>(gridDim.x) * kWarps;
+    const int nchunks = static_cast<int>(width / kVec);
+
+    for (int64_t row = static_cast<int64_t>(blockIdx.x) * kWarps + threadIdx.x / 32; row < rows; row += warp_stride) {
+        const int64_t n = rule.visible(row);
+        const int vis_chunks = static_cast<int>((n + kVec - 1) / kVec);
+        const char* xr = static_cast<const char*>(x) + row * width * static_cast<int64_t>(sizeof(T));
+        char* yr = static_cast<char*>(y) + row * width * static_cast<int64_t>(sizeof(T));
+
+        float v[kChunks][kVec];
+        uint4 raw[kChunks];
+#pragma unroll
+        for (int i = 0; i < kChunks; ++i) {
+            const int c = lane + 32 * i;
+            if (c < vis_chunks) {
+                raw[i] = ld_stream(xr + static_cast<int64_t>(c) * 16);
+            }
+        }
+        float m = -INFINITY;
+#pragma unroll
+        for (int i = 0; i < kChunks; ++i) {
+            const int c = lane + 32 * i;
+            if (c < vis_chunks) {
+                V::unpack(raw[i], v[i]);
+#pragma unroll
+                for (int j = 0; j < kVec; ++j) {
+                    const int64_t k = static_cast<int64_t>(c) * kVec + j;
+                    v[i][j] = k < n ? v[i][j] * scale : -INFINITY;
+                    m = fmaxf(m, v[i][j]);
+                }
+            }
+        }
+        m = group_max<32>(m);
+
+        float sum = 0.0f;
+#pragma unroll
+        for (int i = 0; i < kChunks; ++i) {
+            const int c = lane + 32 * i;
+            if (c < vis_chunks) {
+#pragma unroll
+                for (int j = 0; j < kVec; ++j) {
+                    const int64_t k = static_cast<int64_t>(c) * kVec + j;
+                    v[i][j] = k < n ? expf(v[i][j] - m) : 0.0f;
+                    sum = sum + v[i][j];
+                }
+            }
+        }
+        sum = group_sum<32>(sum);
+        const bool zero_row = Rows::kZeroOnEmpty && sum == 0.0f;
+        const float masked = zero_row ? 0.0f : 0.0f / sum;
+
+#pragma unroll
+        for (int i = 0; i < kChunks; ++i) {
+            const int c = lane + 32 * i;
+            if (c < nchunks) {
+                float out[kVec];
+                if (c < vis_chunks) {
+#pragma unroll
+                    for (int j = 0; j < kVec; ++j) {
+                        const int64_t k = static_cast<int64_t>(c) * kVec + j;
+                        out[j] = k < n ? (zero_row ? 0.0f : v[i][j] / sum) : masked;
+                    }
+                } else {
+#pragma unroll
+                    for (int j = 0; j < kVec; ++j) {
+                        out[j] = masked;
+                    }
+                }
+                st_stream(yr + static_cast<int64_t>(c) * 16, V::pack(out));
+            }
+        }
+    }
+}
+
+// Any width or alignment: three passes over the row (max, sum, write), element by element. Later passes re-read
+// the row from L2.
+template <typename T, typename Rows>
+__global__ void __launch_bounds__(kThreads) softmax_stream_kernel(const void* __restrict__ x, void* __restrict__ y,
+                                                                  int64_t rows, int64_t width, float scale,
+                                                                  Rows rule) {
+    using V = Vec16<T>;
+    const int lane = threadIdx.x & 31;
+    const int64_t warp_stride = static_cast<int64_t>(gridDim.x) * kWarps;
+    for (int64_t row = static_cast<int64_t>(blockIdx.x) * kWarps + threadIdx.x / 32; row < rows; row += warp_stride) {
+        const int64_t n = rule.visible(row);
+        const int64_t base = row * width;
+        float m = -INFINITY;
+        for (int64_t k = lane; k < n; k += 32) {
+            m = fmaxf(m, V::load1(x, base + k) * scale);
+        }
+        m = group_max<32>(m);
+        float sum = 0.0f;
+        for (int64_t k = lane; k < n; k += 32) {
+            sum = sum + expf(V::load1(x, base + k) * scale - m);
+        }
+        sum = group_sum<32>(sum);
+        const bool zero_row = Rows::kZeroOnEmpty && sum == 0.0f;
+        const float masked = zero_row ? 0.0f : 0.0f / sum;
+        for (int64_t k = lane; k < width; k += 32) {
+            float out = masked;
+            if (k < n && !zero_row) {
+                out = expf(V::load1(x, base + k) * scale - m) / sum;
+            }
+            V::store1(y, base + k, out);
+        }
+    }
+}
+
+template <typename T, typename Rows>
+int launch_softmax(const void* x, void* y, int64_t rows, int64_t width, float scale, const Rows& rule, void* stream,
+                   const char* name) {
+    constexpr int kVec = Vec16<T>::kVec;
+    const int64_t per_sm = runtime::max_threads_per_sm() / kThreads;
+    const int64_t wave = static_cast<int64_t>(runtime::sm_count()) * (per_sm > 0 ? per_sm : 1) * 4;
+    const int64_t needed = runtime::ceil_div(rows, kWarps);
+    const auto blocks = static_cast<unsigned>(needed < wave ? needed : wave);
+    const auto s = runtime::as_stream(stream);
+    const bool vector_ok = width % kVec == 0 && runtime::aligned16(x) && runtime::aligned16(y);
+    const int64_t per_lane = runtime::ceil_div(width / kVec, 32);
+    if (vector_ok && per_lane <= 16) {
+        if (per_lane <= 1) {
+            softmax_regs_kernel<T, 1, Rows><<<blocks, kThreads, 0, s>>>(x, y, rows, width, scale, rule);
+        } else if (per_lane <= 2) {
+            softmax_regs_kernel<T, 2, Rows><<<blocks, kThreads, 0, s>>>(x, y, rows, width, scale, rule);
+        } else if (per_lane <= 4) {
+            softmax_regs_kernel<T, 4, Rows><<<blocks, kThreads, 0, s>>>(x, y, rows, width, scale, rule);
+        } else if (per_lane <= 8) {
+            softmax_regs_kernel<T, 8, Rows><<<blocks, kThreads, 0, s>>>(x, y, rows, width, scale, rule);
+        } else {
+            softmax_regs_kernel<T, 16, Rows><<<blocks, kThreads, 0, s>>>(x, y, rows, width, scale, rule);
+        }
+    } else {
+        softmax_stream_kernel<T, Rows><<<blocks, kThreads, 0, s>>>(x, y, rows, width, scale, rule);
+    }
+    return runtime::after_launch(name);
+}
+
+}  // namespace
+}  // namespace cppinf::device
+
+using namespace cppinf::device;
+namespace rt = cppinf::runtime;
+
+extern "C" {
+
+int cppinf_softmax_last_dim(cppinf_dtype dtype, const void* x, void* y, int64_t rows, int64_t width, void* stream) {
+    CPPINF_REQUIRE(rt::valid_dtype(dtype), CPPINF_ERR_INVALID_ARGUMENT,
+                   "softmax_last_dim received an unsupported dtype.");
+    CPPINF_REQUIRE(width > 0, CPPINF_ERR_INVALID_ARGUMENT, "softmax_last_dim requires a non-empty last dimension.");
+    CPPINF_REQUIRE(rows >= 0, CPPINF_ERR_INVALID_ARGUMENT, "softmax_last_dim requires a non-negative row count.");
+    if (rows == 0) {
+        return rt::ok();
+    }
+    CPPINF_REQUIRE(x && y, CPPINF_ERR_INVALID_ARGUMENT, "softmax_last_dim received a null pointer.");
+    const FullRows rule{width};
+    if (dtype == CPPINF_DTYPE_BF16) {
+        return launch_softmax<bf16>(x, y, rows, width, 1.0f, rule, stream, "softmax_last_dim");
+    }
+    return launch_softmax<float>(x, y, rows, width, 1.0f, rule, stream, "softmax_last_dim");
+}
+
+int cppinf_scaled_causal_softmax_f32(const float* x, float* y, int64_t matrices, int64_t query_len, int64_t key_len,
+                                     float scale, void* stream) {
+    CPPINF_REQUIRE(std::isfinite(scale), CPPINF_ERR_INVALID_ARGUMENT,
+                   "scaled_causal_softmax_last_dim requires a finite scale.");
+    CPPINF_REQUIRE(matrices >= 0 && query_len >= 0 && key_len >= 0, CPPINF_ERR_INVALID_ARGUMENT,
+                   "scaled_causal_softmax_last_dim requires non-negative sizes.");
+    CPPINF_REQUIRE(query_len > 0 && key_len > 0, CPPINF_ERR_INVALID_ARGUMENT,
+                   "scaled_causal_softmax_last_dim requires non-empty attention dimensions.");
+    CPPINF_REQUIRE(query_len == key_len, CPPINF_ERR_INVALID_ARGUMENT,
+                   "scaled_causal_softmax_last_dim requires square attention score matrices.");
+    if (matrices == 0) {
+        return rt::ok();
+    }
+    CPPINF_REQUIRE(x && y, CPPINF_ERR_INVALID_ARGUMENT, "scaled_causal_softmax_last_dim received a null pointer.");
+    const SquareCausalRows rule{query_len};
+    return launch_softmax<float>(x, y, matrices * query_len, key_len, scale, rule, stream,
+                                 "scaled_causal_softmax_last_dim");
+}
+
+int cppinf_scaled_position_causal_softmax_f32(const float* x, float* y, int64_t batch, int64_t heads,
+                                              int64_t query_cap, int64_t key_cap, float scale,
+                                              const int64_t* query_offsets, const int64_t* query_lengths,
+                                              const int64_t* key_lengths, void* stream) {
+    CPPINF_REQUIRE(std::isfinite(scale), CPPINF_ERR_INVALID_ARGUMENT,
+                   "qwen_attention batched softmax requires a finite scale.");
+    CPPINF_REQUIRE(batch > 0, CPPINF_ERR_INVALID_ARGUMENT, "qwen_attention batch size must be non-zero.");
+    CPPINF_REQUIRE(heads > 0, CPPINF_ERR_INVALID_ARGUMENT, "qwen_attention head count must be non-zero.");
+    CPPINF_REQUIRE(query_cap > 0, CPPINF_ERR_INVALID_ARGUMENT, "qwen_attention query length must be non-zero.");
+    CPPINF_REQUIRE(key_cap > 0, CPPINF_ERR_INVALID_ARGUMENT, "qwen_attention key length must be non-zero.");
+    CPPINF_REQUIRE(batch <= kMaxBatch, CPPINF_ERR_UNSUPPORTED,
+                   "scaled_position_causal_softmax supports at most 64 batch rows per call.");
+    CPPINF_REQUIRE(query_offsets && query_lengths && key_lengths, CPPINF_ERR_INVALID_ARGUMENT,
+                   "qwen_attention sequence_lengths must match the batch size.");
+    PositionCausalRows rule{};
+    rule.query_cap = query_cap;
+    rule.key_cap = key_cap;
+    rule.heads = heads;
+    for (int64_t b = 0; b < batch; ++b) {
+        CPPINF_REQUIRE(query_offsets[b] >= 0, CPPINF_ERR_INVALID_ARGUMENT,
+                       "qwen_attention query offsets must be non-negative.");
+        CPPINF_REQUIRE(query_lengths[b] >= 0 && query_lengths[b] <= query_cap, CPPINF_ERR_INVALID_ARGUMENT,
+                       "qwen_attention query lengths sequence length exceeds the padded sequence capacity.");
+        CPPINF_REQUIRE(key_lengths[b] >= 0 && key_lengths[b] <= key_cap, CPPINF_ERR_INVALID_ARGUMENT,
+                       "qwen_attention key lengths sequence length exceeds the padded sequence capacity.");
+        rule.query_offsets[b] = query_offsets[b];
+        rule.query_lengths[b] = query_lengths[b];
+        rule.key_lengths[b] = key_lengths[b];
+    }
+    CPPINF_REQUIRE(x && y, CPPINF_ERR_INVALID_ARGUMENT, "qwen_attention batched softmax received a null pointer.");
+    return launch_softmax<float>(x, y, batch * heads * query_cap, key_cap, scale, rule, stream,
+                                 "scaled_position_causal_softmax_last_dim");
+}
+
+}  // extern "C"

@@ -1,0 +1,324 @@
+"""Python mirror of cppinf's op interface (src/ops/nn_ops.h, src/ops/elementwise_ops.h, src/ops/tensor_ops.h:15,
+src/nn/rope.h) running on the sm_100a kernels of the C ABI.
+
+Tensors are torch CUDA tensors, used only as device memory (``data_ptr``) and for the current stream; the arithmetic
+is the library's. Argument meaning, validation order and messages follow the reference functions cited on each op.
+Non-contiguous inputs are materialised with the library's own strided-gather kernel before the op runs.
+
+Also exposed: the fused forms the Qwen3 decoder block uses (residual add + RMSNorm, SiLU(gate)*up, per-head q/k
+RMSNorm + RoPE), the row argmax of the greedy sampler, and the position-aware causal softmax of attention.
+"""
+
+from __future__ import annotations
+
+import math
+import threading
+
+import torch
+
+from . import capi
+
+_DTYPES = {torch.bfloat16: capi.DTYPE_BF16, torch.float32: capi.DTYPE_F32}
+
+
+def _stream() -> int:
+    return torch.cuda.current_stream().cuda_stream
+
+
+def _dtype_code(t: torch.Tensor, op: str) -> int:
+    # ops::detail::validate_supported_float_dtype, src/ops/op_utils.h:18-27
+    code = _DTYPES.get(t.dtype)
+    if code is None:
+        raise ValueError(f"{op} received an unsupported dtype.")
+    return code
+
+
+def _require_cuda(*tensors: torch.Tensor) -> None:
+    for t in tensors:
+        if not t.is_cuda:
+            raise ValueError("cppinf_b200 ops take CUDA tensors; copy host data with .to('cuda') first.")
+
+
+def materialize(t: torch.Tensor) -> torch.Tensor:
+    """Dense copy of a strided view made by the library's gather kernel (no-op for contiguous tensors)."""
+    if t.is_contiguous():
+        return t
+    code = _dtype_code(t, "materialize")
+    out = torch.empty(t.shape, dtype=t.dtype, device=t.device)
+    dims = capi.i64_array(list(t.shape))
+    strides = capi.i64_array(list(t.stride()))
+    capi.call("cppinf_strided_copy", code, t.data_ptr(), t.dim(), dims, strides, out.data_ptr(), _stream())
+    return out
+
+
+# ---- elementwise ------------------------------------------------------------------------------------------------
+
+
+def _validate_elementwise(lhs: torch.Tensor, rhs: torch.Tensor, op: str) -> int:
+    # validate_elementwise_inputs, src/ops/elementwise_ops.cpp:14-24
+    if lhs.dtype != rhs.dtype:
+        raise ValueError(f"{op} requires matching tensor dtypes.")
+    if lhs.shape != rhs.shape:
+        raise ValueError(f"{op} requires matching tensor shapes.")
+    return _dtype_code(lhs, op)
+
+
+def add(lhs: torch.Tensor, rhs: torch.Tensor) -> torch.Tensor:
+    """ops::add, src/ops/elementwise_ops.h:10."""
+    code = _validate_elementwise(lhs, rhs, "add")
+    _require_cuda(lhs, rhs)
+    lhs, rhs = materialize(lhs), materialize(rhs)
+    out = torch.empty_like(lhs)
+    capi.call("cppinf_add", code, lhs.data_ptr(), rhs.data_ptr(), out.data_ptr(), lhs.numel(), _stream())
+    return out
+
+
+def mul(lhs: torch.Tensor, rhs: torch.Tensor) -> torch.Tensor:
+    """ops::mul, src/ops/elementwise_ops.h:14."""
+    code = _validate_elementwise(lhs, rhs, "mul")
+    _require_cuda(lhs, rhs)
+    lhs, rhs = materialize(lhs), materialize(rhs)
+    out = torch.empty_like(lhs)
+    capi.call("cppinf_mul", code, lhs.data_ptr(), rhs.data_ptr(), out.data_ptr(), lhs.numel(), _stream())
+    return out
+
+
+def silu(input: torch.Tensor) -> torch.Tensor:
+    """ops::silu, src/ops/nn_ops.h:9."""
+    code = _dtype_code(input, "silu")
+    _require_cuda(input)
+    x = materialize(input)
+    out = torch.empty_like(x)
+    capi.call("cppinf_silu", code, x.data_ptr(), out.data_ptr(), x.numel(), _stream())
+    return out
+
+
+def cast(input: torch.Tensor, dtype: torch.dtype) -> torch.Tensor:
+    """ops::cast, src/ops/tensor_ops.h:15."""
+    src = _dtype_code(input, "cast")
+    if dtype not in _DTYPES:
+        raise ValueError("cast received an unsupported dtype.")
+    _require_cuda(input)
+    x = materialize(input)
+    out = torch.empty(x.shape, dtype=dtype, device=x.device)
+    capi.call("cppinf_cast", src, x.data_ptr(), _DTYPES[dtype], out.data_ptr(), x.numel(), _stream())
+    return out
+
+
+def silu_mul(gate: torch.Tensor, up: torch.Tensor) -> torch.Tensor:
+    """ops::mul(ops::silu(gate), up) in one pass, as qwen_mlp calls them (src/nn/qwen_mlp.cpp:65-66)."""
+    code = _validate_elementwise(gate, up, "mul")
+    _require_cuda(gate, up)
+    gate, up = materialize(gate), materialize(up)
+    out = torch.empty_like(gate)
+    capi.call("cppinf_silu_mul", code, gate.data_ptr(), up.data_ptr(), out.data_ptr(), gate.numel(), _stream())
+    return out
+
+
+# ---- row reductions ---------------------------------------------------------------------------------------------
+
+
+def _validate_last_dim(input: torch.Tensor, op: str) -> int:
+    # validate_last_dim_operation_input, src/ops/nn_ops.cpp:54-64
+    code = _dtype_code(input, op)
+    if input.dim() == 0:
+        raise ValueError(f"{op} requires a tensor with rank at least 1.")
+    if input.shape[-1] == 0:
+        raise ValueError(f"{op} requires a non-empty last dimension.")
+    return code
+
+
+def _validate_rms(input: torch.Tensor, weight: torch.Tensor, epsilon: float) -> int:
+    # src/ops/nn_ops.cpp:164-183
+    code = _validate_last_dim(input, "rms_norm")
+    if epsilon < 0.0:
+        raise ValueError("rms_norm requires a non-negative epsilon.")
+    if input.dtype != weight.dtype:
+        raise ValueError("rms_norm requires matching tensor dtypes.")
+    if weight.dim() != 1:
+        raise ValueError("rms_norm requires a rank-1 weight tensor.")
+    if weight.shape[0] != input.shape[-1]:
+        raise ValueError("rms_norm weight size must match the input last dimension.")
+    return code
+
+
+def rms_norm(input: torch.Tensor, weight: torch.Tensor, epsilon: float) -> torch.Tensor:
+    """ops::rms_norm, src/ops/nn_ops.h:22. Row-strided inputs (a uniform stride between rows, dense rows) are read in
+    place; other views are materialised first."""
+    code = _validate_rms(input, weight, epsilon)
+    _require_cuda(input, weight)
+    width = input.shape[-1]
+    rows = input.numel() // width
+    x = input
+    row_stride = width
+    if not x.is_contiguous():
+        # A 2-D row-strided view is consumed directly, anything else is gathered to dense first.
+        if x.dim() == 2 and x.stride(1) == 1 and x.stride(0) >= width:
+            row_stride = x.stride(0)
+        else:
+            x = materialize(x)
+    w = materialize(weight)
+    out = torch.empty(input.shape, dtype=input.dtype, device=input.device)
+    capi.call("cppinf_rms_norm", code, x.data_ptr(), row_stride, w.data_ptr(), out.data_ptr(), rows, width,
+              float(epsilon), _stream())
+    return out
+
+
+def add_rms_norm(a: torch.Tensor, b: torch.Tensor, weight: torch.Tensor, epsilon: float,
+                 out_sum: torch.Tensor | None = None) -> tuple[torch.Tensor, torch.Tensor]:
+    """Residual add then RMSNorm (src/nn/qwen_decoder_block.cpp:80-84): returns (a + b, rms_norm(a + b))."""
+    code = _validate_elementwise(a, b, "add")
+    _validate_rms(a, weight, epsilon)
+    _require_cuda(a, b, weight)
+    a, b, w = materialize(a), materialize(b), materialize(weight)
+    width = a.shape[-1]
+    rows = a.numel() // width
+    s = torch.empty_like(a) if out_sum is None else out_sum
+    y = torch.empty_like(a)
+    capi.call("cppinf_add_rms_norm", code, a.data_ptr(), b.data_ptr(), w.data_ptr(), s.data_ptr(), y.data_ptr(),
+              rows, width, float(epsilon), _stream())
+    return s, y
+
+
+def softmax_last_dim(input: torch.Tensor) -> torch.Tensor:
+    """ops::softmax_last_dim, src/ops/nn_ops.h:13."""
+    code = _validate_last_dim(input, "softmax_last_dim")
+    _require_cuda(input)
+    x = materialize(input)
+    width = x.shape[-1]
+    out = torch.empty_like(x)
+    capi.call("cppinf_softmax_last_dim", code, x.data_ptr(), out.data_ptr(), x.numel() // width, width, _stream())
+    return out
+
+
+def scaled_causal_softmax_last_dim(input: torch.Tensor, scale: float) -> torch.Tensor:
+    """ops::scaled_causal_softmax_last_dim, src/ops/nn_ops.h:17 (f32 result, like the reference)."""
+    op = "scaled_causal_softmax_last_dim"
+    _validate_last_dim(input, op)
+    if input.dim() < 2:
+        raise ValueError(f"{op} requires a tensor with rank at least 2.")
+    if not math.isfinite(scale):
+        raise ValueError(f"{op} requires a finite scale.")
+    q, k = input.shape[-2], input.shape[-1]
+    if q == 0 or k == 0:
+        raise ValueError(f"{op} requires non-empty attention dimensions.")
+    if q != k:
+        raise ValueError(f"{op} requires square attention score matrices.")
+    _require_cuda(input)
+    x = materialize(input)
+    if x.dtype != torch.float32:
+        x = cast(x, torch.float32)
+    out = torch.empty(x.shape, dtype=torch.float32, device=x.device)
+    capi.call("cppinf_scaled_causal_softmax_f32", x.data_ptr(), out.data_ptr(), x.numel() // (q * k), q, k,
+              float(scale), _stream())
+    return out
+
+
+def scaled_position_causal_softmax_last_dim(input: torch.Tensor, scale: float, query_position_offsets,
+                                            query_lengths, key_lengths) -> torch.Tensor:
+    """The attention softmax of src/nn/qwen_attention.cpp:164-235 on f32 [batch, heads, Qcap, Kcap]."""
+    if input.dim() != 4:
+        raise ValueError("qwen_attention batched softmax requires a rank-4 tensor.")
+    if not math.isfinite(scale):
+        raise ValueError("qwen_attention batched softmax requires a finite scale.")
+    batch = input.shape[0]
+    for name, seq in (("query offsets", query_position_offsets), ("query lengths", query_lengths),
+                      ("key lengths", key_lengths)):
+        if len(seq) != batch:
+            raise ValueError(f"qwen_attention {name} sequence_lengths must match the batch size.")
+    _require_cuda(input)
+    x = materialize(input)
+    if x.dtype != torch.float32:
+        x = cast(x, torch.float32)
+    out = torch.empty(x.shape, dtype=torch.float32, device=x.device)
+    capi.call("cppinf_scaled_position_causal_softmax_f32", x.data_ptr(), out.data_ptr(), batch, x.shape[1],
+              x.shape[2], x.shape[3], float(scale), capi.i64_array(query_position_offsets),
+              capi.i64_array(query_lengths), capi.i64_array(key_lengths), _stream())
+    return out
+
+
+def row_argmax(logits: torch.Tensor) -> torch.Tensor:
+    """Greedy token pick of src/cli/cli_app.cpp:72-94 for every row of [rows, vocab] logits (int64 [rows])."""
+    code = _dtype_code(logits, "row_argmax")
+    if logits.dim() != 2:
+        raise ValueError("CLI generation requires rank-2 logits.")
+    _require_cuda(logits)
+    rows, cols = logits.shape
+    x = logits
+    if x.stride(-1) != 1:
+        x = materialize(x)
+    row_stride = x.stride(0) if rows > 1 else cols
+    out = torch.empty(rows, dtype=torch.int64, device=logits.device)
+    capi.call("cppinf_row_argmax", code, x.data_ptr(), rows, cols, row_stride, out.data_ptr(), _stream())
+    return out
+
+
+# ---- RoPE -------------------------------------------------------------------------------------------------------
+
+_table_lock = threading.Lock()
+_tables: dict[tuple[float, int, int], torch.Tensor] = {}
+
+
+def rope_table(rope_base: float, head_dim: int, positions: int, device: torch.device | int | None = None):
+    """Device copy of the host-built angle table (cppinf_rope_table), cached per (base, head_dim, device) and grown
+    to cover `positions` (rounded up to a power of two)."""
+    dev = torch.device("cuda", torch.cuda.current_device() if device is None else torch.device(device).index or 0)
+    key = (float(rope_base), int(head_dim), dev.index)
+    with _table_lock:
+        table = _tables.get(key)
+        if table is None or table.shape[0] < positions:
+            n = 1 << max(int(positions - 1).bit_length(), 6)
+            host = capi.rope_table(rope_base, head_dim, n)
+            table = torch.from_numpy(host).to(dev)
+            _tables[key] = table
+    return table
+
+
+def apply_rope(input: torch.Tensor, sequence_position_offset: int = 0, rope_base: float = 1000000.0,
+               sequence_dimension: int = 1) -> torch.Tensor:
+    """nn::apply_rope, src/nn/rope.h:12-13, on a rank-3 tensor."""
+    # validate_rope_input, src/nn/rope.cpp:48-69
+    code = _dtype_code(input, "apply_rope")
+    if input.dim() != 3:
+        raise ValueError("apply_rope requires a rank-3 tensor.")
+    if not math.isfinite(rope_base) or rope_base <= 0.0:
+        raise ValueError("apply_rope requires a positive finite rope base.")
+    if sequence_dimension > 1:
+        raise ValueError("apply_rope requires the sequence dimension to be 0 or 1.")
+    d0, d1, d = input.shape
+    for name, v in (("rope dim 0", d0), ("rope dim 1", d1), ("rope head size", d)):
+        if v == 0:
+            raise ValueError(f"{name} must be non-zero.")
+    if d % 2 != 0:
+        raise ValueError("apply_rope requires an even head size.")
+    _require_cuda(input)
+    seq = input.shape[sequence_dimension]
+    table = rope_table(rope_base, d, sequence_position_offset + seq, input.device)
+    out = torch.empty(input.shape, dtype=input.dtype, device=input.device)
+    s0, s1, s2 = input.stride()
+    capi.call("cppinf_rope", code, input.data_ptr(), d0, d1, d, s0, s1, s2, sequence_dimension,
+              sequence_position_offset, table.data_ptr(), table.shape[0], out.data_ptr(), _stream())
+    return out
+
+
+def qk_norm_rope(q: torch.Tensor, k: torch.Tensor, q_weight: torch.Tensor, k_weight: torch.Tensor,
+                 epsilon: float, position_offset: int = 0, rope_base: float = 1000000.0,
+                 out: tuple[torch.Tensor, torch.Tensor] | None = None) -> tuple[torch.Tensor, torch.Tensor]:
+    """Per-head RMSNorm of q [T, Hq, D] and k [T, Hk, D] followed by RoPE at positions position_offset + t
+    (src/nn/qwen_attention.cpp:383-390), one kernel for both tensors."""
+    code = _validate_rms(q, q_weight, epsilon)
+    _validate_rms(k, k_weight, epsilon)
+    if q.dtype != k.dtype:
+        raise ValueError("qk_norm_rope requires matching tensor dtypes.")
+    if q.dim() != 3 or k.dim() != 3 or q.shape[0] != k.shape[0] or q.shape[2] != k.shape[2]:
+        raise ValueError("qk_norm_rope requires q [T, Hq, D] and k [T, Hk, D].")
+    _require_cuda(q, k, q_weight, k_weight)
+    q, k = materialize(q), materialize(k)
+    tokens, hq, d = q.shape
+    hk = k.shape[1]
+    table = rope_table(rope_base, d, position_offset + tokens, q.device)
+    q_out, k_out = out if out is not None else (torch.empty_like(q), torch.empty_like(k))
+    capi.call("cppinf_qk_norm_rope", code, q.data_ptr(), k.data_ptr(), q_weight.data_ptr(), k_weight.data_ptr(),
+              q_out.data_ptr(), k_out.data_ptr(), tokens, hq, hk, d, position_offset, float(epsilon),
+              table.data_ptr(), table.shape[0], _stream())
+    return q_out, k_out

@@ -1,0 +1,456 @@
+"""Parity of the sm_100a kernels (called through the C ABI via cppinf_b200.ops) with the CPU oracle and the reference's
+golden vectors.
+
+Tolerances:
+- integer / index work (argmax, casts, add, mul, RoPE given its input, residual sums): bit-exact;
+- RMSNorm-family outputs: bit-exact against the oracle, which restates the device reduction order; the reference's
+  own (oneDNN) order is unspecified, and any f32 order stays within 1 bf16 ulp (tests/test_oracle.py);
+- silu*up: bit-exact against one of the two faithful results (the bf16 intermediate may round either way when the
+  f32 silu lies within 2^-20 of a rounding boundary, because exp implementations differ by a few f32 ulps);
+- f32 softmax: 1e-5 relative (+1e-7 absolute), masked entries exactly 0;
+- bf16 softmax / silu: 1 bf16 ulp.
+"""
+
+from __future__ import annotations
+
+import math
+
+import numpy as np
+import pytest
+import torch
+
+from _dev import bf16_bits, seeded_bf16, to_dev, to_host
+from oracle.oracle import as_float, bf16_to_f32, f32_to_bf16, ulp_distance
+
+pytestmark = pytest.mark.gpu
+
+
+@pytest.fixture(scope="module")
+def ops(cuda):
+    from cppinf_b200 import ops as _ops
+
+    return _ops
+
+
+def assert_softmax_close(got: np.ndarray, want: np.ndarray):
+    assert got.shape == want.shape
+    zero = want == 0
+    assert (got[zero] == 0).all(), "masked / zero probabilities must be exactly 0"
+    np.testing.assert_allclose(got, want, rtol=1e-5, atol=1e-7)
+
+
+# ---------------------------------------------------------------------------------------------------------------
+# Reference known-answer tests, through the device path
+# ---------------------------------------------------------------------------------------------------------------
+
+
+def test_kat_add_mul_f32_bf16(ops):
+    # tests/ops/ops_test.cpp:47-61, 229-235
+    a = to_dev(np.array([[1, 2], [3, 4]], np.float32))
+    b = to_dev(np.array([[10, 20], [30, 40]], np.float32))
+    assert to_host(ops.add(a, b)).ravel().tolist() == [11, 22, 33, 44]
+    assert to_host(ops.mul(a, b)).ravel().tolist() == [10, 40, 90, 160]
+    ab = to_dev(bf16_bits([1, 2, 3, 4]))
+    bb = to_dev(bf16_bits([10, 20, 30, 40]))
+    assert (to_host(ops.add(ab, bb)) == bf16_bits([11, 22, 33, 44])).all()
+
+
+def test_kat_cast(ops):
+    # tests/ops/ops_test.cpp:112-124
+    x = to_dev(np.array([[1.5, -2.25], [0.5, -0.75]], np.float32))
+    assert to_host(ops.cast(x, torch.bfloat16)).ravel().tolist() == [0x3FC0, 0xC010, 0x3F00, 0xBF40]
+    xb = to_dev(np.array([0x3FC0, 0xC010, 0x3F00, 0xBF40], np.uint16))
+    assert to_host(ops.cast(xb, torch.float32)).tolist() == [1.5, -2.25, 0.5, -0.75]
+
+
+def test_kat_silu(ops):
+    # tests/ops/ops_test.cpp:260-278
+    x = to_dev(bf16_bits([-1.5, -0.25, 0.5, 2.0, 3.0, -4.5, 1.25, 0.75]).reshape(2, 4))
+    expected = [-0.2734375, -0.109375, 0.310546875, 1.7578125, 2.859375, -0.0495605469, 0.97265625, 0.5078125]
+    np.testing.assert_allclose(bf16_to_f32(to_host(ops.silu(x))).ravel(), expected, atol=1e-6, rtol=0)
+
+
+def test_kat_softmax(ops):
+    # tests/ops/ops_test.cpp:280-298
+    x = to_dev(bf16_bits([1.0, -2.5, 3.25, 0.75, 4.5, 0.5, -1.75, 2.25]).reshape(2, 4))
+    expected = [0.0883789062, 0.0026702881, 0.83984375, 0.0688476562, 0.88671875, 0.0162353516, 0.0017166138,
+                0.09375]
+    np.testing.assert_allclose(bf16_to_f32(to_host(ops.softmax_last_dim(x))).ravel(), expected, atol=1e-6, rtol=0)
+
+
+def test_kat_scaled_causal_softmax(ops):
+    # tests/ops/ops_test.cpp:300-310
+    x = to_dev(np.array([1.0, 1000.0, 3.0, 4.0], np.float32).reshape(1, 2, 2))
+    out = to_host(ops.scaled_causal_softmax_last_dim(x, 1.0)).ravel()
+    np.testing.assert_allclose(out, [1.0, 0.0, 0.2689414322, 0.7310585976], atol=1e-6, rtol=0)
+    assert out[1] == 0.0
+
+
+def test_kat_rms_norm(ops):
+    # tests/ops/ops_test.cpp:312-332
+    x = to_dev(bf16_bits([-1.5, -0.25, 0.5, 2.0, 3.0, -4.5, 1.25, 0.75]).reshape(2, 4))
+    w = to_dev(bf16_bits([1.0, 0.5, -1.5, 2.0]))
+    expected = [-1.171875, -0.09765625, -0.5859375, 3.125, 1.0703125, -0.8046875, -0.66796875, 0.53515625]
+    np.testing.assert_allclose(bf16_to_f32(to_host(ops.rms_norm(x, w, 1e-5))).ravel(), expected, atol=1e-6, rtol=0)
+
+
+def test_kat_rope(ops):
+    # tests/nn/rope_test.cpp:25-50
+    from test_oracle import ROPE_EXPECTED, ROPE_INPUT
+
+    x = to_dev(np.array([1.0, -0.5, 0.25, 1.5], np.float32).reshape(1, 1, 4))
+    assert to_host(ops.apply_rope(x)).ravel().tolist() == [1.0, -0.5, 0.25, 1.5]
+    xb = to_dev(bf16_bits(ROPE_INPUT).reshape(2, 3, 4))
+    np.testing.assert_allclose(bf16_to_f32(to_host(ops.apply_rope(xb, 2))).ravel(), ROPE_EXPECTED, atol=1e-6, rtol=0)
+
+
+def test_kat_mlp_gate_double_rounding(ops, oracle):
+    # tests/nn/qwen_mlp_test.cpp:75-118: the projections come from the oracle, the gate product from the device.
+    from test_oracle import MLP_DOWN, MLP_EXPECTED, MLP_GATE, MLP_HIDDEN, MLP_UP
+
+    x = bf16_bits(MLP_HIDDEN).reshape(3, 6)
+    gate = oracle.linear(x, bf16_bits(MLP_GATE).reshape(10, 6))
+    up = oracle.linear(x, bf16_bits(MLP_UP).reshape(10, 6))
+    gated = to_host(ops.silu_mul(to_dev(gate), to_dev(up)))
+    out = oracle.linear(gated, bf16_bits(MLP_DOWN).reshape(6, 10))
+    np.testing.assert_allclose(bf16_to_f32(out).ravel(), MLP_EXPECTED, atol=1e-6, rtol=0)
+
+
+# ---------------------------------------------------------------------------------------------------------------
+# Reference-code fixtures
+# ---------------------------------------------------------------------------------------------------------------
+
+
+def test_reference_fixtures_elementwise_bit_exact(ops, golden):
+    g = golden("ref_elementwise")
+    for dt in ("bf16", "f32"):
+        a, b = to_dev(g[f"a_{dt}"]), to_dev(g[f"b_{dt}"])
+        assert np.array_equal(to_host(ops.add(a, b)), g[f"add_{dt}"])
+        assert np.array_equal(to_host(ops.mul(a, b)), g[f"mul_{dt}"])
+    assert np.array_equal(to_host(ops.cast(to_dev(g["a_f32"]), torch.bfloat16)), g["cast_f32_bf16"])
+    assert np.array_equal(to_host(ops.cast(to_dev(g["a_bf16"]), torch.float32)), g["cast_bf16_f32"])
+
+
+def test_reference_fixtures_silu(ops, oracle, golden):
+    g = golden("ref_elementwise")
+    assert ulp_distance(to_host(ops.silu(to_dev(g["gate"]))), g["silu_bf16"]).max() <= 1
+    np.testing.assert_allclose(to_host(ops.silu(to_dev(g["a_f32"]))), g["silu_f32"], rtol=1e-6, atol=1e-30)
+    got = to_host(ops.silu_mul(to_dev(g["gate"]), to_dev(g["up"])))
+    out, alt = oracle.silu_mul(g["gate"], g["up"], with_alternative=True)
+    assert np.array_equal(out, g["silu_mul_bf16"])
+    assert ((got == out) | (got == alt)).all()
+
+
+def test_reference_fixtures_rope_bit_exact(ops, golden):
+    g = golden("ref_rope")
+    assert np.array_equal(to_host(ops.apply_rope(to_dev(g["bf16_seq1_x"]), 3, 1e6, 1)), g["bf16_seq1_y"])
+    assert np.array_equal(to_host(ops.apply_rope(to_dev(g["bf16_seq0_x"]), 1000, 1e6, 0)), g["bf16_seq0_y"])
+    assert np.array_equal(to_host(ops.apply_rope(to_dev(g["f32_seq1_x"]), 7, 10000.0, 1)), g["f32_seq1_y"])
+
+
+def test_reference_fixtures_softmax(ops, golden):
+    g = golden("ref_causal_softmax")
+    got = to_host(ops.scaled_causal_softmax_last_dim(to_dev(g["x"]), float(g["scale"])))
+    assert_softmax_close(got, g["y"])
+    g = golden("ref_position_softmax")
+    got = to_host(ops.scaled_position_causal_softmax_last_dim(to_dev(g["x"]), float(g["scale"]), g["offsets"],
+                                                              g["qlens"], g["klens"]))
+    assert_softmax_close(got, g["y"])
+
+
+# ---------------------------------------------------------------------------------------------------------------
+# Seeded parity against the oracle
+# ---------------------------------------------------------------------------------------------------------------
+
+RMS_CASES = [(1, 1024), (3, 1024), (512, 1024), (37, 128), (5, 64), (7, 4096), (2, 8192), (9, 1000), (4, 1001),
+             (6, 8), (3, 24)]
+
+
+@pytest.mark.parametrize("rows,width", RMS_CASES)
+@pytest.mark.parametrize("dtype", ["bf16", "f32"])
+def test_rms_norm_bit_exact(ops, oracle, rows, width, dtype):
+    rng = np.random.default_rng(rows * 7919 + width)
+    x = (rng.standard_normal((rows, width)) * 1.5).astype(np.float32)
+    w = (1 + 0.1 * rng.standard_normal(width)).astype(np.float32)
+    if dtype == "bf16":
+        x, w = f32_to_bf16(x), f32_to_bf16(w)
+    got = to_host(ops.rms_norm(to_dev(x), to_dev(w), 1e-6))
+    assert np.array_equal(got, oracle.rms_norm(x, w, 1e-6))
+
+
+def test_rms_norm_row_strided_view(ops, oracle):
+    rng = np.random.default_rng(11)
+    base = seeded_bf16(rng, (64, 1536))
+    w = seeded_bf16(rng, (1024,), 1.0, 0.1)
+    view = to_dev(base)[:, 256:1280]  # rows of 1024 at a stride of 1536
+    assert not view.is_contiguous()
+    got = to_host(ops.rms_norm(view, to_dev(w), 1e-6))
+    want = oracle.rms_norm(np.ascontiguousarray(base[:, 256:1280]), w, 1e-6)
+    assert np.array_equal(got, want)
+
+
+def test_rms_norm_rank3_and_transposed_view(ops, oracle):
+    rng = np.random.default_rng(12)
+    x = seeded_bf16(rng, (4, 6, 128))
+    w = seeded_bf16(rng, (128,), 1.0, 0.1)
+    assert np.array_equal(to_host(ops.rms_norm(to_dev(x), to_dev(w), 1e-6)), oracle.rms_norm(x, w, 1e-6))
+    t = to_dev(x).transpose(0, 1)  # materialised by the gather kernel first
+    want = oracle.rms_norm(np.ascontiguousarray(x.transpose(1, 0, 2)), w, 1e-6)
+    assert np.array_equal(to_host(ops.rms_norm(t, to_dev(w), 1e-6)), want)
+
+
+@pytest.mark.parametrize("rows,width", [(4096, 1024), (1, 1024), (33, 2048), (3, 9000), (5, 1000), (2, 12)])
+@pytest.mark.parametrize("dtype", ["bf16", "f32"])
+def test_add_rms_norm_bit_exact(ops, oracle, rows, width, dtype):
+    rng = np.random.default_rng(rows + width)
+    a = (rng.standard_normal((rows, width))).astype(np.float32)
+    b = (rng.standard_normal((rows, width))).astype(np.float32)
+    w = (1 + 0.1 * rng.standard_normal(width)).astype(np.float32)
+    if dtype == "bf16":
+        a, b, w = f32_to_bf16(a), f32_to_bf16(b), f32_to_bf16(w)
+    s, y = ops.add_rms_norm(to_dev(a), to_dev(b), to_dev(w), 1e-6)
+    want_s, want_y = oracle.add_rms_norm(a, b, w, 1e-6)
+    assert np.array_equal(to_host(s), want_s)
+    assert np.array_equal(to_host(y), want_y)
+
+
+def test_add_rms_norm_in_place_residual(ops, oracle):
+    rng = np.random.default_rng(13)
+    a, b = seeded_bf16(rng, (64, 1024)), seeded_bf16(rng, (64, 1024))
+    w = seeded_bf16(rng, (1024,), 1.0, 0.1)
+    da = to_dev(a)
+    s, y = ops.add_rms_norm(da, to_dev(b), to_dev(w), 1e-6, out_sum=da)
+    want_s, want_y = oracle.add_rms_norm(a, b, w, 1e-6)
+    assert s.data_ptr() == da.data_ptr()
+    assert np.array_equal(to_host(da), want_s)
+    assert np.array_equal(to_host(y), want_y)
+
+
+@pytest.mark.parametrize("tokens,hq,hk,d,offset", [(2048, 16, 8, 128, 0), (7, 16, 8, 128, 2040), (3, 4, 2, 64, 9),
+                                                   (5, 2, 1, 256, 100), (1, 16, 8, 128, 639), (33, 3, 5, 128, 1)])
+def test_qk_norm_rope_bit_exact(ops, oracle, tokens, hq, hk, d, offset):
+    rng = np.random.default_rng(tokens * 31 + d)
+    q, k = seeded_bf16(rng, (tokens, hq, d)), seeded_bf16(rng, (tokens, hk, d))
+    qw, kw = seeded_bf16(rng, (d,), 1.0, 0.1), seeded_bf16(rng, (d,), 1.0, 0.1)
+    q_out, k_out = ops.qk_norm_rope(to_dev(q), to_dev(k), to_dev(qw), to_dev(kw), 1e-6, offset, 1e6)
+    want_q, want_k = oracle.qk_norm_rope(q, k, qw, kw, 1e-6, offset, 1e6)
+    assert np.array_equal(to_host(q_out), want_q)
+    assert np.array_equal(to_host(k_out), want_k)
+
+
+def test_qk_norm_rope_f32(ops, oracle):
+    rng = np.random.default_rng(14)
+    q = rng.standard_normal((9, 4, 128)).astype(np.float32)
+    k = rng.standard_normal((9, 2, 128)).astype(np.float32)
+    qw = (1 + 0.1 * rng.standard_normal(128)).astype(np.float32)
+    kw = (1 + 0.1 * rng.standard_normal(128)).astype(np.float32)
+    q_out, k_out = ops.qk_norm_rope(to_dev(q), to_dev(k), to_dev(qw), to_dev(kw), 1e-6, 17, 1e6)
+    want_q, want_k = oracle.qk_norm_rope(q, k, qw, kw, 1e-6, 17, 1e6)
+    assert np.array_equal(to_host(q_out), want_q)
+    assert np.array_equal(to_host(k_out), want_k)
+
+
+def test_qk_norm_rope_matches_torch_fixture(ops, golden):
+    g = golden("torch_qk_norm_rope")
+    q_out, k_out = ops.qk_norm_rope(to_dev(g["q"]), to_dev(g["k"]), to_dev(g["qw"]), to_dev(g["kw"]),
+                                    float(g["eps"]), int(g["offset"]), float(g["base"]))
+    for got, want in ((to_host(q_out), g["q_out"]), (to_host(k_out), g["k_out"])):
+        err = np.abs(as_float(got) - as_float(want))
+        assert (err <= np.maximum(np.abs(as_float(want)) * 2.0 ** -7, 2.0 ** -14)).all()
+
+
+def test_qk_norm_rope_equals_rms_norm_then_apply_rope(ops):
+    # The fused kernel against the unfused device ops composed as the reference composes them.
+    rng = np.random.default_rng(15)
+    q, k = seeded_bf16(rng, (12, 16, 128)), seeded_bf16(rng, (12, 8, 128))
+    qw, kw = seeded_bf16(rng, (128,), 1.0, 0.1), seeded_bf16(rng, (128,), 1.0, 0.1)
+    q_out, k_out = ops.qk_norm_rope(to_dev(q), to_dev(k), to_dev(qw), to_dev(kw), 1e-6, 30)
+    q_ref = ops.apply_rope(ops.rms_norm(to_dev(q), to_dev(qw), 1e-6), 30, 1e6, 0)
+    k_ref = ops.apply_rope(ops.rms_norm(to_dev(k), to_dev(kw), 1e-6), 30, 1e6, 0)
+    assert torch.equal(q_out.view(torch.int16), q_ref.view(torch.int16))
+    assert torch.equal(k_out.view(torch.int16), k_ref.view(torch.int16))
+
+
+def test_rope_reference_batched_fixture(ops, golden):
+    # apply_rope_batched (src/nn/qwen_attention.cpp:136-162): per batch row, rope over [seq, heads, D] at its offset.
+    g = golden("ref_rope_batched")
+    x = to_dev(g["x"])
+    for bidx, off in enumerate(g["offsets"]):
+        got = to_host(ops.apply_rope(x[bidx], int(off), 1e6, 0))
+        assert np.array_equal(got, g["y"][bidx])
+
+
+@pytest.mark.parametrize("seq_dim", [0, 1])
+def test_rope_strided_view_bit_exact(ops, oracle, seq_dim):
+    rng = np.random.default_rng(16 + seq_dim)
+    base = seeded_bf16(rng, (6, 10, 128))
+    view_np = base.transpose(1, 0, 2)  # [10, 6, 128], non-contiguous
+    got = to_host(ops.apply_rope(to_dev(base).transpose(0, 1), 5, 1e6, seq_dim))
+    assert np.array_equal(got, oracle.rope(view_np, 5, 1e6, seq_dim))
+
+
+@pytest.mark.parametrize("n", [1, 7, 8, 4099, 1 << 20, 3 * 4096 * 3072 // 7])
+@pytest.mark.parametrize("dtype", ["bf16", "f32"])
+def test_silu_mul_faithful(ops, oracle, n, dtype):
+    rng = np.random.default_rng(n)
+    g = (rng.standard_normal(n) * 3).astype(np.float32)
+    u = rng.standard_normal(n).astype(np.float32)
+    if dtype == "bf16":
+        g, u = f32_to_bf16(g), f32_to_bf16(u)
+    got = to_host(ops.silu_mul(to_dev(g), to_dev(u)))
+    out, alt = oracle.silu_mul(g, u, with_alternative=True)
+    if dtype == "bf16":
+        assert ((got == out) | (got == alt)).all()
+        assert (got == out).mean() > 0.999
+    else:
+        np.testing.assert_allclose(got, out, rtol=1e-6, atol=1e-30)
+
+
+def test_silu_mul_matches_torch_fixture(ops, oracle, golden):
+    g = golden("torch_silu_mul")
+    got = to_host(ops.silu_mul(to_dev(g["gate"]), to_dev(g["up"])))
+    out, alt = oracle.silu_mul(g["gate"], g["up"], with_alternative=True)
+    assert ((got == out) | (got == alt)).all()
+    assert ((got == g["out"]) | (alt == g["out"]) | (out == g["out"])).all()
+
+
+def test_elementwise_unaligned_views_take_scalar_path(ops, oracle):
+    rng = np.random.default_rng(17)
+    a, b = seeded_bf16(rng, 1001), seeded_bf16(rng, 1001)
+    da, db = to_dev(a), to_dev(b)
+    got = to_host(ops.add(da[1:], db[1:]))  # 2-byte offset: not 16-byte aligned
+    assert np.array_equal(got, oracle.add(a[1:], b[1:]))
+    got = to_host(ops.silu_mul(da[3:], db[3:]))
+    out, alt = oracle.silu_mul(a[3:], b[3:], with_alternative=True)
+    assert ((got == out) | (got == alt)).all()
+
+
+@pytest.mark.parametrize("matrices,n", [(1, 1), (2, 64), (3, 129), (16, 2048), (1, 4100), (2, 33)])
+def test_scaled_causal_softmax(ops, oracle, matrices, n):
+    rng = np.random.default_rng(matrices * 1000 + n)
+    x = (rng.standard_normal((matrices, n, n)) * 2.0).astype(np.float32)
+    scale = 1.0 / math.sqrt(128.0)
+    got = to_host(ops.scaled_causal_softmax_last_dim(to_dev(x), scale))
+    assert_softmax_close(got, oracle.scaled_causal_softmax(x, scale))
+
+
+def test_position_causal_softmax_ragged(ops, oracle):
+    rng = np.random.default_rng(18)
+    x = (rng.standard_normal((4, 16, 24, 640)) * 2.0).astype(np.float32)
+    args = (0.088, [0, 100, 616, 3], [24, 11, 24, 0], [24, 111, 640, 3])
+    got = to_host(ops.scaled_position_causal_softmax_last_dim(to_dev(x), *args))
+    assert_softmax_close(got, oracle.position_causal_softmax(x, *args))
+
+
+@pytest.mark.parametrize("rows,width", [(2, 4), (16, 256), (100, 1000), (3, 3001), (8, 151936)])
+@pytest.mark.parametrize("dtype", ["bf16", "f32"])
+def test_softmax_last_dim(ops, oracle, rows, width, dtype):
+    rng = np.random.default_rng(rows + width)
+    x = (rng.standard_normal((rows, width)) * 2).astype(np.float32)
+    if dtype == "bf16":
+        x = f32_to_bf16(x)
+        assert ulp_distance(to_host(ops.softmax_last_dim(to_dev(x))), oracle.softmax_last_dim(x)).max() <= 1
+    else:
+        np.testing.assert_allclose(to_host(ops.softmax_last_dim(to_dev(x))), oracle.softmax_last_dim(x),
+                                   rtol=1e-5, atol=1e-12)
+
+
+def test_row_argmax_fixture_with_ties_nans_and_signed_zeros(ops, golden):
+    g = golden("torch_row_argmax")
+    assert np.array_equal(to_host(ops.row_argmax(to_dev(g["x"]))), g["index"])
+
+
+@pytest.mark.parametrize("rows,cols", [(1, 1), (1, 151936), (64, 151936), (3, 7), (5, 100003), (200, 4096)])
+@pytest.mark.parametrize("dtype", ["bf16", "f32"])
+def test_row_argmax_bit_exact(ops, oracle, rows, cols, dtype):
+    rng = np.random.default_rng(rows * cols)
+    x = (rng.standard_normal((rows, cols)) * 2).astype(np.float32)
+    if dtype == "bf16":
+        x = f32_to_bf16(x)  # many exact ties at bf16 precision
+    got = to_host(ops.row_argmax(to_dev(x)))
+    assert np.array_equal(got, oracle.row_argmax(x))
+
+
+def test_row_argmax_planted_ties_across_cluster_slices(ops, oracle):
+    cols = 151936
+    x = np.zeros((8, cols), np.float32)
+    for r, (i, j) in enumerate([(0, cols - 1), (5, 90000), (18992, 18993), (37983, 37984), (151935, 151934),
+                                (1, 2), (140000, 20), (75000, 75000)]):
+        x[r, i] = 3.0
+        x[r, j] = 3.0
+    x[7, 0] = np.nan
+    got = to_host(ops.row_argmax(to_dev(x)))
+    assert np.array_equal(got, oracle.row_argmax(x))
+    xb = f32_to_bf16(x)
+    assert np.array_equal(to_host(ops.row_argmax(to_dev(xb))), oracle.row_argmax(xb))
+
+
+def test_row_argmax_row_strided_view(ops, oracle):
+    rng = np.random.default_rng(19)
+    base = seeded_bf16(rng, (16, 5000), 0, 2)
+    view = to_dev(base)[:, :4096]
+    assert np.array_equal(to_host(ops.row_argmax(view)), oracle.row_argmax(np.ascontiguousarray(base[:, :4096])))
+
+
+def test_strided_copy_materialises_permutes(ops):
+    x = torch.arange(2 * 3 * 4 * 5, dtype=torch.float32, device="cuda").reshape(2, 3, 4, 5)
+    for perm in ((0, 2, 1, 3), (3, 2, 1, 0), (1, 0, 3, 2)):
+        v = x.permute(*perm)
+        assert torch.equal(ops.materialize(v), v.contiguous())
+    xb = x.to(torch.bfloat16)
+    v = xb[:, 1:, ::2, 1:]
+    assert torch.equal(ops.materialize(v).view(torch.int16), v.contiguous().view(torch.int16))
+
+
+# ---------------------------------------------------------------------------------------------------------------
+# Edge cases and errors
+# ---------------------------------------------------------------------------------------------------------------
+
+
+def test_empty_inputs_launch_nothing(ops):
+    from cppinf_b200 import capi
+
+    before = capi.launch_count()
+    e = torch.empty((0, 1024), dtype=torch.bfloat16, device="cuda")
+    w = torch.ones(1024, dtype=torch.bfloat16, device="cuda")
+    assert ops.rms_norm(e, w, 1e-6).shape == (0, 1024)
+    assert ops.add(e, e).shape == (0, 1024)
+    assert ops.silu_mul(e, e).shape == (0, 1024)
+    assert capi.launch_count() == before
+
+
+def test_error_paths_raise_reference_exception_types(ops):
+    x = torch.zeros((2, 4), dtype=torch.bfloat16, device="cuda")
+    with pytest.raises(ValueError, match="matching tensor dtypes"):
+        ops.add(x, x.float())
+    with pytest.raises(ValueError, match="matching tensor shapes"):
+        ops.mul(x, x.reshape(4, 2))
+    with pytest.raises(ValueError, match="non-negative epsilon"):
+        ops.rms_norm(x, x[0], -1.0)
+    with pytest.raises(ValueError, match="rank-1 weight"):
+        ops.rms_norm(x, x, 1e-6)
+    with pytest.raises(ValueError, match="square attention"):
+        ops.scaled_causal_softmax_last_dim(torch.zeros((1, 2, 3), device="cuda"), 1.0)
+    with pytest.raises(ValueError, match="finite scale"):
+        ops.scaled_causal_softmax_last_dim(torch.zeros((1, 2, 2), device="cuda"), float("inf"))
+    with pytest.raises(ValueError, match="even head size"):
+        ops.apply_rope(torch.zeros((1, 2, 3), device="cuda"))
+    with pytest.raises(ValueError, match="unsupported dtype"):
+        ops.silu(torch.zeros(4, dtype=torch.float16, device="cuda"))
+
+
+def test_kernels_leave_guard_bands_untouched(ops, oracle):
+    # Outputs written into the middle of a larger buffer: the bytes around them must keep their canary values.
+    rng = np.random.default_rng(20)
+    x, w = seeded_bf16(rng, (37, 1000)), seeded_bf16(rng, (1000,), 1.0, 0.1)
+    canary = torch.full((37 * 1000 + 4096,), -7.0, dtype=torch.bfloat16, device="cuda")
+    out = canary[2048:2048 + 37 * 1000].view(37, 1000)
+    from cppinf_b200 import capi
+
+    dx, dw = to_dev(x), to_dev(w)
+    capi.call("cppinf_rms_norm", capi.DTYPE_BF16, dx.data_ptr(), 1000, dw.data_ptr(), out.data_ptr(), 37, 1000,
+              1e-6, torch.cuda.current_stream().cuda_stream)
+    host = to_host(canary)
+    assert (host[:2048] == bf16_bits([-7.0])[0]).all()
+    assert (host[2048 + 37000:] == bf16_bits([-7.0])[0]).all()
+    assert np.array_equal(host[2048:2048 + 37000].reshape(37, 1000), oracle.rms_norm(x, w, 1e-6))
