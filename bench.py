@@ -76,6 +76,7 @@ def parse_args():
     p.add_argument("--op-steps", type=int, default=2000, help="steps per secondary op measurement")
     p.add_argument("--no-ops", action="store_true", help="skip the secondary per-op measurements")
     p.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline")
+    p.add_argument("--no-e2e", action="store_true", help="skip the host-buffer end-to-end measurement")
     p.add_argument("--cpu-seconds", type=float, default=8.0, help="CPU-baseline sample length")
     return p.parse_args()
 
@@ -502,7 +503,7 @@ def run_ours(args) -> None:
     del wl
     torch.cuda.empty_cache()
 
-    e2e = time_e2e(args.workload, rank, device, min(args.steps, 200))
+    e2e = None if args.no_e2e else time_e2e(args.workload, rank, device, min(args.steps, 200))
     e2e_line = None
     if e2e is not None:
         e2e_ms = max_over_ranks(e2e["ms"])

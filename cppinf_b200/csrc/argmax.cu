@@ -44,16 +44,33 @@ __device__ __forceinline__ unsigned long long umax64(unsigned long long a, unsig
     return a > b ? a : b;
 }
 
+// Per-thread running maximum over elements visited in increasing index order: strict '>' keeps the first of equal
+// values (+0 and -0 included) and never takes NaN; `index < 0` marks "no candidate yet" so a leading -inf counts.
+struct Running {
+    float value = -INFINITY;
+    int index = -1;
+
+    __device__ __forceinline__ void visit(float v, int i) {
+        if (v > value || (index < 0 && v == v)) {
+            value = v;
+            index = i;
+        }
+    }
+
+    __device__ __forceinline__ unsigned long long key() const {
+        return index < 0 ? 0ull : argmax_key(value, static_cast<uint32_t>(index));
+    }
+};
+
 template <typename T>
-__device__ __forceinline__ unsigned long long scan_vector(uint4 raw, uint32_t first, unsigned long long best) {
+__device__ __forceinline__ void scan_vector(uint4 raw, int first, Running& run) {
     using V = Vec16<T>;
     float f[V::kVec];
     V::unpack(raw, f);
 #pragma unroll
     for (int j = 0; j < V::kVec; ++j) {
-        best = umax64(best, argmax_key(f[j], first + j));
+        run.visit(f[j], first + j);
     }
-    return best;
 }
 
 template <typename T>
@@ -76,7 +93,8 @@ __global__ void __launch_bounds__(kThreads) row_argmax_kernel(const void* __rest
     const int64_t lo = per_cta * rank;
     const int64_t hi = lo + per_cta < cols ? lo + per_cta : cols;
 
-    unsigned long long best = 0ull;
+    // Each thread visits its elements in increasing index order (vectors v, v + kThreads, ...; then the tail).
+    Running run;
     if (lo < hi) {
         if (vector_ok) {
             const int64_t nvec = (hi - lo) / kVec;
@@ -90,21 +108,22 @@ __global__ void __launch_bounds__(kThreads) row_argmax_kernel(const void* __rest
                 }
 #pragma unroll
                 for (int u = 0; u < kUnroll; ++u) {
-                    best = scan_vector<T>(raw[u], static_cast<uint32_t>(lo + (v + u * kThreads) * kVec), best);
+                    scan_vector<T>(raw[u], static_cast<int>(lo + (v + u * kThreads) * kVec), run);
                 }
             }
             for (; v < nvec; v += kThreads) {
-                best = scan_vector<T>(ld_stream(base + v * 16), static_cast<uint32_t>(lo + v * kVec), best);
+                scan_vector<T>(ld_stream(base + v * 16), static_cast<int>(lo + v * kVec), run);
             }
             for (int64_t e = lo + nvec * kVec + threadIdx.x; e < hi; e += kThreads) {
-                best = umax64(best, argmax_key(V::load1(xr, e), static_cast<uint32_t>(e)));
+                run.visit(V::load1(xr, e), static_cast<int>(e));
             }
         } else {
             for (int64_t e = lo + threadIdx.x; e < hi; e += kThreads) {
-                best = umax64(best, argmax_key(V::load1(xr, e), static_cast<uint32_t>(e)));
+                run.visit(V::load1(xr, e), static_cast<int>(e));
             }
         }
     }
+    unsigned long long best = run.key();
 
 #pragma unroll
     for (int offset = 16; offset > 0; offset >>= 1) {

@@ -8,10 +8,16 @@
 // rotation first*cos - second*sin / second*cos + first*sin is evaluated with separately rounded f32 products and
 // sums (the library is built with --fmad=false).
 //
-// Fused kernel layout: q [T, Hq, D] and k [T, Hk, D] dense; one head vector (D elements) is held by D/kVec lanes,
-// one 16-byte vector each, so a warp covers 32*kVec/D head vectors. The RMSNorm reduction is a butterfly inside the
-// head's lane group (the library's canonical order: lane l owns chunk l). The split-half partner of chunk l is
-// chunk l ^ (lanes/2), fetched with one shuffle per element.
+// Fused kernel layout: q [T, Hq, D] and k [T, Hk, D] dense. A head vector is held by L = D / (2 * kVec) lanes; lane
+// l holds chunk l of the first half (elements l*kVec ..) and chunk l of the second half (D/2 + l*kVec ..), one 16-byte
+// vector each, so every RoPE pair (i, i + D/2) sits in one lane and no shuffle is needed for the rotation. One warp
+// unit covers kIters groups of 32/L heads of one token; all its loads are issued before any arithmetic. The token's
+// table row and the two weight vectors are read once per unit.
+//
+// Reduction order: the sum of squares of a head equals the library's canonical order (lane c sums chunk c, then a
+// butterfly over lane distances 16, 8, ..., 1 over the D/kVec chunks): here a lane adds its first-half partial to its
+// second-half partial, which is the canonical step at distance D/(2 kVec), and then runs the remaining butterfly
+// steps across the head's L lanes.
 //
 // Roofline: HBM-bound. Algorithmic bytes per token: (Hq + Hk) * D * size read + the same written; the table row
 // (D * 4 bytes per position) and the two weight vectors are shared by all heads and come from L1/L2.
@@ -25,7 +31,8 @@ namespace cppinf::device {
 namespace {
 
 constexpr int kThreads = 256;
-constexpr int kWarps = kThreads / 32;
+constexpr int kQkThreads = 128;
+constexpr int kQkWarps = kQkThreads / 32;
 
 struct QkParams {
     const void* q;
@@ -39,114 +46,121 @@ struct QkParams {
     int64_t position_offset;
     int q_heads;
     int k_heads;
+    int units_per_token;
     float eps;
 };
 
-template <typename T, int kLanes>
-__global__ void __launch_bounds__(kThreads) qk_norm_rope_kernel(QkParams p) {
+template <typename T, int kLanes, int kIters>
+__global__ void __launch_bounds__(kQkThreads) qk_norm_rope_kernel(QkParams p) {
     using V = Vec16<T>;
     constexpr int kVec = V::kVec;
-    constexpr int kDim = kLanes * kVec;
-    constexpr int kHalf = kDim / 2;
-    constexpr int kHeadsPerWarp = 32 / kLanes;
+    constexpr int kHalf = kLanes * kVec;  // D / 2
+    constexpr int kDim = 2 * kHalf;
+    constexpr int kHeadsPerIter = 32 / kLanes;
+    constexpr int kHeadsPerUnit = kHeadsPerIter * kIters;
+    constexpr int64_t kHeadBytes = kDim * static_cast<int64_t>(sizeof(T));
+    constexpr int kHalfBytes = kHalf * static_cast<int>(sizeof(T));
+
     const int lane = threadIdx.x & 31;
-    const int hl = lane % kLanes;        // lane within the head group
-    const int group = lane / kLanes;     // head slot within the warp
+    const int hl = lane % kLanes;  // lane within the head
+    const int slot = lane / kLanes;
     const int heads = p.q_heads + p.k_heads;
-    const int64_t total = p.tokens * heads;
-    const int64_t warp_global = static_cast<int64_t>(blockIdx.x) * kWarps + threadIdx.x / 32;
-    const int64_t hv = warp_global * kHeadsPerWarp + group;
-    const bool active = hv < total;
+    const int64_t unit = static_cast<int64_t>(blockIdx.x) * kQkWarps + threadIdx.x / 32;
+    if (unit >= p.tokens * p.units_per_token) {
+        return;  // the whole warp leaves together
+    }
+    const int64_t t = unit / p.units_per_token;
+    const int h0 = static_cast<int>(unit - t * p.units_per_token) * kHeadsPerUnit;
 
-    int64_t t = 0;
-    const char* src = nullptr;
-    char* dst = nullptr;
-    const char* wsrc = nullptr;
-    if (active) {
-        t = hv / heads;
-        const int h = static_cast<int>(hv - t * heads);
-        if (h < p.q_heads) {
-            const int64_t off = (t * p.q_heads + h) * kDim * static_cast<int64_t>(sizeof(T));
-            src = static_cast<const char*>(p.q) + off;
-            dst = static_cast<char*>(p.q_out) + off;
-            wsrc = static_cast<const char*>(p.qw);
+    // All loads of the unit first: kIters x 2 vectors per lane in flight.
+    uint4 first_raw[kIters];
+    uint4 second_raw[kIters];
+#pragma unroll
+    for (int i = 0; i < kIters; ++i) {
+        const int h = h0 + i * kHeadsPerIter + slot;
+        if (h < heads) {
+            const char* src = h < p.q_heads
+                                  ? static_cast<const char*>(p.q) + (t * p.q_heads + h) * kHeadBytes
+                                  : static_cast<const char*>(p.k) + (t * p.k_heads + (h - p.q_heads)) * kHeadBytes;
+            first_raw[i] = ld_stream(src + hl * 16);
+            second_raw[i] = ld_stream(src + kHalfBytes + hl * 16);
+        }
+    }
+
+    // cos / sin of pairs hl*kVec .. hl*kVec + kVec - 1 at this token's position.
+    const float* row = p.table + (p.position_offset + t) * kDim + hl * kVec;
+    float c[kVec];
+    float s[kVec];
+#pragma unroll
+    for (int j = 0; j < kVec; j += 4) {
+        const float4 cv = ld_cached_f4(row + j);
+        const float4 sv = ld_cached_f4(row + kHalf + j);
+        c[j] = cv.x;
+        c[j + 1] = cv.y;
+        c[j + 2] = cv.z;
+        c[j + 3] = cv.w;
+        s[j] = sv.x;
+        s[j + 1] = sv.y;
+        s[j + 2] = sv.z;
+        s[j + 3] = sv.w;
+    }
+    const uint4 qw_first = ld_cached(static_cast<const char*>(p.qw) + hl * 16);
+    const uint4 qw_second = ld_cached(static_cast<const char*>(p.qw) + kHalfBytes + hl * 16);
+    const uint4 kw_first = ld_cached(static_cast<const char*>(p.kw) + hl * 16);
+    const uint4 kw_second = ld_cached(static_cast<const char*>(p.kw) + kHalfBytes + hl * 16);
+
+#pragma unroll
+    for (int i = 0; i < kIters; ++i) {
+        const int h = h0 + i * kHeadsPerIter + slot;
+        const bool active = h < heads;
+        float a[kVec];
+        float b[kVec];
+        if (active) {
+            V::unpack(first_raw[i], a);
+            V::unpack(second_raw[i], b);
         } else {
-            const int64_t off = (t * p.k_heads + (h - p.q_heads)) * kDim * static_cast<int64_t>(sizeof(T));
-            src = static_cast<const char*>(p.k) + off;
-            dst = static_cast<char*>(p.k_out) + off;
-            wsrc = static_cast<const char*>(p.kw);
+#pragma unroll
+            for (int j = 0; j < kVec; ++j) {
+                a[j] = 0.0f;
+                b[j] = 0.0f;
+            }
         }
-    }
-
-    float x[kVec];
-    float ss = 0.0f;
-    if (active) {
-        V::unpack(ld_stream(src + hl * 16), x);
+        float sa = 0.0f;
+        float sb = 0.0f;
 #pragma unroll
         for (int j = 0; j < kVec; ++j) {
-            ss = ss + x[j] * x[j];
+            sa = sa + a[j] * a[j];
         }
-    } else {
 #pragma unroll
         for (int j = 0; j < kVec; ++j) {
-            x[j] = 0.0f;
+            sb = sb + b[j] * b[j];
         }
-    }
-    // All 32 lanes take part in the shuffles; groups never exchange data because every offset is < kLanes.
-    ss = group_sum<kLanes>(ss);
-    const float mean = ss / static_cast<float>(kDim);
-    const float rms = sqrtf(mean + p.eps);
-    const float inv = 1.0f / rms;
-
-    float n[kVec];
-    if (active) {
-        float w[kVec];
-        V::unpack(ld_cached(wsrc + hl * 16), w);
+        // Every lane of the warp takes part; offsets below kLanes never leave the head's lane group.
+        const float ss = group_sum<kLanes>(sa + sb);
+        const float mean = ss / static_cast<float>(kDim);
+        const float rms = sqrtf(mean + p.eps);
+        const float inv = 1.0f / rms;
+        if (active) {
+            const bool is_q = h < p.q_heads;
+            float wa[kVec];
+            float wb[kVec];
+            V::unpack(is_q ? qw_first : kw_first, wa);
+            V::unpack(is_q ? qw_second : kw_second, wb);
+            float out_a[kVec];
+            float out_b[kVec];
 #pragma unroll
-        for (int j = 0; j < kVec; ++j) {
-            // The reference's rms_norm returns a tensor of the model dtype; RoPE reads those rounded values.
-            n[j] = V::quantize((x[j] * inv) * w[j]);
+            for (int j = 0; j < kVec; ++j) {
+                // The reference's rms_norm returns a tensor of the model dtype; RoPE reads those rounded values.
+                const float n1 = V::quantize((a[j] * inv) * wa[j]);
+                const float n2 = V::quantize((b[j] * inv) * wb[j]);
+                out_a[j] = n1 * c[j] - n2 * s[j];  // first  * cos - second * sin  (src/nn/rope.cpp:115-116)
+                out_b[j] = n2 * c[j] + n1 * s[j];  // second * cos + first  * sin  (src/nn/rope.cpp:117-118)
+            }
+            char* dst = h < p.q_heads ? static_cast<char*>(p.q_out) + (t * p.q_heads + h) * kHeadBytes
+                                      : static_cast<char*>(p.k_out) + (t * p.k_heads + (h - p.q_heads)) * kHeadBytes;
+            st_stream(dst + hl * 16, V::pack(out_a));
+            st_stream(dst + kHalfBytes + hl * 16, V::pack(out_b));
         }
-    } else {
-#pragma unroll
-        for (int j = 0; j < kVec; ++j) {
-            n[j] = 0.0f;
-        }
-    }
-
-    float partner[kVec];
-#pragma unroll
-    for (int j = 0; j < kVec; ++j) {
-        partner[j] = __shfl_xor_sync(0xffffffffu, n[j], kLanes / 2);
-    }
-
-    if (active) {
-        const bool first_half = hl < kLanes / 2;
-        const int pair0 = (first_half ? hl : hl - kLanes / 2) * kVec;
-        const float* row = p.table + (p.position_offset + t) * kDim;
-        float c[kVec];
-        float s[kVec];
-#pragma unroll
-        for (int j = 0; j < kVec; j += 4) {
-            const float4 cv = ld_cached_f4(row + pair0 + j);
-            const float4 sv = ld_cached_f4(row + kHalf + pair0 + j);
-            c[j] = cv.x;
-            c[j + 1] = cv.y;
-            c[j + 2] = cv.z;
-            c[j + 3] = cv.w;
-            s[j] = sv.x;
-            s[j + 1] = sv.y;
-            s[j + 2] = sv.z;
-            s[j + 3] = sv.w;
-        }
-        float out[kVec];
-#pragma unroll
-        for (int j = 0; j < kVec; ++j) {
-            // first  = first * cos - second * sin   (src/nn/rope.cpp:115-116)
-            // second = second * cos + first * sin   (src/nn/rope.cpp:117-118)
-            out[j] = first_half ? (n[j] * c[j] - partner[j] * s[j]) : (n[j] * c[j] + partner[j] * s[j]);
-        }
-        st_stream(dst + hl * 16, V::pack(out));
     }
 }
 
@@ -187,16 +201,23 @@ __global__ void __launch_bounds__(kThreads) rope_kernel(RopeParams p, int64_t to
 }
 
 template <typename T, int kLanes>
-void launch_qk(const QkParams& p, cudaStream_t s) {
-    constexpr int kHeadsPerBlock = kWarps * (32 / kLanes);
-    const int64_t total = p.tokens * (p.q_heads + p.k_heads);
-    const auto blocks = static_cast<unsigned>(runtime::ceil_div(total, kHeadsPerBlock));
-    qk_norm_rope_kernel<T, kLanes><<<blocks, kThreads, 0, s>>>(p);
+void launch_qk(QkParams p, cudaStream_t s) {
+    constexpr int kHeadsPerIter = 32 / kLanes;
+    constexpr int kIters = kHeadsPerIter >= 8 ? 1 : 8 / kHeadsPerIter;
+    constexpr int kHeadsPerUnit = kHeadsPerIter * kIters;
+    const int heads = p.q_heads + p.k_heads;
+    p.units_per_token = (heads + kHeadsPerUnit - 1) / kHeadsPerUnit;
+    const int64_t units = p.tokens * p.units_per_token;
+    const auto blocks = static_cast<unsigned>(runtime::ceil_div(units, kQkWarps));
+    qk_norm_rope_kernel<T, kLanes, kIters><<<blocks, kQkThreads, 0, s>>>(p);
 }
 
 template <typename T>
 bool dispatch_qk(const QkParams& p, int lanes, cudaStream_t s) {
     switch (lanes) {
+    case 1:
+        launch_qk<T, 1>(p, s);
+        return true;
     case 2:
         launch_qk<T, 2>(p, s);
         return true;
@@ -208,9 +229,6 @@ bool dispatch_qk(const QkParams& p, int lanes, cudaStream_t s) {
         return true;
     case 16:
         launch_qk<T, 16>(p, s);
-        return true;
-    case 32:
-        launch_qk<T, 32>(p, s);
         return true;
     default:
         return false;
@@ -300,10 +318,10 @@ int cppinf_qk_norm_rope(cppinf_dtype dtype, const void* q, const void* k, const 
     CPPINF_REQUIRE(position_offset + tokens <= table_positions, CPPINF_ERR_OUT_OF_RANGE,
                    "qk_norm_rope positions exceed the rope table.");
     const int vec = dtype == CPPINF_DTYPE_BF16 ? 8 : 4;
-    const int64_t lanes = head_dim / vec;
-    CPPINF_REQUIRE(head_dim % (2 * vec) == 0 && lanes >= 2 && lanes <= 32 && (lanes & (lanes - 1)) == 0,
+    const int64_t lanes = head_dim / (2 * vec);
+    CPPINF_REQUIRE(head_dim % (2 * vec) == 0 && lanes >= 1 && lanes <= 16 && (lanes & (lanes - 1)) == 0,
                    CPPINF_ERR_UNSUPPORTED,
-                   "qk_norm_rope needs head_dim / (16 / element size) to be a power of two between 2 and 32.");
+                   "qk_norm_rope needs head_dim / (2 * (16 / element size)) to be a power of two from 1 to 16.");
     if (tokens == 0 || q_heads + k_heads == 0) {
         return rt::ok();
     }
@@ -313,8 +331,11 @@ int cppinf_qk_norm_rope(cppinf_dtype dtype, const void* q, const void* k, const 
                                                              rt::aligned16(q_out))) &&
                        (k_heads == 0 || (rt::aligned16(k) && rt::aligned16(k_weight) && rt::aligned16(k_out))),
                    CPPINF_ERR_UNSUPPORTED, "qk_norm_rope requires 16-byte aligned operands.");
-    QkParams p{q,      k,        q_weight,        k_weight, q_out, k_out, table, tokens, position_offset,
-               static_cast<int>(q_heads), static_cast<int>(k_heads), eps};
+    // The kernel reads both weight vectors for every unit; a missing one is replaced by the other (never used).
+    const void* qw = q_heads == 0 ? k_weight : q_weight;
+    const void* kw = k_heads == 0 ? q_weight : k_weight;
+    QkParams p{q, k, qw, kw, q_out, k_out, table, tokens, position_offset, static_cast<int>(q_heads),
+               static_cast<int>(k_heads), 0, eps};
     const auto s = rt::as_stream(stream);
     const bool launched = dtype == CPPINF_DTYPE_BF16 ? dispatch_qk<bf16>(p, static_cast<int>(lanes), s)
                                                      : dispatch_qk<float>(p, static_cast<int>(lanes), s);

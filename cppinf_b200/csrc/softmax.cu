@@ -61,9 +61,12 @@ struct PositionCausalRows {
     static constexpr bool kZeroOnEmpty = true;
 };
 
+// Rows of at most 32 * kChunks * kVec elements (<= 4096), so element indices fit 32 bits. At most 128 registers per
+// thread (two blocks per SM): the row occupies kChunks * kVec of them.
 template <typename T, int kChunks, typename Rows>
-__global__ void __launch_bounds__(kThreads) softmax_regs_kernel(const void* __restrict__ x, void* __restrict__ y,
-                                                                int64_t rows, int64_t width, float scale, Rows rule) {
+__global__ void __launch_bounds__(kThreads, 2) softmax_regs_kernel(const void* __restrict__ x, void* __restrict__ y,
+                                                                   int64_t rows, int64_t width, float scale,
+                                                                   Rows rule) {
     using V = Vec16<T>;
     constexpr int kVec = V::kVec;
     const int lane = threadIdx.x & 31;
@@ -71,18 +74,17 @@ __global__ void __launch_bounds__(kThreads) softmax_regs_kernel(const void* __re
     const int nchunks = static_cast<int>(width / kVec);
 
     for (int64_t row = static_cast<int64_t>(blockIdx.x) * kWarps + threadIdx.x / 32; row < rows; row += warp_stride) {
-        const int64_t n = rule.visible(row);
-        const int vis_chunks = static_cast<int>((n + kVec - 1) / kVec);
+        const int n = static_cast<int>(rule.visible(row));
+        const int vis_chunks = (n + kVec - 1) / kVec;
         const char* xr = static_cast<const char*>(x) + row * width * static_cast<int64_t>(sizeof(T));
         char* yr = static_cast<char*>(y) + row * width * static_cast<int64_t>(sizeof(T));
 
         float v[kChunks][kVec];
-        uint4 raw[kChunks];
 #pragma unroll
         for (int i = 0; i < kChunks; ++i) {
             const int c = lane + 32 * i;
             if (c < vis_chunks) {
-                raw[i] = ld_stream(xr + static_cast<int64_t>(c) * 16);
+                V::unpack(ld_stream(xr + c * 16), v[i]);
             }
         }
         float m = -INFINITY;
@@ -90,11 +92,9 @@ __global__ void __launch_bounds__(kThreads) softmax_regs_kernel(const void* __re
         for (int i = 0; i < kChunks; ++i) {
             const int c = lane + 32 * i;
             if (c < vis_chunks) {
-                V::unpack(raw[i], v[i]);
 #pragma unroll
                 for (int j = 0; j < kVec; ++j) {
-                    const int64_t k = static_cast<int64_t>(c) * kVec + j;
-                    v[i][j] = k < n ? v[i][j] * scale : -INFINITY;
+                    v[i][j] = c * kVec + j < n ? v[i][j] * scale : -INFINITY;
                     m = fmaxf(m, v[i][j]);
                 }
             }
@@ -108,8 +108,7 @@ __global__ void __launch_bounds__(kThreads) softmax_regs_kernel(const void* __re
             if (c < vis_chunks) {
 #pragma unroll
                 for (int j = 0; j < kVec; ++j) {
-                    const int64_t k = static_cast<int64_t>(c) * kVec + j;
-                    v[i][j] = k < n ? expf(v[i][j] - m) : 0.0f;
+                    v[i][j] = c * kVec + j < n ? expf(v[i][j] - m) : 0.0f;
                     sum = sum + v[i][j];
                 }
             }
@@ -126,8 +125,7 @@ __global__ void __launch_bounds__(kThreads) softmax_regs_kernel(const void* __re
                 if (c < vis_chunks) {
 #pragma unroll
                     for (int j = 0; j < kVec; ++j) {
-                        const int64_t k = static_cast<int64_t>(c) * kVec + j;
-                        out[j] = k < n ? (zero_row ? 0.0f : v[i][j] / sum) : masked;
+                        out[j] = c * kVec + j < n ? (zero_row ? 0.0f : v[i][j] / sum) : masked;
                     }
                 } else {
 #pragma unroll
@@ -186,17 +184,19 @@ int launch_softmax(const void* x, void* y, int64_t rows, int64_t width, float sc
     const auto s = runtime::as_stream(stream);
     const bool vector_ok = width % kVec == 0 && runtime::aligned16(x) && runtime::aligned16(y);
     const int64_t per_lane = runtime::ceil_div(width / kVec, 32);
-    if (vector_ok && per_lane <= 16) {
+    // A lane holds at most 64 f32 row values in registers: 16 vectors of f32 or 8 of bf16.
+    constexpr int kMaxChunks = sizeof(T) == 2 ? 8 : 16;
+    if (vector_ok && per_lane <= kMaxChunks) {
         if (per_lane <= 1) {
             softmax_regs_kernel<T, 1, Rows><<<blocks, kThreads, 0, s>>>(x, y, rows, width, scale, rule);
         } else if (per_lane <= 2) {
             softmax_regs_kernel<T, 2, Rows><<<blocks, kThreads, 0, s>>>(x, y, rows, width, scale, rule);
         } else if (per_lane <= 4) {
             softmax_regs_kernel<T, 4, Rows><<<blocks, kThreads, 0, s>>>(x, y, rows, width, scale, rule);
-        } else if (per_lane <= 8) {
+        } else if (per_lane <= 8 || kMaxChunks == 8) {
             softmax_regs_kernel<T, 8, Rows><<<blocks, kThreads, 0, s>>>(x, y, rows, width, scale, rule);
         } else {
-            softmax_regs_kernel<T, 16, Rows><<<blocks, kThreads, 0, s>>>(x, y, rows, width, scale, rule);
+            softmax_regs_kernel<T, kMaxChunks, Rows><<<blocks, kThreads, 0, s>>>(x, y, rows, width, scale, rule);
         }
     } else {
         softmax_stream_kernel<T, Rows><<<blocks, kThreads, 0, s>>>(x, y, rows, width, scale, rule);

@@ -198,7 +198,8 @@ void oracle_add_rms_norm(int dtype, const void* a, const void* b, const void* w,
 }
 
 /* ops::softmax_last_dim, src/ops/nn_ops.cpp:74-99 (oneDNN softmax_accurate in the input dtype, computed in f32):
- * y = exp(x - max) / sum, summed left to right. */
+ * y = exp(x - max) / sum. oneDNN's summation order is unspecified; the oracle sums the f32 exponentials in double
+ * and rounds once, the order-free value every f32 order approximates. */
 void oracle_softmax_last_dim(int dtype, const void* x, void* y, int64_t rows, int64_t width) {
 #pragma omp parallel for schedule(static)
     for (int64_t r = 0; r < rows; ++r) {
@@ -208,10 +209,11 @@ void oracle_softmax_last_dim(int dtype, const void* x, void* y, int64_t rows, in
             const float v = load(dtype, x, base + k);
             m = (m < v) ? v : m;
         }
-        float sum = 0.0f;
+        double acc = 0.0;
         for (int64_t k = 0; k < width; ++k) {
-            sum += expf(load(dtype, x, base + k) - m);
+            acc += (double)expf(load(dtype, x, base + k) - m);
         }
+        const float sum = (float)acc;
         for (int64_t k = 0; k < width; ++k) {
             store(dtype, y, base + k, expf(load(dtype, x, base + k) - m) / sum);
         }
