@@ -77,6 +77,7 @@ template <typename T>
 __global__ void __launch_bounds__(kThreads) row_argmax_kernel(const void* __restrict__ x, int64_t cols,
                                                               int64_t row_stride, int64_t* __restrict__ out,
                                                               bool vector_ok) {
+    grid_dependency_begin();
     using V = Vec16<T>;
     constexpr int kVec = V::kVec;
     __shared__ unsigned long long warp_best[kWarps];
@@ -191,28 +192,15 @@ int cppinf_row_argmax(cppinf_dtype dtype, const void* x, int64_t rows, int64_t c
         cluster *= 2;
     }
 
-    cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3(static_cast<unsigned>(rows * cluster), 1, 1);
-    cfg.blockDim = dim3(kThreads, 1, 1);
-    cfg.dynamicSmemBytes = 0;
-    cfg.stream = rt::as_stream(stream);
-    cudaLaunchAttribute attr[1];
-    attr[0].id = cudaLaunchAttributeClusterDimension;
-    attr[0].val.clusterDim.x = static_cast<unsigned>(cluster);
-    attr[0].val.clusterDim.y = 1;
-    attr[0].val.clusterDim.z = 1;
-    cfg.attrs = attr;
-    cfg.numAttrs = 1;
-    cudaError_t err;
-    if (dtype == CPPINF_DTYPE_BF16) {
-        err = cudaLaunchKernelEx(&cfg, row_argmax_kernel<bf16>, x, cols, row_stride, out, vector_ok);
-    } else {
-        err = cudaLaunchKernelEx(&cfg, row_argmax_kernel<float>, x, cols, row_stride, out, vector_ok);
-    }
-    if (err != cudaSuccess) {
-        return rt::cuda_fail(err, "cudaLaunchKernelEx(row_argmax)");
-    }
-    return rt::after_launch("row_argmax");
+    const dim3 grid(static_cast<unsigned>(rows * cluster));
+    const auto s = rt::as_stream(stream);
+    const cudaError_t launch_err =
+        dtype == CPPINF_DTYPE_BF16
+            ? rt::launch(row_argmax_kernel<bf16>, grid, dim3(kThreads), s, static_cast<unsigned>(cluster), x, cols,
+                         row_stride, out, vector_ok)
+            : rt::launch(row_argmax_kernel<float>, grid, dim3(kThreads), s, static_cast<unsigned>(cluster), x, cols,
+                         row_stride, out, vector_ok);
+    return rt::launched(launch_err, "row_argmax");
 }
 
 }  // extern "C"

@@ -17,6 +17,16 @@ namespace cppinf::device {
 
 using bf16 = __nv_bfloat16;
 
+// ---- programmatic dependent launch -------------------------------------------------------------------------------
+
+// First statement of every kernel: waits until the previous grid in the stream has completed and its memory writes
+// are visible (a no-op when the launch did not allow programmatic overlap), then lets the next grid be scheduled
+// as soon as all CTAs of this one have started.
+__device__ __forceinline__ void grid_dependency_begin() {
+    asm volatile("griddepcontrol.wait;" ::: "memory");
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
 // ---- 128-bit memory access -------------------------------------------------------------------------------------
 
 // Read-only, streaming load: bypasses L1 allocation (the data is touched once) and asks L2 for 256-byte sectors so

@@ -35,6 +35,7 @@ __device__ __forceinline__ float silu_f32(float x) {
 template <typename Functor>
 __global__ void __launch_bounds__(kThreads) elementwise_kernel(Functor f, int64_t n_vec, int64_t vec_elems,
                                                                int64_t count) {
+    grid_dependency_begin();
     const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
     const int64_t tid = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
     int64_t i = tid;
@@ -198,6 +199,7 @@ struct StridedParams {
 template <typename E>
 __global__ void __launch_bounds__(kThreads) strided_copy_kernel(const E* __restrict__ x, E* __restrict__ y,
                                                                 StridedParams p, int64_t count) {
+    grid_dependency_begin();
     const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
     for (int64_t e = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; e < count; e += stride) {
         int64_t rem = e;
@@ -223,9 +225,9 @@ int launch_elementwise(const Functor& f, bool vector_ok, int64_t vec_elems, int6
                        const char* name) {
     const int64_t n_vec = vector_ok ? count / vec_elems : 0;
     const int64_t work = n_vec > 0 ? n_vec : count;
-    elementwise_kernel<Functor><<<static_cast<unsigned>(wave_blocks(work)), kThreads, 0, runtime::as_stream(stream)>>>(
+    const cudaError_t launch_err = ::cppinf::runtime::launch(elementwise_kernel<Functor>, dim3(static_cast<unsigned>(wave_blocks(work))), dim3(kThreads), runtime::as_stream(stream), 1u, 
         f, n_vec, vec_elems, count);
-    return runtime::after_launch(name);
+    return runtime::launched(launch_err, name);
 }
 
 int check_common(cppinf_dtype dtype, int64_t count, const char* op) {
@@ -352,14 +354,15 @@ int cppinf_strided_copy(cppinf_dtype dtype, const void* x, int64_t rank, const i
     }
     CPPINF_REQUIRE(x && y, CPPINF_ERR_INVALID_ARGUMENT, "strided_copy received a null pointer.");
     const auto blocks = static_cast<unsigned>(wave_blocks(count));
+    cudaError_t launch_err;
     if (dtype == CPPINF_DTYPE_BF16) {
-        strided_copy_kernel<unsigned short><<<blocks, kThreads, 0, rt::as_stream(stream)>>>(
+        launch_err = ::cppinf::runtime::launch(strided_copy_kernel<unsigned short>, dim3(blocks), dim3(kThreads), rt::as_stream(stream), 1u, 
             static_cast<const unsigned short*>(x), static_cast<unsigned short*>(y), p, count);
     } else {
-        strided_copy_kernel<float><<<blocks, kThreads, 0, rt::as_stream(stream)>>>(static_cast<const float*>(x),
+        launch_err = ::cppinf::runtime::launch(strided_copy_kernel<float>, dim3(blocks), dim3(kThreads), rt::as_stream(stream), 1u, static_cast<const float*>(x),
                                                                                    static_cast<float*>(y), p, count);
     }
-    return rt::after_launch("strided_copy");
+    return rt::launched(launch_err, "strided_copy");
 }
 
 }  // extern "C"

@@ -38,6 +38,7 @@ struct RmsParams {
 // Register-resident variant: each lane holds kChunks 16-byte vectors of its row.
 template <typename T, int kChunks, bool kAdd>
 __global__ void __launch_bounds__(kThreads) rms_norm_regs_kernel(RmsParams p) {
+    grid_dependency_begin();
     using V = Vec16<T>;
     constexpr int kVec = V::kVec;
     const int lane = threadIdx.x & 31;
@@ -113,6 +114,7 @@ __global__ void __launch_bounds__(kThreads) rms_norm_regs_kernel(RmsParams p) {
 // 16-byte vector width, or 1 when the operands are not vector-aligned.
 template <typename T, bool kAdd>
 __global__ void __launch_bounds__(kThreads) rms_norm_stream_kernel(RmsParams p, int chunk) {
+    grid_dependency_begin();
     using V = Vec16<T>;
     const int lane = threadIdx.x & 31;
     const float width_f = static_cast<float>(p.width);
@@ -157,20 +159,21 @@ int launch_rms(const RmsParams& p, bool vector_ok, void* stream, const char* nam
     const auto blocks = static_cast<unsigned>(needed < wave ? needed : wave);
     auto s = runtime::as_stream(stream);
     const int chunks_per_lane = static_cast<int>(runtime::ceil_div(p.width / kVec, 32));
+    cudaError_t launch_err;
     if (vector_ok && chunks_per_lane <= 8) {
         if (chunks_per_lane <= 1) {
-            rms_norm_regs_kernel<T, 1, kAdd><<<blocks, kThreads, 0, s>>>(p);
+            launch_err = ::cppinf::runtime::launch(rms_norm_regs_kernel<T, 1, kAdd>, dim3(blocks), dim3(kThreads), s, 1u, p);
         } else if (chunks_per_lane <= 2) {
-            rms_norm_regs_kernel<T, 2, kAdd><<<blocks, kThreads, 0, s>>>(p);
+            launch_err = ::cppinf::runtime::launch(rms_norm_regs_kernel<T, 2, kAdd>, dim3(blocks), dim3(kThreads), s, 1u, p);
         } else if (chunks_per_lane <= 4) {
-            rms_norm_regs_kernel<T, 4, kAdd><<<blocks, kThreads, 0, s>>>(p);
+            launch_err = ::cppinf::runtime::launch(rms_norm_regs_kernel<T, 4, kAdd>, dim3(blocks), dim3(kThreads), s, 1u, p);
         } else {
-            rms_norm_regs_kernel<T, 8, kAdd><<<blocks, kThreads, 0, s>>>(p);
+            launch_err = ::cppinf::runtime::launch(rms_norm_regs_kernel<T, 8, kAdd>, dim3(blocks), dim3(kThreads), s, 1u, p);
         }
     } else {
-        rms_norm_stream_kernel<T, kAdd><<<blocks, kThreads, 0, s>>>(p, vector_ok ? kVec : 1);
+        launch_err = ::cppinf::runtime::launch(rms_norm_stream_kernel<T, kAdd>, dim3(blocks), dim3(kThreads), s, 1u, p, vector_ok ? kVec : 1);
     }
-    return runtime::after_launch(name);
+    return runtime::launched(launch_err, name);
 }
 
 int validate_rows(cppinf_dtype dtype, int64_t rows, int64_t width, float eps, const char* op) {

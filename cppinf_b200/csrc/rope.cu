@@ -52,6 +52,7 @@ struct QkParams {
 
 template <typename T, int kLanes, int kIters>
 __global__ void __launch_bounds__(kQkThreads) qk_norm_rope_kernel(QkParams p) {
+    grid_dependency_begin();
     using V = Vec16<T>;
     constexpr int kVec = V::kVec;
     constexpr int kHalf = kLanes * kVec;  // D / 2
@@ -178,6 +179,7 @@ struct RopeParams {
 // Standalone apply_rope on a strided rank-3 view: one thread per (dim0, dim1, pair).
 template <typename T>
 __global__ void __launch_bounds__(kThreads) rope_kernel(RopeParams p, int64_t total_pairs) {
+    grid_dependency_begin();
     using V = Vec16<T>;
     const int half = p.head_dim / 2;
     const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
@@ -200,38 +202,48 @@ __global__ void __launch_bounds__(kThreads) rope_kernel(RopeParams p, int64_t to
     }
 }
 
-template <typename T, int kLanes>
-void launch_qk(QkParams p, cudaStream_t s) {
-    constexpr int kHeadsPerIter = 32 / kLanes;
-    constexpr int kIters = kHeadsPerIter >= 8 ? 1 : 8 / kHeadsPerIter;
-    constexpr int kHeadsPerUnit = kHeadsPerIter * kIters;
+template <typename T, int kLanes, int kIters>
+cudaError_t launch_qk_units(QkParams p, cudaStream_t s) {
+    constexpr int kHeadsPerUnit = (32 / kLanes) * kIters;
     const int heads = p.q_heads + p.k_heads;
     p.units_per_token = (heads + kHeadsPerUnit - 1) / kHeadsPerUnit;
     const int64_t units = p.tokens * p.units_per_token;
     const auto blocks = static_cast<unsigned>(runtime::ceil_div(units, kQkWarps));
-    qk_norm_rope_kernel<T, kLanes, kIters><<<blocks, kQkThreads, 0, s>>>(p);
+    return ::cppinf::runtime::launch(qk_norm_rope_kernel<T, kLanes, kIters>, dim3(blocks), dim3(kQkThreads), s, 1u, p);
+}
+
+// A warp unit covers a whole token when its heads fit in at most 8 iterations (the Qwen3 shapes: 24 heads of 128 in
+// 6 iterations of 4), so a 2048-token batch is a single wave of warps; larger head counts take several 8-iteration
+// units per token.
+template <typename T, int kLanes>
+cudaError_t launch_qk(const QkParams& p, cudaStream_t s) {
+    constexpr int kHeadsPerIter = 32 / kLanes;
+    const int iters = (p.q_heads + p.k_heads + kHeadsPerIter - 1) / kHeadsPerIter;
+    if (iters <= 2) {
+        return launch_qk_units<T, kLanes, 2>(p, s);
+    }
+    if (iters <= 4) {
+        return launch_qk_units<T, kLanes, 4>(p, s);
+    }
+    if (iters <= 6) {
+        return launch_qk_units<T, kLanes, 6>(p, s);
+    }
+    return launch_qk_units<T, kLanes, 8>(p, s);
 }
 
 template <typename T>
-bool dispatch_qk(const QkParams& p, int lanes, cudaStream_t s) {
+cudaError_t dispatch_qk(const QkParams& p, int lanes, cudaStream_t s) {
     switch (lanes) {
     case 1:
-        launch_qk<T, 1>(p, s);
-        return true;
+        return launch_qk<T, 1>(p, s);
     case 2:
-        launch_qk<T, 2>(p, s);
-        return true;
+        return launch_qk<T, 2>(p, s);
     case 4:
-        launch_qk<T, 4>(p, s);
-        return true;
+        return launch_qk<T, 4>(p, s);
     case 8:
-        launch_qk<T, 8>(p, s);
-        return true;
-    case 16:
-        launch_qk<T, 16>(p, s);
-        return true;
+        return launch_qk<T, 8>(p, s);
     default:
-        return false;
+        return launch_qk<T, 16>(p, s);
     }
 }
 
@@ -294,12 +306,13 @@ int cppinf_rope(cppinf_dtype dtype, const void* x, int64_t dim0, int64_t dim1, i
     const int64_t wave = static_cast<int64_t>(rt::sm_count()) * (per_sm > 0 ? per_sm : 1);
     const int64_t needed = rt::ceil_div(total_pairs, kThreads);
     const auto blocks = static_cast<unsigned>(needed < wave ? needed : wave);
+    cudaError_t launch_err;
     if (dtype == CPPINF_DTYPE_BF16) {
-        rope_kernel<bf16><<<blocks, kThreads, 0, rt::as_stream(stream)>>>(p, total_pairs);
+        launch_err = ::cppinf::runtime::launch(rope_kernel<bf16>, dim3(blocks), dim3(kThreads), rt::as_stream(stream), 1u, p, total_pairs);
     } else {
-        rope_kernel<float><<<blocks, kThreads, 0, rt::as_stream(stream)>>>(p, total_pairs);
+        launch_err = ::cppinf::runtime::launch(rope_kernel<float>, dim3(blocks), dim3(kThreads), rt::as_stream(stream), 1u, p, total_pairs);
     }
-    return rt::after_launch("rope");
+    return rt::launched(launch_err, "rope");
 }
 
 int cppinf_qk_norm_rope(cppinf_dtype dtype, const void* q, const void* k, const void* q_weight,
@@ -337,10 +350,9 @@ int cppinf_qk_norm_rope(cppinf_dtype dtype, const void* q, const void* k, const 
     QkParams p{q, k, qw, kw, q_out, k_out, table, tokens, position_offset, static_cast<int>(q_heads),
                static_cast<int>(k_heads), 0, eps};
     const auto s = rt::as_stream(stream);
-    const bool launched = dtype == CPPINF_DTYPE_BF16 ? dispatch_qk<bf16>(p, static_cast<int>(lanes), s)
-                                                     : dispatch_qk<float>(p, static_cast<int>(lanes), s);
-    CPPINF_REQUIRE(launched, CPPINF_ERR_UNSUPPORTED, "qk_norm_rope has no kernel for this head size.");
-    return rt::after_launch("qk_norm_rope");
+    const cudaError_t launch_err = dtype == CPPINF_DTYPE_BF16 ? dispatch_qk<bf16>(p, static_cast<int>(lanes), s)
+                                                              : dispatch_qk<float>(p, static_cast<int>(lanes), s);
+    return rt::launched(launch_err, "qk_norm_rope");
 }
 
 }  // extern "C"

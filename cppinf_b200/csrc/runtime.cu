@@ -70,6 +70,14 @@ int after_launch(const char* kernel_name) {
     return ok();
 }
 
+int launched(cudaError_t err, const char* kernel_name) {
+    if (err != cudaSuccess) {
+        cudaGetLastError();  // clear the launch error so it does not leak into later calls
+        return fail(CPPINF_ERR_CUDA, std::string("launch of ") + kernel_name + " failed: " + cudaGetErrorString(err));
+    }
+    return after_launch(kernel_name);
+}
+
 int sm_count() {
     return props_for_current_device().sm_count;
 }

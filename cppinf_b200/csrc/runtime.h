@@ -7,6 +7,7 @@
 #include <atomic>
 #include <cstdint>
 #include <string>
+#include <utility>
 
 #include "cppinf_b200.h"
 
@@ -49,6 +50,38 @@ inline std::size_t dtype_size(cppinf_dtype dtype) {
 inline bool valid_dtype(cppinf_dtype dtype) {
     return dtype == CPPINF_DTYPE_BF16 || dtype == CPPINF_DTYPE_F32;
 }
+
+// Launches `kernel` with programmatic dependent launch allowed: the grid may be scheduled while the previous kernel
+// in the stream is still finishing. Every kernel of this library executes griddepcontrol.wait before it reads global
+// memory, which waits for the previous grid to complete and its writes to become visible, so results are the same
+// as with plain stream order; only launch latency and the previous grid's tail overlap. `cluster_x` > 1 adds a
+// thread-block cluster dimension.
+template <typename... KernelArgs, typename... Args>
+cudaError_t launch(void (*kernel)(KernelArgs...), dim3 grid, dim3 block, cudaStream_t stream, unsigned cluster_x,
+                   Args&&... args) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = 0;
+    cfg.stream = stream;
+    cudaLaunchAttribute attrs[2];
+    attrs[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attrs[0].val.programmaticStreamSerializationAllowed = 1;
+    unsigned n = 1;
+    if (cluster_x > 1) {
+        attrs[1].id = cudaLaunchAttributeClusterDimension;
+        attrs[1].val.clusterDim.x = cluster_x;
+        attrs[1].val.clusterDim.y = 1;
+        attrs[1].val.clusterDim.z = 1;
+        n = 2;
+    }
+    cfg.attrs = attrs;
+    cfg.numAttrs = n;
+    return cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
+}
+
+// Records a failed launch (or checks the one just enqueued) and counts it.
+int launched(cudaError_t err, const char* kernel_name);
 
 }  // namespace cppinf::runtime
 

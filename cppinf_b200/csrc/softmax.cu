@@ -61,12 +61,32 @@ struct PositionCausalRows {
     static constexpr bool kZeroOnEmpty = true;
 };
 
+// Pairwise max / sum of one 16-byte chunk (4 or 8 values).
+template <int kN>
+__device__ __forceinline__ float tree_max(const float (&v)[kN]) {
+    if constexpr (kN == 4) {
+        return fmaxf(fmaxf(v[0], v[1]), fmaxf(v[2], v[3]));
+    } else {
+        return fmaxf(fmaxf(fmaxf(v[0], v[1]), fmaxf(v[2], v[3])), fmaxf(fmaxf(v[4], v[5]), fmaxf(v[6], v[7])));
+    }
+}
+
+template <int kN>
+__device__ __forceinline__ float tree_sum(const float (&v)[kN]) {
+    if constexpr (kN == 4) {
+        return (v[0] + v[1]) + (v[2] + v[3]);
+    } else {
+        return ((v[0] + v[1]) + (v[2] + v[3])) + ((v[4] + v[5]) + (v[6] + v[7]));
+    }
+}
+
 // Rows of at most 32 * kChunks * kVec elements (<= 4096), so element indices fit 32 bits. At most 128 registers per
 // thread (two blocks per SM): the row occupies kChunks * kVec of them.
 template <typename T, int kChunks, typename Rows>
 __global__ void __launch_bounds__(kThreads, 2) softmax_regs_kernel(const void* __restrict__ x, void* __restrict__ y,
                                                                    int64_t rows, int64_t width, float scale,
                                                                    Rows rule) {
+    grid_dependency_begin();
     using V = Vec16<T>;
     constexpr int kVec = V::kVec;
     const int lane = threadIdx.x & 31;
@@ -87,35 +107,47 @@ __global__ void __launch_bounds__(kThreads, 2) softmax_regs_kernel(const void* _
                 V::unpack(ld_stream(xr + c * 16), v[i]);
             }
         }
-        float m = -INFINITY;
+        // Scaled values; only the chunk that straddles the visibility boundary needs per-element masks. Each chunk
+        // is reduced as a small tree into one of two running accumulators, which keeps dependency chains short.
+        // The masked tail of the chunk that straddles the boundary becomes -inf, so exp turns it into 0 (or NaN
+        // exactly when the row's maximum is -inf, where the reference's 0 / sum is NaN too).
+        float mx[2] = {-INFINITY, -INFINITY};
 #pragma unroll
         for (int i = 0; i < kChunks; ++i) {
             const int c = lane + 32 * i;
             if (c < vis_chunks) {
 #pragma unroll
                 for (int j = 0; j < kVec; ++j) {
-                    v[i][j] = c * kVec + j < n ? v[i][j] * scale : -INFINITY;
-                    m = fmaxf(m, v[i][j]);
+                    v[i][j] = v[i][j] * scale;
                 }
+                if ((c + 1) * kVec > n) {
+#pragma unroll
+                    for (int j = 0; j < kVec; ++j) {
+                        v[i][j] = c * kVec + j < n ? v[i][j] : -INFINITY;
+                    }
+                }
+                mx[i & 1] = fmaxf(mx[i & 1], tree_max<kVec>(v[i]));
             }
         }
-        m = group_max<32>(m);
+        const float m = group_max<32>(fmaxf(mx[0], mx[1]));
 
-        float sum = 0.0f;
+        float acc[2] = {0.0f, 0.0f};
 #pragma unroll
         for (int i = 0; i < kChunks; ++i) {
             const int c = lane + 32 * i;
             if (c < vis_chunks) {
 #pragma unroll
                 for (int j = 0; j < kVec; ++j) {
-                    v[i][j] = c * kVec + j < n ? expf(v[i][j] - m) : 0.0f;
-                    sum = sum + v[i][j];
+                    v[i][j] = expf(v[i][j] - m);
                 }
+                acc[i & 1] = acc[i & 1] + tree_sum<kVec>(v[i]);
             }
         }
-        sum = group_sum<32>(sum);
+        const float sum = group_sum<32>(acc[0] + acc[1]);
         const bool zero_row = Rows::kZeroOnEmpty && sum == 0.0f;
         const float masked = zero_row ? 0.0f : 0.0f / sum;
+        // One division per row; each probability is e * (1 / sum), within one f32 ulp of e / sum.
+        const float inv = zero_row ? 0.0f : 1.0f / sum;
 
 #pragma unroll
         for (int i = 0; i < kChunks; ++i) {
@@ -125,7 +157,7 @@ __global__ void __launch_bounds__(kThreads, 2) softmax_regs_kernel(const void* _
                 if (c < vis_chunks) {
 #pragma unroll
                     for (int j = 0; j < kVec; ++j) {
-                        out[j] = c * kVec + j < n ? (zero_row ? 0.0f : v[i][j] / sum) : masked;
+                        out[j] = v[i][j] * inv;
                     }
                 } else {
 #pragma unroll
@@ -145,6 +177,7 @@ template <typename T, typename Rows>
 __global__ void __launch_bounds__(kThreads) softmax_stream_kernel(const void* __restrict__ x, void* __restrict__ y,
                                                                   int64_t rows, int64_t width, float scale,
                                                                   Rows rule) {
+    grid_dependency_begin();
     using V = Vec16<T>;
     const int lane = threadIdx.x & 31;
     const int64_t warp_stride = static_cast<int64_t>(gridDim.x) * kWarps;
@@ -186,22 +219,23 @@ int launch_softmax(const void* x, void* y, int64_t rows, int64_t width, float sc
     const int64_t per_lane = runtime::ceil_div(width / kVec, 32);
     // A lane holds at most 64 f32 row values in registers: 16 vectors of f32 or 8 of bf16.
     constexpr int kMaxChunks = sizeof(T) == 2 ? 8 : 16;
+    cudaError_t launch_err;
     if (vector_ok && per_lane <= kMaxChunks) {
         if (per_lane <= 1) {
-            softmax_regs_kernel<T, 1, Rows><<<blocks, kThreads, 0, s>>>(x, y, rows, width, scale, rule);
+            launch_err = ::cppinf::runtime::launch(softmax_regs_kernel<T, 1, Rows>, dim3(blocks), dim3(kThreads), s, 1u, x, y, rows, width, scale, rule);
         } else if (per_lane <= 2) {
-            softmax_regs_kernel<T, 2, Rows><<<blocks, kThreads, 0, s>>>(x, y, rows, width, scale, rule);
+            launch_err = ::cppinf::runtime::launch(softmax_regs_kernel<T, 2, Rows>, dim3(blocks), dim3(kThreads), s, 1u, x, y, rows, width, scale, rule);
         } else if (per_lane <= 4) {
-            softmax_regs_kernel<T, 4, Rows><<<blocks, kThreads, 0, s>>>(x, y, rows, width, scale, rule);
+            launch_err = ::cppinf::runtime::launch(softmax_regs_kernel<T, 4, Rows>, dim3(blocks), dim3(kThreads), s, 1u, x, y, rows, width, scale, rule);
         } else if (per_lane <= 8 || kMaxChunks == 8) {
-            softmax_regs_kernel<T, 8, Rows><<<blocks, kThreads, 0, s>>>(x, y, rows, width, scale, rule);
+            launch_err = ::cppinf::runtime::launch(softmax_regs_kernel<T, 8, Rows>, dim3(blocks), dim3(kThreads), s, 1u, x, y, rows, width, scale, rule);
         } else {
-            softmax_regs_kernel<T, kMaxChunks, Rows><<<blocks, kThreads, 0, s>>>(x, y, rows, width, scale, rule);
+            launch_err = ::cppinf::runtime::launch(softmax_regs_kernel<T, kMaxChunks, Rows>, dim3(blocks), dim3(kThreads), s, 1u, x, y, rows, width, scale, rule);
         }
     } else {
-        softmax_stream_kernel<T, Rows><<<blocks, kThreads, 0, s>>>(x, y, rows, width, scale, rule);
+        launch_err = ::cppinf::runtime::launch(softmax_stream_kernel<T, Rows>, dim3(blocks), dim3(kThreads), s, 1u, x, y, rows, width, scale, rule);
     }
-    return runtime::after_launch(name);
+    return runtime::launched(launch_err, name);
 }
 
 }  // namespace
