@@ -384,58 +384,80 @@ def time_e2e(wl_name: str, rank: int, device, steps: int) -> dict:
 # ---------------------------------------------------------------------------------------------------------------
 
 
-def cpu_qk_norm_rope_step(kind: str, oracle, reference, data, threads: int) -> None:
-    """One full 2048-token qk_norm_rope step on the host."""
-    q, k, qw, kw = data
-    if kind == "port":
-        oracle.qk_norm_rope(q, k, qw, kw, 1e-6, 0, 1e6)
-        return
-    # Reference sequence (src/nn/qwen_attention.cpp:383-390): ops::rms_norm per head -- restated, its reference
-    # needs oneDNN -- then the reference's own nn::apply_rope (rope.cpp) over token chunks in parallel threads.
-    tokens = q.shape[0]
-    qn = oracle.rms_norm(q.reshape(-1, q.shape[-1]), qw, 1e-6).reshape(q.shape)
-    kn = oracle.rms_norm(k.reshape(-1, k.shape[-1]), kw, 1e-6).reshape(k.shape)
-    chunk = max(1, tokens // threads)
-    jobs = []
-    with ThreadPoolExecutor(max_workers=threads) as pool:
-        for t0 in range(0, tokens, chunk):
-            for x in (qn, kn):
-                jobs.append(pool.submit(reference.apply_rope, x[t0:t0 + chunk], t0, 1e6, 0))
+def qk_bytes(tokens: int) -> int:
+    """Algorithmic bytes of the q/k RMSNorm + RoPE over `tokens` token rows (16 q + 8 k heads of 128, bf16)."""
+    return 2 * tokens * 24 * 128 * 2 + 2 * 128 * 2
+
+
+class CpuQkNormRope:
+    """The q/k RMSNorm + RoPE configuration on the host, as the CPU baseline.
+
+    kind "port": the C restatement (oracle/oracle.c, OpenMP over head vectors).
+    kind "reference": the reference's sequence of src/nn/qwen_attention.cpp:383-390 -- ops::rms_norm per head (run
+    by the restatement, because the reference's rms_norm needs oneDNN, which is not available here), then the
+    reference's own nn::apply_rope from src/nn/rope.cpp (compiled in place under oracle/_ref), over token chunks on
+    all host threads.
+    """
+
+    def __init__(self, kind: str):
+        import numpy as np
+
+        from oracle.oracle import Oracle, Reference, f32_to_bf16, reference_available
+
+        self.threads = os.cpu_count() or 1
+        os.environ.setdefault("OMP_NUM_THREADS", str(self.threads))
+        self.oracle = Oracle()
+        if kind == "reference" and not reference_available():
+            kind = "port"
+        self.kind = kind
+        self.reference = Reference() if kind == "reference" else None
+        self.pool = ThreadPoolExecutor(max_workers=self.threads) if kind == "reference" else None
+        rng = np.random.default_rng(5)
+        self.q = f32_to_bf16(rng.standard_normal((2048, 16, 128)).astype(np.float32))
+        self.k = f32_to_bf16(rng.standard_normal((2048, 8, 128)).astype(np.float32))
+        self.qw = f32_to_bf16((1 + 0.1 * rng.standard_normal(128)).astype(np.float32))
+        self.kw = f32_to_bf16((1 + 0.1 * rng.standard_normal(128)).astype(np.float32))
+
+    def step(self, tokens: int = 2048) -> None:
+        q, k = self.q[:tokens], self.k[:tokens]
+        if self.kind == "port":
+            self.oracle.qk_norm_rope(q, k, self.qw, self.kw, 1e-6, 0, 1e6)
+            return
+        qn = self.oracle.rms_norm(q.reshape(-1, 128), self.qw, 1e-6).reshape(q.shape)
+        kn = self.oracle.rms_norm(k.reshape(-1, 128), self.kw, 1e-6).reshape(k.shape)
+        chunk = max(1, -(-tokens // self.threads))
+        jobs = [self.pool.submit(self.reference.apply_rope, x[t0:t0 + chunk], t0, 1e6, 0)
+                for t0 in range(0, tokens, chunk) for x in (qn, kn)]
         for j in jobs:
             j.result()
 
+    def describe(self) -> str:
+        if self.kind == "reference":
+            return ("the reference's own rope.cpp (oracle/_ref) over token chunks on all threads, after the C "
+                    "restatement of rms_norm (the reference's needs oneDNN, absent here)")
+        return "the C restatement (oracle/oracle.c, OpenMP over head vectors)"
+
+    def close(self) -> None:
+        if self.pool is not None:
+            self.pool.shutdown()
+
 
 def measure_cpu(kind: str, seconds: float) -> dict:
-    import numpy as np
-
-    from oracle.oracle import Oracle, Reference, f32_to_bf16, reference_available
-
-    threads = os.cpu_count() or 1
-    os.environ.setdefault("OMP_NUM_THREADS", str(threads))
-    oracle = Oracle()
-    reference = Reference() if kind == "reference" and reference_available() else None
-    if kind == "reference" and reference is None:
-        kind = "port"
-    rng = np.random.default_rng(5)
-    data = (f32_to_bf16(rng.standard_normal((2048, 16, 128)).astype(np.float32)),
-            f32_to_bf16(rng.standard_normal((2048, 8, 128)).astype(np.float32)),
-            f32_to_bf16((1 + 0.1 * rng.standard_normal(128)).astype(np.float32)),
-            f32_to_bf16((1 + 0.1 * rng.standard_normal(128)).astype(np.float32)))
-    cpu_qk_norm_rope_step(kind, oracle, reference, data, threads)  # warm-up
+    """Full 2048-token steps repeated for about `seconds`."""
+    cpu = CpuQkNormRope(kind)
+    cpu.step()  # warm-up
     n = 0
     t0 = time.perf_counter()
     while True:
-        cpu_qk_norm_rope_step(kind, oracle, reference, data, threads)
+        cpu.step()
         n += 1
         elapsed = time.perf_counter() - t0
         if elapsed >= seconds:
             break
-    gbs = n * CONFIGS["qk_norm_rope"]["bytes"] / elapsed / 1e9
-    what = ("the reference's own rope.cpp (oracle/_ref, token chunks over threads) after the C restatement of "
-            "rms_norm (its reference needs oneDNN, absent here)" if kind == "reference"
-            else "the C restatement (oracle/oracle.c, OpenMP over head vectors)")
-    return {"value": round(gbs, 3), "unit": UNIT, "cores": threads, "kind": kind,
-            "sample": f"{n} full 2048-token q/k steps in {elapsed:.1f} s: {what}"}
+    cpu.close()
+    gbs = n * qk_bytes(2048) / elapsed / 1e9
+    return {"value": round(gbs, 3), "unit": UNIT, "cores": cpu.threads, "kind": cpu.kind,
+            "sample": f"{n} full 2048-token q/k steps in {elapsed:.1f} s: {cpu.describe()}"}
 
 
 # ---------------------------------------------------------------------------------------------------------------
@@ -444,21 +466,33 @@ def measure_cpu(kind: str, seconds: float) -> dict:
 
 
 def run_reference(args) -> None:
+    """The reference's CPU path on this host: exactly --steps timed steps after --warmup, each step a bounded token
+    sample of the 2048-token configuration, sized so the whole run takes about --cpu-seconds."""
     rank, world, _ = dist_env()
     if rank != 0:
         return
-    import platform
-
-    base = measure_cpu("reference", max(args.cpu_seconds, 2.0))
-    # Each step of this arm is one full configuration pass; report the per-step time over the sample.
-    value = base["value"]
+    cpu = CpuQkNormRope("reference")
+    t0 = time.perf_counter()
+    cpu.step(256)
+    per_token = (time.perf_counter() - t0) / 256
+    budget = max(args.cpu_seconds, 2.0)
+    tokens = int(min(2048, max(1, budget / max(args.steps, 1) / per_token)))
+    for _ in range(args.warmup):
+        cpu.step(tokens)
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        cpu.step(tokens)
+    elapsed = time.perf_counter() - t0
+    cpu.close()
+    value = round(args.steps * qk_bytes(tokens) / elapsed / 1e9, 3)
+    sample = f"{args.steps} steps of {tokens} of the 2048 token rows in {elapsed:.1f} s: {cpu.describe()}"
     line = {
         "impl": "reference", "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
-        "warmup": args.warmup, "ms_per_step": round(CONFIGS[HEADLINE]["bytes"] / (value * 1e9) * 1e3, 4),
+        "warmup": args.warmup, "ms_per_step": round(elapsed / args.steps * 1e3, 4),
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
         "data": "synthetic (seeded N(0,1) q/k, N(1,0.1) norm weights)",
-        "config": {"workload": CONFIGS[HEADLINE]["desc"], "host": platform.processor() or platform.machine()},
-        "cpu_baseline": base,
+        "config": {"workload": f"qk_norm_rope: {CONFIGS[HEADLINE]['desc']}", "tokens_per_step": tokens},
+        "cpu_baseline": {"value": value, "unit": UNIT, "cores": cpu.threads, "kind": cpu.kind, "sample": sample},
         "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)

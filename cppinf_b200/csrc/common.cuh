@@ -48,6 +48,27 @@ __device__ __forceinline__ float4 ld_cached_f4(const float* ptr) {
     return __ldg(reinterpret_cast<const float4*>(ptr));
 }
 
+// 256-bit (32-byte) accesses, sm_100: one instruction moves a whole 32-byte sector, which halves the memory
+// instructions of a streaming kernel and lets a copy reach the measured HBM peak. Addresses must be 32-byte aligned.
+struct U8 {
+    uint32_t r[8];
+};
+
+__device__ __forceinline__ U8 ld_stream32(const void* ptr) {
+    U8 v;
+    asm volatile("ld.global.nc.L1::no_allocate.v8.b32 {%0, %1, %2, %3, %4, %5, %6, %7}, [%8];"
+                 : "=r"(v.r[0]), "=r"(v.r[1]), "=r"(v.r[2]), "=r"(v.r[3]), "=r"(v.r[4]), "=r"(v.r[5]), "=r"(v.r[6]),
+                   "=r"(v.r[7])
+                 : "l"(ptr));
+    return v;
+}
+
+__device__ __forceinline__ void st_stream32(void* ptr, const U8& v) {
+    asm volatile("st.global.v8.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8};" ::"l"(ptr), "r"(v.r[0]), "r"(v.r[1]),
+                 "r"(v.r[2]), "r"(v.r[3]), "r"(v.r[4]), "r"(v.r[5]), "r"(v.r[6]), "r"(v.r[7])
+                 : "memory");
+}
+
 // Plain 128-bit store.
 __device__ __forceinline__ void st_v4(void* ptr, uint4 v) {
     asm volatile("st.global.v4.u32 [%0], {%1, %2, %3, %4};" ::"l"(ptr), "r"(v.x), "r"(v.y), "r"(v.z), "r"(v.w)
@@ -131,6 +152,60 @@ struct Vec16<float> {
     }
     __device__ __forceinline__ static void store1(void* base, int64_t i, float v) {
         reinterpret_cast<float*>(base)[i] = v;
+    }
+};
+
+// ---- 16- or 32-byte chunks of T as f32 ---------------------------------------------------------------------------
+
+template <typename T, int kBytes>
+struct Chunk {
+    static constexpr int kElems = kBytes / static_cast<int>(sizeof(T));
+
+    __device__ __forceinline__ static void load(const void* p, float (&f)[kElems]) {
+        if constexpr (kBytes == 32) {
+            const U8 v = ld_stream32(p);
+#pragma unroll
+            for (int i = 0; i < 8; ++i) {
+                unpack_word(v.r[i], f, i);
+            }
+        } else {
+            const uint4 v = ld_stream(p);
+            unpack_word(v.x, f, 0);
+            unpack_word(v.y, f, 1);
+            unpack_word(v.z, f, 2);
+            unpack_word(v.w, f, 3);
+        }
+    }
+
+    __device__ __forceinline__ static void store(void* p, const float (&f)[kElems]) {
+        if constexpr (kBytes == 32) {
+            U8 v;
+#pragma unroll
+            for (int i = 0; i < 8; ++i) {
+                v.r[i] = pack_word(f, i);
+            }
+            st_stream32(p, v);
+        } else {
+            st_stream(p, make_uint4(pack_word(f, 0), pack_word(f, 1), pack_word(f, 2), pack_word(f, 3)));
+        }
+    }
+
+  private:
+    __device__ __forceinline__ static void unpack_word(uint32_t w, float (&f)[kElems], int i) {
+        if constexpr (sizeof(T) == 2) {
+            f[2 * i] = bf16_lo(w);
+            f[2 * i + 1] = bf16_hi(w);
+        } else {
+            f[i] = __uint_as_float(w);
+        }
+    }
+
+    __device__ __forceinline__ static uint32_t pack_word(const float (&f)[kElems], int i) {
+        if constexpr (sizeof(T) == 2) {
+            return pack_bf16x2(f[2 * i], f[2 * i + 1]);
+        } else {
+            return __float_as_uint(f[i]);
+        }
     }
 };
 

@@ -2,10 +2,10 @@
 // (src/ops/nn_ops.cpp:68-72), ops::cast (src/ops/tensor_ops.cpp:138-143), the fused silu*up product of the Qwen MLP
 // (src/nn/qwen_mlp.cpp:65-66) and the strided gather that materialises non-contiguous views.
 //
-// Every kernel is HBM-bound (<= 1 flop per byte). Layout: dense arrays, 16-byte vectors, a grid of one full wave of
-// resident blocks (SM count x blocks per SM) striding over the vectors with kUnroll independent vectors per thread
-// per iteration so each thread keeps several 16-byte loads in flight. A misaligned operand or a ragged tail runs the
-// scalar path of the same kernel.
+// Every kernel is HBM-bound (<= 1 flop per byte). Layout: dense arrays walked in packs of 32 bytes (256-bit loads
+// and stores, when every operand is 32-byte aligned), else 16 bytes, else single elements; the result is the same on
+// every path because each element is computed alone. The grid is two waves of resident blocks striding over the
+// packs, kUnroll independent packs per thread per iteration, so each thread keeps several loads in flight.
 #include "common.cuh"
 #include "runtime.h"
 
@@ -13,7 +13,76 @@ namespace cppinf::device {
 namespace {
 
 constexpr int kThreads = 256;
-constexpr int kUnroll = 4;
+constexpr int kUnroll = 2;
+
+// kBytes of consecutive elements held as 32-bit words.
+template <int kBytes>
+struct Words {
+    static constexpr int kCount = kBytes / 4;
+    uint32_t w[kCount];
+
+    __device__ __forceinline__ static Words load(const void* p) {
+        Words out;
+        if constexpr (kBytes == 32) {
+            const U8 v = ld_stream32(p);
+#pragma unroll
+            for (int i = 0; i < 8; ++i) {
+                out.w[i] = v.r[i];
+            }
+        } else {
+            const uint4 v = ld_stream(p);
+            out.w[0] = v.x;
+            out.w[1] = v.y;
+            out.w[2] = v.z;
+            out.w[3] = v.w;
+        }
+        return out;
+    }
+
+    __device__ __forceinline__ void store(void* p) const {
+        if constexpr (kBytes == 32) {
+            U8 v;
+#pragma unroll
+            for (int i = 0; i < 8; ++i) {
+                v.r[i] = w[i];
+            }
+            st_stream32(p, v);
+        } else {
+            st_stream(p, make_uint4(w[0], w[1], w[2], w[3]));
+        }
+    }
+};
+
+// Elements of T in a pack, as f32.
+template <typename T, int kBytes>
+struct PackOf {
+    static constexpr int kElems = kBytes / static_cast<int>(sizeof(T));
+
+    __device__ __forceinline__ static void unpack(const Words<kBytes>& p, float (&f)[kElems]) {
+#pragma unroll
+        for (int i = 0; i < Words<kBytes>::kCount; ++i) {
+            if constexpr (sizeof(T) == 2) {
+                f[2 * i] = bf16_lo(p.w[i]);
+                f[2 * i + 1] = bf16_hi(p.w[i]);
+            } else {
+                f[i] = __uint_as_float(p.w[i]);
+            }
+        }
+    }
+
+    __device__ __forceinline__ static Words<kBytes> pack(const float (&f)[kElems]) {
+        Words<kBytes> p;
+#pragma unroll
+        for (int i = 0; i < Words<kBytes>::kCount; ++i) {
+            if constexpr (sizeof(T) == 2) {
+                p.w[i] = pack_bf16x2(f[2 * i], f[2 * i + 1]);
+            } else {
+                p.w[i] = __float_as_uint(f[i]);
+            }
+        }
+        return p;
+    }
+};
 
 enum class BinaryOp { Add, Mul };
 
@@ -31,27 +100,29 @@ __device__ __forceinline__ float silu_f32(float x) {
     return x / (1.0f + expf(-x));
 }
 
-// Generic grid-stride driver. `Functor::vec(i)` handles 16-byte vector i, `Functor::scalar(i)` element i.
-template <typename Functor>
+// Generic grid-stride driver. `Functor::load<kBytes>(i)` / `compute_store<kBytes>(i, loaded)` handle pack i,
+// `Functor::scalar(e)` element e.
+template <typename Functor, int kBytes>
 __global__ void __launch_bounds__(kThreads) elementwise_kernel(Functor f, int64_t n_vec, int64_t vec_elems,
                                                                int64_t count) {
     grid_dependency_begin();
+    using Loaded = typename Functor::template Loaded<kBytes>;
     const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
     const int64_t tid = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
     int64_t i = tid;
     for (; i + (kUnroll - 1) * stride < n_vec; i += kUnroll * stride) {
-        typename Functor::Loaded loaded[kUnroll];
+        Loaded loaded[kUnroll];
 #pragma unroll
         for (int u = 0; u < kUnroll; ++u) {
-            loaded[u] = f.load(i + u * stride);
+            loaded[u] = f.template load<kBytes>(i + u * stride);
         }
 #pragma unroll
         for (int u = 0; u < kUnroll; ++u) {
-            f.compute_store(i + u * stride, loaded[u]);
+            f.template compute_store<kBytes>(i + u * stride, loaded[u]);
         }
     }
     for (; i < n_vec; i += stride) {
-        f.compute_store(i, f.load(i));
+        f.template compute_store<kBytes>(i, f.template load<kBytes>(i));
     }
     // Scalar tail (or the whole array when the vector path is off).
     for (int64_t e = n_vec * vec_elems + tid; e < count; e += stride) {
@@ -61,132 +132,165 @@ __global__ void __launch_bounds__(kThreads) elementwise_kernel(Functor f, int64_
 
 template <typename T, BinaryOp op>
 struct BinaryFunctor {
-    using V = Vec16<T>;
+    template <int kBytes>
     struct Loaded {
-        uint4 a, b;
+        Words<kBytes> a, b;
     };
-    const uint4* lhs;
-    const uint4* rhs;
-    uint4* out;
-    const void* lhs_s;
-    const void* rhs_s;
-    void* out_s;
+    const char* lhs;
+    const char* rhs;
+    char* out;
 
-    __device__ __forceinline__ Loaded load(int64_t i) const { return {ld_stream(lhs + i), ld_stream(rhs + i)}; }
-    __device__ __forceinline__ void compute_store(int64_t i, const Loaded& l) const {
-        float a[V::kVec], b[V::kVec];
-        V::unpack(l.a, a);
-        V::unpack(l.b, b);
+    template <int kBytes>
+    __device__ __forceinline__ Loaded<kBytes> load(int64_t i) const {
+        return {Words<kBytes>::load(lhs + i * kBytes), Words<kBytes>::load(rhs + i * kBytes)};
+    }
+    template <int kBytes>
+    __device__ __forceinline__ void compute_store(int64_t i, const Loaded<kBytes>& l) const {
+        using P = PackOf<T, kBytes>;
+        float a[P::kElems], b[P::kElems];
+        P::unpack(l.a, a);
+        P::unpack(l.b, b);
 #pragma unroll
-        for (int j = 0; j < V::kVec; ++j) {
+        for (int j = 0; j < P::kElems; ++j) {
             a[j] = apply_binary<op>(a[j], b[j]);
         }
-        st_stream(out + i, V::pack(a));
+        P::pack(a).store(out + i * kBytes);
     }
     __device__ __forceinline__ void scalar(int64_t e) const {
-        V::store1(out_s, e, apply_binary<op>(V::load1(lhs_s, e), V::load1(rhs_s, e)));
+        Vec16<T>::store1(out, e, apply_binary<op>(Vec16<T>::load1(lhs, e), Vec16<T>::load1(rhs, e)));
     }
 };
 
 template <typename T>
 struct SiluFunctor {
-    using V = Vec16<T>;
-    using Loaded = uint4;
-    const uint4* x;
-    uint4* y;
-    const void* x_s;
-    void* y_s;
+    template <int kBytes>
+    using Loaded = Words<kBytes>;
+    const char* x;
+    char* y;
 
-    __device__ __forceinline__ Loaded load(int64_t i) const { return ld_stream(x + i); }
-    __device__ __forceinline__ void compute_store(int64_t i, const Loaded& l) const {
-        float a[V::kVec];
-        V::unpack(l, a);
+    template <int kBytes>
+    __device__ __forceinline__ Loaded<kBytes> load(int64_t i) const {
+        return Words<kBytes>::load(x + i * kBytes);
+    }
+    template <int kBytes>
+    __device__ __forceinline__ void compute_store(int64_t i, const Loaded<kBytes>& l) const {
+        using P = PackOf<T, kBytes>;
+        float a[P::kElems];
+        P::unpack(l, a);
 #pragma unroll
-        for (int j = 0; j < V::kVec; ++j) {
+        for (int j = 0; j < P::kElems; ++j) {
             a[j] = silu_f32(a[j]);
         }
-        st_stream(y + i, V::pack(a));
+        P::pack(a).store(y + i * kBytes);
     }
-    __device__ __forceinline__ void scalar(int64_t e) const { V::store1(y_s, e, silu_f32(V::load1(x_s, e))); }
+    __device__ __forceinline__ void scalar(int64_t e) const { Vec16<T>::store1(y, e, silu_f32(Vec16<T>::load1(x, e))); }
 };
 
 // out = T(T(silu(gate)) * up): the reference rounds the silu tensor to T before ops::mul reads it.
 template <typename T>
 struct SiluMulFunctor {
-    using V = Vec16<T>;
+    template <int kBytes>
     struct Loaded {
-        uint4 g, u;
+        Words<kBytes> g, u;
     };
-    const uint4* gate;
-    const uint4* up;
-    uint4* out;
-    const void* gate_s;
-    const void* up_s;
-    void* out_s;
+    const char* gate;
+    const char* up;
+    char* out;
 
-    __device__ __forceinline__ Loaded load(int64_t i) const { return {ld_stream(gate + i), ld_stream(up + i)}; }
-    __device__ __forceinline__ void compute_store(int64_t i, const Loaded& l) const {
-        float g[V::kVec], u[V::kVec];
-        V::unpack(l.g, g);
-        V::unpack(l.u, u);
+    template <int kBytes>
+    __device__ __forceinline__ Loaded<kBytes> load(int64_t i) const {
+        return {Words<kBytes>::load(gate + i * kBytes), Words<kBytes>::load(up + i * kBytes)};
+    }
+    template <int kBytes>
+    __device__ __forceinline__ void compute_store(int64_t i, const Loaded<kBytes>& l) const {
+        using P = PackOf<T, kBytes>;
+        float g[P::kElems], u[P::kElems];
+        P::unpack(l.g, g);
+        P::unpack(l.u, u);
 #pragma unroll
-        for (int j = 0; j < V::kVec; ++j) {
-            g[j] = V::quantize(silu_f32(g[j])) * u[j];
+        for (int j = 0; j < P::kElems; ++j) {
+            g[j] = Vec16<T>::quantize(silu_f32(g[j])) * u[j];
         }
-        st_stream(out + i, V::pack(g));
+        P::pack(g).store(out + i * kBytes);
     }
     __device__ __forceinline__ void scalar(int64_t e) const {
-        const float s = V::quantize(silu_f32(V::load1(gate_s, e)));
-        V::store1(out_s, e, s * V::load1(up_s, e));
+        const float s = Vec16<T>::quantize(silu_f32(Vec16<T>::load1(gate, e)));
+        Vec16<T>::store1(out, e, s * Vec16<T>::load1(up, e));
     }
 };
 
-// bf16 -> f32: one 16-byte load of 8 bf16 produces two 16-byte stores.
+// bf16 -> f32: a pack of kBytes of bf16 produces two packs of f32.
 struct CastBf16ToF32Functor {
-    using Loaded = uint4;
-    const uint4* x;
-    uint4* y;
-    const void* x_s;
-    void* y_s;
+    template <int kBytes>
+    using Loaded = Words<kBytes>;
+    const char* x;
+    char* y;
 
-    __device__ __forceinline__ Loaded load(int64_t i) const { return ld_stream(x + i); }
-    __device__ __forceinline__ void compute_store(int64_t i, const Loaded& l) const {
-        st_stream(y + 2 * i, make_uint4(l.x << 16, l.x & 0xffff0000u, l.y << 16, l.y & 0xffff0000u));
-        st_stream(y + 2 * i + 1, make_uint4(l.z << 16, l.z & 0xffff0000u, l.w << 16, l.w & 0xffff0000u));
+    template <int kBytes>
+    __device__ __forceinline__ Loaded<kBytes> load(int64_t i) const {
+        return Words<kBytes>::load(x + i * kBytes);
     }
-    __device__ __forceinline__ void scalar(int64_t e) const { Vec16<float>::store1(y_s, e, Vec16<bf16>::load1(x_s, e)); }
+    template <int kBytes>
+    __device__ __forceinline__ void compute_store(int64_t i, const Loaded<kBytes>& l) const {
+        Words<kBytes> lo, hi;
+        constexpr int kHalf = Words<kBytes>::kCount / 2;
+#pragma unroll
+        for (int k = 0; k < kHalf; ++k) {
+            lo.w[2 * k] = l.w[k] << 16;
+            lo.w[2 * k + 1] = l.w[k] & 0xffff0000u;
+            hi.w[2 * k] = l.w[kHalf + k] << 16;
+            hi.w[2 * k + 1] = l.w[kHalf + k] & 0xffff0000u;
+        }
+        lo.store(y + 2 * i * kBytes);
+        hi.store(y + 2 * i * kBytes + kBytes);
+    }
+    __device__ __forceinline__ void scalar(int64_t e) const { Vec16<float>::store1(y, e, Vec16<bf16>::load1(x, e)); }
 };
 
-// f32 -> bf16: two 16-byte loads of 4 f32 produce one 16-byte store.
+// f32 -> bf16: two packs of f32 produce one pack of bf16.
 struct CastF32ToBf16Functor {
+    template <int kBytes>
     struct Loaded {
-        uint4 a, b;
+        Words<kBytes> a, b;
     };
-    const uint4* x;
-    uint4* y;
-    const void* x_s;
-    void* y_s;
+    const char* x;
+    char* y;
 
-    __device__ __forceinline__ Loaded load(int64_t i) const { return {ld_stream(x + 2 * i), ld_stream(x + 2 * i + 1)}; }
-    __device__ __forceinline__ void compute_store(int64_t i, const Loaded& l) const {
-        st_stream(y + i, make_uint4(pack_bf16x2(__uint_as_float(l.a.x), __uint_as_float(l.a.y)),
-                                    pack_bf16x2(__uint_as_float(l.a.z), __uint_as_float(l.a.w)),
-                                    pack_bf16x2(__uint_as_float(l.b.x), __uint_as_float(l.b.y)),
-                                    pack_bf16x2(__uint_as_float(l.b.z), __uint_as_float(l.b.w))));
+    template <int kBytes>
+    __device__ __forceinline__ Loaded<kBytes> load(int64_t i) const {
+        return {Words<kBytes>::load(x + 2 * i * kBytes), Words<kBytes>::load(x + 2 * i * kBytes + kBytes)};
     }
-    __device__ __forceinline__ void scalar(int64_t e) const { Vec16<bf16>::store1(y_s, e, Vec16<float>::load1(x_s, e)); }
+    template <int kBytes>
+    __device__ __forceinline__ void compute_store(int64_t i, const Loaded<kBytes>& l) const {
+        Words<kBytes> o;
+        constexpr int kHalf = Words<kBytes>::kCount / 2;
+#pragma unroll
+        for (int k = 0; k < kHalf; ++k) {
+            o.w[k] = pack_bf16x2(__uint_as_float(l.a.w[2 * k]), __uint_as_float(l.a.w[2 * k + 1]));
+            o.w[kHalf + k] = pack_bf16x2(__uint_as_float(l.b.w[2 * k]), __uint_as_float(l.b.w[2 * k + 1]));
+        }
+        o.store(y + i * kBytes);
+    }
+    __device__ __forceinline__ void scalar(int64_t e) const { Vec16<bf16>::store1(y, e, Vec16<float>::load1(x, e)); }
 };
 
 struct CopyFunctor {
-    using Loaded = uint4;
-    const uint4* x;
-    uint4* y;
-    const unsigned char* x_s;
-    unsigned char* y_s;
+    template <int kBytes>
+    using Loaded = Words<kBytes>;
+    const char* x;
+    char* y;
 
-    __device__ __forceinline__ Loaded load(int64_t i) const { return ld_stream(x + i); }
-    __device__ __forceinline__ void compute_store(int64_t i, const Loaded& l) const { st_stream(y + i, l); }
-    __device__ __forceinline__ void scalar(int64_t e) const { y_s[e] = x_s[e]; }
+    template <int kBytes>
+    __device__ __forceinline__ Loaded<kBytes> load(int64_t i) const {
+        return Words<kBytes>::load(x + i * kBytes);
+    }
+    template <int kBytes>
+    __device__ __forceinline__ void compute_store(int64_t i, const Loaded<kBytes>& l) const {
+        l.store(y + i * kBytes);
+    }
+    __device__ __forceinline__ void scalar(int64_t e) const {
+        reinterpret_cast<unsigned char*>(y)[e] = reinterpret_cast<const unsigned char*>(x)[e];
+    }
 };
 
 // Strided gather of a rank <= 8 view into dense storage; one thread per output element.
@@ -213,20 +317,42 @@ __global__ void __launch_bounds__(kThreads) strided_copy_kernel(const E* __restr
     }
 }
 
-int64_t wave_blocks(int64_t work_items) {
+// Two waves of resident blocks, or fewer when the work is small.
+int64_t grid_blocks(int64_t work_items) {
     const int64_t per_sm = runtime::max_threads_per_sm() / kThreads;
-    const int64_t wave = static_cast<int64_t>(runtime::sm_count()) * (per_sm > 0 ? per_sm : 1);
+    const int64_t waves = 2 * static_cast<int64_t>(runtime::sm_count()) * (per_sm > 0 ? per_sm : 1);
     const int64_t needed = runtime::ceil_div(work_items, kThreads);
-    return needed < wave ? (needed > 0 ? needed : 1) : wave;
+    return needed < waves ? (needed > 0 ? needed : 1) : waves;
 }
 
+bool aligned32(const void* p) {
+    return (reinterpret_cast<std::uintptr_t>(p) & 31u) == 0;
+}
+
+// Picks the widest pack every operand is aligned for: 32 bytes, 16 bytes, or none (scalar). `elems16` is the number
+// of elements in 16 bytes of the functor's pack unit (32-byte packs hold twice as many).
 template <typename Functor>
-int launch_elementwise(const Functor& f, bool vector_ok, int64_t vec_elems, int64_t count, void* stream,
-                       const char* name) {
-    const int64_t n_vec = vector_ok ? count / vec_elems : 0;
-    const int64_t work = n_vec > 0 ? n_vec : count;
-    const cudaError_t launch_err = ::cppinf::runtime::launch(elementwise_kernel<Functor>, dim3(static_cast<unsigned>(wave_blocks(work))), dim3(kThreads), runtime::as_stream(stream), 1u, 
-        f, n_vec, vec_elems, count);
+int launch_elementwise(const Functor& f, std::initializer_list<const void*> operands, int64_t elems16, int64_t count,
+                       void* stream, const char* name) {
+    bool a32 = true;
+    bool a16 = true;
+    for (const void* p : operands) {
+        a32 = a32 && aligned32(p);
+        a16 = a16 && runtime::aligned16(p);
+    }
+    const auto s = runtime::as_stream(stream);
+    cudaError_t launch_err;
+    if (a32) {
+        const int64_t n_vec = count / (2 * elems16);
+        const int64_t work = n_vec > 0 ? n_vec : count;
+        launch_err = runtime::launch(elementwise_kernel<Functor, 32>, dim3(static_cast<unsigned>(grid_blocks(work))),
+                                     dim3(kThreads), s, 1u, f, n_vec, 2 * elems16, count);
+    } else {
+        const int64_t n_vec = a16 ? count / elems16 : 0;
+        const int64_t work = n_vec > 0 ? n_vec : count;
+        launch_err = runtime::launch(elementwise_kernel<Functor, 16>, dim3(static_cast<unsigned>(grid_blocks(work))),
+                                     dim3(kThreads), s, 1u, f, n_vec, elems16, count);
+    }
     return runtime::launched(launch_err, name);
 }
 
@@ -247,15 +373,13 @@ int binary_entry(cppinf_dtype dtype, const void* lhs, const void* rhs, void* out
         return runtime::ok();
     }
     CPPINF_REQUIRE(lhs && rhs && out, CPPINF_ERR_INVALID_ARGUMENT, std::string(name) + " received a null pointer.");
-    const bool vec = runtime::aligned16(lhs) && runtime::aligned16(rhs) && runtime::aligned16(out);
+    const auto* a = static_cast<const char*>(lhs);
+    const auto* b = static_cast<const char*>(rhs);
+    auto* o = static_cast<char*>(out);
     if (dtype == CPPINF_DTYPE_BF16) {
-        BinaryFunctor<bf16, op> f{static_cast<const uint4*>(lhs), static_cast<const uint4*>(rhs),
-                                  static_cast<uint4*>(out), lhs, rhs, out};
-        return launch_elementwise(f, vec, 8, count, stream, name);
+        return launch_elementwise(BinaryFunctor<bf16, op>{a, b, o}, {lhs, rhs, out}, 8, count, stream, name);
     }
-    BinaryFunctor<float, op> f{static_cast<const uint4*>(lhs), static_cast<const uint4*>(rhs), static_cast<uint4*>(out),
-                               lhs, rhs, out};
-    return launch_elementwise(f, vec, 4, count, stream, name);
+    return launch_elementwise(BinaryFunctor<float, op>{a, b, o}, {lhs, rhs, out}, 4, count, stream, name);
 }
 
 }  // namespace
@@ -282,13 +406,12 @@ int cppinf_silu(cppinf_dtype dtype, const void* x, void* y, int64_t count, void*
         return rt::ok();
     }
     CPPINF_REQUIRE(x && y, CPPINF_ERR_INVALID_ARGUMENT, "silu received a null pointer.");
-    const bool vec = rt::aligned16(x) && rt::aligned16(y);
+    const auto* xs = static_cast<const char*>(x);
+    auto* ys = static_cast<char*>(y);
     if (dtype == CPPINF_DTYPE_BF16) {
-        SiluFunctor<bf16> f{static_cast<const uint4*>(x), static_cast<uint4*>(y), x, y};
-        return launch_elementwise(f, vec, 8, count, stream, "silu");
+        return launch_elementwise(SiluFunctor<bf16>{xs, ys}, {x, y}, 8, count, stream, "silu");
     }
-    SiluFunctor<float> f{static_cast<const uint4*>(x), static_cast<uint4*>(y), x, y};
-    return launch_elementwise(f, vec, 4, count, stream, "silu");
+    return launch_elementwise(SiluFunctor<float>{xs, ys}, {x, y}, 4, count, stream, "silu");
 }
 
 int cppinf_silu_mul(cppinf_dtype dtype, const void* gate, const void* up, void* out, int64_t count, void* stream) {
@@ -299,15 +422,13 @@ int cppinf_silu_mul(cppinf_dtype dtype, const void* gate, const void* up, void* 
         return rt::ok();
     }
     CPPINF_REQUIRE(gate && up && out, CPPINF_ERR_INVALID_ARGUMENT, "silu_mul received a null pointer.");
-    const bool vec = rt::aligned16(gate) && rt::aligned16(up) && rt::aligned16(out);
+    const auto* g = static_cast<const char*>(gate);
+    const auto* u = static_cast<const char*>(up);
+    auto* o = static_cast<char*>(out);
     if (dtype == CPPINF_DTYPE_BF16) {
-        SiluMulFunctor<bf16> f{static_cast<const uint4*>(gate), static_cast<const uint4*>(up), static_cast<uint4*>(out),
-                               gate, up, out};
-        return launch_elementwise(f, vec, 8, count, stream, "silu_mul");
+        return launch_elementwise(SiluMulFunctor<bf16>{g, u, o}, {gate, up, out}, 8, count, stream, "silu_mul");
     }
-    SiluMulFunctor<float> f{static_cast<const uint4*>(gate), static_cast<const uint4*>(up), static_cast<uint4*>(out),
-                            gate, up, out};
-    return launch_elementwise(f, vec, 4, count, stream, "silu_mul");
+    return launch_elementwise(SiluMulFunctor<float>{g, u, o}, {gate, up, out}, 4, count, stream, "silu_mul");
 }
 
 int cppinf_cast(cppinf_dtype src_dtype, const void* x, cppinf_dtype dst_dtype, void* y, int64_t count, void* stream) {
@@ -318,19 +439,17 @@ int cppinf_cast(cppinf_dtype src_dtype, const void* x, cppinf_dtype dst_dtype, v
         return rt::ok();
     }
     CPPINF_REQUIRE(x && y, CPPINF_ERR_INVALID_ARGUMENT, "cast received a null pointer.");
-    const bool vec = rt::aligned16(x) && rt::aligned16(y);
+    const auto* xs = static_cast<const char*>(x);
+    auto* ys = static_cast<char*>(y);
     if (src_dtype == dst_dtype) {
         const int64_t bytes = count * static_cast<int64_t>(rt::dtype_size(src_dtype));
-        CopyFunctor f{static_cast<const uint4*>(x), static_cast<uint4*>(y), static_cast<const unsigned char*>(x),
-                      static_cast<unsigned char*>(y)};
-        return launch_elementwise(f, vec, 16, bytes, stream, "cast_copy");
+        return launch_elementwise(CopyFunctor{xs, ys}, {x, y}, 16, bytes, stream, "cast_copy");
     }
+    // The pack unit is counted on the bf16 side: 16 bytes of bf16 are 8 elements.
     if (src_dtype == CPPINF_DTYPE_BF16) {
-        CastBf16ToF32Functor f{static_cast<const uint4*>(x), static_cast<uint4*>(y), x, y};
-        return launch_elementwise(f, vec, 8, count, stream, "cast_bf16_f32");
+        return launch_elementwise(CastBf16ToF32Functor{xs, ys}, {x, y}, 8, count, stream, "cast_bf16_f32");
     }
-    CastF32ToBf16Functor f{static_cast<const uint4*>(x), static_cast<uint4*>(y), x, y};
-    return launch_elementwise(f, vec, 8, count, stream, "cast_f32_bf16");
+    return launch_elementwise(CastF32ToBf16Functor{xs, ys}, {x, y}, 8, count, stream, "cast_f32_bf16");
 }
 
 int cppinf_strided_copy(cppinf_dtype dtype, const void* x, int64_t rank, const int64_t* dims, const int64_t* strides,
@@ -353,14 +472,15 @@ int cppinf_strided_copy(cppinf_dtype dtype, const void* x, int64_t rank, const i
         return rt::ok();
     }
     CPPINF_REQUIRE(x && y, CPPINF_ERR_INVALID_ARGUMENT, "strided_copy received a null pointer.");
-    const auto blocks = static_cast<unsigned>(wave_blocks(count));
+    const auto blocks = static_cast<unsigned>(grid_blocks(count));
     cudaError_t launch_err;
     if (dtype == CPPINF_DTYPE_BF16) {
-        launch_err = ::cppinf::runtime::launch(strided_copy_kernel<unsigned short>, dim3(blocks), dim3(kThreads), rt::as_stream(stream), 1u, 
-            static_cast<const unsigned short*>(x), static_cast<unsigned short*>(y), p, count);
+        launch_err = rt::launch(strided_copy_kernel<unsigned short>, dim3(blocks), dim3(kThreads),
+                                rt::as_stream(stream), 1u, static_cast<const unsigned short*>(x),
+                                static_cast<unsigned short*>(y), p, count);
     } else {
-        launch_err = ::cppinf::runtime::launch(strided_copy_kernel<float>, dim3(blocks), dim3(kThreads), rt::as_stream(stream), 1u, static_cast<const float*>(x),
-                                                                                   static_cast<float*>(y), p, count);
+        launch_err = rt::launch(strided_copy_kernel<float>, dim3(blocks), dim3(kThreads), rt::as_stream(stream), 1u,
+                                static_cast<const float*>(x), static_cast<float*>(y), p, count);
     }
     return rt::launched(launch_err, "strided_copy");
 }

@@ -212,23 +212,14 @@ cudaError_t launch_qk_units(QkParams p, cudaStream_t s) {
     return ::cppinf::runtime::launch(qk_norm_rope_kernel<T, kLanes, kIters>, dim3(blocks), dim3(kQkThreads), s, 1u, p);
 }
 
-// A warp unit covers a whole token when its heads fit in at most 8 iterations (the Qwen3 shapes: 24 heads of 128 in
-// 6 iterations of 4), so a 2048-token batch is a single wave of warps; larger head counts take several 8-iteration
-// units per token.
+// A warp unit covers 8 heads of one token (two iterations of 4 heads at D = 128 bf16): measured on B200 against
+// units of 4, 12 and 24 heads for the [2048, 16 + 8, 128] configuration, it balances loads in flight per warp against
+// warps per SM best.
 template <typename T, int kLanes>
 cudaError_t launch_qk(const QkParams& p, cudaStream_t s) {
     constexpr int kHeadsPerIter = 32 / kLanes;
-    const int iters = (p.q_heads + p.k_heads + kHeadsPerIter - 1) / kHeadsPerIter;
-    if (iters <= 2) {
-        return launch_qk_units<T, kLanes, 2>(p, s);
-    }
-    if (iters <= 4) {
-        return launch_qk_units<T, kLanes, 4>(p, s);
-    }
-    if (iters <= 6) {
-        return launch_qk_units<T, kLanes, 6>(p, s);
-    }
-    return launch_qk_units<T, kLanes, 8>(p, s);
+    constexpr int kIters = kHeadsPerIter >= 8 ? 1 : 8 / kHeadsPerIter;
+    return launch_qk_units<T, kLanes, kIters>(p, s);
 }
 
 template <typename T>

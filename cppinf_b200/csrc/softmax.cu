@@ -4,7 +4,7 @@
 //  - the position-aware variant of attention, scaled_position_causal_softmax_last_dim
 //    (src/nn/qwen_attention.cpp:164-235), f32 [batch, heads, Qcap, Kcap] with per-batch offsets and lengths.
 //
-// One warp owns one row. Only the visible prefix of a row is read (16-byte vectors into registers); the whole row is
+// One warp owns one row. Only the visible prefix of a row is read (32- or 16-byte chunks into registers); the whole row is
 // written, masked columns included. Per row, following the reference: m = max over visible k of (x*scale),
 // e_k = exp(x_k*scale - m) for visible k and 0 otherwise, sum = sum of e, out_k = e_k / sum. Masked columns hold
 // 0 / sum, which is 0 unless the sum is NaN, as in the reference's division loop. The position-aware variant writes
@@ -61,34 +61,50 @@ struct PositionCausalRows {
     static constexpr bool kZeroOnEmpty = true;
 };
 
-// Pairwise max / sum of one 16-byte chunk (4 or 8 values).
+// Pairwise (tree) max / sum of one chunk of kN values (kN a power of two).
 template <int kN>
 __device__ __forceinline__ float tree_max(const float (&v)[kN]) {
-    if constexpr (kN == 4) {
-        return fmaxf(fmaxf(v[0], v[1]), fmaxf(v[2], v[3]));
-    } else {
-        return fmaxf(fmaxf(fmaxf(v[0], v[1]), fmaxf(v[2], v[3])), fmaxf(fmaxf(v[4], v[5]), fmaxf(v[6], v[7])));
+    float t[kN];
+#pragma unroll
+    for (int i = 0; i < kN; ++i) {
+        t[i] = v[i];
     }
+#pragma unroll
+    for (int width = kN / 2; width > 0; width /= 2) {
+#pragma unroll
+        for (int i = 0; i < width; ++i) {
+            t[i] = fmaxf(t[2 * i], t[2 * i + 1]);
+        }
+    }
+    return t[0];
 }
 
 template <int kN>
 __device__ __forceinline__ float tree_sum(const float (&v)[kN]) {
-    if constexpr (kN == 4) {
-        return (v[0] + v[1]) + (v[2] + v[3]);
-    } else {
-        return ((v[0] + v[1]) + (v[2] + v[3])) + ((v[4] + v[5]) + (v[6] + v[7]));
+    float t[kN];
+#pragma unroll
+    for (int i = 0; i < kN; ++i) {
+        t[i] = v[i];
     }
+#pragma unroll
+    for (int width = kN / 2; width > 0; width /= 2) {
+#pragma unroll
+        for (int i = 0; i < width; ++i) {
+            t[i] = t[2 * i] + t[2 * i + 1];
+        }
+    }
+    return t[0];
 }
 
 // Rows of at most 32 * kChunks * kVec elements (<= 4096), so element indices fit 32 bits. At most 128 registers per
 // thread (two blocks per SM): the row occupies kChunks * kVec of them.
-template <typename T, int kChunks, typename Rows>
+template <typename T, int kBytes, int kChunks, typename Rows>
 __global__ void __launch_bounds__(kThreads, 2) softmax_regs_kernel(const void* __restrict__ x, void* __restrict__ y,
                                                                    int64_t rows, int64_t width, float scale,
                                                                    Rows rule) {
     grid_dependency_begin();
-    using V = Vec16<T>;
-    constexpr int kVec = V::kVec;
+    using V = Chunk<T, kBytes>;
+    constexpr int kVec = V::kElems;
     const int lane = threadIdx.x & 31;
     const int64_t warp_stride = static_cast<int64_t>(gridDim.x) * kWarps;
     const int nchunks = static_cast<int>(width / kVec);
@@ -104,7 +120,7 @@ __global__ void __launch_bounds__(kThreads, 2) softmax_regs_kernel(const void* _
         for (int i = 0; i < kChunks; ++i) {
             const int c = lane + 32 * i;
             if (c < vis_chunks) {
-                V::unpack(ld_stream(xr + c * 16), v[i]);
+                V::load(xr + c * kBytes, v[i]);
             }
         }
         // Scaled values; only the chunk that straddles the visibility boundary needs per-element masks. Each chunk
@@ -165,7 +181,7 @@ __global__ void __launch_bounds__(kThreads, 2) softmax_regs_kernel(const void* _
                         out[j] = masked;
                     }
                 }
-                st_stream(yr + static_cast<int64_t>(c) * 16, V::pack(out));
+                V::store(yr + static_cast<int64_t>(c) * kBytes, out);
             }
         }
     }
@@ -215,25 +231,42 @@ int launch_softmax(const void* x, void* y, int64_t rows, int64_t width, float sc
     const int64_t needed = runtime::ceil_div(rows, kWarps);
     const auto blocks = static_cast<unsigned>(needed < wave ? needed : wave);
     const auto s = runtime::as_stream(stream);
-    const bool vector_ok = width % kVec == 0 && runtime::aligned16(x) && runtime::aligned16(y);
-    const int64_t per_lane = runtime::ceil_div(width / kVec, 32);
-    // A lane holds at most 64 f32 row values in registers: 16 vectors of f32 or 8 of bf16.
-    constexpr int kMaxChunks = sizeof(T) == 2 ? 8 : 16;
+    // 32-byte chunks when rows are 32-byte aligned, else 16-byte chunks, else the element-wise streaming kernel.
+    // A lane holds at most 64 f32 row values in registers.
+    const bool rows32 = width % (32 / static_cast<int64_t>(sizeof(T))) == 0 &&
+                        (reinterpret_cast<std::uintptr_t>(x) & 31u) == 0 && (reinterpret_cast<std::uintptr_t>(y) & 31u) == 0;
+    const bool rows16 = width % kVec == 0 && runtime::aligned16(x) && runtime::aligned16(y);
+    constexpr int kElems32 = 32 / static_cast<int>(sizeof(T));
+    const int64_t per_lane32 = runtime::ceil_div(width / kElems32, 32);
+    const int64_t per_lane16 = runtime::ceil_div(width / kVec, 32);
     cudaError_t launch_err;
-    if (vector_ok && per_lane <= kMaxChunks) {
-        if (per_lane <= 1) {
-            launch_err = ::cppinf::runtime::launch(softmax_regs_kernel<T, 1, Rows>, dim3(blocks), dim3(kThreads), s, 1u, x, y, rows, width, scale, rule);
-        } else if (per_lane <= 2) {
-            launch_err = ::cppinf::runtime::launch(softmax_regs_kernel<T, 2, Rows>, dim3(blocks), dim3(kThreads), s, 1u, x, y, rows, width, scale, rule);
-        } else if (per_lane <= 4) {
-            launch_err = ::cppinf::runtime::launch(softmax_regs_kernel<T, 4, Rows>, dim3(blocks), dim3(kThreads), s, 1u, x, y, rows, width, scale, rule);
-        } else if (per_lane <= 8 || kMaxChunks == 8) {
-            launch_err = ::cppinf::runtime::launch(softmax_regs_kernel<T, 8, Rows>, dim3(blocks), dim3(kThreads), s, 1u, x, y, rows, width, scale, rule);
+    if (rows32 && per_lane32 * kElems32 <= 64) {
+        if (per_lane32 <= 1) {
+            launch_err = runtime::launch(softmax_regs_kernel<T, 32, 1, Rows>, dim3(blocks), dim3(kThreads), s, 1u, x, y,
+                                         rows, width, scale, rule);
+        } else if (per_lane32 <= 2) {
+            launch_err = runtime::launch(softmax_regs_kernel<T, 32, 2, Rows>, dim3(blocks), dim3(kThreads), s, 1u, x, y,
+                                         rows, width, scale, rule);
+        } else if (per_lane32 <= 4) {
+            launch_err = runtime::launch(softmax_regs_kernel<T, 32, 4, Rows>, dim3(blocks), dim3(kThreads), s, 1u, x, y,
+                                         rows, width, scale, rule);
         } else {
-            launch_err = ::cppinf::runtime::launch(softmax_regs_kernel<T, kMaxChunks, Rows>, dim3(blocks), dim3(kThreads), s, 1u, x, y, rows, width, scale, rule);
+            constexpr int kMax = 64 / kElems32;  // 8 chunks of f32; bf16 never gets here (4 * 16 = 64)
+            launch_err = runtime::launch(softmax_regs_kernel<T, 32, kMax, Rows>, dim3(blocks), dim3(kThreads), s, 1u, x,
+                                         y, rows, width, scale, rule);
+        }
+    } else if (rows16 && per_lane16 * kVec <= 64) {
+        if (per_lane16 <= 2) {
+            launch_err = runtime::launch(softmax_regs_kernel<T, 16, 2, Rows>, dim3(blocks), dim3(kThreads), s, 1u, x, y,
+                                         rows, width, scale, rule);
+        } else {
+            constexpr int kMax = 64 / kVec;  // 16 chunks of f32, 8 of bf16
+            launch_err = runtime::launch(softmax_regs_kernel<T, 16, kMax, Rows>, dim3(blocks), dim3(kThreads), s, 1u, x,
+                                         y, rows, width, scale, rule);
         }
     } else {
-        launch_err = ::cppinf::runtime::launch(softmax_stream_kernel<T, Rows>, dim3(blocks), dim3(kThreads), s, 1u, x, y, rows, width, scale, rule);
+        launch_err = runtime::launch(softmax_stream_kernel<T, Rows>, dim3(blocks), dim3(kThreads), s, 1u, x, y, rows,
+                                     width, scale, rule);
     }
     return runtime::launched(launch_err, name);
 }

@@ -325,7 +325,8 @@ def test_elementwise_unaligned_views_take_scalar_path(ops, oracle):
     assert ((got == out) | (got == alt)).all()
 
 
-@pytest.mark.parametrize("matrices,n", [(1, 1), (2, 64), (3, 129), (16, 2048), (1, 4100), (2, 33)])
+@pytest.mark.parametrize("matrices,n", [(1, 1), (2, 64), (3, 129), (16, 2048), (1, 4100), (2, 33), (2, 8),
+                                         (2, 16), (2, 256), (2, 1024), (2, 520)])
 def test_scaled_causal_softmax(ops, oracle, matrices, n):
     rng = np.random.default_rng(matrices * 1000 + n)
     x = (rng.standard_normal((matrices, n, n)) * 2.0).astype(np.float32)
@@ -342,7 +343,8 @@ def test_position_causal_softmax_ragged(ops, oracle):
     assert_softmax_close(got, oracle.position_causal_softmax(x, *args))
 
 
-@pytest.mark.parametrize("rows,width", [(2, 4), (16, 256), (100, 1000), (3, 3001), (8, 151936)])
+@pytest.mark.parametrize("rows,width", [(2, 4), (16, 256), (100, 1000), (3, 3001), (8, 151936), (5, 2048),
+                                        (7, 600), (9, 512), (4, 1024), (6, 24), (3, 40)])
 @pytest.mark.parametrize("dtype", ["bf16", "f32"])
 def test_softmax_last_dim(ops, oracle, rows, width, dtype):
     rng = np.random.default_rng(rows + width)
