@@ -4,13 +4,16 @@
 // Semantics of the reference's scan (best = x[0]; for i >= 1: if (x[i] > best) take i):
 //  - the largest value wins, ties go to the lowest index (strict '>'), +0 and -0 compare equal;
 //  - NaN never wins, except that a NaN at index 0 is never replaced, so the result is 0.
-// These are reproduced exactly with an order-independent key: key(i) = (orderable(x[i]) << 32) | (2^32 - 1 - i),
-// where orderable() maps floats to unsigned integers monotonically (after folding -0 into +0) and NaN to 0 ("no
-// candidate"). max(key) is the reference's answer whenever x[0] is not NaN.
+// Each thread keeps a running (value, index) over the elements it visits in increasing index order with the same
+// strict '>' rule. Across threads the partial results are combined with an order-independent key,
+// key(i) = (orderable(x[i]) << 32) | (2^32 - 1 - i), where orderable() maps floats to unsigned integers monotonically
+// (after folding -0 into +0): max(key) is the lowest index of the largest value. A row whose element 0 is NaN
+// yields 0.
 //
-// Layout: a row is split across a thread-block cluster of up to 8 CTAs, each CTA scanning a contiguous column range
-// with 16-byte vector loads, 4 in flight per thread. CTA partials are combined through distributed shared memory
-// (cluster rank 0 reads the other CTAs' shared slots), so no global scratch and no second launch are needed.
+// Layout: a row is split across a thread-block cluster of up to 8 CTAs of 256 threads, each CTA scanning a
+// contiguous column range with 32-byte loads (16-byte or scalar loads when the rows are not aligned for them), a
+// thread's loads issued together. CTA partials are combined through distributed shared memory (cluster rank 0 reads
+// the other CTAs' shared slots), so no global scratch and no second launch are needed.
 //
 // Roofline: HBM-bound. Algorithmic bytes per row: cols * size read + 8 bytes written.
 #include <cooperative_groups.h>
@@ -25,7 +28,7 @@ namespace {
 
 constexpr int kThreads = 256;
 constexpr int kWarps = kThreads / 32;
-constexpr int kUnroll = 4;
+constexpr int kUnroll = 5;
 constexpr int kMaxCluster = 8;
 
 __device__ __forceinline__ unsigned long long argmax_key(float v, uint32_t index) {
@@ -62,24 +65,12 @@ struct Running {
     }
 };
 
-template <typename T>
-__device__ __forceinline__ void scan_vector(uint4 raw, int first, Running& run) {
-    using V = Vec16<T>;
-    float f[V::kVec];
-    V::unpack(raw, f);
-#pragma unroll
-    for (int j = 0; j < V::kVec; ++j) {
-        run.visit(f[j], first + j);
-    }
-}
-
-template <typename T>
-__global__ void __launch_bounds__(kThreads) row_argmax_kernel(const void* __restrict__ x, int64_t cols,
-                                                              int64_t row_stride, int64_t* __restrict__ out,
-                                                              bool vector_ok) {
+// kBytes: 32 or 16 for vector loads of the row, 0 for element loads.
+template <typename T, int kBytes>
+__global__ void __launch_bounds__(kThreads, 4) row_argmax_kernel(const void* __restrict__ x, int64_t cols,
+                                                              int64_t row_stride, int64_t* __restrict__ out) {
     grid_dependency_begin();
-    using V = Vec16<T>;
-    constexpr int kVec = V::kVec;
+    constexpr int kVec = kBytes == 0 ? 1 : kBytes / static_cast<int>(sizeof(T));
     __shared__ unsigned long long warp_best[kWarps];
     __shared__ unsigned long long cta_best;
 
@@ -89,39 +80,61 @@ __global__ void __launch_bounds__(kThreads) row_argmax_kernel(const void* __rest
     const int64_t row = blockIdx.x / csize;
     const char* xr = static_cast<const char*>(x) + row * row_stride * static_cast<int64_t>(sizeof(T));
 
-    // Column range of this CTA, cut at 16-byte vector boundaries.
+    // Column range of this CTA, cut at vector boundaries so every vector load stays aligned.
     const int64_t per_cta = ((cols + csize - 1) / csize + kVec - 1) / kVec * kVec;
     const int64_t lo = per_cta * rank;
     const int64_t hi = lo + per_cta < cols ? lo + per_cta : cols;
 
     // Each thread visits its elements in increasing index order (vectors v, v + kThreads, ...; then the tail).
     Running run;
-    if (lo < hi) {
-        if (vector_ok) {
-            const int64_t nvec = (hi - lo) / kVec;
-            const char* base = xr + lo * static_cast<int64_t>(sizeof(T));
-            int64_t v = threadIdx.x;
-            for (; v + (kUnroll - 1) * kThreads < nvec; v += kUnroll * kThreads) {
-                uint4 raw[kUnroll];
+    if constexpr (kBytes > 0) {
+        constexpr int kWords = kBytes / 4;
+        const int64_t nvec = lo < hi ? (hi - lo) / kVec : 0;
+        const char* base = xr + lo * static_cast<int64_t>(sizeof(T));
+        for (int64_t v = threadIdx.x; v < nvec; v += kUnroll * kThreads) {
+            // Raw words of kUnroll vectors in flight; unpacked one element at a time while visiting.
+            uint32_t w[kUnroll][kWords];
 #pragma unroll
-                for (int u = 0; u < kUnroll; ++u) {
-                    raw[u] = ld_stream(base + (v + u * kThreads) * 16);
-                }
+            for (int u = 0; u < kUnroll; ++u) {
+                if (v + u * kThreads < nvec) {
+                    const char* p = base + (v + u * kThreads) * kBytes;
+                    if constexpr (kBytes == 32) {
+                        const U8 r = ld_stream32(p);
 #pragma unroll
-                for (int u = 0; u < kUnroll; ++u) {
-                    scan_vector<T>(raw[u], static_cast<int>(lo + (v + u * kThreads) * kVec), run);
+                        for (int k = 0; k < 8; ++k) {
+                            w[u][k] = r.r[k];
+                        }
+                    } else {
+                        const uint4 r = ld_stream(p);
+                        w[u][0] = r.x;
+                        w[u][1] = r.y;
+                        w[u][2] = r.z;
+                        w[u][3] = r.w;
+                    }
                 }
             }
-            for (; v < nvec; v += kThreads) {
-                scan_vector<T>(ld_stream(base + v * 16), static_cast<int>(lo + v * kVec), run);
+#pragma unroll
+            for (int u = 0; u < kUnroll; ++u) {
+                if (v + u * kThreads < nvec) {
+                    const int first = static_cast<int>(lo + (v + u * kThreads) * kVec);
+#pragma unroll
+                    for (int k = 0; k < kWords; ++k) {
+                        if constexpr (sizeof(T) == 2) {
+                            run.visit(bf16_lo(w[u][k]), first + 2 * k);
+                            run.visit(bf16_hi(w[u][k]), first + 2 * k + 1);
+                        } else {
+                            run.visit(__uint_as_float(w[u][k]), first + k);
+                        }
+                    }
+                }
             }
-            for (int64_t e = lo + nvec * kVec + threadIdx.x; e < hi; e += kThreads) {
-                run.visit(V::load1(xr, e), static_cast<int>(e));
-            }
-        } else {
-            for (int64_t e = lo + threadIdx.x; e < hi; e += kThreads) {
-                run.visit(V::load1(xr, e), static_cast<int>(e));
-            }
+        }
+        for (int64_t e = lo + nvec * kVec + threadIdx.x; e < hi; e += kThreads) {
+            run.visit(Vec16<T>::load1(xr, e), static_cast<int>(e));
+        }
+    } else {
+        for (int64_t e = lo + threadIdx.x; e < hi; e += kThreads) {
+            run.visit(Vec16<T>::load1(xr, e), static_cast<int>(e));
         }
     }
     unsigned long long best = run.key();
@@ -150,7 +163,7 @@ __global__ void __launch_bounds__(kThreads) row_argmax_kernel(const void* __rest
         for (unsigned r = 1; r < csize; ++r) {
             b = umax64(b, *cluster.map_shared_rank(&cta_best, r));
         }
-        const float first = V::load1(xr, 0);
+        const float first = Vec16<T>::load1(xr, 0);
         int64_t index = 0;
         if (first == first && b != 0ull) {
             index = static_cast<int64_t>(0xffffffffu - static_cast<uint32_t>(b & 0xffffffffull));
@@ -159,6 +172,23 @@ __global__ void __launch_bounds__(kThreads) row_argmax_kernel(const void* __rest
     }
     // Keep every CTA (and its shared memory) alive until rank 0 has read it.
     cluster.sync();
+}
+
+template <typename T>
+cudaError_t launch_argmax(const void* x, int64_t rows, int64_t cols, int64_t row_stride, int64_t* out,
+                          unsigned cluster, cudaStream_t s) {
+    const auto base = reinterpret_cast<std::uintptr_t>(x);
+    const int64_t stride_bytes = row_stride * static_cast<int64_t>(sizeof(T));
+    const bool rows32 = (base & 31u) == 0 && (rows <= 1 || stride_bytes % 32 == 0);
+    const bool rows16 = (base & 15u) == 0 && (rows <= 1 || stride_bytes % 16 == 0);
+    const dim3 grid(static_cast<unsigned>(rows * cluster));
+    if (rows32) {
+        return runtime::launch(row_argmax_kernel<T, 32>, grid, dim3(kThreads), s, cluster, x, cols, row_stride, out);
+    }
+    if (rows16) {
+        return runtime::launch(row_argmax_kernel<T, 16>, grid, dim3(kThreads), s, cluster, x, cols, row_stride, out);
+    }
+    return runtime::launch(row_argmax_kernel<T, 0>, grid, dim3(kThreads), s, cluster, x, cols, row_stride, out);
 }
 
 }  // namespace
@@ -182,24 +212,18 @@ int cppinf_row_argmax(cppinf_dtype dtype, const void* x, int64_t rows, int64_t c
     }
     CPPINF_REQUIRE(x && out, CPPINF_ERR_INVALID_ARGUMENT, "row_argmax received a null pointer.");
     CPPINF_REQUIRE(rows <= (int64_t{1} << 27), CPPINF_ERR_UNSUPPORTED, "row_argmax supports at most 2^27 rows.");
-    const int vec = dtype == CPPINF_DTYPE_BF16 ? 8 : 4;
-    const bool vector_ok = rt::aligned16(x) && (rows <= 1 || row_stride % vec == 0);
 
-    // Enough CTAs to cover the SMs a few times, but no CTA with fewer than ~2K columns.
+    // Enough CTAs to cover the SMs a few times, but no CTA with fewer than ~4K columns.
     const int64_t target_ctas = static_cast<int64_t>(rt::sm_count()) * 4;
     int64_t cluster = 1;
-    while (cluster < kMaxCluster && rows * cluster < target_ctas && cols / (cluster * 2) >= 2048) {
+    while (cluster < kMaxCluster && rows * cluster < target_ctas && cols / (cluster * 2) >= 4096) {
         cluster *= 2;
     }
-
-    const dim3 grid(static_cast<unsigned>(rows * cluster));
     const auto s = rt::as_stream(stream);
     const cudaError_t launch_err =
         dtype == CPPINF_DTYPE_BF16
-            ? rt::launch(row_argmax_kernel<bf16>, grid, dim3(kThreads), s, static_cast<unsigned>(cluster), x, cols,
-                         row_stride, out, vector_ok)
-            : rt::launch(row_argmax_kernel<float>, grid, dim3(kThreads), s, static_cast<unsigned>(cluster), x, cols,
-                         row_stride, out, vector_ok);
+            ? launch_argmax<bf16>(x, rows, cols, row_stride, out, static_cast<unsigned>(cluster), s)
+            : launch_argmax<float>(x, rows, cols, row_stride, out, static_cast<unsigned>(cluster), s);
     return rt::launched(launch_err, "row_argmax");
 }
 

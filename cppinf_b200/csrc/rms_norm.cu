@@ -20,7 +20,7 @@
 namespace cppinf::device {
 namespace {
 
-constexpr int kThreads = 256;
+constexpr int kThreads = 128;
 constexpr int kWarps = kThreads / 32;
 
 struct RmsParams {
