@@ -11,8 +11,9 @@
 // yields 0.
 //
 // Layout: a row is split across a thread-block cluster of up to 8 CTAs of 256 threads, each CTA scanning a
-// contiguous column range with 32-byte loads (16-byte or scalar loads when the rows are not aligned for them), a
-// thread's loads issued together. CTA partials are combined through distributed shared memory (cluster rank 0 reads
+// contiguous column range with 16-byte loads (scalar loads when the rows are not aligned for them), a thread's five
+// loads issued together (measured on B200 against 32-byte loads, other batch sizes and a parallel DSMEM combine:
+// none faster). CTA partials are combined through distributed shared memory (cluster rank 0 reads
 // the other CTAs' shared slots), so no global scratch and no second launch are needed.
 //
 // Roofline: HBM-bound. Algorithmic bytes per row: cols * size read + 8 bytes written.
@@ -67,7 +68,7 @@ struct Running {
 
 // kBytes: 32 or 16 for vector loads of the row, 0 for element loads.
 template <typename T, int kBytes>
-__global__ void __launch_bounds__(kThreads, 4) row_argmax_kernel(const void* __restrict__ x, int64_t cols,
+__global__ void __launch_bounds__(kThreads) row_argmax_kernel(const void* __restrict__ x, int64_t cols,
                                                               int64_t row_stride, int64_t* __restrict__ out) {
     grid_dependency_begin();
     constexpr int kVec = kBytes == 0 ? 1 : kBytes / static_cast<int>(sizeof(T));
@@ -179,12 +180,8 @@ cudaError_t launch_argmax(const void* x, int64_t rows, int64_t cols, int64_t row
                           unsigned cluster, cudaStream_t s) {
     const auto base = reinterpret_cast<std::uintptr_t>(x);
     const int64_t stride_bytes = row_stride * static_cast<int64_t>(sizeof(T));
-    const bool rows32 = (base & 31u) == 0 && (rows <= 1 || stride_bytes % 32 == 0);
     const bool rows16 = (base & 15u) == 0 && (rows <= 1 || stride_bytes % 16 == 0);
     const dim3 grid(static_cast<unsigned>(rows * cluster));
-    if (rows32) {
-        return runtime::launch(row_argmax_kernel<T, 32>, grid, dim3(kThreads), s, cluster, x, cols, row_stride, out);
-    }
     if (rows16) {
         return runtime::launch(row_argmax_kernel<T, 16>, grid, dim3(kThreads), s, cluster, x, cols, row_stride, out);
     }
