@@ -74,12 +74,47 @@ _SIGNATURES = {
     "cppinf_qk_norm_rope": [
         _int, _ptr, _ptr, _ptr, _ptr, _ptr, _ptr, _i64, _i64, _i64, _i64, _i64, _f32, _ptr, _i64, _ptr,
     ],
+    "cppinf_linear": [_ptr, _i64, _ptr, _ptr, _i64, _i64, _i64, _ptr],
+    "cppinf_linear_residual": [_ptr, _i64, _ptr, _ptr, _ptr, _i64, _i64, _i64, _ptr],
+    "cppinf_linear_silu_mul": [_ptr, _i64, _ptr, _ptr, _ptr, _i64, _i64, _i64, _ptr],
+    "cppinf_linear_argmax": [_ptr, _ptr, _ptr, _i64, _i64, _ptr, _ptr, _ptr],
+    "cppinf_linear_argmax_scratch_bytes": [_i64, _i64],
+    "cppinf_decoder_attention": [_ptr, _ptr, _ptr, _ptr, _i64, _i64, _i64, _i64, _i64, _i64, _ptr],
+    "cppinf_embedding": [_ptr, _i64, _i64, _ptr, _i64, _ptr, _ptr],
+    "cppinf_qwen3_create": [ctypes.c_void_p, _i64, ctypes.POINTER(_ptr)],
+    "cppinf_qwen3_destroy": [_ptr],
+    "cppinf_qwen3_set_weight": [_ptr, ctypes.c_char_p, _ptr, _i64, _int],
+    "cppinf_qwen3_forward": [_ptr, ctypes.POINTER(_i64), _i64, _ptr, _int, ctypes.POINTER(_i64), _ptr],
+    "cppinf_qwen3_decode": [_ptr, _i64, ctypes.POINTER(_i64), _ptr],
+    "cppinf_qwen3_reset": [_ptr, _ptr],
+    "cppinf_qwen3_length": [_ptr],
+    "cppinf_qwen3_step_launches": [_ptr],
 }
 _RESTYPES = {
     "cppinf_last_error": ctypes.c_char_p,
     "cppinf_status_name": ctypes.c_char_p,
     "cppinf_launch_count": ctypes.c_uint64,
+    "cppinf_linear_argmax_scratch_bytes": _i64,
+    "cppinf_qwen3_destroy": None,
+    "cppinf_qwen3_length": _i64,
+    "cppinf_qwen3_step_launches": _i64,
 }
+
+
+class Qwen3ConfigC(ctypes.Structure):
+    """cppinf_qwen3_config."""
+
+    _fields_ = [
+        ("vocab_size", _i64),
+        ("hidden_size", _i64),
+        ("intermediate_size", _i64),
+        ("num_hidden_layers", _i64),
+        ("num_attention_heads", _i64),
+        ("num_key_value_heads", _i64),
+        ("head_dim", _i64),
+        ("rms_norm_eps", _f32),
+        ("rope_theta", _f32),
+    ]
 
 _lib: ctypes.CDLL | None = None
 

@@ -1,0 +1,320 @@
+// Causal grouped-query attention of the Qwen3 decoder over the KV cache: fused_causal_attention of
+// src/nn/qwen_attention.cpp:236-333 (scores q k^T in f32, the position-causal softmax of :164-235, probabilities
+// cast to bf16, probabilities times V in bf16) for one sequence, query t at position pos0 + t seeing keys
+// 0 .. pos0 + t, query head h reading key/value head h / (Hq / Hkv) (the repeat_interleave of :290-291).
+//
+// One thread-block cluster of 8 CTAs (128 threads each) per (query, head); CTA c owns the c-th of 8 parts of the
+// visible keys (P = ceil(L / 8) consecutive keys each). The order of every sum is fixed, and the CPU oracle
+// restates it (oracle_decoder_attention):
+//  - score: the head vector is cut into 8 segments of D / 8 dims, each summed in order by one lane, the 8 partials
+//    combined by a butterfly over lane distances 4, 2, 1; x_j = score * (1 / sqrt(D));
+//  - max over all parts (DSMEM exchange); e_j = exp(x_j - max) with the portable exp of pexp.cuh;
+//  - part sum: thread i adds e_j for j = lo + i, lo + i + 128, ... in order; warp butterfly; the 4 warp sums in
+//    order; then the 8 part sums in order (every CTA reads all 8 over DSMEM and gets the same total);
+//  - p_j = bf16(e_j / total);
+//  - context: warp w adds p_j v_j for j = lo + w, lo + w + 4, ... in order; the 4 warp sums in order; the 8 part
+//    sums in order (CTA c finishes dims [cD/8, (c+1)D/8)); stored in bf16.
+// Nothing but DSMEM carries partial results, so the kernel needs no global scratch.
+//
+// Roofline: HBM/L2-bound on the cache reads (2 * L * D * 2 bytes per query head, shared by the 2 heads of a group
+// through L2); the decode step reads every cached key and value once per layer.
+#include <cooperative_groups.h>
+
+#include "common.cuh"
+#include "decoder.h"
+#include "pexp.cuh"
+#include "runtime.h"
+
+namespace cg = cooperative_groups;
+
+namespace cppinf::device {
+namespace {
+
+constexpr int kParts = 8;
+constexpr int kThreads = 128;
+constexpr int kWarps = kThreads / 32;
+constexpr int kSegments = 8;  // lanes per key in the score dot product
+
+template <int kD>
+struct VRow;  // a lane's kD / 32 values of one V row
+
+template <>
+struct VRow<64> {
+    static __device__ __forceinline__ void load(const bf16* p, float (&v)[2]) {
+        const uint32_t w = __ldg(reinterpret_cast<const unsigned int*>(p));
+        v[0] = bf16_lo(w);
+        v[1] = bf16_hi(w);
+    }
+};
+
+template <>
+struct VRow<128> {
+    static __device__ __forceinline__ void load(const bf16* p, float (&v)[4]) {
+        const uint2 w = __ldg(reinterpret_cast<const uint2*>(p));
+        v[0] = bf16_lo(w.x);
+        v[1] = bf16_hi(w.x);
+        v[2] = bf16_lo(w.y);
+        v[3] = bf16_hi(w.y);
+    }
+};
+
+template <>
+struct VRow<256> {
+    static __device__ __forceinline__ void load(const bf16* p, float (&v)[8]) {
+        Vec16<bf16>::unpack(ld_cached(p), v);
+    }
+};
+
+__device__ __forceinline__ float dot8(uint4 a, uint4 b, float acc) {
+    acc = acc + bf16_lo(a.x) * bf16_lo(b.x);
+    acc = acc + bf16_hi(a.x) * bf16_hi(b.x);
+    acc = acc + bf16_lo(a.y) * bf16_lo(b.y);
+    acc = acc + bf16_hi(a.y) * bf16_hi(b.y);
+    acc = acc + bf16_lo(a.z) * bf16_lo(b.z);
+    acc = acc + bf16_hi(a.z) * bf16_hi(b.z);
+    acc = acc + bf16_lo(a.w) * bf16_lo(b.w);
+    acc = acc + bf16_hi(a.w) * bf16_hi(b.w);
+    return acc;
+}
+
+template <int kD>
+__global__ void __launch_bounds__(kThreads) decoder_attention_kernel(const AttentionParams p) {
+    constexpr int kSeg = kD / kSegments;       // dims per score segment
+    constexpr int kSegChunks = kSeg / 8;       // 16-byte chunks per segment
+    constexpr int kKeysPerIter = 32 / kSegments;
+    constexpr int kDimsPerLane = kD / 32;
+    constexpr int kFinal = kD / kParts;        // context dims each CTA finishes
+    extern __shared__ float s_e[];             // this part's scores, then exp values, then probabilities
+    __shared__ float s_red[kWarps];
+    __shared__ float s_max;
+    __shared__ float s_sum;
+    __shared__ float s_acc[kWarps][kD];
+    __shared__ float s_part[kD];
+
+    grid_dependency_begin();
+    cg::cluster_group cluster = cg::this_cluster();
+    const int rank = static_cast<int>(cluster.block_rank());
+    const int lane = threadIdx.x & 31;
+    const int warp = threadIdx.x >> 5;
+    const int64_t unit = blockIdx.x / kParts;
+    const int64_t t = unit / p.q_heads;
+    const int h = static_cast<int>(unit - t * p.q_heads);
+    const int kvh = h / (p.q_heads / p.kv_heads);
+    const int64_t pos = p.pos0 + (p.position != nullptr ? static_cast<int64_t>(*p.position) : 0) + t;
+    if (pos >= p.capacity) {
+        return;  // the whole cluster leaves together (same t); no DSMEM access happens
+    }
+    const int64_t L = pos + 1;
+    const int64_t P = (L + kParts - 1) / kParts;
+    const int64_t lo = rank * P < L ? rank * P : L;
+    const int64_t hi = lo + P < L ? lo + P : L;
+    const int64_t n = hi - lo;
+    const int64_t kv_row = static_cast<int64_t>(p.kv_heads) * kD;
+    const float scale = 1.0f / sqrtf(static_cast<float>(kD));
+
+    // Scores: 4 keys per warp iteration, 8 lanes per key.
+    const int sub = lane % kSegments;
+    const int slot = lane / kSegments;
+    uint4 qv[kSegChunks];
+    const bf16* qrow = p.q + (t * p.q_heads + h) * kD + sub * kSeg;
+#pragma unroll
+    for (int c = 0; c < kSegChunks; ++c) {
+        qv[c] = ld_cached(qrow + c * 8);
+    }
+    for (int64_t j0 = lo + warp * kKeysPerIter; j0 < hi; j0 += kWarps * kKeysPerIter) {
+        const int64_t j = j0 + slot;
+        float s = 0.0f;
+        if (j < hi) {
+            const bf16* krow = p.k_cache + j * kv_row + kvh * kD + sub * kSeg;
+#pragma unroll
+            for (int c = 0; c < kSegChunks; ++c) {
+                s = dot8(qv[c], ld_cached(krow + c * 8), s);
+            }
+        }
+#pragma unroll
+        for (int offset = kSegments / 2; offset > 0; offset >>= 1) {
+            s = s + __shfl_xor_sync(0xffffffffu, s, offset);
+        }
+        if (j < hi && sub == 0) {
+            s_e[j - lo] = s * scale;
+        }
+    }
+    __syncthreads();
+
+    // Maximum over all parts.
+    float mx = -INFINITY;
+    for (int64_t i = threadIdx.x; i < n; i += kThreads) {
+        mx = fmaxf(mx, s_e[i]);
+    }
+    mx = group_max<32>(mx);
+    if (lane == 0) {
+        s_red[warp] = mx;
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        float m = s_red[0];
+#pragma unroll
+        for (int w = 1; w < kWarps; ++w) {
+            m = fmaxf(m, s_red[w]);
+        }
+        s_max = m;
+    }
+    cluster.sync();
+    float gmax = *cluster.map_shared_rank(&s_max, 0);
+#pragma unroll
+    for (int r = 1; r < kParts; ++r) {
+        gmax = fmaxf(gmax, *cluster.map_shared_rank(&s_max, r));
+    }
+
+    // exp and the part sum.
+    float sum = 0.0f;
+    for (int64_t i = threadIdx.x; i < n; i += kThreads) {
+        const float e = pexp(s_e[i] - gmax);
+        s_e[i] = e;
+        sum = sum + e;
+    }
+    sum = group_sum<32>(sum);
+    __syncthreads();  // s_red is reused
+    if (lane == 0) {
+        s_red[warp] = sum;
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        float s = s_red[0];
+#pragma unroll
+        for (int w = 1; w < kWarps; ++w) {
+            s = s + s_red[w];
+        }
+        s_sum = s;
+    }
+    cluster.sync();
+    float total = *cluster.map_shared_rank(&s_sum, 0);
+#pragma unroll
+    for (int r = 1; r < kParts; ++r) {
+        total = total + *cluster.map_shared_rank(&s_sum, r);
+    }
+
+    for (int64_t i = threadIdx.x; i < n; i += kThreads) {
+        s_e[i] = round_to_bf16(s_e[i] / total);
+    }
+    __syncthreads();
+
+    // Probabilities times V.
+    float a[kDimsPerLane];
+#pragma unroll
+    for (int d = 0; d < kDimsPerLane; ++d) {
+        a[d] = 0.0f;
+    }
+    for (int64_t j = lo + warp; j < hi; j += kWarps) {
+        const float pj = s_e[j - lo];
+        float v[kDimsPerLane];
+        VRow<kD>::load(p.v_cache + j * kv_row + kvh * kD + lane * kDimsPerLane, v);
+#pragma unroll
+        for (int d = 0; d < kDimsPerLane; ++d) {
+            a[d] = a[d] + pj * v[d];
+        }
+    }
+#pragma unroll
+    for (int d = 0; d < kDimsPerLane; ++d) {
+        s_acc[warp][lane * kDimsPerLane + d] = a[d];
+    }
+    __syncthreads();
+    for (int d = threadIdx.x; d < kD; d += kThreads) {
+        float s = s_acc[0][d];
+#pragma unroll
+        for (int w = 1; w < kWarps; ++w) {
+            s = s + s_acc[w][d];
+        }
+        s_part[d] = s;
+    }
+    cluster.sync();
+    if (threadIdx.x < kFinal) {
+        const int d = rank * kFinal + threadIdx.x;
+        float c = *cluster.map_shared_rank(&s_part[d], 0);
+#pragma unroll
+        for (int r = 1; r < kParts; ++r) {
+            c = c + *cluster.map_shared_rank(&s_part[d], r);
+        }
+        Vec16<bf16>::store1(p.ctx, (t * p.q_heads + h) * kD + d, c);
+    }
+    // Keep every CTA's shared memory alive until the others have read it.
+    cluster.sync();
+}
+
+template <int kD>
+cudaError_t launch_attention_dim(const AttentionParams& p, int64_t max_keys, cudaStream_t s) {
+    const int64_t per_part = (max_keys + kParts - 1) / kParts;
+    const std::size_t smem = static_cast<std::size_t>(per_part < 1 ? 1 : per_part) * sizeof(float);
+    auto kernel = decoder_attention_kernel<kD>;
+    if (smem > 32 * 1024) {
+        const cudaError_t err =
+            cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
+        if (err != cudaSuccess) {
+            return err;
+        }
+    }
+    const int64_t blocks = p.T * p.q_heads * kParts;
+    return runtime::launch_smem(kernel, dim3(static_cast<unsigned>(blocks)), dim3(kThreads), smem, s,
+                                static_cast<unsigned>(kParts), p);
+}
+
+}  // namespace
+
+cudaError_t launch_decoder_attention(const AttentionParams& p, int64_t max_keys, cudaStream_t s) {
+    switch (p.head_dim) {
+    case 64:
+        return launch_attention_dim<64>(p, max_keys, s);
+    case 128:
+        return launch_attention_dim<128>(p, max_keys, s);
+    case 256:
+        return launch_attention_dim<256>(p, max_keys, s);
+    default:
+        return cudaErrorInvalidValue;
+    }
+}
+
+}  // namespace cppinf::device
+
+using namespace cppinf::device;
+namespace rt = cppinf::runtime;
+
+extern "C" {
+
+int cppinf_decoder_attention(const void* q, const void* k_cache, const void* v_cache, void* ctx, int64_t tokens,
+                             int64_t q_heads, int64_t kv_heads, int64_t head_dim, int64_t position, int64_t capacity,
+                             void* stream) {
+    CPPINF_REQUIRE(tokens >= 0 && q_heads > 0 && kv_heads > 0 && head_dim > 0, CPPINF_ERR_INVALID_ARGUMENT,
+                   "qwen_attention requires non-zero head configuration.");
+    CPPINF_REQUIRE(q_heads % kv_heads == 0, CPPINF_ERR_INVALID_ARGUMENT,
+                   "qwen_attention requires query heads to divide by key/value heads.");
+    CPPINF_REQUIRE(head_dim == 64 || head_dim == 128 || head_dim == 256, CPPINF_ERR_UNSUPPORTED,
+                   "decoder attention supports head_dim 64, 128 or 256.");
+    CPPINF_REQUIRE(position >= 0, CPPINF_ERR_INVALID_ARGUMENT, "qwen_attention query offsets must be non-negative.");
+    CPPINF_REQUIRE(position + tokens <= capacity, CPPINF_ERR_OUT_OF_RANGE,
+                   "qwen_attention key lengths exceed the cache capacity.");
+    CPPINF_REQUIRE(tokens * q_heads * 8 < (int64_t{1} << 31), CPPINF_ERR_UNSUPPORTED,
+                   "decoder attention supports fewer than 2^28 query heads in one call.");
+    CPPINF_REQUIRE((capacity + 7) / 8 * 4 <= 200 * 1024, CPPINF_ERR_UNSUPPORTED,
+                   "decoder attention supports caches of up to 409600 positions.");
+    if (tokens == 0) {
+        return rt::ok();
+    }
+    CPPINF_REQUIRE(q && k_cache && v_cache && ctx, CPPINF_ERR_INVALID_ARGUMENT,
+                   "qwen_attention received a null pointer.");
+    CPPINF_REQUIRE(rt::aligned16(q) && rt::aligned16(k_cache) && rt::aligned16(v_cache), CPPINF_ERR_UNSUPPORTED,
+                   "decoder attention requires 16-byte aligned operands.");
+    AttentionParams p{static_cast<const bf16*>(q),
+                      static_cast<const bf16*>(k_cache),
+                      static_cast<const bf16*>(v_cache),
+                      static_cast<bf16*>(ctx),
+                      tokens,
+                      static_cast<int>(q_heads),
+                      static_cast<int>(kv_heads),
+                      static_cast<int>(head_dim),
+                      position,
+                      nullptr,
+                      capacity};
+    return rt::launched(launch_decoder_attention(p, position + tokens, rt::as_stream(stream)), "decoder_attention");
+}
+
+}  // extern "C"

@@ -1,0 +1,97 @@
+// Internal interface of the decoder kernels (linear.cu, attention.cu) used by the model runtime (qwen3.cu) and by
+// the C ABI entry points. Host and device share these parameter blocks; all pointers are device pointers.
+#pragma once
+
+#include <cuda_bf16.h>
+#include <cuda_runtime.h>
+
+#include <cstdint>
+
+namespace cppinf::device {
+
+// What a linear kernel does with each finished dot product (bf16-rounded once, as the reference's bf16 matmul
+// result):
+//  kStore     out segment k gets the value (rows [seg[k], seg[k+1]) of the weight matrix go to segment k);
+//  kResidual  out0 = bf16(residual + value), the residual edge of src/nn/qwen_decoder_block.cpp:80-89;
+//  kSiluMul   two weight matrices (gate, up): out0 = bf16(bf16(silu(gate)) * up), src/nn/qwen_mlp.cpp:61-66;
+//  kArgmax    the greedy token of the row (src/cli/cli_app.cpp:72-94), optionally also storing the logits.
+enum class LinearEpilogue : int { kStore = 0, kResidual = 1, kSiluMul = 2, kArgmax = 3 };
+
+struct LinearParams {
+    LinearEpilogue epilogue;
+    // Input rows x[m, 0..K): x + m * x_stride, or, when `tokens` is set, the embedding row
+    // x + tokens[token_base + m] * x_stride (token_base read from *position when `position` is set).
+    const __nv_bfloat16* x;
+    int64_t x_stride;
+    const int64_t* tokens;
+    int64_t vocab;             // rows of the embedding table (token ids are clamped into range on the device)
+    __nv_bfloat16* x_copy;     // single-row kernel only: the raw input row is also stored here (residual stream)
+    const __nv_bfloat16* norm_weight;  // single-row kernel only: x is RMS-normalised first (ops::rms_norm)
+    float eps;
+
+    const __nv_bfloat16* w0;   // [N, K] row-major ([out_features, in_features], the checkpoint layout)
+    const __nv_bfloat16* w1;   // second [N, K] matrix for kSiluMul
+    int64_t M;
+    int64_t N;
+    int64_t K;
+
+    // Output segments: row n of the weights with seg[k] <= n < seg[k + 1] is stored at
+    // out[k] + (m + row_offset[k]) * ld[k] + (n - seg[k]); segment 2's row offset adds *position when set.
+    __nv_bfloat16* out[3];
+    int64_t ld[3];
+    int64_t seg[4];
+    int64_t row_offset[3];
+    const int* position;       // device sequence length (decode steps)
+
+    const __nv_bfloat16* residual;  // kResidual: [M, N] with row stride res_ld
+    int64_t res_ld;
+
+    // kArgmax: tokens_out[*position + advance] = argmax over the row; *position += advance. `partial` holds one
+    // 64-bit key per CTA and `counter` must be zero before the launch (the last CTA resets it).
+    int64_t* tokens_out;
+    int* position_out;
+    int64_t advance;
+    unsigned long long* partial;
+    unsigned int* counter;
+};
+
+// Single-row (decode) linear: one warp per output row at a time, the weights streamed once. Supports every
+// epilogue, the embedding gather and the RMSNorm prologue. Requires K % 8 == 0 and 16-byte aligned rows.
+cudaError_t launch_gemv(const LinearParams& p, cudaStream_t s);
+
+// Grid the single-row kernel uses for `p` (the size the kArgmax scratch `partial` must have).
+int gemv_grid(const LinearParams& p);
+
+// Multi-row linear (prefill): tiles of up to 16 input rows staged in shared memory, kStore / kResidual / kSiluMul.
+// Requires K % 8 == 0 and 16-byte aligned rows.
+cudaError_t launch_linear_rows(const LinearParams& p, cudaStream_t s);
+
+struct AttentionParams {
+    const __nv_bfloat16* q;        // [T, Hq, D]
+    const __nv_bfloat16* k_cache;  // [cap, Hkv, D]
+    const __nv_bfloat16* v_cache;  // [cap, Hkv, D]
+    __nv_bfloat16* ctx;            // [T, Hq, D]
+    int64_t T;
+    int q_heads;
+    int kv_heads;
+    int head_dim;
+    int64_t pos0;                  // position of query 0 (added to *position when set)
+    const int* position;
+    int64_t capacity;              // cache rows; queries past it are skipped
+};
+
+// Causal GQA attention of one sequence in the fixed partition order (see attention.cu). head_dim 64, 128 or 256.
+cudaError_t launch_decoder_attention(const AttentionParams& p, int64_t max_keys, cudaStream_t s);
+
+// q/k per-head RMSNorm + RoPE (rope.cu) at the device-side position: token t is rotated for position
+// *position + t and its k row is written to k_cache row *position + t; q_out is [tokens, q_heads, head_dim].
+cudaError_t launch_qk_norm_rope_at(const __nv_bfloat16* q, const __nv_bfloat16* k, const __nv_bfloat16* q_weight,
+                                   const __nv_bfloat16* k_weight, __nv_bfloat16* q_out, __nv_bfloat16* k_cache,
+                                   int64_t tokens, int q_heads, int k_heads, int head_dim, const int* position,
+                                   float eps, const float* table, int64_t table_positions, cudaStream_t s);
+
+// Embedding lookup (src/models/qwen3/qwen3_model.cpp:132-165): out[t] = table[tokens[t]], ids clamped into range.
+cudaError_t launch_embedding(const __nv_bfloat16* table, int64_t vocab, int64_t hidden, const int64_t* tokens,
+                             int64_t count, __nv_bfloat16* out, cudaStream_t s);
+
+}  // namespace cppinf::device

@@ -1,0 +1,642 @@
+// Linear projections of the Qwen3 decoder: y = x W^T with W [out_features, in_features] in bf16, the
+// linear_project of src/nn/qwen_common.cpp:15-37 (ops::matmul, src/ops/matmul.cpp:85-114, bf16 in, bf16 out).
+//
+// Accumulation order (shared with the CPU oracle, so greedy tokens are compared bit for bit): one warp owns an
+// output; its row is cut into 16-byte chunks of 8 elements, lane l adds the products of chunks l, l + 32, ... in
+// increasing element order starting from +0, and the 32 partials are combined by a butterfly over lane distances
+// 16 .. 1 -- the same order as the RMSNorm sum of squares. A product of two bf16 values is exact in f32, so every
+// step is one rounded f32 addition. The result is rounded to bf16 once.
+//
+// Two kernels:
+//  - gemv_kernel (one input row, the decode step): each warp streams whole weight rows with 16 loads of 16 bytes
+//    per lane in flight. The first batch of weights is loaded before griddepcontrol.wait, so under programmatic
+//    dependent launch it overlaps the previous kernel's tail (weights never depend on it). Fused prologues: the
+//    embedding gather of the token at the device-side position and ops::rms_norm of the input row; fused epilogues:
+//    segment stores (q | k | v, v straight into the KV cache), residual add, SiLU(gate) * up, and the greedy argmax
+//    over the vocabulary (the last CTA to finish combines the per-CTA maxima).
+//  - linear_rows_kernel (prefill): tiles of 16 input rows staged in shared memory; each weight chunk a lane loads
+//    is unpacked once and used for the 16 rows.
+//
+// Roofline: the decode projections are HBM-bound on the weights (N * K * 2 bytes per token); the prefill tiles are
+// bound by f32 issue (two instructions per multiply-add with separately rounded operations).
+#include "common.cuh"
+#include "decoder.h"
+#include "pexp.cuh"
+#include "runtime.h"
+
+namespace cppinf::device {
+namespace {
+
+constexpr int kThreads = 256;
+constexpr int kWarps = kThreads / 32;
+constexpr int kLoads = 16;  // 16-byte weight loads a lane keeps in flight in the single-row kernel
+constexpr int kTileRows = 16;
+
+__device__ __forceinline__ float dot_chunk(uint4 x, uint4 w, float acc) {
+    acc = acc + bf16_lo(x.x) * bf16_lo(w.x);
+    acc = acc + bf16_hi(x.x) * bf16_hi(w.x);
+    acc = acc + bf16_lo(x.y) * bf16_lo(w.y);
+    acc = acc + bf16_hi(x.y) * bf16_hi(w.y);
+    acc = acc + bf16_lo(x.z) * bf16_lo(w.z);
+    acc = acc + bf16_hi(x.z) * bf16_hi(w.z);
+    acc = acc + bf16_lo(x.w) * bf16_lo(w.w);
+    acc = acc + bf16_hi(x.w) * bf16_hi(w.w);
+    return acc;
+}
+
+// Same products with the weight chunk already unpacked.
+__device__ __forceinline__ float dot_chunk(uint4 x, const float (&w)[8], float acc) {
+    acc = acc + bf16_lo(x.x) * w[0];
+    acc = acc + bf16_hi(x.x) * w[1];
+    acc = acc + bf16_lo(x.y) * w[2];
+    acc = acc + bf16_hi(x.y) * w[3];
+    acc = acc + bf16_lo(x.z) * w[4];
+    acc = acc + bf16_hi(x.z) * w[5];
+    acc = acc + bf16_lo(x.w) * w[6];
+    acc = acc + bf16_hi(x.w) * w[7];
+    return acc;
+}
+
+__device__ __forceinline__ int64_t clamp_token(int64_t t, int64_t vocab) {
+    return t < 0 ? 0 : (t >= vocab ? vocab - 1 : t);
+}
+
+// Start of input row m (after the optional embedding gather).
+__device__ __forceinline__ const bf16* input_row(const LinearParams& p, int64_t m, int64_t token_base) {
+    if (p.tokens != nullptr) {
+        return reinterpret_cast<const bf16*>(p.x) + clamp_token(p.tokens[token_base + m], p.vocab) * p.x_stride;
+    }
+    return reinterpret_cast<const bf16*>(p.x) + m * p.x_stride;
+}
+
+__device__ __forceinline__ void store_segment(const LinearParams& p, int64_t m, int64_t n, float v, int64_t pos) {
+    const int k = n >= p.seg[2] ? 2 : (n >= p.seg[1] ? 1 : 0);
+    const int64_t row = m + p.row_offset[k] + (k == 2 ? pos : 0);
+    Vec16<bf16>::store1(p.out[k], row * p.ld[k] + (n - p.seg[k]), v);
+}
+
+// Argmax key of a bf16 logit (the reference compares the stored bf16 values): larger value first, then lower index;
+// NaN never wins; a NaN at index 0 forces index 0 (the reference's scan never replaces its starting element).
+__device__ __forceinline__ unsigned long long logit_key(float v, int64_t n) {
+    uint32_t u = __float_as_uint(v);
+    if ((u & 0x7fffffffu) > 0x7f800000u) {
+        return n == 0 ? ~0ull : 0ull;
+    }
+    if ((u & 0x7fffffffu) == 0u) {
+        u = 0u;
+    }
+    const uint32_t ord = (u & 0x80000000u) ? ~u : (u | 0x80000000u);
+    return (static_cast<unsigned long long>(ord) << 32) | (0xffffffffull - static_cast<unsigned long long>(n));
+}
+
+__device__ __forceinline__ unsigned long long umax64(unsigned long long a, unsigned long long b) {
+    return a > b ? a : b;
+}
+
+template <LinearEpilogue kEpi, int kRows>
+__global__ void __launch_bounds__(kThreads, 2) gemv_kernel(const LinearParams p) {
+    extern __shared__ uint4 smem_x[];  // the input row, K / 8 chunks
+    __shared__ float s_inv;
+    __shared__ unsigned long long s_best[kWarps];
+    __shared__ int s_last;
+
+    // Dependents may be scheduled at once: they only prefetch weights before their own wait.
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+
+    constexpr int kMats = kEpi == LinearEpilogue::kSiluMul ? 2 : 1;
+    constexpr int kSlots = kRows * kMats;
+    constexpr int kBatch = kLoads / kSlots;  // chunk iterations per lane per batch
+    const int lane = threadIdx.x & 31;
+    const int warp = threadIdx.x >> 5;
+    const int64_t nchunks = p.K / 8;
+    const int64_t iters = (nchunks + 31) / 32;  // chunk iterations of lane 0
+    const int64_t groups = (p.N + kRows - 1) / kRows;
+    const int64_t gstride = static_cast<int64_t>(gridDim.x) * kWarps;
+    int64_t g = static_cast<int64_t>(blockIdx.x) * kWarps + warp;
+    const int64_t row_bytes = p.K * 2;
+
+    uint4 wreg[kSlots][kBatch];
+    auto issue = [&](int64_t grp, int64_t i0) {
+#pragma unroll
+        for (int r = 0; r < kRows; ++r) {
+            const int64_t n = grp * kRows + r;
+#pragma unroll
+            for (int mat = 0; mat < kMats; ++mat) {
+                const char* wrow = reinterpret_cast<const char*>(mat == 0 ? p.w0 : p.w1) + n * row_bytes;
+#pragma unroll
+                for (int b = 0; b < kBatch; ++b) {
+                    const int64_t c = lane + 32 * (i0 + b);
+                    if (n < p.N && c < nchunks) {
+                        wreg[r * kMats + mat][b] = ld_stream(wrow + c * 16);
+                    } else {
+                        wreg[r * kMats + mat][b] = make_uint4(0u, 0u, 0u, 0u);
+                    }
+                }
+            }
+        }
+    };
+    bool pending = g < groups;
+    if (pending) {
+        issue(g, 0);
+    }
+
+    asm volatile("griddepcontrol.wait;" ::: "memory");
+
+    const int64_t pos = p.position != nullptr ? static_cast<int64_t>(*p.position) : 0;
+    const bf16* xrow = input_row(p, 0, pos);
+    for (int64_t i = threadIdx.x; i < nchunks; i += kThreads) {
+        const uint4 v = ld_cached(xrow + i * 8);
+        smem_x[i] = v;
+        if (p.x_copy != nullptr && blockIdx.x == 0) {
+            st_v4(p.x_copy + i * 8, v);
+        }
+    }
+    __syncthreads();
+    if (p.norm_weight != nullptr) {
+        // ops::rms_norm of the row, sum of squares in the canonical lane order (identical to rms_norm.cu).
+        if (warp == 0) {
+            float s = 0.0f;
+            for (int64_t c = lane; c < nchunks; c += 32) {
+                float f[8];
+                Vec16<bf16>::unpack(smem_x[c], f);
+#pragma unroll
+                for (int e = 0; e < 8; ++e) {
+                    s = s + f[e] * f[e];
+                }
+            }
+            s = group_sum<32>(s);
+            if (lane == 0) {
+                const float mean = s / static_cast<float>(p.K);
+                const float rms = sqrtf(mean + p.eps);
+                s_inv = 1.0f / rms;
+            }
+        }
+        __syncthreads();
+        const float inv = s_inv;
+        for (int64_t i = threadIdx.x; i < nchunks; i += kThreads) {
+            float f[8];
+            float w[8];
+            Vec16<bf16>::unpack(smem_x[i], f);
+            Vec16<bf16>::unpack(ld_cached(p.norm_weight + i * 8), w);
+#pragma unroll
+            for (int e = 0; e < 8; ++e) {
+                f[e] = (f[e] * inv) * w[e];
+            }
+            smem_x[i] = Vec16<bf16>::pack(f);
+        }
+        __syncthreads();
+    }
+
+    unsigned long long best = 0ull;
+    for (; g < groups; g += gstride) {
+        float acc[kSlots];
+#pragma unroll
+        for (int j = 0; j < kSlots; ++j) {
+            acc[j] = 0.0f;
+        }
+        for (int64_t i0 = 0; i0 < iters; i0 += kBatch) {
+            if (pending) {
+                pending = false;
+            } else {
+                issue(g, i0);
+            }
+#pragma unroll
+            for (int b = 0; b < kBatch; ++b) {
+                const int64_t c = lane + 32 * (i0 + b);
+                if (c < nchunks) {
+                    const uint4 xv = smem_x[c];
+#pragma unroll
+                    for (int j = 0; j < kSlots; ++j) {
+                        acc[j] = dot_chunk(xv, wreg[j][b], acc[j]);
+                    }
+                }
+            }
+        }
+#pragma unroll
+        for (int j = 0; j < kSlots; ++j) {
+            acc[j] = group_sum<32>(acc[j]);
+        }
+#pragma unroll
+        for (int r = 0; r < kRows; ++r) {
+            const int64_t n = g * kRows + r;
+            if (n >= p.N) {
+                break;
+            }
+            if constexpr (kEpi == LinearEpilogue::kArgmax) {
+                const float logit = round_to_bf16(acc[r]);
+                best = umax64(best, logit_key(logit, n));
+                if (lane == r && p.out[0] != nullptr) {
+                    store_segment(p, 0, n, logit, 0);
+                }
+            } else if (lane == r) {
+                if constexpr (kEpi == LinearEpilogue::kStore) {
+                    store_segment(p, 0, n, acc[r], pos);
+                } else if constexpr (kEpi == LinearEpilogue::kResidual) {
+                    const float res = Vec16<bf16>::load1(p.residual, n);
+                    Vec16<bf16>::store1(p.out[0], n, res + round_to_bf16(acc[r]));
+                } else {
+                    const float gate = round_to_bf16(acc[r * 2]);
+                    const float up = round_to_bf16(acc[r * 2 + 1]);
+                    Vec16<bf16>::store1(p.out[0], n, round_to_bf16(silu_pexp(gate)) * up);
+                }
+            }
+        }
+    }
+
+    if constexpr (kEpi == LinearEpilogue::kArgmax) {
+        // Every lane holds the same `best`; combine the warps, then the CTAs (the last CTA to arrive).
+        if (lane == 0) {
+            s_best[warp] = best;
+        }
+        __syncthreads();
+        if (threadIdx.x == 0) {
+            unsigned long long b = s_best[0];
+#pragma unroll
+            for (int w = 1; w < kWarps; ++w) {
+                b = umax64(b, s_best[w]);
+            }
+            p.partial[blockIdx.x] = b;
+            __threadfence();
+            const unsigned ticket = atomicAdd(p.counter, 1u);
+            s_last = ticket == gridDim.x - 1 ? 1 : 0;
+        }
+        __syncthreads();
+        if (s_last) {
+            __threadfence();
+            unsigned long long b = 0ull;
+            for (int64_t i = threadIdx.x; i < gridDim.x; i += kThreads) {
+                b = umax64(b, __ldcg(p.partial + i));
+            }
+#pragma unroll
+            for (int offset = 16; offset > 0; offset >>= 1) {
+                b = umax64(b, __shfl_xor_sync(0xffffffffu, b, offset));
+            }
+            __syncthreads();
+            if (lane == 0) {
+                s_best[warp] = b;
+            }
+            __syncthreads();
+            if (threadIdx.x == 0) {
+                unsigned long long all = s_best[0];
+#pragma unroll
+                for (int w = 1; w < kWarps; ++w) {
+                    all = umax64(all, s_best[w]);
+                }
+                int64_t index = 0;
+                if (all != ~0ull && all != 0ull) {
+                    index = static_cast<int64_t>(0xffffffffull - (all & 0xffffffffull));
+                }
+                const int base = *p.position_out;
+                p.tokens_out[base + p.advance] = index;
+                *p.position_out = base + static_cast<int>(p.advance);
+                *p.counter = 0u;
+            }
+        }
+    }
+}
+
+template <LinearEpilogue kEpi>
+__global__ void __launch_bounds__(kThreads) linear_rows_kernel(const LinearParams p) {
+    extern __shared__ uint4 smem_x[];  // kTileRows rows of K / 8 chunks
+    grid_dependency_begin();
+    constexpr int kMats = kEpi == LinearEpilogue::kSiluMul ? 2 : 1;
+    constexpr int kBatch = 4;
+    const int lane = threadIdx.x & 31;
+    const int warp = threadIdx.x >> 5;
+    const int64_t nchunks = p.K / 8;
+    const int64_t m0 = static_cast<int64_t>(blockIdx.y) * kTileRows;
+    const int64_t mt = p.M - m0 < kTileRows ? p.M - m0 : kTileRows;
+    const int64_t row_bytes = p.K * 2;
+
+    for (int64_t i = threadIdx.x; i < kTileRows * nchunks; i += kThreads) {
+        const int64_t m = i / nchunks;
+        const int64_t c = i - m * nchunks;
+        smem_x[i] = m < mt ? ld_cached(input_row(p, m0 + m, 0) + c * 8) : make_uint4(0u, 0u, 0u, 0u);
+    }
+    __syncthreads();
+
+    for (int64_t n = static_cast<int64_t>(blockIdx.x) * kWarps + warp; n < p.N;
+         n += static_cast<int64_t>(gridDim.x) * kWarps) {
+        float acc[kMats][kTileRows];
+#pragma unroll
+        for (int mat = 0; mat < kMats; ++mat) {
+#pragma unroll
+            for (int m = 0; m < kTileRows; ++m) {
+                acc[mat][m] = 0.0f;
+            }
+        }
+        for (int64_t i0 = 0; lane + 32 * i0 < nchunks; i0 += kBatch) {
+            uint4 wraw[kMats][kBatch];
+#pragma unroll
+            for (int mat = 0; mat < kMats; ++mat) {
+                const char* wrow = reinterpret_cast<const char*>(mat == 0 ? p.w0 : p.w1) + n * row_bytes;
+#pragma unroll
+                for (int b = 0; b < kBatch; ++b) {
+                    const int64_t c = lane + 32 * (i0 + b);
+                    wraw[mat][b] = c < nchunks ? ld_stream(wrow + c * 16) : make_uint4(0u, 0u, 0u, 0u);
+                }
+            }
+#pragma unroll
+            for (int b = 0; b < kBatch; ++b) {
+                const int64_t c = lane + 32 * (i0 + b);
+                if (c < nchunks) {
+#pragma unroll
+                    for (int mat = 0; mat < kMats; ++mat) {
+                        float w[8];
+                        Vec16<bf16>::unpack(wraw[mat][b], w);
+#pragma unroll
+                        for (int m = 0; m < kTileRows; ++m) {
+                            acc[mat][m] = dot_chunk(smem_x[m * nchunks + c], w, acc[mat][m]);
+                        }
+                    }
+                }
+            }
+        }
+#pragma unroll
+        for (int mat = 0; mat < kMats; ++mat) {
+#pragma unroll
+            for (int m = 0; m < kTileRows; ++m) {
+                acc[mat][m] = group_sum<32>(acc[mat][m]);
+            }
+        }
+#pragma unroll
+        for (int m = 0; m < kTileRows; ++m) {
+            if (lane == m && m < mt) {
+                const int64_t row = m0 + m;
+                if constexpr (kEpi == LinearEpilogue::kStore) {
+                    store_segment(p, row, n, acc[0][m], 0);
+                } else if constexpr (kEpi == LinearEpilogue::kResidual) {
+                    const float res = Vec16<bf16>::load1(p.residual, row * p.res_ld + n);
+                    Vec16<bf16>::store1(p.out[0], row * p.ld[0] + n, res + round_to_bf16(acc[0][m]));
+                } else {
+                    const float gate = round_to_bf16(acc[0][m]);
+                    const float up = round_to_bf16(acc[1][m]);
+                    Vec16<bf16>::store1(p.out[0], row * p.ld[0] + n, round_to_bf16(silu_pexp(gate)) * up);
+                }
+            }
+        }
+    }
+}
+
+__global__ void __launch_bounds__(kThreads) embedding_kernel(const bf16* table, int64_t vocab, int64_t hidden,
+                                                             const int64_t* tokens, int64_t count, bf16* out) {
+    grid_dependency_begin();
+    const int64_t chunks = hidden / 8;
+    for (int64_t i = static_cast<int64_t>(blockIdx.x) * kThreads + threadIdx.x; i < count * chunks;
+         i += static_cast<int64_t>(gridDim.x) * kThreads) {
+        const int64_t t = i / chunks;
+        const int64_t c = i - t * chunks;
+        const int64_t row = clamp_token(tokens[t], vocab);
+        st_v4(out + t * hidden + c * 8, ld_cached(table + row * hidden + c * 8));
+    }
+}
+
+template <LinearEpilogue kEpi, int kRows>
+int gemv_grid_for(const LinearParams& p) {
+    const int64_t groups = (p.N + kRows - 1) / kRows;
+    const int64_t want = (groups + kWarps - 1) / kWarps;
+    const int64_t cap = static_cast<int64_t>(runtime::sm_count()) * 2;
+    return static_cast<int>(want < cap ? want : cap);
+}
+
+// Rows per warp so that a lane keeps about kLoads 16-byte loads in flight.
+int rows_for(const LinearParams& p, int mats) {
+    const int64_t per_lane = (p.K / 8 + 31) / 32;
+    const int64_t rows = kLoads / (mats * (per_lane < 1 ? 1 : per_lane));
+    return rows >= 4 ? 4 : (rows >= 2 ? 2 : 1);
+}
+
+template <LinearEpilogue kEpi, int kRows>
+cudaError_t launch_gemv_rows(const LinearParams& p, cudaStream_t s) {
+    const std::size_t smem = static_cast<std::size_t>(p.K) * 2;
+    auto kernel = gemv_kernel<kEpi, kRows>;
+    if (smem > 48 * 1024) {
+        const cudaError_t err =
+            cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
+        if (err != cudaSuccess) {
+            return err;
+        }
+    }
+    return runtime::launch_smem(kernel, dim3(gemv_grid_for<kEpi, kRows>(p)), dim3(kThreads), smem, s, 1u, p);
+}
+
+template <LinearEpilogue kEpi>
+cudaError_t launch_gemv_epi(const LinearParams& p, cudaStream_t s) {
+    switch (rows_for(p, kEpi == LinearEpilogue::kSiluMul ? 2 : 1)) {
+    case 4:
+        return launch_gemv_rows<kEpi, 4>(p, s);
+    case 2:
+        return launch_gemv_rows<kEpi, 2>(p, s);
+    default:
+        return launch_gemv_rows<kEpi, 1>(p, s);
+    }
+}
+
+template <LinearEpilogue kEpi>
+cudaError_t launch_rows_epi(const LinearParams& p, cudaStream_t s) {
+    const std::size_t smem = static_cast<std::size_t>(kTileRows) * p.K * 2;
+    auto kernel = linear_rows_kernel<kEpi>;
+    if (smem > 48 * 1024) {
+        const cudaError_t err =
+            cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
+        if (err != cudaSuccess) {
+            return err;
+        }
+    }
+    const int64_t tiles = (p.M + kTileRows - 1) / kTileRows;
+    const int64_t want = (static_cast<int64_t>(runtime::sm_count()) * 4 + tiles - 1) / tiles;
+    const int64_t row_blocks = (p.N + kWarps - 1) / kWarps;
+    const int64_t gx = want < row_blocks ? want : row_blocks;
+    return runtime::launch_smem(kernel, dim3(static_cast<unsigned>(gx < 1 ? 1 : gx), static_cast<unsigned>(tiles)),
+                                dim3(kThreads), smem, s, 1u, p);
+}
+
+}  // namespace
+
+int gemv_grid(const LinearParams& p) {
+    switch (rows_for(p, 1)) {
+    case 4:
+        return gemv_grid_for<LinearEpilogue::kArgmax, 4>(p);
+    case 2:
+        return gemv_grid_for<LinearEpilogue::kArgmax, 2>(p);
+    default:
+        return gemv_grid_for<LinearEpilogue::kArgmax, 1>(p);
+    }
+}
+
+cudaError_t launch_gemv(const LinearParams& p, cudaStream_t s) {
+    switch (p.epilogue) {
+    case LinearEpilogue::kStore:
+        return launch_gemv_epi<LinearEpilogue::kStore>(p, s);
+    case LinearEpilogue::kResidual:
+        return launch_gemv_epi<LinearEpilogue::kResidual>(p, s);
+    case LinearEpilogue::kSiluMul:
+        return launch_gemv_epi<LinearEpilogue::kSiluMul>(p, s);
+    default:
+        return launch_gemv_epi<LinearEpilogue::kArgmax>(p, s);
+    }
+}
+
+cudaError_t launch_linear_rows(const LinearParams& p, cudaStream_t s) {
+    switch (p.epilogue) {
+    case LinearEpilogue::kStore:
+        return launch_rows_epi<LinearEpilogue::kStore>(p, s);
+    case LinearEpilogue::kResidual:
+        return launch_rows_epi<LinearEpilogue::kResidual>(p, s);
+    case LinearEpilogue::kSiluMul:
+        return launch_rows_epi<LinearEpilogue::kSiluMul>(p, s);
+    default:
+        return cudaErrorInvalidValue;
+    }
+}
+
+cudaError_t launch_embedding(const bf16* table, int64_t vocab, int64_t hidden, const int64_t* tokens, int64_t count,
+                             bf16* out, cudaStream_t s) {
+    const int64_t work = count * (hidden / 8);
+    const int64_t want = (work + kThreads - 1) / kThreads;
+    const int64_t cap = static_cast<int64_t>(runtime::sm_count()) * 4;
+    const int64_t blocks = want < cap ? want : cap;
+    return runtime::launch(embedding_kernel, dim3(static_cast<unsigned>(blocks < 1 ? 1 : blocks)), dim3(kThreads), s,
+                           1u, table, vocab, hidden, tokens, count, out);
+}
+
+}  // namespace cppinf::device
+
+using namespace cppinf::device;
+namespace rt = cppinf::runtime;
+
+namespace {
+
+constexpr int64_t kScratchHeader = 16;  // u32 counter, i32 position slot, padding; then one u64 per CTA
+
+int check_linear(const void* x, int64_t x_row_stride, const void* weight, const void* y, int64_t rows,
+                 int64_t in_features, int64_t out_features) {
+    CPPINF_REQUIRE(rows >= 0 && in_features > 0 && out_features >= 0, CPPINF_ERR_INVALID_ARGUMENT,
+                   "matmul requires non-negative dimensions and a non-empty inner dimension.");
+    CPPINF_REQUIRE(rows <= 1 || x_row_stride >= in_features, CPPINF_ERR_INVALID_ARGUMENT,
+                   "linear requires a row stride of at least in_features.");
+    CPPINF_REQUIRE(in_features % 8 == 0, CPPINF_ERR_UNSUPPORTED, "linear requires in_features to be a multiple of 8.");
+    CPPINF_REQUIRE(in_features <= (rows > 1 ? 6144 : 65536), CPPINF_ERR_UNSUPPORTED,
+                   "linear supports in_features up to 6144 (65536 for a single row).");
+    CPPINF_REQUIRE(out_features < (int64_t{1} << 31), CPPINF_ERR_OVERFLOW, "linear supports fewer than 2^31 outputs.");
+    if (rows == 0 || out_features == 0) {
+        return CPPINF_OK;
+    }
+    CPPINF_REQUIRE(x && weight && y, CPPINF_ERR_INVALID_ARGUMENT, "linear received a null pointer.");
+    CPPINF_REQUIRE(rt::aligned16(x) && rt::aligned16(weight) && (rows <= 1 || (x_row_stride * 2) % 16 == 0),
+                   CPPINF_ERR_UNSUPPORTED, "linear requires 16-byte aligned input rows and weights.");
+    return CPPINF_OK;
+}
+
+LinearParams linear_params(LinearEpilogue epi, const void* x, int64_t x_row_stride, const void* w0, const void* w1,
+                           void* y, int64_t rows, int64_t in_features, int64_t out_features) {
+    LinearParams p{};
+    p.epilogue = epi;
+    p.x = static_cast<const bf16*>(x);
+    p.x_stride = rows <= 1 ? in_features : x_row_stride;
+    p.w0 = static_cast<const bf16*>(w0);
+    p.w1 = static_cast<const bf16*>(w1);
+    p.M = rows;
+    p.N = out_features;
+    p.K = in_features;
+    p.out[0] = static_cast<bf16*>(y);
+    p.ld[0] = out_features;
+    p.seg[0] = 0;
+    p.seg[1] = p.seg[2] = p.seg[3] = out_features;
+    return p;
+}
+
+int run_linear(const LinearParams& p, void* stream, const char* name) {
+    const auto s = rt::as_stream(stream);
+    return rt::launched(p.M == 1 ? launch_gemv(p, s) : launch_linear_rows(p, s), name);
+}
+
+}  // namespace
+
+extern "C" {
+
+int cppinf_linear(const void* x, int64_t x_row_stride, const void* weight, void* y, int64_t rows, int64_t in_features,
+                  int64_t out_features, void* stream) {
+    const int st = check_linear(x, x_row_stride, weight, y, rows, in_features, out_features);
+    if (st != CPPINF_OK || rows == 0 || out_features == 0) {
+        return st == CPPINF_OK ? rt::ok() : st;
+    }
+    return run_linear(linear_params(LinearEpilogue::kStore, x, x_row_stride, weight, nullptr, y, rows, in_features,
+                                    out_features),
+                      stream, "linear");
+}
+
+int cppinf_linear_residual(const void* x, int64_t x_row_stride, const void* weight, const void* residual, void* y,
+                           int64_t rows, int64_t in_features, int64_t out_features, void* stream) {
+    const int st = check_linear(x, x_row_stride, weight, y, rows, in_features, out_features);
+    if (st != CPPINF_OK || rows == 0 || out_features == 0) {
+        return st == CPPINF_OK ? rt::ok() : st;
+    }
+    CPPINF_REQUIRE(residual, CPPINF_ERR_INVALID_ARGUMENT, "linear received a null pointer.");
+    LinearParams p = linear_params(LinearEpilogue::kResidual, x, x_row_stride, weight, nullptr, y, rows, in_features,
+                                   out_features);
+    p.residual = static_cast<const bf16*>(residual);
+    p.res_ld = out_features;
+    return run_linear(p, stream, "linear_residual");
+}
+
+int cppinf_linear_silu_mul(const void* x, int64_t x_row_stride, const void* gate, const void* up, void* y, int64_t rows,
+                           int64_t in_features, int64_t out_features, void* stream) {
+    const int st = check_linear(x, x_row_stride, gate, y, rows, in_features, out_features);
+    if (st != CPPINF_OK || rows == 0 || out_features == 0) {
+        return st == CPPINF_OK ? rt::ok() : st;
+    }
+    CPPINF_REQUIRE(up, CPPINF_ERR_INVALID_ARGUMENT, "linear received a null pointer.");
+    CPPINF_REQUIRE(rt::aligned16(up), CPPINF_ERR_UNSUPPORTED, "linear requires 16-byte aligned input rows and weights.");
+    return run_linear(linear_params(LinearEpilogue::kSiluMul, x, x_row_stride, gate, up, y, rows, in_features,
+                                    out_features),
+                      stream, "linear_silu_mul");
+}
+
+int64_t cppinf_linear_argmax_scratch_bytes(int64_t out_features, int64_t in_features) {
+    if (out_features <= 0 || in_features <= 0) {
+        return kScratchHeader;
+    }
+    LinearParams p{};
+    p.N = out_features;
+    p.K = in_features;
+    return kScratchHeader + 8 * static_cast<int64_t>(gemv_grid(p));
+}
+
+int cppinf_linear_argmax(const void* x, const void* weight, void* logits, int64_t in_features, int64_t out_features,
+                         int64_t* out_token, void* scratch, void* stream) {
+    CPPINF_REQUIRE(out_features > 0, CPPINF_ERR_INVALID_ARGUMENT, "logits vocab size must be non-zero.");
+    const int st = check_linear(x, in_features, weight, out_token, 1, in_features, out_features);
+    if (st != CPPINF_OK) {
+        return st;
+    }
+    CPPINF_REQUIRE(scratch, CPPINF_ERR_INVALID_ARGUMENT, "linear_argmax received a null scratch pointer.");
+    CPPINF_REQUIRE(rt::aligned16(scratch), CPPINF_ERR_UNSUPPORTED, "linear_argmax requires a 16-byte aligned scratch.");
+    LinearParams p = linear_params(LinearEpilogue::kArgmax, x, in_features, weight, nullptr, logits, 1, in_features,
+                                   out_features);
+    char* base = static_cast<char*>(scratch);
+    p.counter = reinterpret_cast<unsigned int*>(base);
+    p.position_out = reinterpret_cast<int*>(base + 4);
+    p.partial = reinterpret_cast<unsigned long long*>(base + kScratchHeader);
+    p.tokens_out = out_token;
+    p.advance = 0;
+    return run_linear(p, stream, "linear_argmax");
+}
+
+int cppinf_embedding(const void* table, int64_t vocab, int64_t hidden, const int64_t* token_ids, int64_t count,
+                     void* out, void* stream) {
+    CPPINF_REQUIRE(vocab > 0 && hidden > 0 && count >= 0, CPPINF_ERR_INVALID_ARGUMENT,
+                   "embedding_lookup requires a non-empty rank-2 embedding table.");
+    CPPINF_REQUIRE(hidden % 8 == 0, CPPINF_ERR_UNSUPPORTED, "embedding requires hidden to be a multiple of 8.");
+    if (count == 0) {
+        return rt::ok();
+    }
+    CPPINF_REQUIRE(table && token_ids && out, CPPINF_ERR_INVALID_ARGUMENT, "embedding received a null pointer.");
+    CPPINF_REQUIRE(rt::aligned16(table) && rt::aligned16(out), CPPINF_ERR_UNSUPPORTED,
+                   "embedding requires 16-byte aligned rows.");
+    return rt::launched(launch_embedding(static_cast<const bf16*>(table), vocab, hidden, token_ids, count,
+                                         static_cast<bf16*>(out), rt::as_stream(stream)),
+                        "embedding");
+}
+
+}  // extern "C"

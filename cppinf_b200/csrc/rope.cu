@@ -25,6 +25,7 @@
 #include <vector>
 
 #include "common.cuh"
+#include "decoder.h"
 #include "runtime.h"
 
 namespace cppinf::device {
@@ -48,6 +49,10 @@ struct QkParams {
     int k_heads;
     int units_per_token;
     float eps;
+    // Decode steps: when set, *position is added to the RoPE position and to the k_out row (k_out is then the KV
+    // cache base), and tokens at or past table_positions are skipped.
+    const int* position;
+    int64_t table_positions;
 };
 
 template <typename T, int kLanes, int kIters>
@@ -72,6 +77,10 @@ __global__ void __launch_bounds__(kQkThreads) qk_norm_rope_kernel(QkParams p) {
     }
     const int64_t t = unit / p.units_per_token;
     const int h0 = static_cast<int>(unit - t * p.units_per_token) * kHeadsPerUnit;
+    const int64_t shift = p.position != nullptr ? static_cast<int64_t>(*p.position) : 0;
+    if (p.position != nullptr && p.position_offset + shift + t >= p.table_positions) {
+        return;
+    }
 
     // All loads of the unit first: kIters x 2 vectors per lane in flight.
     uint4 first_raw[kIters];
@@ -89,7 +98,7 @@ __global__ void __launch_bounds__(kQkThreads) qk_norm_rope_kernel(QkParams p) {
     }
 
     // cos / sin of pairs hl*kVec .. hl*kVec + kVec - 1 at this token's position.
-    const float* row = p.table + (p.position_offset + t) * kDim + hl * kVec;
+    const float* row = p.table + (p.position_offset + shift + t) * kDim + hl * kVec;
     float c[kVec];
     float s[kVec];
 #pragma unroll
@@ -158,7 +167,8 @@ __global__ void __launch_bounds__(kQkThreads) qk_norm_rope_kernel(QkParams p) {
                 out_b[j] = n2 * c[j] + n1 * s[j];  // second * cos + first  * sin  (src/nn/rope.cpp:117-118)
             }
             char* dst = h < p.q_heads ? static_cast<char*>(p.q_out) + (t * p.q_heads + h) * kHeadBytes
-                                      : static_cast<char*>(p.k_out) + (t * p.k_heads + (h - p.q_heads)) * kHeadBytes;
+                                      : static_cast<char*>(p.k_out) +
+                                            ((shift + t) * p.k_heads + (h - p.q_heads)) * kHeadBytes;
             st_stream(dst + hl * 16, V::pack(out_a));
             st_stream(dst + kHalfBytes + hl * 16, V::pack(out_b));
         }
@@ -239,6 +249,20 @@ cudaError_t dispatch_qk(const QkParams& p, int lanes, cudaStream_t s) {
 }
 
 }  // namespace
+
+cudaError_t launch_qk_norm_rope_at(const bf16* q, const bf16* k, const bf16* q_weight, const bf16* k_weight,
+                                   bf16* q_out, bf16* k_cache, int64_t tokens, int q_heads, int k_heads,
+                                   int head_dim, const int* position, float eps, const float* table,
+                                   int64_t table_positions, cudaStream_t s) {
+    const int lanes = head_dim / 16;
+    if (head_dim % 16 != 0 || lanes < 1 || lanes > 16 || (lanes & (lanes - 1)) != 0) {
+        return cudaErrorInvalidValue;
+    }
+    QkParams p{q, k, q_weight, k_weight, q_out, k_cache, table, tokens, 0, q_heads, k_heads, 0, eps, position,
+               table_positions};
+    return dispatch_qk<bf16>(p, lanes, s);
+}
+
 }  // namespace cppinf::device
 
 using namespace cppinf::device;
@@ -339,7 +363,7 @@ int cppinf_qk_norm_rope(cppinf_dtype dtype, const void* q, const void* k, const 
     const void* qw = q_heads == 0 ? k_weight : q_weight;
     const void* kw = k_heads == 0 ? q_weight : k_weight;
     QkParams p{q, k, qw, kw, q_out, k_out, table, tokens, position_offset, static_cast<int>(q_heads),
-               static_cast<int>(k_heads), 0, eps};
+               static_cast<int>(k_heads), 0, eps, nullptr, table_positions};
     const auto s = rt::as_stream(stream);
     const cudaError_t launch_err = dtype == CPPINF_DTYPE_BF16 ? dispatch_qk<bf16>(p, static_cast<int>(lanes), s)
                                                               : dispatch_qk<float>(p, static_cast<int>(lanes), s);

@@ -70,6 +70,10 @@ int after_launch(const char* kernel_name) {
     return ok();
 }
 
+void count_launches(int64_t n) {
+    g_launches.fetch_add(static_cast<uint64_t>(n), std::memory_order_relaxed);
+}
+
 int launched(cudaError_t err, const char* kernel_name) {
     if (err != cudaSuccess) {
         cudaGetLastError();  // clear the launch error so it does not leak into later calls

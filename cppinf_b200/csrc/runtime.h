@@ -51,18 +51,18 @@ inline bool valid_dtype(cppinf_dtype dtype) {
     return dtype == CPPINF_DTYPE_BF16 || dtype == CPPINF_DTYPE_F32;
 }
 
-// Launches `kernel` with programmatic dependent launch allowed: the grid may be scheduled while the previous kernel
-// in the stream is still finishing. Every kernel of this library executes griddepcontrol.wait before it reads global
-// memory, which waits for the previous grid to complete and its writes to become visible, so results are the same
-// as with plain stream order; only launch latency and the previous grid's tail overlap. `cluster_x` > 1 adds a
-// thread-block cluster dimension.
+// Launches `kernel` with `smem_bytes` of dynamic shared memory and programmatic dependent launch allowed: the grid
+// may be scheduled while the previous kernel in the stream is still finishing. Every kernel of this library executes
+// griddepcontrol.wait before it reads memory another kernel writes, which waits for the previous grid to complete
+// and its writes to become visible, so results are the same as with plain stream order; only launch latency and the
+// previous grid's tail overlap. `cluster_x` > 1 adds a thread-block cluster dimension.
 template <typename... KernelArgs, typename... Args>
-cudaError_t launch(void (*kernel)(KernelArgs...), dim3 grid, dim3 block, cudaStream_t stream, unsigned cluster_x,
-                   Args&&... args) {
+cudaError_t launch_smem(void (*kernel)(KernelArgs...), dim3 grid, dim3 block, std::size_t smem_bytes,
+                        cudaStream_t stream, unsigned cluster_x, Args&&... args) {
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = grid;
     cfg.blockDim = block;
-    cfg.dynamicSmemBytes = 0;
+    cfg.dynamicSmemBytes = smem_bytes;
     cfg.stream = stream;
     cudaLaunchAttribute attrs[2];
     attrs[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
@@ -79,6 +79,16 @@ cudaError_t launch(void (*kernel)(KernelArgs...), dim3 grid, dim3 block, cudaStr
     cfg.numAttrs = n;
     return cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
 }
+
+template <typename... KernelArgs, typename... Args>
+cudaError_t launch(void (*kernel)(KernelArgs...), dim3 grid, dim3 block, cudaStream_t stream, unsigned cluster_x,
+                   Args&&... args) {
+    return launch_smem(kernel, grid, block, 0, stream, cluster_x, std::forward<Args>(args)...);
+}
+
+// Adds `n` (possibly negative) to the launch count: replays of a captured graph, or captured launches that only
+// execute when the graph is replayed.
+void count_launches(int64_t n);
 
 // Records a failed launch (or checks the one just enqueued) and counts it.
 int launched(cudaError_t err, const char* kernel_name);

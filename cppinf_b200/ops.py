@@ -322,3 +322,99 @@ def qk_norm_rope(q: torch.Tensor, k: torch.Tensor, q_weight: torch.Tensor, k_wei
               q_out.data_ptr(), k_out.data_ptr(), tokens, hq, hk, d, position_offset, float(epsilon),
               table.data_ptr(), table.shape[0], _stream())
     return q_out, k_out
+
+
+# ---- decoder: projections and attention ---------------------------------------------------------------------------
+
+
+def _validate_linear(input: torch.Tensor, weight: torch.Tensor, op: str) -> tuple[torch.Tensor, int, int, int]:
+    # validate_projection_weight, src/nn/qwen_common.cpp:39-49, and matmul's dtype rules, src/ops/matmul.cpp:28-45
+    if input.dtype != torch.bfloat16 or weight.dtype != torch.bfloat16:
+        raise ValueError(f"{op} requires bf16 input and weight.")
+    if weight.dim() != 2:
+        raise ValueError(f"{op} weight must be rank-2.")
+    if input.dim() < 1 or input.shape[-1] != weight.shape[1]:
+        raise ValueError("matmul inner dimensions must match.")
+    _require_cuda(input, weight)
+    x = materialize(input).reshape(-1, input.shape[-1])
+    return x, x.shape[0], weight.shape[1], weight.shape[0]
+
+
+def linear(input: torch.Tensor, weight: torch.Tensor) -> torch.Tensor:
+    """nn::detail::linear_project, src/nn/qwen_common.cpp:15-37: input [..., in] times weight [out, in]^T, bf16."""
+    x, rows, fin, fout = _validate_linear(input, weight, "linear")
+    out = torch.empty(*input.shape[:-1], fout, dtype=torch.bfloat16, device=input.device)
+    capi.call("cppinf_linear", x.data_ptr(), fin, materialize(weight).data_ptr(), out.data_ptr(), rows, fin, fout,
+              _stream())
+    return out
+
+
+def linear_residual(input: torch.Tensor, weight: torch.Tensor, residual: torch.Tensor,
+                    out: torch.Tensor | None = None) -> torch.Tensor:
+    """residual + linear(input, weight) (src/nn/qwen_decoder_block.cpp:80-89); `out` may be `residual`."""
+    x, rows, fin, fout = _validate_linear(input, weight, "linear_residual")
+    if residual.dtype != torch.bfloat16 or residual.shape != (*input.shape[:-1], fout):
+        raise ValueError("add requires matching tensor shapes.")
+    residual = materialize(residual)
+    out = torch.empty_like(residual) if out is None else out
+    capi.call("cppinf_linear_residual", x.data_ptr(), fin, materialize(weight).data_ptr(), residual.data_ptr(),
+              out.data_ptr(), rows, fin, fout, _stream())
+    return out
+
+
+def linear_silu_mul(input: torch.Tensor, gate_weight: torch.Tensor, up_weight: torch.Tensor) -> torch.Tensor:
+    """silu(linear(input, gate)) * linear(input, up), the MLP front of src/nn/qwen_mlp.cpp:58-66."""
+    x, rows, fin, fout = _validate_linear(input, gate_weight, "linear_silu_mul")
+    if up_weight.shape != gate_weight.shape or up_weight.dtype != torch.bfloat16:
+        raise ValueError("qwen_mlp up_proj_weight has an unexpected shape.")
+    out = torch.empty(*input.shape[:-1], fout, dtype=torch.bfloat16, device=input.device)
+    capi.call("cppinf_linear_silu_mul", x.data_ptr(), fin, materialize(gate_weight).data_ptr(),
+              materialize(up_weight).data_ptr(), out.data_ptr(), rows, fin, fout, _stream())
+    return out
+
+
+def linear_argmax(input: torch.Tensor, weight: torch.Tensor, with_logits: bool = False):
+    """Greedy token of one row's logits input @ weight^T, computed without materialising the logits unless asked
+    (the LM head of src/models/qwen3/qwen3_model.cpp:306-311 and src/cli/cli_app.cpp:72-94). Returns an int64
+    device tensor [1] (and the bf16 logits [out] when with_logits)."""
+    x, rows, fin, fout = _validate_linear(input, weight, "linear_argmax")
+    if rows != 1:
+        raise ValueError("linear_argmax takes a single row.")
+    nbytes = int(capi.load().cppinf_linear_argmax_scratch_bytes(fout, fin))
+    scratch = torch.zeros(nbytes, dtype=torch.uint8, device=input.device)
+    token = torch.empty(1, dtype=torch.int64, device=input.device)
+    logits = torch.empty(fout, dtype=torch.bfloat16, device=input.device) if with_logits else None
+    capi.call("cppinf_linear_argmax", x.data_ptr(), materialize(weight).data_ptr(),
+              logits.data_ptr() if logits is not None else None, fin, fout, token.data_ptr(), scratch.data_ptr(),
+              _stream())
+    return (token, logits) if with_logits else token
+
+
+def decoder_attention(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tensor, position: int) -> torch.Tensor:
+    """Causal GQA attention of one sequence (src/nn/qwen_attention.cpp:236-333): q [T, Hq, D] at positions
+    position .. position + T - 1, caches [capacity, Hkv, D]; returns the bf16 context [T, Hq, D]."""
+    if q.dim() != 3 or k_cache.dim() != 3 or v_cache.shape != k_cache.shape:
+        raise ValueError("qwen_attention requires rank-4 query, key, and value tensors.")
+    if q.dtype != torch.bfloat16 or k_cache.dtype != torch.bfloat16 or v_cache.dtype != torch.bfloat16:
+        raise ValueError("qwen_attention requires matching tensor dtypes.")
+    if q.shape[2] != k_cache.shape[2]:
+        raise ValueError("qwen_attention requires matching query/key/value head sizes.")
+    _require_cuda(q, k_cache, v_cache)
+    q, k_cache, v_cache = materialize(q), materialize(k_cache), materialize(v_cache)
+    ctx = torch.empty_like(q)
+    capi.call("cppinf_decoder_attention", q.data_ptr(), k_cache.data_ptr(), v_cache.data_ptr(), ctx.data_ptr(),
+              q.shape[0], q.shape[1], k_cache.shape[1], q.shape[2], int(position), k_cache.shape[0], _stream())
+    return ctx
+
+
+def embedding(table: torch.Tensor, token_ids: torch.Tensor) -> torch.Tensor:
+    """Embedding lookup, src/models/qwen3/qwen3_model.cpp:132-165 (ids must be in range; they are checked here)."""
+    if table.dim() != 2:
+        raise ValueError("embedding_lookup requires a rank-2 embedding table.")
+    ids = token_ids.to(device=table.device, dtype=torch.int64).contiguous()
+    if ids.numel() and (int(ids.min()) < 0 or int(ids.max()) >= table.shape[0]):
+        raise IndexError("Qwen3Model token id is out of vocabulary range.")
+    out = torch.empty(ids.numel(), table.shape[1], dtype=table.dtype, device=table.device)
+    capi.call("cppinf_embedding", materialize(table).data_ptr(), table.shape[0], table.shape[1], ids.data_ptr(),
+              ids.numel(), out.data_ptr(), _stream())
+    return out.reshape(*token_ids.shape, table.shape[1])

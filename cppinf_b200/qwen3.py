@@ -1,0 +1,213 @@
+"""Qwen3 decoder on the device: configuration, seeded random weights and the model object.
+
+Mirrors the reference's model interface (src/models/qwen3/qwen3_model.h): ``Qwen3Model.forward(token_ids)`` returns
+bf16 logits [T, vocab]; ``make_cache(max_sequence_length)`` / ``forward_cached(token_ids, cache)`` run the cached
+path; ``generate`` is the greedy loop of src/cli/cli_app.cpp (temperature 0: argmax of the last logits row).
+The model itself lives in libcppinf_b200.so (cppinf_qwen3_* in include/cppinf_b200.h): weights, KV cache and
+activations stay in HBM, and one decode step is a captured CUDA graph whose kernels read the position and the
+previous token from device memory.
+"""
+
+from __future__ import annotations
+
+import dataclasses
+from dataclasses import dataclass
+
+import numpy as np
+
+
+@dataclass(frozen=True)
+class Qwen3Config:
+    """The fields of the reference's HfConfig that the decoder uses (src/loaders/hf/hf_config.h)."""
+
+    vocab_size: int
+    hidden_size: int
+    intermediate_size: int
+    num_hidden_layers: int
+    num_attention_heads: int
+    num_key_value_heads: int
+    head_dim: int
+    rms_norm_eps: float = 1e-6
+    rope_theta: float = 1_000_000.0
+
+    @staticmethod
+    def qwen3_0_6b() -> "Qwen3Config":
+        """Qwen3-0.6B: 28 layers, hidden 1024, 16 query / 8 key-value heads of 128, MLP 3072, vocab 151936."""
+        return Qwen3Config(vocab_size=151936, hidden_size=1024, intermediate_size=3072, num_hidden_layers=28,
+                           num_attention_heads=16, num_key_value_heads=8, head_dim=128)
+
+    def replace(self, **kw) -> "Qwen3Config":
+        return dataclasses.replace(self, **kw)
+
+    def weight_shapes(self) -> dict[str, tuple[int, ...]]:
+        """Tensor names and shapes of a tied-embedding checkpoint (Hugging Face naming, as the reference loads)."""
+        h, d = self.hidden_size, self.head_dim
+        shapes: dict[str, tuple[int, ...]] = {"model.embed_tokens.weight": (self.vocab_size, h)}
+        for i in range(self.num_hidden_layers):
+            p = f"model.layers.{i}."
+            shapes.update({
+                p + "input_layernorm.weight": (h,),
+                p + "self_attn.q_proj.weight": (self.num_attention_heads * d, h),
+                p + "self_attn.k_proj.weight": (self.num_key_value_heads * d, h),
+                p + "self_attn.v_proj.weight": (self.num_key_value_heads * d, h),
+                p + "self_attn.q_norm.weight": (d,),
+                p + "self_attn.k_norm.weight": (d,),
+                p + "self_attn.o_proj.weight": (h, self.num_attention_heads * d),
+                p + "post_attention_layernorm.weight": (h,),
+                p + "mlp.gate_proj.weight": (self.intermediate_size, h),
+                p + "mlp.up_proj.weight": (self.intermediate_size, h),
+                p + "mlp.down_proj.weight": (h, self.intermediate_size),
+            })
+        shapes["model.norm.weight"] = (h,)
+        return shapes
+
+    def parameter_count(self) -> int:
+        return sum(int(np.prod(s)) for s in self.weight_shapes().values())
+
+
+def f32_to_bf16_bits(x: np.ndarray) -> np.ndarray:
+    """Round-to-nearest-even f32 -> bf16 bit patterns (uint16)."""
+    bits = np.ascontiguousarray(x, dtype=np.float32).view(np.uint32)
+    rounded = bits + (np.uint32(0x7FFF) + ((bits >> np.uint32(16)) & np.uint32(1)))
+    return (rounded >> np.uint32(16)).astype(np.uint16)
+
+
+def random_weights(config: Qwen3Config, seed: int = 0, std: float = 0.02) -> dict[str, np.ndarray]:
+    """Seeded random initialisation: matrices ~N(0, std) rounded to bf16, norm weights 1.0 (bf16 0x3f80).
+
+    Tensor i draws from numpy's PCG64 seeded with (seed, i), so the arrays do not depend on generation order."""
+    out: dict[str, np.ndarray] = {}
+    for i, (name, shape) in enumerate(config.weight_shapes().items()):
+        if len(shape) == 1:
+            out[name] = np.full(shape, 0x3F80, dtype=np.uint16)
+            continue
+        rng = np.random.Generator(np.random.PCG64([seed, i]))
+        out[name] = f32_to_bf16_bits(rng.standard_normal(shape, dtype=np.float32) * np.float32(std))
+    return out
+
+
+class Qwen3Model:
+    """Device-resident Qwen3 with one cached sequence (libcppinf_b200.so, cppinf_qwen3_*).
+
+    ``forward(token_ids)`` returns the bf16 logits [T, vocab] of a fresh sequence (Qwen3Model::forward,
+    src/models/qwen3/qwen3_model.cpp:202-206); ``forward_cached(token_ids)`` appends to the cached sequence
+    (:269-273); ``generate(prompt, steps)`` is greedy decoding (src/cli/cli_app.cpp, temperature 0).
+    """
+
+    def __init__(self, config: Qwen3Config, max_sequence_length: int, weights: dict | None = None,
+                 device: int | None = None):
+        import ctypes
+
+        import torch
+
+        from . import capi
+
+        self.config = config
+        self.capacity = int(max_sequence_length)
+        self.device = torch.device("cuda", torch.cuda.current_device() if device is None else device)
+        self._capi = capi
+        lib = capi.load()
+        cfg = capi.Qwen3ConfigC(config.vocab_size, config.hidden_size, config.intermediate_size,
+                                config.num_hidden_layers, config.num_attention_heads, config.num_key_value_heads,
+                                config.head_dim, config.rms_norm_eps, config.rope_theta)
+        handle = ctypes.c_void_p()
+        with torch.cuda.device(self.device):
+            capi.check(lib.cppinf_qwen3_create(ctypes.byref(cfg), self.capacity, ctypes.byref(handle)),
+                       "cppinf_qwen3_create")
+        self._handle = handle
+        if weights is not None:
+            self.load_weights(weights)
+
+    def close(self) -> None:
+        if getattr(self, "_handle", None) is not None and self._handle.value:
+            self._capi.load().cppinf_qwen3_destroy(self._handle)
+            self._handle = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    def load_weights(self, weights: dict) -> None:
+        """Copies checkpoint tensors (numpy uint16 bf16 bits, or torch bf16 tensors on host or device)."""
+        import torch
+
+        shapes = self.config.weight_shapes()
+        missing = sorted(set(shapes) - set(weights))
+        if missing:
+            raise ValueError(f"Qwen3Model is missing tensor '{missing[0]}'.")
+        with torch.cuda.device(self.device):
+            for name, value in weights.items():
+                if isinstance(value, np.ndarray):
+                    arr = np.ascontiguousarray(value)
+                    if arr.dtype != np.uint16 or arr.shape != shapes.get(name, arr.shape):
+                        raise ValueError(f"Qwen3Model tensor '{name}' has an unexpected shape or dtype.")
+                    self._capi.call("cppinf_qwen3_set_weight", self._handle, name.encode(), arr.ctypes.data,
+                                    arr.nbytes, 0)
+                else:
+                    t = value.contiguous()
+                    if t.dtype != torch.bfloat16:
+                        raise ValueError(f"Qwen3Model tensor '{name}' must be bf16.")
+                    self._capi.call("cppinf_qwen3_set_weight", self._handle, name.encode(), t.data_ptr(),
+                                    t.numel() * 2, 1 if t.is_cuda else 0)
+            torch.cuda.synchronize(self.device)
+
+    @property
+    def length(self) -> int:
+        return int(self._capi.load().cppinf_qwen3_length(self._handle))
+
+    @property
+    def step_launches(self) -> int:
+        return int(self._capi.load().cppinf_qwen3_step_launches(self._handle))
+
+    def reset(self) -> None:
+        import torch
+
+        with torch.cuda.device(self.device):
+            self._capi.call("cppinf_qwen3_reset", self._handle, torch.cuda.current_stream().cuda_stream)
+
+    def forward_cached(self, token_ids, logits: str | None = "last"):
+        """Appends token_ids; returns (next greedy token, logits) with logits None, the last row [1, vocab] or all
+        rows [T, vocab] (bf16 device tensor) for logits=None / "last" / "all"."""
+        import ctypes
+
+        import torch
+
+        ids = [int(t) for t in token_ids]
+        arr = self._capi.i64_array(ids)
+        nxt = ctypes.c_int64(0)
+        out = None
+        with torch.cuda.device(self.device):
+            if logits == "all":
+                out = torch.empty(len(ids), self.config.vocab_size, dtype=torch.bfloat16, device=self.device)
+            elif logits == "last":
+                out = torch.empty(1, self.config.vocab_size, dtype=torch.bfloat16, device=self.device)
+            self._capi.call("cppinf_qwen3_forward", self._handle, arr, len(ids),
+                            out.data_ptr() if out is not None else None, 1 if logits == "all" else 0,
+                            ctypes.byref(nxt), torch.cuda.current_stream().cuda_stream)
+        return int(nxt.value), out
+
+    def forward(self, token_ids):
+        """Qwen3Model::forward: logits [T, vocab] of `token_ids` as a fresh sequence."""
+        self.reset()
+        return self.forward_cached(token_ids, logits="all")[1]
+
+    def decode(self, steps: int) -> list[int]:
+        """`steps` greedy decode steps from the cached state (one captured CUDA graph per step)."""
+        import torch
+
+        if steps <= 0:
+            return []
+        buf = self._capi.i64_array([0] * steps)
+        with torch.cuda.device(self.device):
+            self._capi.call("cppinf_qwen3_decode", self._handle, int(steps), buf,
+                            torch.cuda.current_stream().cuda_stream)
+        return [int(buf[i]) for i in range(steps)]
+
+    def generate(self, prompt, steps: int) -> list[int]:
+        """Greedy generation: prefill `prompt` as a fresh sequence, then `steps` tokens in total (the first from the
+        prompt's last logits row, the rest from decode steps)."""
+        self.reset()
+        first, _ = self.forward_cached(prompt, logits=None)
+        return [first] + self.decode(steps - 1)

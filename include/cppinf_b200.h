@@ -10,7 +10,8 @@
  *    returns without synchronising, so results are ready once the stream has reached that point.
  *  - Every call returns CPPINF_OK (0) or a negative cppinf_status. On failure cppinf_last_error() returns the
  *    message for the calling thread. The messages reuse the reference's validation texts where one exists.
- *  - No entry point allocates device memory and none falls back to the CPU.
+ *  - No entry point allocates device memory (except cppinf_qwen3_create, which allocates a model's weights, cache
+ *    and workspace once) and none falls back to the CPU.
  *  - Results are written to dense (contiguous) outputs. Outputs must not alias inputs unless the entry point says so.
  */
 #ifndef CPPINF_B200_H
@@ -158,6 +159,114 @@ CPPINF_API int cppinf_qk_norm_rope(cppinf_dtype dtype, const void* q, const void
                         const void* k_weight, void* q_out, void* k_out, int64_t tokens, int64_t q_heads,
                         int64_t k_heads, int64_t head_dim, int64_t position_offset, float eps, const float* table,
                         int64_t table_positions, void* stream);
+
+/* ---------------------------------------------------------------------------------------------------------------
+ * Qwen3 decoder (bf16). Linear projections, attention and the model runtime on the device.
+ *
+ * Accumulation orders are fixed so that a CPU restatement reproduces every bit, and with it every greedy token:
+ *  - linear: each output is a dot product whose in_features are cut into 16-byte chunks of 8; lane l (0..31) adds
+ *    the products of chunks l, l+32, ... in element order starting from +0; the 32 partials are combined by a
+ *    butterfly over lane distances 16..1; the sum is rounded to bf16 once. in_features must be a multiple of 8.
+ *  - exp (softmax, SiLU): Cody-Waite reduction with a 12-bit ln2 head, degree-7 Taylor polynomial, exponent-field
+ *    scaling, each step one IEEE f32 operation.
+ *  - attention: see cppinf_decoder_attention.
+ * The reference computes the same quantities through oneDNN, whose order is unspecified; these results agree with
+ * it within a bf16 ulp per op, not bit for bit.
+ * ------------------------------------------------------------------------------------------------------------- */
+
+/* y[rows, out] = bf16(x[rows, in] * weight[out, in]^T): nn::detail::linear_project (src/nn/qwen_common.cpp:15-37)
+ * over ops::matmul with bf16 operands and result (src/ops/matmul.cpp:85-114). Row r of x starts at r * x_row_stride;
+ * y is dense. x, weight and x_row_stride * 2 bytes must be 16-byte aligned. */
+CPPINF_API int cppinf_linear(const void* x, int64_t x_row_stride, const void* weight, void* y, int64_t rows,
+                             int64_t in_features, int64_t out_features, void* stream);
+
+/* y = bf16(residual + bf16(x * weight^T)): a projection followed by the residual ops::add of
+ * src/nn/qwen_decoder_block.cpp:80-89. residual and y are dense [rows, out]; y may alias residual. */
+CPPINF_API int cppinf_linear_residual(const void* x, int64_t x_row_stride, const void* weight, const void* residual,
+                                      void* y, int64_t rows, int64_t in_features, int64_t out_features, void* stream);
+
+/* y = bf16(bf16(silu(bf16(x * gate^T))) * bf16(x * up^T)): the gated MLP front of src/nn/qwen_mlp.cpp:58-66
+ * (gate_proj, up_proj, ops::silu, ops::mul), fused. gate and up are [out, in]. */
+CPPINF_API int cppinf_linear_silu_mul(const void* x, int64_t x_row_stride, const void* gate, const void* up, void* y,
+                                      int64_t rows, int64_t in_features, int64_t out_features, void* stream);
+
+/* Greedy token of one logits row computed on the fly: out_token (DEVICE int64) = argmax over n of
+ * bf16(x * weight[n]^T), the LM head of src/models/qwen3/qwen3_model.cpp:306-311 followed by
+ * cli::detail::select_argmax_token_id (src/cli/cli_app.cpp:72-94: first maximum, NaN never selected unless at
+ * index 0). x is one row [in]; if logits is non-NULL the bf16 logits [out] are stored too. Needs a DEVICE
+ * scratch of cppinf_linear_argmax_scratch_bytes(out, in) bytes, 16-byte aligned, whose first 16 bytes are zero
+ * before the first call (each call leaves them zero again); calls sharing a scratch must not overlap. */
+CPPINF_API int cppinf_linear_argmax(const void* x, const void* weight, void* logits, int64_t in_features,
+                                    int64_t out_features, int64_t* out_token, void* scratch, void* stream);
+CPPINF_API int64_t cppinf_linear_argmax_scratch_bytes(int64_t out_features, int64_t in_features);
+
+/* Causal grouped-query attention of one sequence over its KV cache: fused_causal_attention of
+ * src/nn/qwen_attention.cpp:236-333 with the position-causal softmax of :164-235. q [tokens, q_heads, head_dim]
+ * (after q-norm and RoPE), k_cache/v_cache [capacity, kv_heads, head_dim], ctx [tokens, q_heads, head_dim], all
+ * bf16. Query t sits at position `position` + t and sees keys 0 .. position + t; query head h reads kv head
+ * h / (q_heads / kv_heads). Scores in f32, probabilities rounded to bf16, context rounded to bf16.
+ * Order: per (query, head) the visible keys are split into 8 parts of ceil(L/8); score dot products in 8 segments
+ * of head_dim/8 dims combined by a butterfly; parts, warps and slots summed in the fixed order of
+ * oracle_decoder_attention. head_dim 64, 128 or 256; position + tokens <= capacity. */
+CPPINF_API int cppinf_decoder_attention(const void* q, const void* k_cache, const void* v_cache, void* ctx,
+                                        int64_t tokens, int64_t q_heads, int64_t kv_heads, int64_t head_dim,
+                                        int64_t position, int64_t capacity, void* stream);
+
+/* Embedding lookup (src/models/qwen3/qwen3_model.cpp:132-165): out[t] = table[token_ids[t]], table [vocab, hidden]
+ * bf16, token_ids a DEVICE int64 array. Ids are validated on the host by the model; here they are clamped into
+ * range. hidden must be a multiple of 8. */
+CPPINF_API int cppinf_embedding(const void* table, int64_t vocab, int64_t hidden, const int64_t* token_ids,
+                                int64_t count, void* out, void* stream);
+
+/* The Qwen3 model (src/models/qwen3/qwen3_model.h): tied embeddings, bf16 weights, one cached sequence. */
+typedef struct cppinf_qwen3_config {
+    int64_t vocab_size;
+    int64_t hidden_size;
+    int64_t intermediate_size;
+    int64_t num_hidden_layers;
+    int64_t num_attention_heads;
+    int64_t num_key_value_heads;
+    int64_t head_dim;
+    float rms_norm_eps;
+    float rope_theta;
+} cppinf_qwen3_config;
+
+typedef struct cppinf_qwen3 cppinf_qwen3;
+
+/* Creates a model on the current device with room for `max_sequence_length` cached tokens (make_cache,
+ * qwen3_model.cpp:222-245). Weights start zeroed; load them with cppinf_qwen3_set_weight. Validation follows
+ * validate_model_config (qwen3_model.cpp:44-61): hidden and intermediate sizes multiples of 8, head_dim 64/128/256,
+ * query heads a multiple of key-value heads. */
+CPPINF_API int cppinf_qwen3_create(const cppinf_qwen3_config* config, int64_t max_sequence_length,
+                                   cppinf_qwen3** model);
+CPPINF_API void cppinf_qwen3_destroy(cppinf_qwen3* model);
+
+/* Copies one checkpoint tensor (Hugging Face name, e.g. "model.layers.3.mlp.up_proj.weight", bf16, exactly the
+ * tensor's bytes) from `data` (HOST memory when on_device == 0, DEVICE memory otherwise) into the model. */
+CPPINF_API int cppinf_qwen3_set_weight(cppinf_qwen3* model, const char* name, const void* data, int64_t bytes,
+                                       int on_device);
+
+/* Qwen3Model::forward_cached (qwen3_model.cpp:275-311): appends `count` HOST token ids to the cached sequence.
+ * logits (DEVICE bf16, may be NULL) receives [count, vocab] when all_rows != 0, else the last row [vocab].
+ * next_token (HOST, may be NULL) receives the greedy token of the last row (cli_app.cpp:72-94); the call then
+ * synchronises `stream`. */
+CPPINF_API int cppinf_qwen3_forward(cppinf_qwen3* model, const int64_t* token_ids, int64_t count, void* logits,
+                                    int all_rows, int64_t* next_token, void* stream);
+
+/* Greedy decoding from the cached state: `steps` decode steps, each feeding the previous greedy token (the last
+ * cppinf_qwen3_forward's, then each step's own). Writes the `steps` generated tokens to the HOST array `tokens` and
+ * synchronises `stream`. One step is a captured CUDA graph of the whole decoder (the device-side sequence length
+ * selects the cache row, the rotary position and the input token). */
+CPPINF_API int cppinf_qwen3_decode(cppinf_qwen3* model, int64_t steps, int64_t* tokens, void* stream);
+
+/* Forgets the cached sequence (a fresh make_cache). */
+CPPINF_API int cppinf_qwen3_reset(cppinf_qwen3* model, void* stream);
+
+/* Number of cached tokens. */
+CPPINF_API int64_t cppinf_qwen3_length(const cppinf_qwen3* model);
+
+/* Kernel launches of one decode step (for launch accounting). */
+CPPINF_API int64_t cppinf_qwen3_step_launches(const cppinf_qwen3* model);
 
 #ifdef __cplusplus
 }

@@ -18,6 +18,7 @@
  */
 #include <math.h>
 #include <stdint.h>
+#include <stdlib.h>
 #include <string.h>
 
 #define DT_BF16 0
@@ -390,5 +391,278 @@ void oracle_linear(int dtype, const void* x, const void* weight, void* y, int64_
             }
             store(dtype, y, r * out + o, acc);
         }
+    }
+}
+
+/* ==== Qwen3 decoder (src/nn/qwen_decoder_block.cpp, qwen_attention.cpp, qwen_mlp.cpp, models/qwen3) =============
+ *
+ * The reference runs its decoder through oneDNN matmul/eltwise primitives whose accumulation order and exp are
+ * unspecified. The device decoder fixes both, and these functions restate exactly what it computes:
+ *  - linear (src/nn/qwen_common.cpp:15-37, ops::matmul src/ops/matmul.cpp:85-114 with bf16 in and out): each output
+ *    is a dot product in the canonical lane order (chunk 8 when K % 8 == 0, else 1; lane l adds chunks l, l+32, ...
+ *    in increasing element order, starting from +0; butterfly over lane distances 16..1), rounded to bf16 once;
+ *  - exp: the portable exponential below, in the attention softmax and in SiLU;
+ *  - attention (qwen_attention.cpp:236-333 with the softmax of :164-235): the fixed partition order of
+ *    oracle_decoder_attention.
+ * A product of two bf16 values is exact in f32 (8 + 8 significant bits) unless it underflows, so accumulating
+ * `acc + a * b` equals an FMA for every operand pair that occurs here. */
+
+/* Portable exp, written from the mathematics: Cody-Waite argument reduction x = n ln2 + r with ln2 split into a
+ * 12-bit head (so n * head is exact for |n| <= 2^12) and an f32 tail, e^r by its Taylor polynomial to degree 7 in
+ * Horner form (|r| <= ln2/2, truncation error below 6e-9 relative), then scaling by 2^n through the exponent field.
+ * Every step is one IEEE f32 operation, so the device evaluates the same value bit for bit. */
+#define PEXP_LOG2E 0x1.715476p+0f
+#define PEXP_LN2_HI 0x1.62ep-1f
+#define PEXP_LN2_LO 0x1.0bfbe8p-15f
+
+static inline float pow2i(int e) { /* 2^e for -126 <= e <= 127 */
+    const uint32_t bits = (uint32_t)(e + 127) << 23;
+    float f;
+    memcpy(&f, &bits, sizeof f);
+    return f;
+}
+
+float oracle_pexp(float x) {
+    if (x != x) {
+        return x;
+    }
+    if (x > 88.8f) {
+        return INFINITY;
+    }
+    if (x < -104.0f) {
+        return 0.0f;
+    }
+    const float n = rintf(x * PEXP_LOG2E);
+    const float r = (x - n * PEXP_LN2_HI) - n * PEXP_LN2_LO;
+    float p = 0x1.a01a02p-13f;
+    p = p * r + 0x1.6c16c2p-10f;
+    p = p * r + 0x1.111112p-7f;
+    p = p * r + 0x1.555556p-5f;
+    p = p * r + 0x1.555556p-3f;
+    p = p * r + 0.5f;
+    p = p * r + 1.0f;
+    p = p * r + 1.0f;
+    int e = (int)n;
+    if (e > 127) {
+        p = p * 2.0f;
+        e -= 1;
+    }
+    if (e < -126) {
+        p = p * 0x1p-64f;
+        e += 64;
+    }
+    return p * pow2i(e);
+}
+
+void oracle_pexp_array(const float* x, float* y, int64_t n) {
+    for (int64_t i = 0; i < n; ++i) {
+        y[i] = oracle_pexp(x[i]);
+    }
+}
+
+/* SiLU (src/ops/nn_ops.cpp:44-48, x / (1 + exp(-x))) with the portable exp, stored in bf16, times up, stored in
+ * bf16: the decoder's gate/up epilogue (src/nn/qwen_mlp.cpp:65-66). */
+void oracle_silu_mul_pexp(const uint16_t* gate, const uint16_t* up, uint16_t* out, int64_t n) {
+#pragma omp parallel for schedule(static)
+    for (int64_t i = 0; i < n; ++i) {
+        const float g = bf16_to_f32(gate[i]);
+        const float s = bf16_to_f32(f32_to_bf16(g / (1.0f + oracle_pexp(-g))));
+        out[i] = f32_to_bf16(s * bf16_to_f32(up[i]));
+    }
+}
+
+static void butterfly32(float* partial) {
+    float next[32];
+    for (int d = 16; d > 0; d >>= 1) {
+        for (int lane = 0; lane < 32; ++lane) {
+            next[lane] = partial[lane] + partial[lane ^ d];
+        }
+        memcpy(partial, next, sizeof next);
+    }
+}
+
+/* y[m, n] = sum_k x[m, k] w[n, k] in the canonical lane order; x [M, K] with row stride x_stride, w [N, K] dense.
+ * Results go to y_bf16 [M, N] (rounded once) and/or y_f32 [M, N] (unrounded) when non-null. Rows of x are processed
+ * in blocks of 64 with the block transposed, so the inner loop runs over rows and vectorises. */
+void oracle_linear_canonical(const uint16_t* x, int64_t x_stride, const uint16_t* w, int64_t M, int64_t K, int64_t N,
+                             uint16_t* y_bf16, float* y_f32) {
+    enum { MB = 64 };
+    const int64_t chunk = K % 8 == 0 ? 8 : 1;
+    const int64_t nchunks = K / chunk;
+    if (M == 1) {
+        float* xf = (float*)malloc(sizeof(float) * (size_t)K);
+        for (int64_t k = 0; k < K; ++k) {
+            xf[k] = bf16_to_f32(x[k]);
+        }
+#pragma omp parallel for schedule(static)
+        for (int64_t n = 0; n < N; ++n) {
+            float partial[32] = {0};
+            const uint16_t* wr = w + n * K;
+            for (int64_t c = 0; c < nchunks; ++c) {
+                float a = partial[c & 31];
+                for (int64_t e = c * chunk; e < (c + 1) * chunk; ++e) {
+                    a = a + xf[e] * bf16_to_f32(wr[e]);
+                }
+                partial[c & 31] = a;
+            }
+            butterfly32(partial);
+            if (y_bf16) {
+                y_bf16[n] = f32_to_bf16(partial[0]);
+            }
+            if (y_f32) {
+                y_f32[n] = partial[0];
+            }
+        }
+        free(xf);
+        return;
+    }
+    float* xt = (float*)malloc(sizeof(float) * (size_t)K * MB);
+    for (int64_t m0 = 0; m0 < M; m0 += MB) {
+        const int64_t mb = M - m0 < MB ? M - m0 : MB;
+        for (int64_t k = 0; k < K; ++k) {
+            for (int64_t mm = 0; mm < MB; ++mm) {
+                xt[k * MB + mm] = mm < mb ? bf16_to_f32(x[(m0 + mm) * x_stride + k]) : 0.0f;
+            }
+        }
+#pragma omp parallel for schedule(static)
+        for (int64_t n = 0; n < N; ++n) {
+            float acc[32][MB];
+            memset(acc, 0, sizeof acc);
+            const uint16_t* wr = w + n * K;
+            for (int64_t c = 0; c < nchunks; ++c) {
+                float* a = acc[c & 31];
+                for (int64_t e = c * chunk; e < (c + 1) * chunk; ++e) {
+                    const float wv = bf16_to_f32(wr[e]);
+                    const float* xk = xt + e * MB;
+                    for (int mm = 0; mm < MB; ++mm) {
+                        a[mm] = a[mm] + xk[mm] * wv;
+                    }
+                }
+            }
+            for (int64_t mm = 0; mm < mb; ++mm) {
+                float partial[32];
+                for (int lane = 0; lane < 32; ++lane) {
+                    partial[lane] = acc[lane][mm];
+                }
+                butterfly32(partial);
+                if (y_bf16) {
+                    y_bf16[(m0 + mm) * N + n] = f32_to_bf16(partial[0]);
+                }
+                if (y_f32) {
+                    y_f32[(m0 + mm) * N + n] = partial[0];
+                }
+            }
+        }
+    }
+    free(xt);
+}
+
+/* Causal grouped-query attention of one sequence in the device decoder's order. q [T, Hq, D] bf16 (after q-norm and
+ * RoPE); key/value caches [cap, Hkv, D] bf16; query t sits at position pos0 + t and sees keys 0 .. pos0 + t; query
+ * head h reads key/value head h / (Hq / Hkv) (ops::repeat_interleave, src/ops/tensor_ops.cpp). ctx [T, Hq, D] bf16.
+ *
+ * Per (t, h), with L visible keys:
+ *  - score s_j: the head vector is cut into G segments of D / G consecutive dims (G = 8, 4, 2 or 1, the largest
+ *    dividing D), each summed in order from +0, the G partials combined by a butterfly over distances G/2 .. 1;
+ *  - x_j = s_j * scale, scale = 1 / sqrt(D); M = max_j x_j; e_j = pexp(x_j - M) (qwen_attention.cpp:205-222);
+ *  - the keys are split into 8 parts of P = ceil(L / 8) consecutive keys (part c: [cP, min(L, cP + P)));
+ *  - sum: in each part, slot i (0..127) adds e_j for j = lo + i, lo + i + 128, ... in order; slots 32w .. 32w+31 are
+ *    combined by a butterfly; the 4 results, then the 8 part sums, are added in order;
+ *  - p_j = bf16(e_j / sum) (the probabilities' bf16 cast, qwen_attention.cpp:321-327);
+ *  - ctx_d: in each part, group w (0..3) adds p_j v_jd for j = lo + w, lo + w + 4, ... in order; the 4 group sums,
+ *    then the 8 part sums, are added in order; stored in bf16. */
+void oracle_decoder_attention(const uint16_t* q, const uint16_t* kc, const uint16_t* vc, uint16_t* ctx, int64_t T,
+                              int64_t hq, int64_t hkv, int64_t D, int64_t pos0) {
+    enum { PARTS = 8, SLOTS = 128, WARPS = 4 };
+    const float scale = 1.0f / sqrtf((float)D);
+    const int64_t group = hq / hkv;
+    const int64_t G = D % 8 == 0 ? 8 : D % 4 == 0 ? 4 : D % 2 == 0 ? 2 : 1;
+    const int64_t seg = D / G;
+#pragma omp parallel for schedule(dynamic)
+    for (int64_t th = 0; th < T * hq; ++th) {
+        const int64_t t = th / hq;
+        const int64_t h = th % hq;
+        const int64_t kvh = h / group;
+        const int64_t L = pos0 + t + 1;
+        const uint16_t* qv = q + (t * hq + h) * D;
+        float* e = (float*)malloc(sizeof(float) * (size_t)L);
+        float* acc = (float*)calloc((size_t)D, sizeof(float));
+        float* grp = (float*)malloc(sizeof(float) * (size_t)D * WARPS);
+        float mx = -INFINITY;
+        for (int64_t j = 0; j < L; ++j) {
+            const uint16_t* kv = kc + (j * hkv + kvh) * D;
+            float partial[8];
+            for (int64_t g = 0; g < G; ++g) {
+                float s = 0.0f;
+                for (int64_t d = g * seg; d < (g + 1) * seg; ++d) {
+                    s = s + bf16_to_f32(qv[d]) * bf16_to_f32(kv[d]);
+                }
+                partial[g] = s;
+            }
+            for (int64_t dist = G / 2; dist > 0; dist >>= 1) {
+                float next[8];
+                for (int64_t g = 0; g < G; ++g) {
+                    next[g] = partial[g] + partial[g ^ dist];
+                }
+                memcpy(partial, next, sizeof next);
+            }
+            e[j] = partial[0] * scale;
+            mx = e[j] > mx ? e[j] : mx;
+        }
+        for (int64_t j = 0; j < L; ++j) {
+            e[j] = oracle_pexp(e[j] - mx);
+        }
+        const int64_t P = (L + PARTS - 1) / PARTS;
+        float sum = 0.0f;
+        for (int c = 0; c < PARTS; ++c) {
+            const int64_t lo = c * P < L ? c * P : L;
+            const int64_t hi = lo + P < L ? lo + P : L;
+            float slots[SLOTS];
+            for (int i = 0; i < SLOTS; ++i) {
+                float s = 0.0f;
+                for (int64_t j = lo + i; j < hi; j += SLOTS) {
+                    s = s + e[j];
+                }
+                slots[i] = s;
+            }
+            float part = 0.0f;
+            for (int w = 0; w < WARPS; ++w) {
+                butterfly32(slots + 32 * w);
+                part = w == 0 ? slots[0] : part + slots[32 * w];
+            }
+            sum = c == 0 ? part : sum + part;
+        }
+        for (int64_t j = 0; j < L; ++j) {
+            e[j] = bf16_to_f32(f32_to_bf16(e[j] / sum));
+        }
+        for (int c = 0; c < PARTS; ++c) {
+            const int64_t lo = c * P < L ? c * P : L;
+            const int64_t hi = lo + P < L ? lo + P : L;
+            for (int w = 0; w < WARPS; ++w) {
+                float* a = grp + w * D;
+                for (int64_t d = 0; d < D; ++d) {
+                    a[d] = 0.0f;
+                }
+                for (int64_t j = lo + w; j < hi; j += WARPS) {
+                    const uint16_t* vv = vc + (j * hkv + kvh) * D;
+                    for (int64_t d = 0; d < D; ++d) {
+                        a[d] = a[d] + e[j] * bf16_to_f32(vv[d]);
+                    }
+                }
+            }
+            for (int64_t d = 0; d < D; ++d) {
+                float p = grp[d];
+                for (int w = 1; w < WARPS; ++w) {
+                    p = p + grp[w * D + d];
+                }
+                acc[d] = c == 0 ? p : acc[d] + p;
+            }
+        }
+        for (int64_t d = 0; d < D; ++d) {
+            ctx[(t * hq + h) * D + d] = f32_to_bf16(acc[d]);
+        }
+        free(e);
+        free(acc);
+        free(grp);
     }
 }

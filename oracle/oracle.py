@@ -102,6 +102,10 @@ class Oracle:
             "oracle_qk_norm_rope": [_i, _p, _p, _p, _p, _p, _p, _l, _l, _l, _l, _l, _f, _f, _i],
             "oracle_row_argmax": [_i, _p, _l, _l, _l, _p],
             "oracle_linear": [_i, _p, _p, _p, _l, _l, _l],
+            "oracle_pexp_array": [_p, _p, _l],
+            "oracle_silu_mul_pexp": [_p, _p, _p, _l],
+            "oracle_linear_canonical": [_p, _l, _p, _l, _l, _l, _p, _p],
+            "oracle_decoder_attention": [_p, _p, _p, _p, _l, _l, _l, _l, _l],
         }
         for name, args in sig.items():
             fn = getattr(self.lib, name)
@@ -234,6 +238,39 @@ class Oracle:
         fout = weight.shape[0]
         out = np.empty((rows, fout), dtype=x.dtype)
         self.lib.oracle_linear(dtype_code(x), _ptr(x), _ptr(weight), _ptr(out), rows, fin, fout)
+        return out
+
+    # -- decoder (fixed-order restatements of the device decoder) --
+    def pexp(self, x):
+        x = np.ascontiguousarray(x, dtype=np.float32)
+        out = np.empty_like(x)
+        self.lib.oracle_pexp_array(_ptr(x), _ptr(out), x.size)
+        return out
+
+    def silu_mul_pexp(self, gate, up):
+        gate, up = np.ascontiguousarray(gate), np.ascontiguousarray(up)
+        out = np.empty_like(gate)
+        self.lib.oracle_silu_mul_pexp(_ptr(gate), _ptr(up), _ptr(out), gate.size)
+        return out
+
+    def linear_canonical(self, x, weight, f32_out: bool = False):
+        """x [M, K] bf16 times weight [N, K] bf16 transposed, canonical lane order; bf16 [M, N] (or f32)."""
+        x, weight = np.ascontiguousarray(x), np.ascontiguousarray(weight)
+        m, k = x.shape
+        n = weight.shape[0]
+        out = np.empty((m, n), dtype=np.float32 if f32_out else np.uint16)
+        self.lib.oracle_linear_canonical(_ptr(x), k, _ptr(weight), m, k, n, None if f32_out else _ptr(out),
+                                         _ptr(out) if f32_out else None)
+        return out
+
+    def decoder_attention(self, q, k_cache, v_cache, pos0: int):
+        """q [T, Hq, D], caches [cap, Hkv, D] (bf16); query t at position pos0 + t. Returns ctx [T, Hq, D]."""
+        q = np.ascontiguousarray(q)
+        k_cache, v_cache = np.ascontiguousarray(k_cache), np.ascontiguousarray(v_cache)
+        t, hq, d = q.shape
+        hkv = k_cache.shape[1]
+        out = np.empty_like(q)
+        self.lib.oracle_decoder_attention(_ptr(q), _ptr(k_cache), _ptr(v_cache), _ptr(out), t, hq, hkv, d, pos0)
         return out
 
 

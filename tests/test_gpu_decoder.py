@@ -1,0 +1,263 @@
+"""Parity of the device decoder (projections, attention, the Qwen3 model) with the CPU oracle, through the C ABI.
+
+The oracle restates the device decoder's accumulation orders (oracle/oracle.c: oracle_linear_canonical,
+oracle_decoder_attention, oracle_pexp) and is pinned to the reference's tiny-model golden logits and to Hugging
+Face Qwen3 logits (tests/test_decoder_oracle.py). Every comparison here is bit for bit: logits, contexts and greedy
+tokens.
+"""
+
+from __future__ import annotations
+
+import numpy as np
+import pytest
+import torch
+
+from _dev import seeded_bf16, to_dev, to_host
+from oracle.oracle import bf16_to_f32, f32_to_bf16
+
+pytestmark = pytest.mark.gpu
+
+
+@pytest.fixture(scope="module")
+def ops(cuda):
+    from cppinf_b200 import ops as _ops
+
+    return _ops
+
+
+def assert_bits_equal(got: np.ndarray, want: np.ndarray, what: str):
+    assert got.shape == want.shape, (got.shape, want.shape)
+    bad = np.flatnonzero(got.reshape(-1) != want.reshape(-1))
+    assert bad.size == 0, (f"{what}: {bad.size} of {want.size} differ; first at {bad[0]}: "
+                           f"{bf16_to_f32(got.reshape(-1)[bad[:4]])} vs {bf16_to_f32(want.reshape(-1)[bad[:4]])}")
+
+
+# ---------------------------------------------------------------------------------------------------------------
+# Projections
+# ---------------------------------------------------------------------------------------------------------------
+
+LINEAR_SHAPES = [
+    (1, 1024, 4096),   # decode q|k|v
+    (1, 2048, 1024),   # decode o_proj
+    (1, 3072, 1024),   # decode down_proj
+    (1, 8, 5),         # one chunk
+    (1, 264, 77),      # chunks not a multiple of 32 lanes
+    (3, 1024, 300),
+    (16, 512, 64),
+    (37, 3072, 128),   # partial tile
+    (512, 1024, 256),  # prefill
+]
+
+
+@pytest.mark.parametrize("m,k,n", LINEAR_SHAPES)
+def test_linear_bit_exact(ops, oracle, m, k, n):
+    rng = np.random.default_rng(1000 + m + k + n)
+    x = seeded_bf16(rng, (m, k))
+    w = seeded_bf16(rng, (n, k), std=0.05)
+    got = to_host(ops.linear(to_dev(x), to_dev(w)))
+    assert_bits_equal(got, oracle.linear_canonical(x, w), "linear")
+
+
+def test_linear_strided_rows(ops, oracle):
+    rng = np.random.default_rng(7)
+    big = seeded_bf16(rng, (9, 1032))
+    w = seeded_bf16(rng, (40, 1024), std=0.05)
+    got = to_host(ops.linear(to_dev(big)[:, 8:], to_dev(w)))  # materialised, then dense rows
+    assert_bits_equal(got, oracle.linear_canonical(np.ascontiguousarray(big[:, 8:]), w), "strided linear")
+
+
+@pytest.mark.parametrize("m,k,n", [(1, 1024, 1024), (1, 3072, 1024), (19, 2048, 256)])
+def test_linear_residual_bit_exact(ops, oracle, m, k, n):
+    rng = np.random.default_rng(m * 7 + k)
+    x = seeded_bf16(rng, (m, k))
+    w = seeded_bf16(rng, (n, k), std=0.03)
+    res = seeded_bf16(rng, (m, n))
+    want = oracle.add(res, oracle.linear_canonical(x, w))
+    got = to_host(ops.linear_residual(to_dev(x), to_dev(w), to_dev(res)))
+    assert_bits_equal(got, want, "linear_residual")
+    # in place on the residual, as the decoder uses it
+    r = to_dev(res)
+    ops.linear_residual(to_dev(x), to_dev(w), r, out=r)
+    assert_bits_equal(to_host(r), want, "linear_residual in place")
+
+
+@pytest.mark.parametrize("m,k,n", [(1, 1024, 3072), (1, 256, 100), (24, 1024, 512)])
+def test_linear_silu_mul_bit_exact(ops, oracle, m, k, n):
+    rng = np.random.default_rng(m + 3 * n)
+    x = seeded_bf16(rng, (m, k))
+    g = seeded_bf16(rng, (n, k), std=0.08)
+    u = seeded_bf16(rng, (n, k), std=0.08)
+    want = oracle.silu_mul_pexp(oracle.linear_canonical(x, g), oracle.linear_canonical(x, u))
+    got = to_host(ops.linear_silu_mul(to_dev(x), to_dev(g), to_dev(u)))
+    assert_bits_equal(got, want, "linear_silu_mul")
+
+
+@pytest.mark.parametrize("k,n", [(1024, 151936), (1024, 1000), (64, 7), (256, 40000)])
+def test_linear_argmax_matches_oracle(ops, oracle, k, n):
+    rng = np.random.default_rng(k + n)
+    x = seeded_bf16(rng, (1, k))
+    w = seeded_bf16(rng, (n, k), std=0.02)
+    logits = oracle.linear_canonical(x, w)
+    token, got_logits = ops.linear_argmax(to_dev(x), to_dev(w), with_logits=True)
+    assert_bits_equal(to_host(got_logits), logits[0], "argmax logits")
+    assert int(token.item()) == int(oracle.row_argmax(logits)[0])
+    assert int(ops.linear_argmax(to_dev(x), to_dev(w)).item()) == int(oracle.row_argmax(logits)[0])
+
+
+def test_linear_argmax_ties_and_nan(ops, oracle):
+    rng = np.random.default_rng(5)
+    k, n = 64, 5000
+    x = seeded_bf16(rng, (1, k))
+    w = seeded_bf16(rng, (n, k), std=0.02)
+    w[4321] = w[1234] = f32_to_bf16(np.full(k, 0.5, np.float32) * np.sign(bf16_to_f32(x[0]) + 1e-9))
+    logits = oracle.linear_canonical(x, w)
+    assert int(oracle.row_argmax(logits)[0]) == 1234  # equal maxima: the lowest index wins
+    assert int(ops.linear_argmax(to_dev(x), to_dev(w)).item()) == 1234
+    # NaN logits never win, except at index 0, where the reference's scan starts (cli_app.cpp:80-91)
+    w_nan = w.copy()
+    w_nan[77, 3] = 0x7FC0
+    assert int(ops.linear_argmax(to_dev(x), to_dev(w_nan)).item()) == 1234
+    w_nan[0, 3] = 0x7FC0
+    assert int(ops.linear_argmax(to_dev(x), to_dev(w_nan)).item()) == 0
+
+
+def test_embedding(ops):
+    rng = np.random.default_rng(3)
+    table = seeded_bf16(rng, (1000, 256))
+    ids = np.array([5, 0, 999, 5, 17], np.int64)
+    got = to_host(ops.embedding(to_dev(table), torch.from_numpy(ids)))
+    assert (got == table[ids]).all()
+    with pytest.raises(IndexError):
+        ops.embedding(to_dev(table), torch.tensor([1000]))
+
+
+# ---------------------------------------------------------------------------------------------------------------
+# Attention
+# ---------------------------------------------------------------------------------------------------------------
+
+
+@pytest.mark.parametrize("t,pos,hq,hkv,d", [
+    (1, 0, 16, 8, 128),     # first decode position: one key
+    (1, 1, 16, 8, 128),
+    (1, 7, 16, 8, 128),     # fewer keys than parts
+    (1, 100, 16, 8, 128),
+    (1, 639, 16, 8, 128),   # last row of a 640-token cache
+    (33, 5, 16, 8, 128),    # prefill chunk after a cached prefix
+    (64, 0, 4, 4, 64),
+    (9, 300, 8, 2, 256),
+])
+def test_decoder_attention_bit_exact(ops, oracle, t, pos, hq, hkv, d):
+    rng = np.random.default_rng(t * 1000 + pos + d)
+    cap = max(pos + t, 640)
+    q = seeded_bf16(rng, (t, hq, d), std=2.0)
+    kc = np.zeros((cap, hkv, d), np.uint16)
+    vc = np.zeros((cap, hkv, d), np.uint16)
+    kc[:pos + t] = seeded_bf16(rng, (pos + t, hkv, d), std=2.0)
+    vc[:pos + t] = seeded_bf16(rng, (pos + t, hkv, d))
+    want = oracle.decoder_attention(q, kc, vc, pos)
+    got = to_host(ops.decoder_attention(to_dev(q), to_dev(kc), to_dev(vc), pos))
+    assert_bits_equal(got, want, "decoder attention")
+
+
+def test_decoder_attention_rejects_overflow(ops):
+    q = torch.zeros(2, 2, 128, dtype=torch.bfloat16, device="cuda")
+    kc = torch.zeros(8, 1, 128, dtype=torch.bfloat16, device="cuda")
+    with pytest.raises(IndexError):
+        ops.decoder_attention(q, kc, kc, 7)
+    with pytest.raises(NotImplementedError):
+        ops.decoder_attention(q[..., :96], kc[..., :96], kc[..., :96], 0)
+
+
+# ---------------------------------------------------------------------------------------------------------------
+# The model
+# ---------------------------------------------------------------------------------------------------------------
+
+
+def small_config():
+    from cppinf_b200.qwen3 import Qwen3Config
+
+    return Qwen3Config(vocab_size=1000, hidden_size=256, intermediate_size=512, num_hidden_layers=2,
+                       num_attention_heads=4, num_key_value_heads=2, head_dim=128)
+
+
+@pytest.fixture(scope="module")
+def small_pair(cuda):
+    from cppinf_b200.qwen3 import Qwen3Model, random_weights
+    from oracle.qwen3 import OracleQwen3
+
+    cfg = small_config()
+    w = random_weights(cfg, seed=11, std=0.05)
+    return cfg, Qwen3Model(cfg, 700, w), OracleQwen3(cfg, w, 700)
+
+
+def test_model_forward_logits_bit_exact(small_pair):
+    cfg, model, ref = small_pair
+    tokens = np.random.default_rng(1).integers(0, cfg.vocab_size, 40)
+    got = to_host(model.forward(tokens))
+    ref.reset()
+    want = ref.forward_cached(tokens, all_logits=True)
+    assert_bits_equal(got, want, "model logits")
+
+
+def test_model_chunked_prefill_and_decode_tokens(small_pair):
+    # 600 prompt tokens: two prefill chunks (512 + 88); then 24 graph-replayed decode steps
+    cfg, model, ref = small_pair
+    prompt = np.random.default_rng(2).integers(0, cfg.vocab_size, 600)
+    got = model.generate(prompt, 25)
+    ref.reset()
+    want = ref.generate(prompt, 25)
+    assert got == want
+    assert model.length == 600 + 24
+
+
+def test_model_cached_logits_match_full_forward(small_pair):
+    cfg, model, ref = small_pair
+    tokens = np.random.default_rng(3).integers(0, cfg.vocab_size, 12)
+    full = to_host(model.forward(tokens))
+    model.reset()
+    model.forward_cached(tokens[:9], logits=None)
+    rows = [to_host(model.forward_cached([t], logits="last")[1]) for t in tokens[9:]]
+    assert_bits_equal(np.concatenate(rows), full[9:], "cached rows")
+
+
+def test_model_validation(small_pair):
+    cfg, model, _ = small_pair
+    model.reset()
+    with pytest.raises(IndexError):
+        model.forward_cached([cfg.vocab_size])
+    with pytest.raises(ValueError):
+        model.decode(1)  # empty cache
+    with pytest.raises(IndexError):
+        model.forward_cached(np.zeros(701, np.int64))
+
+
+def test_model_matches_hf_fixture_bit_exact_with_oracle(cuda, golden, oracle):
+    # the Hugging Face fixture's model: device logits equal the oracle's bit for bit (the oracle is pinned to the
+    # Hugging Face logits in tests/test_decoder_oracle.py)
+    from cppinf_b200.qwen3 import Qwen3Model, random_weights
+    from golden.make_decoder_golden import HF_SMALL
+    from oracle.qwen3 import OracleQwen3
+
+    fx = golden("qwen3_hf_small")
+    w = random_weights(HF_SMALL, int(fx["seed"]), float(fx["std"]))
+    got = to_host(Qwen3Model(HF_SMALL, 64, w).forward(fx["tokens"]))
+    want = OracleQwen3(HF_SMALL, w, 64, oracle).forward_cached(fx["tokens"], all_logits=True)
+    assert_bits_equal(got, want, "hf-fixture model logits")
+    assert np.abs(bf16_to_f32(got) - bf16_to_f32(fx["logits"])).max() <= 0.0625
+
+
+def test_qwen3_0_6b_greedy_tokens_bit_exact(cuda, oracle):
+    """Random-init Qwen3-0.6B (weights ~N(0, 0.02), norm weights 1): 512-token seeded prompt, then greedy decode;
+    every generated token equals the oracle's."""
+    from cppinf_b200.qwen3 import Qwen3Config, Qwen3Model, random_weights
+    from oracle.qwen3 import OracleQwen3
+
+    cfg = Qwen3Config.qwen3_0_6b()
+    w = random_weights(cfg, seed=0)
+    prompt = np.random.default_rng(0).integers(0, cfg.vocab_size, 512)
+    steps = 24
+    model = Qwen3Model(cfg, 512 + steps, w)
+    got = model.generate(prompt, steps)
+    model.close()
+    want = OracleQwen3(cfg, w, 512 + steps, oracle).generate(prompt, steps)
+    assert got == want
