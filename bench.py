@@ -25,6 +25,11 @@ public API from pinned host buffers (H2D, kernel, D2H pipelined over three strea
 --impl reference times the reference's CPU implementation of the same workload on this host (the reference's own
 rope.cpp compiled under oracle/_ref, and the C restatement of rms_norm whose reference needs oneDNN), with all host
 threads; under torchrun only rank 0 runs it.
+
+The line also carries `decode`: random-init Qwen3-0.6B (weights ~N(0,0.02), unit norm weights) on the device
+decoder, a seeded 512-token prompt then 128 greedy tokens (1 from the prefill, 127 graph-replayed decode steps);
+tok/s of the decode steps (CUDA events), the prefill time, the weight-streaming roofline, and e2e through
+Qwen3Model.generate with host token ids. Across GPUs decode runs one independent replica per GPU.
 """
 
 from __future__ import annotations
@@ -78,6 +83,8 @@ def parse_args():
     p.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline")
     p.add_argument("--no-e2e", action="store_true", help="skip the host-buffer end-to-end measurement")
     p.add_argument("--cpu-seconds", type=float, default=8.0, help="CPU-baseline sample length")
+    p.add_argument("--no-decode", action="store_true", help="skip the Qwen3-0.6B greedy-decode measurement")
+    p.add_argument("--decode-runs", type=int, default=3, help="timed prefill + decode runs")
     return p.parse_args()
 
 
@@ -461,6 +468,106 @@ def measure_cpu(kind: str, seconds: float) -> dict:
 
 
 # ---------------------------------------------------------------------------------------------------------------
+# Qwen3-0.6B greedy decode (random init), replicas only across GPUs
+# ---------------------------------------------------------------------------------------------------------------
+
+DECODE_PROMPT = 512
+DECODE_NEW = 128
+
+
+def decode_bytes_per_token(cfg, context: int) -> int:
+    """Algorithmic HBM bytes of one decode step: every weight once (the tied embedding as the LM head; the embedding
+    gather reads one row) plus the key and value rows of `context` positions in every layer."""
+    weights = cfg.parameter_count() * 2
+    kv = 2 * context * cfg.num_key_value_heads * cfg.head_dim * 2 * cfg.num_hidden_layers
+    return weights + kv
+
+
+def device_random_weights(cfg, device, seed: int = 0) -> dict:
+    """~N(0, 0.02) bf16 matrices and unit norm weights, drawn on the device (seeded torch generator)."""
+    import torch
+
+    g = torch.Generator(device=device).manual_seed(seed)
+    out = {}
+    for name, shape in cfg.weight_shapes().items():
+        if len(shape) == 1:
+            out[name] = torch.ones(shape, dtype=torch.bfloat16, device=device)
+        else:
+            out[name] = (torch.randn(shape, generator=g, device=device) * 0.02).to(torch.bfloat16)
+    return out
+
+
+def measure_decode(device, runs: int) -> dict:
+    """Prefill a seeded 512-token prompt, then 127 graph-replayed decode steps (128 generated tokens), `runs` times
+    after one warm-up run. Device time from CUDA events on the launch stream; e2e is the wall time of the public
+    Qwen3Model.generate call (host token ids in, host token ids out)."""
+    import numpy as np
+    import torch
+
+    from cppinf_b200 import capi
+    from cppinf_b200.qwen3 import Qwen3Config, Qwen3Model
+
+    cfg = Qwen3Config.qwen3_0_6b()
+    model = Qwen3Model(cfg, DECODE_PROMPT + DECODE_NEW, device_random_weights(cfg, device))
+    prompt = np.random.default_rng(0).integers(0, cfg.vocab_size, DECODE_PROMPT).tolist()
+    model.generate(prompt, DECODE_NEW)  # warm-up, captures the decode-step graph
+    stream = torch.cuda.current_stream(device)
+    prefill_ms, decode_ms, launches = [], [], 0
+    tokens = None
+    for _ in range(runs):
+        model.reset()
+        e0, e1, e2 = (torch.cuda.Event(enable_timing=True) for _ in range(3))
+        torch.cuda.synchronize(device)
+        before = capi.launch_count()
+        e0.record(stream)
+        first, _ = model.forward_cached(prompt, logits=None)
+        e1.record(stream)
+        rest = model.decode(DECODE_NEW - 1)
+        e2.record(stream)
+        torch.cuda.synchronize(device)
+        launches = capi.launch_count() - before
+        prefill_ms.append(e0.elapsed_time(e1))
+        decode_ms.append(e1.elapsed_time(e2))
+        tokens = [first] + rest
+    t0 = time.perf_counter()
+    again = model.generate(prompt, DECODE_NEW)
+    torch.cuda.synchronize(device)
+    e2e_s = time.perf_counter() - t0
+    model.close()
+    dec = statistics.median(decode_ms)
+    return {"decode_ms": dec, "prefill_ms": statistics.median(prefill_ms), "e2e_s": e2e_s,
+            "launches_per_run": launches, "step_launches": 5 * cfg.num_hidden_layers + 1, "tokens": tokens,
+            "deterministic": again == tokens, "cfg": cfg}
+
+
+def measure_cpu_decode(seconds: float) -> dict:
+    """The C restatement of the decoder (oracle/qwen3.py over oracle/oracle.c, OpenMP) on this host: a 16-token
+    prompt, then greedy decode steps for about `seconds`."""
+    import numpy as np
+
+    from cppinf_b200.qwen3 import Qwen3Config, random_weights
+    from oracle.qwen3 import OracleQwen3
+
+    cfg = Qwen3Config.qwen3_0_6b()
+    model = OracleQwen3(cfg, random_weights(cfg, 0), 16 + 256)
+    prompt = np.random.default_rng(0).integers(0, cfg.vocab_size, 16)
+    logits = model.forward_cached(prompt)
+    tok = int(model.o.row_argmax(logits)[0])
+    n = 0
+    t0 = time.perf_counter()
+    while n < 256 - 1:
+        logits = model.forward_cached([tok])
+        tok = int(model.o.row_argmax(logits)[0])
+        n += 1
+        if time.perf_counter() - t0 >= seconds:
+            break
+    elapsed = time.perf_counter() - t0
+    return {"value": round(n / elapsed, 3), "unit": "tok/s", "cores": os.cpu_count(), "kind": "port",
+            "sample": f"{n} greedy decode steps after a 16-token prompt in {elapsed:.1f} s: the C restatement of "
+                      "the decoder (oracle/qwen3.py, OpenMP over output rows)"}
+
+
+# ---------------------------------------------------------------------------------------------------------------
 # Arms
 # ---------------------------------------------------------------------------------------------------------------
 
@@ -495,6 +602,13 @@ def run_reference(args) -> None:
         "cpu_baseline": {"value": value, "unit": UNIT, "cores": cpu.threads, "kind": cpu.kind, "sample": sample},
         "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
+    if not args.no_decode:
+        # The reference's decoder needs oneDNN (absent here); its CPU path is timed through the C restatement.
+        dec = measure_cpu_decode(max(args.cpu_seconds, 2.0))
+        line["decode"] = {"metric": "random-init Qwen3-0.6B greedy decode tok/s", "value": dec["value"],
+                          "unit": "tok/s", "cpu_baseline": dec,
+                          "e2e": {"value": dec["value"], "unit": "tok/s", "h2d_bytes_per_step": 0,
+                                  "d2h_bytes_per_step": 0}}
     print(json.dumps(line), flush=True)
 
 
@@ -565,6 +679,37 @@ def run_ours(args) -> None:
     if rank == 0 and world == 1 and not args.no_cpu:
         cpu = measure_cpu("port", args.cpu_seconds)
 
+    decode = None
+    if not args.no_decode:
+        barrier()
+        d = measure_decode(device, max(args.decode_runs, 1))
+        dec_ms = max_over_ranks(d["decode_ms"])
+        steps = DECODE_NEW - 1
+        tok_s = world * steps / (dec_ms * 1e-3)
+        cfg = d["cfg"]
+        mean_ctx = DECODE_PROMPT + steps / 2 + 1
+        bpt = decode_bytes_per_token(cfg, int(mean_ctx))
+        achieved_dec = bpt * steps / (d["decode_ms"] * 1e-3) / 1e9
+        e2e_s = max_over_ranks(d["e2e_s"])
+        decode = {
+            "metric": "random-init Qwen3-0.6B greedy decode tok/s", "value": round(tok_s, 1), "unit": "tok/s",
+            "ms_per_token": round(dec_ms / steps, 4), "prefill_ms": round(max_over_ranks(d["prefill_ms"]), 2),
+            "config": {"model": "Qwen3-0.6B, random init N(0,0.02) bf16, unit norm weights, tied embeddings",
+                       "prompt_tokens": DECODE_PROMPT, "generated_tokens": DECODE_NEW, "batch": 1,
+                       "parallelism": f"{world} independent replica(s), one per GPU (decode does not shard)"},
+            "roofline": {"bound": "hbm", "achieved": round(achieved_dec, 1), "peak": peak, "unit": UNIT,
+                         "frac": round(achieved_dec / peak, 4),
+                         "bytes_per_token": bpt, "note": "weights once per step + KV rows at the mean context"},
+            "e2e": {"value": round(world * DECODE_NEW / e2e_s, 1), "unit": "tok/s",
+                    "h2d_bytes_per_step": DECODE_PROMPT * 8, "d2h_bytes_per_step": DECODE_NEW * 8,
+                    "how": "Qwen3Model.generate(prompt, 128): host token ids in, prefill + 127 decode steps, "
+                           "host token ids out"},
+            "gpu_launches_per_run": d["launches_per_run"], "launches_per_step": d["step_launches"],
+            "deterministic": d["deterministic"], "first_tokens": d["tokens"][:8],
+        }
+        if rank == 0 and world == 1 and not args.no_cpu:
+            decode["cpu_baseline"] = measure_cpu_decode(args.cpu_seconds)
+
     if rank == 0:
         line = {
             "metric": METRIC, "value": round(value, 2), "unit": UNIT, "n_gpus": world, "steps": args.steps,
@@ -587,6 +732,7 @@ def run_ours(args) -> None:
             "clocks": clock_info,
             "ops": per_op,
             "cpu_baseline": cpu,
+            "decode": decode,
         }
         print(json.dumps(line), flush=True)
     if world > 1:

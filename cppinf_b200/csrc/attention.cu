@@ -35,13 +35,15 @@ constexpr int kThreads = 128;
 constexpr int kWarps = kThreads / 32;
 constexpr int kSegments = 8;  // lanes per key in the score dot product
 
+// A lane's kD / 32 values of one V row, loaded raw (so several rows can be in flight) and unpacked at use.
 template <int kD>
-struct VRow;  // a lane's kD / 32 values of one V row
+struct VRow;
 
 template <>
 struct VRow<64> {
-    static __device__ __forceinline__ void load(const bf16* p, float (&v)[2]) {
-        const uint32_t w = __ldg(reinterpret_cast<const unsigned int*>(p));
+    using Raw = uint32_t;
+    static __device__ __forceinline__ Raw load(const bf16* p) { return __ldg(reinterpret_cast<const unsigned int*>(p)); }
+    static __device__ __forceinline__ void unpack(Raw w, float (&v)[2]) {
         v[0] = bf16_lo(w);
         v[1] = bf16_hi(w);
     }
@@ -49,8 +51,9 @@ struct VRow<64> {
 
 template <>
 struct VRow<128> {
-    static __device__ __forceinline__ void load(const bf16* p, float (&v)[4]) {
-        const uint2 w = __ldg(reinterpret_cast<const uint2*>(p));
+    using Raw = uint2;
+    static __device__ __forceinline__ Raw load(const bf16* p) { return __ldg(reinterpret_cast<const uint2*>(p)); }
+    static __device__ __forceinline__ void unpack(Raw w, float (&v)[4]) {
         v[0] = bf16_lo(w.x);
         v[1] = bf16_hi(w.x);
         v[2] = bf16_lo(w.y);
@@ -60,9 +63,9 @@ struct VRow<128> {
 
 template <>
 struct VRow<256> {
-    static __device__ __forceinline__ void load(const bf16* p, float (&v)[8]) {
-        Vec16<bf16>::unpack(ld_cached(p), v);
-    }
+    using Raw = uint4;
+    static __device__ __forceinline__ Raw load(const bf16* p) { return ld_cached(p); }
+    static __device__ __forceinline__ void unpack(Raw w, float (&v)[8]) { Vec16<bf16>::unpack(w, v); }
 };
 
 __device__ __forceinline__ float dot8(uint4 a, uint4 b, float acc) {
@@ -77,19 +80,72 @@ __device__ __forceinline__ float dot8(uint4 a, uint4 b, float acc) {
     return acc;
 }
 
+// Per-head RMSNorm + RoPE of one raw head vector into shared memory, with exactly the arithmetic of
+// qk_norm_rope_kernel (rope.cu): kD / 16 lanes, lane hl holding dims [8 hl, 8 hl + 8) and the matching dims of the
+// second half; the sum of squares in the canonical lane order; normalised values rounded to bf16; then
+// (first * cos - second * sin, second * cos + first * sin) rounded to bf16 (src/nn/rope.cpp:115-118).
 template <int kD>
+__device__ __forceinline__ void norm_rope_head(const bf16* src, const bf16* weight, const float* table_row,
+                                               float eps, bf16* dst, int lane) {
+    constexpr int kLanes = kD / 16;
+    constexpr int kHalf = kD / 2;
+    const int hl = lane % kLanes;
+    float a[8];
+    float b[8];
+    Vec16<bf16>::unpack(ld_cached(src + hl * 8), a);
+    Vec16<bf16>::unpack(ld_cached(src + kHalf + hl * 8), b);
+    float sa = 0.0f;
+    float sb = 0.0f;
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+        sa = sa + a[j] * a[j];
+    }
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+        sb = sb + b[j] * b[j];
+    }
+    const float ss = group_sum<kLanes>(sa + sb);
+    const float mean = ss / static_cast<float>(kD);
+    const float rms = sqrtf(mean + eps);
+    const float inv = 1.0f / rms;
+    float wa[8];
+    float wb[8];
+    Vec16<bf16>::unpack(ld_cached(weight + hl * 8), wa);
+    Vec16<bf16>::unpack(ld_cached(weight + kHalf + hl * 8), wb);
+    float out_a[8];
+    float out_b[8];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+        const float c = table_row[hl * 8 + j];
+        const float s = table_row[kHalf + hl * 8 + j];
+        const float n1 = round_to_bf16((a[j] * inv) * wa[j]);
+        const float n2 = round_to_bf16((b[j] * inv) * wb[j]);
+        out_a[j] = n1 * c - n2 * s;
+        out_b[j] = n2 * c + n1 * s;
+    }
+    if (lane < kLanes) {
+        *reinterpret_cast<uint4*>(dst + hl * 8) = Vec16<bf16>::pack(out_a);
+        *reinterpret_cast<uint4*>(dst + kHalf + hl * 8) = Vec16<bf16>::pack(out_b);
+    }
+}
+
+template <int kD, bool kFused>
 __global__ void __launch_bounds__(kThreads) decoder_attention_kernel(const AttentionParams p) {
     constexpr int kSeg = kD / kSegments;       // dims per score segment
     constexpr int kSegChunks = kSeg / 8;       // 16-byte chunks per segment
     constexpr int kKeysPerIter = 32 / kSegments;
     constexpr int kDimsPerLane = kD / 32;
     constexpr int kFinal = kD / kParts;        // context dims each CTA finishes
+    constexpr int kScoreBatch = 4;             // warp iterations of score loads issued together
+    constexpr int kValueBatch = 8;             // V rows a warp loads together
     extern __shared__ float s_e[];             // this part's scores, then exp values, then probabilities
     __shared__ float s_red[kWarps];
     __shared__ float s_max;
     __shared__ float s_sum;
     __shared__ float s_acc[kWarps][kD];
     __shared__ float s_part[kD];
+    __shared__ __align__(16) bf16 s_q[kFused ? kD : 8];
+    __shared__ __align__(16) bf16 s_knew[kFused ? kD : 8];
 
     grid_dependency_begin();
     cg::cluster_group cluster = cg::this_cluster();
@@ -99,7 +155,8 @@ __global__ void __launch_bounds__(kThreads) decoder_attention_kernel(const Atten
     const int64_t unit = blockIdx.x / kParts;
     const int64_t t = unit / p.q_heads;
     const int h = static_cast<int>(unit - t * p.q_heads);
-    const int kvh = h / (p.q_heads / p.kv_heads);
+    const int group = p.q_heads / p.kv_heads;
+    const int kvh = h / group;
     const int64_t pos = p.pos0 + (p.position != nullptr ? static_cast<int64_t>(*p.position) : 0) + t;
     if (pos >= p.capacity) {
         return;  // the whole cluster leaves together (same t); no DSMEM access happens
@@ -112,31 +169,66 @@ __global__ void __launch_bounds__(kThreads) decoder_attention_kernel(const Atten
     const int64_t kv_row = static_cast<int64_t>(p.kv_heads) * kD;
     const float scale = 1.0f / sqrtf(static_cast<float>(kD));
 
-    // Scores: 4 keys per warp iteration, 8 lanes per key.
+    if constexpr (kFused) {
+        // q-norm + RoPE of this head and k-norm + RoPE of the new key (computed by every CTA that needs them).
+        const float* trow = p.rope_table + pos * kD;
+        if (warp == 0) {
+            norm_rope_head<kD>(p.q + (t * p.q_heads + h) * kD, p.q_norm, trow, p.eps, s_q, lane);
+        } else if (warp == 1) {
+            norm_rope_head<kD>(p.k_new + (t * p.kv_heads + kvh) * kD, p.k_norm, trow, p.eps, s_knew, lane);
+        }
+        __syncthreads();
+        if (rank == 0 && h % group == 0 && threadIdx.x < kD / 8) {
+            // One CTA per key/value head stores the new key row; nobody reads that row in this launch.
+            st_v4(const_cast<bf16*>(p.k_cache) + pos * kv_row + kvh * kD + threadIdx.x * 8,
+                  *reinterpret_cast<const uint4*>(s_knew + threadIdx.x * 8));
+        }
+    }
+
+    // Scores: 4 keys per warp iteration, 8 lanes per key; kScoreBatch iterations' loads in flight.
     const int sub = lane % kSegments;
     const int slot = lane / kSegments;
     uint4 qv[kSegChunks];
-    const bf16* qrow = p.q + (t * p.q_heads + h) * kD + sub * kSeg;
 #pragma unroll
     for (int c = 0; c < kSegChunks; ++c) {
-        qv[c] = ld_cached(qrow + c * 8);
+        if constexpr (kFused) {
+            qv[c] = *reinterpret_cast<const uint4*>(s_q + sub * kSeg + c * 8);
+        } else {
+            qv[c] = ld_cached(p.q + (t * p.q_heads + h) * kD + sub * kSeg + c * 8);
+        }
     }
-    for (int64_t j0 = lo + warp * kKeysPerIter; j0 < hi; j0 += kWarps * kKeysPerIter) {
-        const int64_t j = j0 + slot;
-        float s = 0.0f;
-        if (j < hi) {
-            const bf16* krow = p.k_cache + j * kv_row + kvh * kD + sub * kSeg;
+    constexpr int kIterKeys = kWarps * kKeysPerIter;
+    for (int64_t j0 = lo + warp * kKeysPerIter; j0 < hi; j0 += kIterKeys * kScoreBatch) {
+        uint4 kv[kScoreBatch][kSegChunks];
+#pragma unroll
+        for (int u = 0; u < kScoreBatch; ++u) {
+            const int64_t j = j0 + u * kIterKeys + slot;
 #pragma unroll
             for (int c = 0; c < kSegChunks; ++c) {
-                s = dot8(qv[c], ld_cached(krow + c * 8), s);
+                if (j >= hi) {
+                    kv[u][c] = make_uint4(0u, 0u, 0u, 0u);
+                } else if (kFused && j == L - 1) {
+                    kv[u][c] = *reinterpret_cast<const uint4*>(s_knew + sub * kSeg + c * 8);
+                } else {
+                    kv[u][c] = ld_cached(p.k_cache + j * kv_row + kvh * kD + sub * kSeg + c * 8);
+                }
             }
         }
 #pragma unroll
-        for (int offset = kSegments / 2; offset > 0; offset >>= 1) {
-            s = s + __shfl_xor_sync(0xffffffffu, s, offset);
-        }
-        if (j < hi && sub == 0) {
-            s_e[j - lo] = s * scale;
+        for (int u = 0; u < kScoreBatch; ++u) {
+            const int64_t j = j0 + u * kIterKeys + slot;
+            float s = 0.0f;
+#pragma unroll
+            for (int c = 0; c < kSegChunks; ++c) {
+                s = dot8(qv[c], kv[u][c], s);
+            }
+#pragma unroll
+            for (int offset = kSegments / 2; offset > 0; offset >>= 1) {
+                s = s + __shfl_xor_sync(0xffffffffu, s, offset);
+            }
+            if (j < hi && sub == 0) {
+                s_e[j - lo] = s * scale;
+            }
         }
     }
     __syncthreads();
@@ -174,7 +266,6 @@ __global__ void __launch_bounds__(kThreads) decoder_attention_kernel(const Atten
         sum = sum + e;
     }
     sum = group_sum<32>(sum);
-    __syncthreads();  // s_red is reused
     if (lane == 0) {
         s_red[warp] = sum;
     }
@@ -199,19 +290,34 @@ __global__ void __launch_bounds__(kThreads) decoder_attention_kernel(const Atten
     }
     __syncthreads();
 
-    // Probabilities times V.
+    // Probabilities times V: warp w takes keys lo + w, lo + w + 4, ..., kValueBatch rows in flight.
     float a[kDimsPerLane];
 #pragma unroll
     for (int d = 0; d < kDimsPerLane; ++d) {
         a[d] = 0.0f;
     }
-    for (int64_t j = lo + warp; j < hi; j += kWarps) {
-        const float pj = s_e[j - lo];
-        float v[kDimsPerLane];
-        VRow<kD>::load(p.v_cache + j * kv_row + kvh * kD + lane * kDimsPerLane, v);
+    const bf16* vbase = p.v_cache + kvh * kD + lane * kDimsPerLane;
+    for (int64_t j0 = lo + warp; j0 < hi; j0 += kWarps * kValueBatch) {
+        typename VRow<kD>::Raw raw[kValueBatch];
 #pragma unroll
-        for (int d = 0; d < kDimsPerLane; ++d) {
-            a[d] = a[d] + pj * v[d];
+        for (int u = 0; u < kValueBatch; ++u) {
+            const int64_t j = j0 + u * kWarps;
+            if (j < hi) {
+                raw[u] = VRow<kD>::load(vbase + j * kv_row);
+            }
+        }
+#pragma unroll
+        for (int u = 0; u < kValueBatch; ++u) {
+            const int64_t j = j0 + u * kWarps;
+            if (j < hi) {
+                const float pj = s_e[j - lo];
+                float v[kDimsPerLane];
+                VRow<kD>::unpack(raw[u], v);
+#pragma unroll
+                for (int d = 0; d < kDimsPerLane; ++d) {
+                    a[d] = a[d] + pj * v[d];
+                }
+            }
         }
     }
 #pragma unroll
@@ -245,7 +351,7 @@ template <int kD>
 cudaError_t launch_attention_dim(const AttentionParams& p, int64_t max_keys, cudaStream_t s) {
     const int64_t per_part = (max_keys + kParts - 1) / kParts;
     const std::size_t smem = static_cast<std::size_t>(per_part < 1 ? 1 : per_part) * sizeof(float);
-    auto kernel = decoder_attention_kernel<kD>;
+    auto kernel = p.q_norm != nullptr ? decoder_attention_kernel<kD, true> : decoder_attention_kernel<kD, false>;
     if (smem > 32 * 1024) {
         const cudaError_t err =
             cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
@@ -313,7 +419,12 @@ int cppinf_decoder_attention(const void* q, const void* k_cache, const void* v_c
                       static_cast<int>(head_dim),
                       position,
                       nullptr,
-                      capacity};
+                      capacity,
+                      nullptr,
+                      nullptr,
+                      nullptr,
+                      nullptr,
+                      0.0f};
     return rt::launched(launch_decoder_attention(p, position + tokens, rt::as_stream(stream)), "decoder_attention");
 }
 

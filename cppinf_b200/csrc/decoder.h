@@ -78,6 +78,14 @@ struct AttentionParams {
     int64_t pos0;                  // position of query 0 (added to *position when set)
     const int* position;
     int64_t capacity;              // cache rows; queries past it are skipped
+    // Decode steps (T = 1): when q_norm is set, q and k_new are the raw projections of the new token; the kernel
+    // applies the per-head q/k RMSNorm + RoPE itself (rope.cu's arithmetic), writes the new key row to k_cache and
+    // uses it for the last position.
+    const __nv_bfloat16* k_new;    // [Hkv, D]
+    const __nv_bfloat16* q_norm;
+    const __nv_bfloat16* k_norm;
+    const float* rope_table;       // [capacity, D]
+    float eps;
 };
 
 // Causal GQA attention of one sequence in the fixed partition order (see attention.cu). head_dim 64, 128 or 256.

@@ -93,6 +93,222 @@ __device__ __forceinline__ unsigned long long umax64(unsigned long long a, unsig
     return a > b ? a : b;
 }
 
+template <LinearEpilogue kEpi>
+__host__ __device__ constexpr int mats_of() {
+    return kEpi == LinearEpilogue::kSiluMul ? 2 : 1;
+}
+
+// Stores (or, for kArgmax, folds into `best`) the kRows finished dot products of row group g; every lane holds
+// every sum, lane r stores row r.
+template <LinearEpilogue kEpi, int kRows>
+__device__ __forceinline__ void gemv_epilogue(const LinearParams& p, int64_t g, const float* acc, int lane,
+                                              int64_t pos, unsigned long long& best) {
+#pragma unroll
+    for (int r = 0; r < kRows; ++r) {
+        const int64_t n = g * kRows + r;
+        if (n >= p.N) {
+            break;
+        }
+        if constexpr (kEpi == LinearEpilogue::kArgmax) {
+            const float logit = round_to_bf16(acc[r]);
+            best = umax64(best, logit_key(logit, n));
+            if (lane == r && p.out[0] != nullptr) {
+                store_segment(p, 0, n, logit, 0);
+            }
+        } else if (lane == r) {
+            if constexpr (kEpi == LinearEpilogue::kStore) {
+                store_segment(p, 0, n, acc[r], pos);
+            } else if constexpr (kEpi == LinearEpilogue::kResidual) {
+                const float res = Vec16<bf16>::load1(p.residual, n);
+                Vec16<bf16>::store1(p.out[0], n, res + round_to_bf16(acc[r]));
+            } else {
+                const float gate = round_to_bf16(acc[r * 2]);
+                const float up = round_to_bf16(acc[r * 2 + 1]);
+                Vec16<bf16>::store1(p.out[0], n, round_to_bf16(silu_pexp(gate)) * up);
+            }
+        }
+    }
+}
+
+// kArgmax: combines the warps' keys, then the CTAs' (the last CTA to arrive writes the token, advances the
+// position and re-arms the counter). `best` is the same in every lane of a warp.
+__device__ __forceinline__ void argmax_finish(const LinearParams& p, unsigned long long best,
+                                              unsigned long long* s_best, int* s_last) {
+    const int lane = threadIdx.x & 31;
+    const int warp = threadIdx.x >> 5;
+    if (lane == 0) {
+        s_best[warp] = best;
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        unsigned long long b = s_best[0];
+#pragma unroll
+        for (int w = 1; w < kWarps; ++w) {
+            b = umax64(b, s_best[w]);
+        }
+        p.partial[blockIdx.x] = b;
+        __threadfence();
+        const unsigned ticket = atomicAdd(p.counter, 1u);
+        *s_last = ticket == gridDim.x - 1 ? 1 : 0;
+    }
+    __syncthreads();
+    if (*s_last) {
+        __threadfence();
+        unsigned long long b = 0ull;
+        for (int64_t i = threadIdx.x; i < gridDim.x; i += kThreads) {
+            b = umax64(b, __ldcg(p.partial + i));
+        }
+#pragma unroll
+        for (int offset = 16; offset > 0; offset >>= 1) {
+            b = umax64(b, __shfl_xor_sync(0xffffffffu, b, offset));
+        }
+        __syncthreads();
+        if (lane == 0) {
+            s_best[warp] = b;
+        }
+        __syncthreads();
+        if (threadIdx.x == 0) {
+            unsigned long long all = s_best[0];
+#pragma unroll
+            for (int w = 1; w < kWarps; ++w) {
+                all = umax64(all, s_best[w]);
+            }
+            int64_t index = 0;
+            if (all != ~0ull && all != 0ull) {
+                index = static_cast<int64_t>(0xffffffffull - (all & 0xffffffffull));
+            }
+            const int base = *p.position_out;
+            p.tokens_out[base + p.advance] = index;
+            *p.position_out = base + static_cast<int>(p.advance);
+            *p.counter = 0u;
+        }
+    }
+}
+
+// Fast single-row kernel for K = 256 * kC: every lane holds exactly kC chunks of the input (in registers) and of
+// each weight row, so a warp's whole row group is one batch of loads. The input row is normalised inside each
+// warp (the lane partial over its chunks is the canonical one), with no shared memory and no block barrier. One
+// CTA per SM, so the next kernel in the stream (launched early) can prefetch its weights on the same SM.
+template <LinearEpilogue kEpi, int kC, int kRows>
+__global__ void __launch_bounds__(kThreads, 2) gemv_fast_kernel(const LinearParams p) {
+    __shared__ unsigned long long s_best[kWarps];
+    __shared__ int s_last;
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+
+    constexpr int kMats = mats_of<kEpi>();
+    constexpr int kSlots = kRows * kMats;
+    const int lane = threadIdx.x & 31;
+    const int warp = threadIdx.x >> 5;
+    const int64_t groups = (p.N + kRows - 1) / kRows;
+    const int64_t gstride = static_cast<int64_t>(gridDim.x) * kWarps;
+    int64_t g = static_cast<int64_t>(blockIdx.x) * kWarps + warp;
+    constexpr int64_t kRowBytes = kC * 32 * 16;
+
+    uint4 wv[kSlots][kC];
+    auto issue = [&](int64_t grp) {
+#pragma unroll
+        for (int r = 0; r < kRows; ++r) {
+            const int64_t n = grp * kRows + r;
+#pragma unroll
+            for (int mat = 0; mat < kMats; ++mat) {
+                const char* wrow = reinterpret_cast<const char*>(mat == 0 ? p.w0 : p.w1) + n * kRowBytes;
+#pragma unroll
+                for (int i = 0; i < kC; ++i) {
+                    wv[r * kMats + mat][i] = n < p.N ? ld_stream(wrow + (lane + 32 * i) * 16) : make_uint4(0u, 0u, 0u, 0u);
+                }
+            }
+        }
+    };
+    if (g < groups) {
+        issue(g);
+    }
+
+    asm volatile("griddepcontrol.wait;" ::: "memory");
+
+    const int64_t pos = p.position != nullptr ? static_cast<int64_t>(*p.position) : 0;
+    const bf16* xrow = input_row(p, 0, pos);
+    // Up to 4 chunks per lane the input row stays in registers (and may be normalised); longer rows are re-read
+    // from L1 chunk by chunk while multiplying.
+    constexpr bool kHoldX = kC <= 4;
+    uint4 xv[kHoldX ? kC : 1];
+    if constexpr (kHoldX) {
+#pragma unroll
+        for (int i = 0; i < kC; ++i) {
+            xv[i] = ld_cached(xrow + (lane + 32 * i) * 8);
+        }
+        if (p.x_copy != nullptr && blockIdx.x == 0 && warp == 0) {
+#pragma unroll
+            for (int i = 0; i < kC; ++i) {
+                st_v4(p.x_copy + (lane + 32 * i) * 8, xv[i]);
+            }
+        }
+        if (p.norm_weight != nullptr) {
+            // ops::rms_norm of the row: lane l's chunks are l, l + 32, ..., so its partial is the canonical one.
+            float s = 0.0f;
+#pragma unroll
+            for (int i = 0; i < kC; ++i) {
+                float f[8];
+                Vec16<bf16>::unpack(xv[i], f);
+#pragma unroll
+                for (int e = 0; e < 8; ++e) {
+                    s = s + f[e] * f[e];
+                }
+            }
+            s = group_sum<32>(s);
+            const float mean = s / static_cast<float>(kC * 256);
+            const float rms = sqrtf(mean + p.eps);
+            const float inv = 1.0f / rms;
+#pragma unroll
+            for (int i = 0; i < kC; ++i) {
+                float f[8];
+                float w[8];
+                Vec16<bf16>::unpack(xv[i], f);
+                Vec16<bf16>::unpack(ld_cached(p.norm_weight + (lane + 32 * i) * 8), w);
+#pragma unroll
+                for (int e = 0; e < 8; ++e) {
+                    f[e] = (f[e] * inv) * w[e];
+                }
+                xv[i] = Vec16<bf16>::pack(f);
+            }
+        }
+    }
+
+    unsigned long long best = 0ull;
+    bool first = true;
+    for (; g < groups; g += gstride) {
+        if (!first) {
+            issue(g);
+        }
+        first = false;
+        float acc[kSlots];
+#pragma unroll
+        for (int j = 0; j < kSlots; ++j) {
+            acc[j] = 0.0f;
+        }
+#pragma unroll
+        for (int i = 0; i < kC; ++i) {
+            uint4 x;
+            if constexpr (kHoldX) {
+                x = xv[i];
+            } else {
+                x = ld_cached(xrow + (lane + 32 * i) * 8);
+            }
+#pragma unroll
+            for (int j = 0; j < kSlots; ++j) {
+                acc[j] = dot_chunk(x, wv[j][i], acc[j]);
+            }
+        }
+#pragma unroll
+        for (int j = 0; j < kSlots; ++j) {
+            acc[j] = group_sum<32>(acc[j]);
+        }
+        gemv_epilogue<kEpi, kRows>(p, g, acc, lane, pos, best);
+    }
+    if constexpr (kEpi == LinearEpilogue::kArgmax) {
+        argmax_finish(p, best, s_best, &s_last);
+    }
+}
+
 template <LinearEpilogue kEpi, int kRows>
 __global__ void __launch_bounds__(kThreads, 2) gemv_kernel(const LinearParams p) {
     extern __shared__ uint4 smem_x[];  // the input row, K / 8 chunks
@@ -216,82 +432,10 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_kernel(const LinearParams p)
         for (int j = 0; j < kSlots; ++j) {
             acc[j] = group_sum<32>(acc[j]);
         }
-#pragma unroll
-        for (int r = 0; r < kRows; ++r) {
-            const int64_t n = g * kRows + r;
-            if (n >= p.N) {
-                break;
-            }
-            if constexpr (kEpi == LinearEpilogue::kArgmax) {
-                const float logit = round_to_bf16(acc[r]);
-                best = umax64(best, logit_key(logit, n));
-                if (lane == r && p.out[0] != nullptr) {
-                    store_segment(p, 0, n, logit, 0);
-                }
-            } else if (lane == r) {
-                if constexpr (kEpi == LinearEpilogue::kStore) {
-                    store_segment(p, 0, n, acc[r], pos);
-                } else if constexpr (kEpi == LinearEpilogue::kResidual) {
-                    const float res = Vec16<bf16>::load1(p.residual, n);
-                    Vec16<bf16>::store1(p.out[0], n, res + round_to_bf16(acc[r]));
-                } else {
-                    const float gate = round_to_bf16(acc[r * 2]);
-                    const float up = round_to_bf16(acc[r * 2 + 1]);
-                    Vec16<bf16>::store1(p.out[0], n, round_to_bf16(silu_pexp(gate)) * up);
-                }
-            }
-        }
+        gemv_epilogue<kEpi, kRows>(p, g, acc, lane, pos, best);
     }
-
     if constexpr (kEpi == LinearEpilogue::kArgmax) {
-        // Every lane holds the same `best`; combine the warps, then the CTAs (the last CTA to arrive).
-        if (lane == 0) {
-            s_best[warp] = best;
-        }
-        __syncthreads();
-        if (threadIdx.x == 0) {
-            unsigned long long b = s_best[0];
-#pragma unroll
-            for (int w = 1; w < kWarps; ++w) {
-                b = umax64(b, s_best[w]);
-            }
-            p.partial[blockIdx.x] = b;
-            __threadfence();
-            const unsigned ticket = atomicAdd(p.counter, 1u);
-            s_last = ticket == gridDim.x - 1 ? 1 : 0;
-        }
-        __syncthreads();
-        if (s_last) {
-            __threadfence();
-            unsigned long long b = 0ull;
-            for (int64_t i = threadIdx.x; i < gridDim.x; i += kThreads) {
-                b = umax64(b, __ldcg(p.partial + i));
-            }
-#pragma unroll
-            for (int offset = 16; offset > 0; offset >>= 1) {
-                b = umax64(b, __shfl_xor_sync(0xffffffffu, b, offset));
-            }
-            __syncthreads();
-            if (lane == 0) {
-                s_best[warp] = b;
-            }
-            __syncthreads();
-            if (threadIdx.x == 0) {
-                unsigned long long all = s_best[0];
-#pragma unroll
-                for (int w = 1; w < kWarps; ++w) {
-                    all = umax64(all, s_best[w]);
-                }
-                int64_t index = 0;
-                if (all != ~0ull && all != 0ull) {
-                    index = static_cast<int64_t>(0xffffffffull - (all & 0xffffffffull));
-                }
-                const int base = *p.position_out;
-                p.tokens_out[base + p.advance] = index;
-                *p.position_out = base + static_cast<int>(p.advance);
-                *p.counter = 0u;
-            }
-        }
+        argmax_finish(p, best, s_best, &s_last);
     }
 }
 
@@ -391,23 +535,78 @@ __global__ void __launch_bounds__(kThreads) embedding_kernel(const bf16* table, 
     }
 }
 
-template <LinearEpilogue kEpi, int kRows>
-int gemv_grid_for(const LinearParams& p) {
-    const int64_t groups = (p.N + kRows - 1) / kRows;
+// Launch plan of the single-row kernels. K = 256 * c with c in {1, 2, 3, 4, 6, 8, 12} (c <= 4 with the RMSNorm
+// prologue or the input copy) takes the fast kernel with
+// kRows rows per warp (a lane's whole row group, kRows * mats * c 16-byte loads, in flight at once); other K take
+// the generic kernel. Grids: one CTA per SM, two for the vocabulary-sized argmax head.
+struct GemvPlan {
+    bool fast;
+    int chunks;  // c
+    int rows;    // kRows
+    int grid;
+};
+
+GemvPlan plan_gemv(const LinearParams& p, int mats) {
+    GemvPlan plan{};
+    const int64_t c = p.K % 256 == 0 ? p.K / 256 : 0;
+    plan.fast = c == 1 || c == 2 || c == 3 || c == 4 || c == 6 || c == 8 || (c == 12 && mats == 1);
+    if (c > 4 && (p.norm_weight != nullptr || p.x_copy != nullptr)) {
+        plan.fast = false;  // the fast kernel keeps (and normalises) the input in registers only up to K = 1024
+    }
+    if (plan.fast) {
+        plan.chunks = static_cast<int>(c);
+        const int64_t r = kLoads / (mats * c);
+        plan.rows = r >= 4 ? 4 : (r >= 2 ? 2 : 1);
+    } else {
+        const int64_t per_lane = (p.K / 8 + 31) / 32;
+        const int64_t r = kLoads / (mats * (per_lane < 1 ? 1 : per_lane));
+        plan.rows = r >= 4 ? 4 : (r >= 2 ? 2 : 1);
+    }
+    const int64_t groups = (p.N + plan.rows - 1) / plan.rows;
     const int64_t want = (groups + kWarps - 1) / kWarps;
-    const int64_t cap = static_cast<int64_t>(runtime::sm_count()) * 2;
-    return static_cast<int>(want < cap ? want : cap);
+    const int64_t per_sm = p.epilogue == LinearEpilogue::kArgmax || !plan.fast ? 2 : 1;
+    const int64_t cap = static_cast<int64_t>(runtime::sm_count()) * per_sm;
+    plan.grid = static_cast<int>(want < cap ? want : cap);
+    return plan;
 }
 
-// Rows per warp so that a lane keeps about kLoads 16-byte loads in flight.
-int rows_for(const LinearParams& p, int mats) {
-    const int64_t per_lane = (p.K / 8 + 31) / 32;
-    const int64_t rows = kLoads / (mats * (per_lane < 1 ? 1 : per_lane));
-    return rows >= 4 ? 4 : (rows >= 2 ? 2 : 1);
+template <LinearEpilogue kEpi, int kC, int kRows>
+cudaError_t launch_fast(const LinearParams& p, int grid, cudaStream_t s) {
+    return runtime::launch(gemv_fast_kernel<kEpi, kC, kRows>, dim3(grid), dim3(kThreads), s, 1u, p);
+}
+
+template <LinearEpilogue kEpi, int kC>
+cudaError_t launch_fast_rows(const LinearParams& p, const GemvPlan& plan, cudaStream_t s) {
+    constexpr int kMats = mats_of<kEpi>();
+    constexpr int kR = kLoads / (kMats * kC) >= 4 ? 4 : (kLoads / (kMats * kC) >= 2 ? 2 : 1);
+    return launch_fast<kEpi, kC, kR>(p, plan.grid, s);
+}
+
+template <LinearEpilogue kEpi>
+cudaError_t launch_fast_epi(const LinearParams& p, const GemvPlan& plan, cudaStream_t s) {
+    switch (plan.chunks) {
+    case 1:
+        return launch_fast_rows<kEpi, 1>(p, plan, s);
+    case 2:
+        return launch_fast_rows<kEpi, 2>(p, plan, s);
+    case 3:
+        return launch_fast_rows<kEpi, 3>(p, plan, s);
+    case 4:
+        return launch_fast_rows<kEpi, 4>(p, plan, s);
+    case 6:
+        return launch_fast_rows<kEpi, 6>(p, plan, s);
+    case 8:
+        return launch_fast_rows<kEpi, 8>(p, plan, s);
+    default:
+        if constexpr (mats_of<kEpi>() == 1) {
+            return launch_fast_rows<kEpi, 12>(p, plan, s);
+        }
+        return cudaErrorInvalidValue;
+    }
 }
 
 template <LinearEpilogue kEpi, int kRows>
-cudaError_t launch_gemv_rows(const LinearParams& p, cudaStream_t s) {
+cudaError_t launch_gemv_rows(const LinearParams& p, int grid, cudaStream_t s) {
     const std::size_t smem = static_cast<std::size_t>(p.K) * 2;
     auto kernel = gemv_kernel<kEpi, kRows>;
     if (smem > 48 * 1024) {
@@ -417,18 +616,22 @@ cudaError_t launch_gemv_rows(const LinearParams& p, cudaStream_t s) {
             return err;
         }
     }
-    return runtime::launch_smem(kernel, dim3(gemv_grid_for<kEpi, kRows>(p)), dim3(kThreads), smem, s, 1u, p);
+    return runtime::launch_smem(kernel, dim3(grid), dim3(kThreads), smem, s, 1u, p);
 }
 
 template <LinearEpilogue kEpi>
 cudaError_t launch_gemv_epi(const LinearParams& p, cudaStream_t s) {
-    switch (rows_for(p, kEpi == LinearEpilogue::kSiluMul ? 2 : 1)) {
+    const GemvPlan plan = plan_gemv(p, mats_of<kEpi>());
+    if (plan.fast) {
+        return launch_fast_epi<kEpi>(p, plan, s);
+    }
+    switch (plan.rows) {
     case 4:
-        return launch_gemv_rows<kEpi, 4>(p, s);
+        return launch_gemv_rows<kEpi, 4>(p, plan.grid, s);
     case 2:
-        return launch_gemv_rows<kEpi, 2>(p, s);
+        return launch_gemv_rows<kEpi, 2>(p, plan.grid, s);
     default:
-        return launch_gemv_rows<kEpi, 1>(p, s);
+        return launch_gemv_rows<kEpi, 1>(p, plan.grid, s);
     }
 }
 
@@ -454,14 +657,9 @@ cudaError_t launch_rows_epi(const LinearParams& p, cudaStream_t s) {
 }  // namespace
 
 int gemv_grid(const LinearParams& p) {
-    switch (rows_for(p, 1)) {
-    case 4:
-        return gemv_grid_for<LinearEpilogue::kArgmax, 4>(p);
-    case 2:
-        return gemv_grid_for<LinearEpilogue::kArgmax, 2>(p);
-    default:
-        return gemv_grid_for<LinearEpilogue::kArgmax, 1>(p);
-    }
+    LinearParams q = p;
+    q.epilogue = LinearEpilogue::kArgmax;
+    return plan_gemv(q, 1).grid;
 }
 
 cudaError_t launch_gemv(const LinearParams& p, cudaStream_t s) {

@@ -12,8 +12,9 @@
 // projection (v rows written straight into the cache), fused q/k-norm + RoPE (k rows into the cache), attention,
 // o_proj with the residual add, rms_norm, gate/up with SiLU * up, down_proj with the residual add -- and finally
 // the last row's final norm + LM head + argmax in one kernel.
-// decode(): one step is 6 kernels per layer + 1 (QKV with the input norm and, in layer 0, the embedding gather;
-// q/k-norm + RoPE; attention; o_proj + residual; gate/up with the post-attention norm and SiLU * up;
+// decode(): one step is 5 kernels per layer + 1 (QKV with the input norm and, in layer 0, the embedding gather;
+// attention with the q/k-norm + RoPE of the new token fused in; o_proj + residual; gate/up with the
+// post-attention norm and SiLU * up;
 // down_proj + residual; final norm + LM head + argmax), captured once as a CUDA graph. Every kernel reads the
 // sequence length from device memory, and the last one advances it, so the same graph is replayed for every step.
 #include <cstring>
@@ -171,15 +172,11 @@ int enqueue_step(cppinf_qwen3* m, cudaStream_t s, int64_t* launches) {
         qkv.eps = c.rms_norm_eps;
         set_qkv_outputs(m, l, qkv, 0, m->d_len);
         QWEN3_TRY(cppinf::device::launch_gemv(qkv, s), "qwen3_qkv");
-        QWEN3_TRY(cppinf::device::launch_qk_norm_rope_at(m->q, m->k, l.q_norm, l.k_norm, m->qr, l.k_cache, 1,
-                                                         static_cast<int>(c.num_attention_heads),
-                                                         static_cast<int>(c.num_key_value_heads),
-                                                         static_cast<int>(c.head_dim), m->d_len, c.rms_norm_eps,
-                                                         m->rope, m->cap, s),
-                  "qwen3_qk_norm_rope");
-        AttentionParams ap{m->qr, l.k_cache, l.v_cache, m->ctx, 1,
+        // q/k-norm + RoPE and the new key's cache row are fused into the attention kernel.
+        AttentionParams ap{m->q, l.k_cache, l.v_cache, m->ctx, 1,
                            static_cast<int>(c.num_attention_heads), static_cast<int>(c.num_key_value_heads),
-                           static_cast<int>(c.head_dim), 0, m->d_len, m->cap};
+                           static_cast<int>(c.head_dim), 0, m->d_len, m->cap,
+                           m->k, l.q_norm, l.k_norm, m->rope, c.rms_norm_eps};
         QWEN3_TRY(cppinf::device::launch_decoder_attention(ap, m->cap, s), "qwen3_attention");
         LinearParams o = params_for(LinearEpilogue::kResidual, m->ctx, m->q_dim, l.wo, nullptr, 1, H, m->q_dim);
         o.residual = m->h;
@@ -200,7 +197,7 @@ int enqueue_step(cppinf_qwen3* m, cudaStream_t s, int64_t* launches) {
         d.out[0] = m->h;
         d.ld[0] = H;
         QWEN3_TRY(cppinf::device::launch_gemv(d, s), "qwen3_down_proj");
-        n += 6;
+        n += 5;
     }
     QWEN3_TRY(cppinf::device::launch_gemv(lm_head_params(m, m->h, 1, nullptr), s), "qwen3_lm_head_argmax");
     *launches = n + 1;
@@ -510,7 +507,7 @@ int64_t cppinf_qwen3_length(const cppinf_qwen3* model) {
 }
 
 int64_t cppinf_qwen3_step_launches(const cppinf_qwen3* model) {
-    return model != nullptr ? 6 * model->c.num_hidden_layers + 1 : 0;
+    return model != nullptr ? 5 * model->c.num_hidden_layers + 1 : 0;
 }
 
 int cppinf_qwen3_forward(cppinf_qwen3* model, const int64_t* token_ids, int64_t count, void* logits, int all_rows,

@@ -75,14 +75,29 @@ def f32_to_bf16_bits(x: np.ndarray) -> np.ndarray:
 def random_weights(config: Qwen3Config, seed: int = 0, std: float = 0.02) -> dict[str, np.ndarray]:
     """Seeded random initialisation: matrices ~N(0, std) rounded to bf16, norm weights 1.0 (bf16 0x3f80).
 
-    Tensor i draws from numpy's PCG64 seeded with (seed, i), so the arrays do not depend on generation order."""
+    Rows [4096 b, 4096 (b + 1)) of tensor i (in weight_shapes() order) draw from numpy's PCG64 seeded with
+    (seed, i, b), so the values do not depend on generation order; the blocks are generated on a thread pool."""
+    import os
+    from concurrent.futures import ThreadPoolExecutor
+
+    block = 4096
     out: dict[str, np.ndarray] = {}
+    jobs = []
     for i, (name, shape) in enumerate(config.weight_shapes().items()):
         if len(shape) == 1:
             out[name] = np.full(shape, 0x3F80, dtype=np.uint16)
             continue
-        rng = np.random.Generator(np.random.PCG64([seed, i]))
-        out[name] = f32_to_bf16_bits(rng.standard_normal(shape, dtype=np.float32) * np.float32(std))
+        out[name] = np.empty(shape, dtype=np.uint16)
+        jobs += [(name, i, b) for b in range((shape[0] + block - 1) // block)]
+
+    def fill(job):
+        name, i, b = job
+        dst = out[name][b * block:(b + 1) * block]
+        rng = np.random.Generator(np.random.PCG64([seed, i, b]))
+        dst[...] = f32_to_bf16_bits(rng.standard_normal(dst.shape, dtype=np.float32) * np.float32(std))
+
+    with ThreadPoolExecutor(max(1, min(16, os.cpu_count() or 1))) as pool:
+        list(pool.map(fill, jobs))
     return out
 
 
