@@ -19,6 +19,9 @@
 //
 // Roofline: the decode projections are HBM-bound on the weights (N * K * 2 bytes per token); the prefill tiles are
 // bound by f32 issue (two instructions per multiply-add with separately rounded operations).
+#include <mutex>
+#include <string>
+
 #include "common.cuh"
 #include "decoder.h"
 #include "pexp.cuh"
@@ -707,6 +710,36 @@ namespace {
 
 constexpr int64_t kScratchHeader = 16;  // u32 counter, i32 position slot, padding; then one u64 per CTA
 
+// Scratch of cppinf_linear_argmax_noalloc: one per device, in the module's static device memory, which the CUDA
+// runtime zero-fills when it loads the module on a device (the counter and position slot must start at zero; each
+// call leaves them zero). Room for 1024 CTAs, four times the grid of a 148-SM B200.
+constexpr int64_t kStaticScratchCtas = 1024;
+static __device__ __align__(256) unsigned char g_argmax_scratch[kScratchHeader + 8 * kStaticScratchCtas];
+
+// Device address of g_argmax_scratch on the current device, looked up once per device.
+cudaError_t static_argmax_scratch(void** out) {
+    constexpr int kMaxDevices = 64;
+    static std::mutex mu;
+    static void* addresses[kMaxDevices] = {};
+    int device = 0;
+    cudaError_t err = cudaGetDevice(&device);
+    if (err != cudaSuccess) {
+        return err;
+    }
+    if (device < 0 || device >= kMaxDevices) {
+        return cudaErrorInvalidDevice;
+    }
+    std::lock_guard<std::mutex> lock(mu);
+    if (addresses[device] == nullptr) {
+        err = cudaGetSymbolAddress(&addresses[device], g_argmax_scratch);
+        if (err != cudaSuccess) {
+            return err;
+        }
+    }
+    *out = addresses[device];
+    return cudaSuccess;
+}
+
 int check_linear(const void* x, int64_t x_row_stride, const void* weight, const void* y, int64_t rows,
                  int64_t in_features, int64_t out_features) {
     CPPINF_REQUIRE(rows >= 0 && in_features > 0 && out_features >= 0, CPPINF_ERR_INVALID_ARGUMENT,
@@ -819,6 +852,24 @@ int cppinf_linear_argmax(const void* x, const void* weight, void* logits, int64_
     p.tokens_out = out_token;
     p.advance = 0;
     return run_linear(p, stream, "linear_argmax");
+}
+
+int cppinf_linear_argmax_noalloc(const void* x, const void* weight, void* logits, int64_t in_features,
+                                 int64_t out_features, int64_t* out_token, void* stream) {
+    CPPINF_REQUIRE(out_features > 0, CPPINF_ERR_INVALID_ARGUMENT, "logits vocab size must be non-zero.");
+    const int st = check_linear(x, in_features, weight, out_token, 1, in_features, out_features);
+    if (st != CPPINF_OK) {
+        return st;
+    }
+    const int64_t needed = cppinf_linear_argmax_scratch_bytes(out_features, in_features);
+    const auto capacity = static_cast<int64_t>(sizeof(g_argmax_scratch));
+    CPPINF_REQUIRE(needed <= capacity, CPPINF_ERR_UNSUPPORTED,
+                   "linear_argmax_noalloc needs " + std::to_string(needed) + " bytes of scratch for this launch but "
+                       "its static scratch holds " + std::to_string(capacity) + " bytes; use cppinf_linear_argmax "
+                       "with a caller-provided scratch.");
+    void* scratch = nullptr;
+    CPPINF_CUDA_TRY(static_argmax_scratch(&scratch));
+    return cppinf_linear_argmax(x, weight, logits, in_features, out_features, out_token, scratch, stream);
 }
 
 int cppinf_embedding(const void* table, int64_t vocab, int64_t hidden, const int64_t* token_ids, int64_t count,

@@ -390,6 +390,19 @@ def linear_argmax(input: torch.Tensor, weight: torch.Tensor, with_logits: bool =
     return (token, logits) if with_logits else token
 
 
+def linear_argmax_noalloc(input: torch.Tensor, weight: torch.Tensor, with_logits: bool = False):
+    """linear_argmax with the library's static per-device scratch (cppinf_linear_argmax_noalloc): no scratch tensor
+    is allocated. Calls on one device must not overlap in time (one stream, or synchronised)."""
+    x, rows, fin, fout = _validate_linear(input, weight, "linear_argmax")
+    if rows != 1:
+        raise ValueError("linear_argmax takes a single row.")
+    token = torch.empty(1, dtype=torch.int64, device=input.device)
+    logits = torch.empty(fout, dtype=torch.bfloat16, device=input.device) if with_logits else None
+    capi.call("cppinf_linear_argmax_noalloc", x.data_ptr(), materialize(weight).data_ptr(),
+              logits.data_ptr() if logits is not None else None, fin, fout, token.data_ptr(), _stream())
+    return (token, logits) if with_logits else token
+
+
 def decoder_attention(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tensor, position: int) -> torch.Tensor:
     """Causal GQA attention of one sequence (src/nn/qwen_attention.cpp:236-333): q [T, Hq, D] at positions
     position .. position + T - 1, caches [capacity, Hkv, D]; returns the bf16 context [T, Hq, D]."""

@@ -200,6 +200,16 @@ CPPINF_API int cppinf_linear_argmax(const void* x, const void* weight, void* log
                                     int64_t out_features, int64_t* out_token, void* scratch, void* stream);
 CPPINF_API int64_t cppinf_linear_argmax_scratch_bytes(int64_t out_features, int64_t in_features);
 
+/* cppinf_linear_argmax without a caller-provided scratch: the per-CTA maxima and the arrival counter live in a
+ * static device array of this library (one per device, zero-filled when the module loads; every call leaves the
+ * counter at zero again). No device memory is allocated. This entry point has no counterpart in the reference (its
+ * CLI argmax runs on host logits and needs no scratch). Limits: the launch must fit the static scratch (1024 CTAs,
+ * 8208 bytes; CPPINF_ERR_UNSUPPORTED with the sizes in the message otherwise). Calls on one device share the
+ * scratch, so two calls that overlap in time -- on different streams, or from different threads without ordering
+ * -- race and may return a wrong token; issue them on one stream or synchronise between them. */
+CPPINF_API int cppinf_linear_argmax_noalloc(const void* x, const void* weight, void* logits, int64_t in_features,
+                                            int64_t out_features, int64_t* out_token, void* stream);
+
 /* Causal grouped-query attention of one sequence over its KV cache: fused_causal_attention of
  * src/nn/qwen_attention.cpp:236-333 with the position-causal softmax of :164-235. q [tokens, q_heads, head_dim]
  * (after q-norm and RoPE), k_cache/v_cache [capacity, kv_heads, head_dim], ctx [tokens, q_heads, head_dim], all
