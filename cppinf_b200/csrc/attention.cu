@@ -83,10 +83,11 @@ __device__ __forceinline__ float dot8(uint4 a, uint4 b, float acc) {
 // Per-head RMSNorm + RoPE of one raw head vector into shared memory, with exactly the arithmetic of
 // qk_norm_rope_kernel (rope.cu): kD / 16 lanes, lane hl holding dims [8 hl, 8 hl + 8) and the matching dims of the
 // second half; the sum of squares in the canonical lane order; normalised values rounded to bf16; then
-// (first * cos - second * sin, second * cos + first * sin) rounded to bf16 (src/nn/rope.cpp:115-118).
+// (first * cos - second * sin, second * cos + first * sin) rounded to bf16 (src/nn/rope.cpp:115-118). The weights
+// (w_first, w_second) and the angles (c, s) of the lane's pairs are loaded by the caller.
 template <int kD>
-__device__ __forceinline__ void norm_rope_head(const bf16* src, const bf16* weight, const float* table_row,
-                                               float eps, bf16* dst, int lane) {
+__device__ __forceinline__ void norm_rope_head(const bf16* src, uint4 w_first, uint4 w_second, const float (&c)[8],
+                                               const float (&s)[8], float eps, bf16* dst, int lane) {
     constexpr int kLanes = kD / 16;
     constexpr int kHalf = kD / 2;
     const int hl = lane % kLanes;
@@ -110,18 +111,16 @@ __device__ __forceinline__ void norm_rope_head(const bf16* src, const bf16* weig
     const float inv = 1.0f / rms;
     float wa[8];
     float wb[8];
-    Vec16<bf16>::unpack(ld_cached(weight + hl * 8), wa);
-    Vec16<bf16>::unpack(ld_cached(weight + kHalf + hl * 8), wb);
+    Vec16<bf16>::unpack(w_first, wa);
+    Vec16<bf16>::unpack(w_second, wb);
     float out_a[8];
     float out_b[8];
 #pragma unroll
     for (int j = 0; j < 8; ++j) {
-        const float c = table_row[hl * 8 + j];
-        const float s = table_row[kHalf + hl * 8 + j];
         const float n1 = round_to_bf16((a[j] * inv) * wa[j]);
         const float n2 = round_to_bf16((b[j] * inv) * wb[j]);
-        out_a[j] = n1 * c - n2 * s;
-        out_b[j] = n2 * c + n1 * s;
+        out_a[j] = n1 * c[j] - n2 * s[j];
+        out_b[j] = n2 * c[j] + n1 * s[j];
     }
     if (lane < kLanes) {
         *reinterpret_cast<uint4*>(dst + hl * 8) = Vec16<bf16>::pack(out_a);
@@ -129,8 +128,8 @@ __device__ __forceinline__ void norm_rope_head(const bf16* src, const bf16* weig
     }
 }
 
-template <int kD, bool kFused>
-__global__ void __launch_bounds__(kThreads) decoder_attention_kernel(const AttentionParams p) {
+template <int kD, bool kFused, bool kStage>
+__global__ void __launch_bounds__(kThreads) decoder_attention_kernel(const AttentionParams p, int64_t max_part) {
     constexpr int kSeg = kD / kSegments;       // dims per score segment
     constexpr int kSegChunks = kSeg / 8;       // 16-byte chunks per segment
     constexpr int kKeysPerIter = 32 / kSegments;
@@ -138,7 +137,9 @@ __global__ void __launch_bounds__(kThreads) decoder_attention_kernel(const Atten
     constexpr int kFinal = kD / kParts;        // context dims each CTA finishes
     constexpr int kScoreBatch = 4;             // warp iterations of score loads issued together
     constexpr int kValueBatch = 8;             // V rows a warp loads together
-    extern __shared__ float s_e[];             // this part's scores, then exp values, then probabilities
+    // Dynamic shared memory: this part's scores (then exp values, then probabilities), and with kStage the part's
+    // cached key and value rows.
+    extern __shared__ __align__(16) float s_e[];
     __shared__ float s_red[kWarps];
     __shared__ float s_max;
     __shared__ float s_sum;
@@ -146,8 +147,8 @@ __global__ void __launch_bounds__(kThreads) decoder_attention_kernel(const Atten
     __shared__ float s_part[kD];
     __shared__ __align__(16) bf16 s_q[kFused ? kD : 8];
     __shared__ __align__(16) bf16 s_knew[kFused ? kD : 8];
+    __shared__ __align__(8) uint64_t s_bar;
 
-    grid_dependency_begin();
     cg::cluster_group cluster = cg::this_cluster();
     const int rank = static_cast<int>(cluster.block_rank());
     const int lane = threadIdx.x & 31;
@@ -157,8 +158,14 @@ __global__ void __launch_bounds__(kThreads) decoder_attention_kernel(const Atten
     const int h = static_cast<int>(unit - t * p.q_heads);
     const int group = p.q_heads / p.kv_heads;
     const int kvh = h / group;
+    if constexpr (!kStage) {
+        grid_dependency_begin();
+    }
     const int64_t pos = p.pos0 + (p.position != nullptr ? static_cast<int64_t>(*p.position) : 0) + t;
     if (pos >= p.capacity) {
+        if constexpr (kStage) {
+            grid_dependency_begin();
+        }
         return;  // the whole cluster leaves together (same t); no DSMEM access happens
     }
     const int64_t L = pos + 1;
@@ -169,19 +176,71 @@ __global__ void __launch_bounds__(kThreads) decoder_attention_kernel(const Atten
     const int64_t kv_row = static_cast<int64_t>(p.kv_heads) * kD;
     const float scale = 1.0f / sqrtf(static_cast<float>(kD));
 
+    // kStage: rows [lo, staged_hi) (every cached row of this part before the new token) go to shared memory now;
+    // the previous kernel in the stream writes neither them nor the sequence length.
+    bf16* s_kt = reinterpret_cast<bf16*>(s_e + ((max_part + 3) / 4) * 4);
+    bf16* s_vt = s_kt + max_part * kD;
+    const int64_t staged_hi = hi < pos ? hi : pos;
+    const int64_t staged = staged_hi > lo ? staged_hi - lo : 0;
+    float c_rope[kFused ? 8 : 1];
+    float s_rope[kFused ? 8 : 1];
+    uint4 wq_a, wq_b, wk_a, wk_b;
+    if constexpr (kStage) {
+        if (threadIdx.x == 0) {
+            mbar_init(&s_bar, 1);
+            mbar_arrive_expect_tx(&s_bar, static_cast<uint32_t>(staged * kD * 2 * 2));
+        }
+        __syncthreads();
+        if (warp == 0) {
+            for (int64_t r = lane; r < staged; r += 32) {
+                const int64_t off = (lo + r) * kv_row + kvh * kD;
+                bulk_copy_g2s(s_kt + r * kD, p.k_cache + off, kD * 2, &s_bar);
+                bulk_copy_g2s(s_vt + r * kD, p.v_cache + off, kD * 2, &s_bar);
+            }
+        }
+    }
+    if constexpr (kFused) {
+        // RoPE angles of this position and the q/k norm weights: constants, read before the wait.
+        constexpr int kLanes = kD / 16;
+        const int hl = lane % kLanes;
+        const float* trow = p.rope_table + pos * kD;
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+            c_rope[j] = trow[hl * 8 + j];
+            s_rope[j] = trow[kD / 2 + hl * 8 + j];
+        }
+        wq_a = ld_cached(p.q_norm + hl * 8);
+        wq_b = ld_cached(p.q_norm + kD / 2 + hl * 8);
+        wk_a = ld_cached(p.k_norm + hl * 8);
+        wk_b = ld_cached(p.k_norm + kD / 2 + hl * 8);
+    }
+    if constexpr (kStage) {
+        grid_dependency_begin();
+    }
+
     if constexpr (kFused) {
         // q-norm + RoPE of this head and k-norm + RoPE of the new key (computed by every CTA that needs them).
-        const float* trow = p.rope_table + pos * kD;
         if (warp == 0) {
-            norm_rope_head<kD>(p.q + (t * p.q_heads + h) * kD, p.q_norm, trow, p.eps, s_q, lane);
+            norm_rope_head<kD>(p.q + (t * p.q_heads + h) * kD, wq_a, wq_b, c_rope, s_rope, p.eps, s_q, lane);
         } else if (warp == 1) {
-            norm_rope_head<kD>(p.k_new + (t * p.kv_heads + kvh) * kD, p.k_norm, trow, p.eps, s_knew, lane);
+            norm_rope_head<kD>(p.k_new + (t * p.kv_heads + kvh) * kD, wk_a, wk_b, c_rope, s_rope, p.eps, s_knew,
+                               lane);
         }
         __syncthreads();
         if (rank == 0 && h % group == 0 && threadIdx.x < kD / 8) {
             // One CTA per key/value head stores the new key row; nobody reads that row in this launch.
             st_v4(const_cast<bf16*>(p.k_cache) + pos * kv_row + kvh * kD + threadIdx.x * 8,
                   *reinterpret_cast<const uint4*>(s_knew + threadIdx.x * 8));
+        }
+    }
+    bool stage_failed = false;
+    if constexpr (kStage) {
+        const bool arrived = mbar_wait_bounded(&s_bar, 0);
+        // On a timeout the kernel still runs every cluster barrier below (with meaningless values), so no CTA of
+        // the cluster is left waiting; the host sees the error flag.
+        stage_failed = __syncthreads_or(arrived ? 0 : 1) != 0;
+        if (stage_failed && threadIdx.x == 0) {
+            atomicOr(p.error, 1u);
         }
     }
 
@@ -209,6 +268,8 @@ __global__ void __launch_bounds__(kThreads) decoder_attention_kernel(const Atten
                     kv[u][c] = make_uint4(0u, 0u, 0u, 0u);
                 } else if (kFused && j == L - 1) {
                     kv[u][c] = *reinterpret_cast<const uint4*>(s_knew + sub * kSeg + c * 8);
+                } else if (kStage) {
+                    kv[u][c] = *reinterpret_cast<const uint4*>(s_kt + (j - lo) * kD + sub * kSeg + c * 8);
                 } else {
                     kv[u][c] = ld_cached(p.k_cache + j * kv_row + kvh * kD + sub * kSeg + c * 8);
                 }
@@ -303,7 +364,12 @@ __global__ void __launch_bounds__(kThreads) decoder_attention_kernel(const Atten
         for (int u = 0; u < kValueBatch; ++u) {
             const int64_t j = j0 + u * kWarps;
             if (j < hi) {
-                raw[u] = VRow<kD>::load(vbase + j * kv_row);
+                if (kStage && j < staged_hi) {
+                    raw[u] = *reinterpret_cast<const typename VRow<kD>::Raw*>(s_vt + (j - lo) * kD +
+                                                                             lane * kDimsPerLane);
+                } else {
+                    raw[u] = VRow<kD>::load(vbase + j * kv_row);
+                }
             }
         }
 #pragma unroll
@@ -345,14 +411,18 @@ __global__ void __launch_bounds__(kThreads) decoder_attention_kernel(const Atten
     }
     // Keep every CTA's shared memory alive until the others have read it.
     cluster.sync();
+    if (kStage && stage_failed) {
+        mbar_wait_bounded(&s_bar, 0);  // no bulk copy may land after this CTA has left
+    }
 }
 
-template <int kD>
-cudaError_t launch_attention_dim(const AttentionParams& p, int64_t max_keys, cudaStream_t s) {
-    const int64_t per_part = (max_keys + kParts - 1) / kParts;
-    const std::size_t smem = static_cast<std::size_t>(per_part < 1 ? 1 : per_part) * sizeof(float);
-    auto kernel = p.q_norm != nullptr ? decoder_attention_kernel<kD, true> : decoder_attention_kernel<kD, false>;
-    if (smem > 32 * 1024) {
+// Staged parts up to this size leave room in the SM's shared memory for the neighbouring kernels' CTAs.
+constexpr std::size_t kMaxStagedBytes = 110 * 1024;
+
+template <int kD, bool kFused, bool kStage>
+cudaError_t launch_attention_variant(const AttentionParams& p, int64_t max_part, std::size_t smem, cudaStream_t s) {
+    auto kernel = decoder_attention_kernel<kD, kFused, kStage>;
+    if (smem > 48 * 1024) {
         const cudaError_t err =
             cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
         if (err != cudaSuccess) {
@@ -361,7 +431,22 @@ cudaError_t launch_attention_dim(const AttentionParams& p, int64_t max_keys, cud
     }
     const int64_t blocks = p.T * p.q_heads * kParts;
     return runtime::launch_smem(kernel, dim3(static_cast<unsigned>(blocks)), dim3(kThreads), smem, s,
-                                static_cast<unsigned>(kParts), p);
+                                static_cast<unsigned>(kParts), p, max_part);
+}
+
+template <int kD>
+cudaError_t launch_attention_dim(const AttentionParams& p, int64_t max_keys, cudaStream_t s) {
+    const int64_t per_part = (max_keys + kParts - 1) / kParts;
+    const int64_t max_part = per_part < 1 ? 1 : per_part;
+    const std::size_t score_bytes = static_cast<std::size_t>((max_part + 3) / 4 * 4) * sizeof(float);
+    const std::size_t staged_bytes = score_bytes + static_cast<std::size_t>(max_part) * kD * 2 * 2;
+    if (p.q_norm != nullptr) {
+        if (p.error != nullptr && p.T == 1 && staged_bytes <= kMaxStagedBytes) {
+            return launch_attention_variant<kD, true, true>(p, max_part, staged_bytes, s);
+        }
+        return launch_attention_variant<kD, true, false>(p, max_part, score_bytes, s);
+    }
+    return launch_attention_variant<kD, false, false>(p, max_part, score_bytes, s);
 }
 
 }  // namespace
@@ -424,7 +509,8 @@ int cppinf_decoder_attention(const void* q, const void* k_cache, const void* v_c
                       nullptr,
                       nullptr,
                       nullptr,
-                      0.0f};
+                      0.0f,
+                      nullptr};
     return rt::launched(launch_decoder_attention(p, position + tokens, rt::as_stream(stream)), "decoder_attention");
 }
 

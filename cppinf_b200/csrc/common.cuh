@@ -81,6 +81,59 @@ __device__ __forceinline__ void st_stream(void* ptr, uint4 v) {
                  : "memory");
 }
 
+// ---- bulk asynchronous copies (TMA engine) into shared memory, completed on an mbarrier ---------------------------
+// Plain global -> shared bulk copies of one CTA (no multicast). Addresses and sizes must be multiples of 16 bytes.
+
+__device__ __forceinline__ uint32_t smem_addr(const void* p) {
+    return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+__device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_addr(bar)), "r"(count) : "memory");
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+}
+
+// One arrival that also announces `bytes` of bulk-copy data the barrier's current phase must receive.
+__device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t* bar, uint32_t bytes) {
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_addr(bar)), "r"(bytes)
+                 : "memory");
+}
+
+__device__ __forceinline__ void bulk_copy_g2s(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
+    asm volatile(
+        "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+            smem_addr(dst)),
+        "l"(src), "r"(bytes), "r"(smem_addr(bar))
+        : "memory");
+}
+
+__device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t phase) {
+    uint32_t done;
+    asm volatile(
+        "{\n"
+        ".reg .pred p;\n"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n"
+        "selp.u32 %0, 1, 0, p;\n"
+        "}\n"
+        : "=r"(done)
+        : "r"(smem_addr(bar)), "r"(phase)
+        : "memory");
+    return done != 0;
+}
+
+// Waits for phase `phase` of `bar` with a bounded number of polls (each try_wait may itself suspend the thread for
+// a short, hardware-chosen time). Returns false if the limit ran out; the caller records the error and must not
+// use the copied data.
+__device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t phase) {
+    constexpr uint32_t kMaxPolls = 1u << 24;
+    for (uint32_t i = 0; i < kMaxPolls; ++i) {
+        if (mbar_try_wait(bar, phase)) {
+            return true;
+        }
+    }
+    return false;
+}
+
 // ---- bf16 / f32 packing ------------------------------------------------------------------------------------------
 
 __device__ __forceinline__ float bf16_lo(uint32_t packed) {

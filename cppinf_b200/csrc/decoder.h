@@ -53,6 +53,10 @@ struct LinearParams {
     int64_t advance;
     unsigned long long* partial;
     unsigned int* counter;
+
+    // Single-row kernel only: when set, the CTA's slice of weight rows is staged in shared memory by bulk copies
+    // issued before griddepcontrol.wait (if it fits), and a bounded wait that runs out sets *error to 1.
+    unsigned int* error;
 };
 
 // Single-row (decode) linear: one warp per output row at a time, the weights streamed once. Supports every
@@ -86,6 +90,11 @@ struct AttentionParams {
     const __nv_bfloat16* k_norm;
     const float* rope_table;       // [capacity, D]
     float eps;
+    // Decode steps: when set (and the part's rows fit in shared memory), the cached key/value rows before the new
+    // token are staged into shared memory by bulk copies issued before griddepcontrol.wait (the sequence length is
+    // then read before the wait too, so the preceding kernel must not write it); a bounded wait that runs out
+    // sets *error to 1.
+    unsigned int* error;
 };
 
 // Causal GQA attention of one sequence in the fixed partition order (see attention.cu). head_dim 64, 128 or 256.

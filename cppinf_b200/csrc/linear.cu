@@ -312,6 +312,147 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_fast_kernel(const LinearPara
     }
 }
 
+// Single-row kernel with the CTA's slice of weight rows (rows_per_cta rows of every matrix, contiguous in the
+// checkpoint layout) staged in shared memory by bulk copies that thread 0 issues before griddepcontrol.wait. Under
+// programmatic dependent launch the CTA starts while the previous kernel is still running, so the slice streams
+// from HBM during the previous kernel instead of after it. After the wait the input row is read (and normalised)
+// as in gemv_fast_kernel and each warp takes rows r, r + 8, ... of the slice from shared memory.
+template <LinearEpilogue kEpi, int kC>
+__global__ void __launch_bounds__(kThreads, 2) gemv_staged_kernel(const LinearParams p, int64_t rows_per_cta) {
+    extern __shared__ __align__(128) uint4 s_w[];
+    __shared__ __align__(8) uint64_t s_bar;
+    __shared__ unsigned long long s_best[kWarps];
+    __shared__ int s_last;
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+
+    constexpr int kMats = mats_of<kEpi>();
+    constexpr int64_t kRowBytes = kC * 512;
+    constexpr int64_t kRowChunks = kC * 32;
+    constexpr int64_t kPiece = 32 * 1024;  // bytes per bulk copy
+    const int lane = threadIdx.x & 31;
+    const int warp = threadIdx.x >> 5;
+    const int64_t r0 = static_cast<int64_t>(blockIdx.x) * rows_per_cta;
+    const int64_t r1 = r0 + rows_per_cta < p.N ? r0 + rows_per_cta : p.N;
+    const int64_t nrows = r1 > r0 ? r1 - r0 : 0;
+    if (threadIdx.x == 0) {
+        mbar_init(&s_bar, 1);
+        const int64_t bytes = nrows * kRowBytes;
+        mbar_arrive_expect_tx(&s_bar, static_cast<uint32_t>(bytes * kMats));
+#pragma unroll
+        for (int mat = 0; mat < kMats; ++mat) {
+            const char* src = reinterpret_cast<const char*>(mat == 0 ? p.w0 : p.w1) + r0 * kRowBytes;
+            char* dst = reinterpret_cast<char*>(s_w) + mat * rows_per_cta * kRowBytes;
+            for (int64_t off = 0; off < bytes; off += kPiece) {
+                const int64_t len = bytes - off < kPiece ? bytes - off : kPiece;
+                bulk_copy_g2s(dst + off, src + off, static_cast<uint32_t>(len), &s_bar);
+            }
+        }
+    }
+    __syncthreads();  // the barrier is initialised before anyone polls it
+
+    constexpr bool kHoldX = kC <= 4;
+    // Constants the previous kernel does not write are read before the wait.
+    uint4 nw[kHoldX ? kC : 1];
+    if constexpr (kHoldX) {
+        if (p.norm_weight != nullptr) {
+#pragma unroll
+            for (int i = 0; i < kC; ++i) {
+                nw[i] = ld_cached(p.norm_weight + (lane + 32 * i) * 8);
+            }
+        }
+    }
+
+    asm volatile("griddepcontrol.wait;" ::: "memory");
+
+    const int64_t pos = p.position != nullptr ? static_cast<int64_t>(*p.position) : 0;
+    const bf16* xrow = input_row(p, 0, pos);
+    uint4 xv[kHoldX ? kC : 1];
+    if constexpr (kHoldX) {
+#pragma unroll
+        for (int i = 0; i < kC; ++i) {
+            xv[i] = ld_cached(xrow + (lane + 32 * i) * 8);
+        }
+        if (p.x_copy != nullptr && blockIdx.x == 0 && warp == 0) {
+#pragma unroll
+            for (int i = 0; i < kC; ++i) {
+                st_v4(p.x_copy + (lane + 32 * i) * 8, xv[i]);
+            }
+        }
+        if (p.norm_weight != nullptr) {
+            // ops::rms_norm of the row: lane l's chunks are l, l + 32, ..., so its partial is the canonical one.
+            float s = 0.0f;
+#pragma unroll
+            for (int i = 0; i < kC; ++i) {
+                float f[8];
+                Vec16<bf16>::unpack(xv[i], f);
+#pragma unroll
+                for (int e = 0; e < 8; ++e) {
+                    s = s + f[e] * f[e];
+                }
+            }
+            s = group_sum<32>(s);
+            const float mean = s / static_cast<float>(kC * 256);
+            const float rms = sqrtf(mean + p.eps);
+            const float inv = 1.0f / rms;
+#pragma unroll
+            for (int i = 0; i < kC; ++i) {
+                float f[8];
+                float w[8];
+                Vec16<bf16>::unpack(xv[i], f);
+                Vec16<bf16>::unpack(nw[i], w);
+#pragma unroll
+                for (int e = 0; e < 8; ++e) {
+                    f[e] = (f[e] * inv) * w[e];
+                }
+                xv[i] = Vec16<bf16>::pack(f);
+            }
+        }
+    }
+
+    const bool arrived = mbar_wait_bounded(&s_bar, 0);
+    if (__syncthreads_or(arrived ? 0 : 1)) {
+        // The copies did not complete within the poll limit: report it, give them one more bounded wait so no
+        // copy lands in shared memory after this CTA has left, and produce nothing.
+        if (threadIdx.x == 0) {
+            atomicOr(p.error, 1u);
+        }
+        mbar_wait_bounded(&s_bar, 0);
+        return;
+    }
+
+    // Each warp takes rows warp, warp + 8, ... of the slice, one at a time (measured on B200: interleaving four
+    // rows per warp was slower).
+    unsigned long long best = 0ull;
+    for (int64_t r = warp; r < nrows; r += kWarps) {
+        float acc[kMats];
+#pragma unroll
+        for (int mat = 0; mat < kMats; ++mat) {
+            acc[mat] = 0.0f;
+        }
+#pragma unroll
+        for (int i = 0; i < kC; ++i) {
+            uint4 x;
+            if constexpr (kHoldX) {
+                x = xv[i];
+            } else {
+                x = ld_cached(xrow + (lane + 32 * i) * 8);
+            }
+#pragma unroll
+            for (int mat = 0; mat < kMats; ++mat) {
+                acc[mat] = dot_chunk(x, s_w[(mat * rows_per_cta + r) * kRowChunks + lane + 32 * i], acc[mat]);
+            }
+        }
+#pragma unroll
+        for (int mat = 0; mat < kMats; ++mat) {
+            acc[mat] = group_sum<32>(acc[mat]);
+        }
+        gemv_epilogue<kEpi, 1>(p, r0 + r, acc, lane, pos, best);
+    }
+    if constexpr (kEpi == LinearEpilogue::kArgmax) {
+        argmax_finish(p, best, s_best, &s_last);
+    }
+}
+
 template <LinearEpilogue kEpi, int kRows>
 __global__ void __launch_bounds__(kThreads, 2) gemv_kernel(const LinearParams p) {
     extern __shared__ uint4 smem_x[];  // the input row, K / 8 chunks
@@ -544,10 +685,16 @@ __global__ void __launch_bounds__(kThreads) embedding_kernel(const bf16* table, 
 // the generic kernel. Grids: one CTA per SM, two for the vocabulary-sized argmax head.
 struct GemvPlan {
     bool fast;
-    int chunks;  // c
-    int rows;    // kRows
+    bool staged;            // gemv_staged_kernel: the CTA's weight rows staged in shared memory
+    int chunks;             // c
+    int rows;               // kRows
     int grid;
+    int64_t rows_per_cta;   // staged kernel
+    std::size_t smem;       // staged kernel
 };
+
+// A staged slice up to this size leaves room in the 228 KB of shared memory of an SM for the next kernel's slice.
+constexpr std::size_t kMaxStagedBytes = 100 * 1024;
 
 GemvPlan plan_gemv(const LinearParams& p, int mats) {
     GemvPlan plan{};
@@ -565,6 +712,18 @@ GemvPlan plan_gemv(const LinearParams& p, int mats) {
         const int64_t r = kLoads / (mats * (per_lane < 1 ? 1 : per_lane));
         plan.rows = r >= 4 ? 4 : (r >= 2 ? 2 : 1);
     }
+    if (plan.fast && p.error != nullptr && p.N > 0) {
+        const int64_t sms = runtime::sm_count();
+        const int64_t rpc = (p.N + sms - 1) / sms;
+        const std::size_t bytes = static_cast<std::size_t>(rpc) * mats * p.K * 2;
+        if (bytes <= kMaxStagedBytes) {
+            plan.staged = true;
+            plan.rows_per_cta = rpc;
+            plan.smem = bytes;
+            plan.grid = static_cast<int>((p.N + rpc - 1) / rpc);
+            return plan;
+        }
+    }
     const int64_t groups = (p.N + plan.rows - 1) / plan.rows;
     const int64_t want = (groups + kWarps - 1) / kWarps;
     const int64_t per_sm = p.epilogue == LinearEpilogue::kArgmax || !plan.fast ? 2 : 1;
@@ -580,6 +739,18 @@ cudaError_t launch_fast(const LinearParams& p, int grid, cudaStream_t s) {
 
 template <LinearEpilogue kEpi, int kC>
 cudaError_t launch_fast_rows(const LinearParams& p, const GemvPlan& plan, cudaStream_t s) {
+    if (plan.staged) {
+        auto kernel = gemv_staged_kernel<kEpi, kC>;
+        if (plan.smem > 48 * 1024) {
+            const cudaError_t err = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                                         static_cast<int>(plan.smem));
+            if (err != cudaSuccess) {
+                return err;
+            }
+        }
+        return runtime::launch_smem(kernel, dim3(plan.grid), dim3(kThreads), plan.smem, s, 1u, p,
+                                    plan.rows_per_cta);
+    }
     constexpr int kMats = mats_of<kEpi>();
     constexpr int kR = kLoads / (kMats * kC) >= 4 ? 4 : (kLoads / (kMats * kC) >= 2 ? 2 : 1);
     return launch_fast<kEpi, kC, kR>(p, plan.grid, s);

@@ -74,6 +74,7 @@ struct cppinf_qwen3 {
     int* d_len = nullptr;
     int64_t* d_tokens = nullptr;
     unsigned int* d_counter = nullptr;
+    unsigned int* d_error = nullptr;  // set by a decode kernel whose bounded wait ran out
     unsigned long long* d_partial = nullptr;
     bf16* h = nullptr;
     bf16* xn = nullptr;
@@ -171,24 +172,27 @@ int enqueue_step(cppinf_qwen3* m, cudaStream_t s, int64_t* launches) {
         qkv.norm_weight = l.in_norm;
         qkv.eps = c.rms_norm_eps;
         set_qkv_outputs(m, l, qkv, 0, m->d_len);
+        qkv.error = m->d_error;
         QWEN3_TRY(cppinf::device::launch_gemv(qkv, s), "qwen3_qkv");
         // q/k-norm + RoPE and the new key's cache row are fused into the attention kernel.
         AttentionParams ap{m->q, l.k_cache, l.v_cache, m->ctx, 1,
                            static_cast<int>(c.num_attention_heads), static_cast<int>(c.num_key_value_heads),
                            static_cast<int>(c.head_dim), 0, m->d_len, m->cap,
-                           m->k, l.q_norm, l.k_norm, m->rope, c.rms_norm_eps};
+                           m->k, l.q_norm, l.k_norm, m->rope, c.rms_norm_eps, m->d_error};
         QWEN3_TRY(cppinf::device::launch_decoder_attention(ap, m->cap, s), "qwen3_attention");
         LinearParams o = params_for(LinearEpilogue::kResidual, m->ctx, m->q_dim, l.wo, nullptr, 1, H, m->q_dim);
         o.residual = m->h;
         o.res_ld = H;
         o.out[0] = m->h;
         o.ld[0] = H;
+        o.error = m->d_error;
         QWEN3_TRY(cppinf::device::launch_gemv(o, s), "qwen3_o_proj");
         LinearParams gu = params_for(LinearEpilogue::kSiluMul, m->h, H, l.wg, l.wu, 1, c.intermediate_size, H);
         gu.norm_weight = l.post_norm;
         gu.eps = c.rms_norm_eps;
         gu.out[0] = m->act;
         gu.ld[0] = c.intermediate_size;
+        gu.error = m->d_error;
         QWEN3_TRY(cppinf::device::launch_gemv(gu, s), "qwen3_gate_up");
         LinearParams d = params_for(LinearEpilogue::kResidual, m->act, c.intermediate_size, l.wd, nullptr, 1, H,
                                     c.intermediate_size);
@@ -196,6 +200,7 @@ int enqueue_step(cppinf_qwen3* m, cudaStream_t s, int64_t* launches) {
         d.res_ld = H;
         d.out[0] = m->h;
         d.ld[0] = H;
+        d.error = m->d_error;
         QWEN3_TRY(cppinf::device::launch_gemv(d, s), "qwen3_down_proj");
         n += 5;
     }
@@ -404,6 +409,7 @@ int cppinf_qwen3_create(const cppinf_qwen3_config* config, int64_t max_sequence_
     const std::size_t rope_off = wtake(static_cast<std::size_t>(m->cap * c.head_dim) * sizeof(float));
     const std::size_t len_off = wtake(sizeof(int));
     const std::size_t counter_off = wtake(sizeof(unsigned int));
+    const std::size_t error_off = wtake(sizeof(unsigned int));
     const std::size_t partial_off = wtake(static_cast<std::size_t>(partials) * 8);
     const std::size_t tokens_off = wtake(static_cast<std::size_t>(m->cap + 1) * 8);
     const int64_t rows = kChunkRows < m->cap ? kChunkRows : m->cap;
@@ -450,6 +456,7 @@ int cppinf_qwen3_create(const cppinf_qwen3_config* config, int64_t max_sequence_
     m->rope = reinterpret_cast<float*>(m->work + rope_off);
     m->d_len = reinterpret_cast<int*>(m->work + len_off);
     m->d_counter = reinterpret_cast<unsigned int*>(m->work + counter_off);
+    m->d_error = reinterpret_cast<unsigned int*>(m->work + error_off);
     m->d_partial = reinterpret_cast<unsigned long long*>(m->work + partial_off);
     m->d_tokens = reinterpret_cast<int64_t*>(m->work + tokens_off);
     m->h = reinterpret_cast<bf16*>(m->work + h_off);
@@ -590,10 +597,14 @@ int cppinf_qwen3_decode(cppinf_qwen3* model, int64_t steps, int64_t* tokens, voi
         CPPINF_CUDA_TRY(cudaGraphLaunch(model->step, s));
         rt::count_launches(model->step_launches);
     }
+    unsigned int error = 0;
     CPPINF_CUDA_TRY(cudaMemcpyAsync(tokens, model->d_tokens + model->len + 1, static_cast<std::size_t>(steps) * 8,
                                     cudaMemcpyDeviceToHost, s));
+    CPPINF_CUDA_TRY(cudaMemcpyAsync(&error, model->d_error, sizeof(error), cudaMemcpyDeviceToHost, s));
     CPPINF_CUDA_TRY(cudaStreamSynchronize(s));
     model->len += steps;
+    CPPINF_REQUIRE(error == 0, CPPINF_ERR_CUDA,
+                   "qwen3_decode: a device wait for staged weights ran out of its poll limit; results are invalid.");
     return rt::ok();
 }
 
