@@ -317,12 +317,14 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_fast_kernel(const LinearPara
 // programmatic dependent launch the CTA starts while the previous kernel is still running, so the slice streams
 // from HBM during the previous kernel instead of after it. After the wait the input row is read (and normalised)
 // as in gemv_fast_kernel and each warp takes rows r, r + 8, ... of the slice from shared memory.
+constexpr int kStagedThreads = 512;
+constexpr int kStagedWarps = kStagedThreads / 32;
+constexpr int kStagedRowIters = 4;  // rows a warp may own: kStagedWarps * 4 rows per CTA at most
+
 template <LinearEpilogue kEpi, int kC>
-__global__ void __launch_bounds__(kThreads, 2) gemv_staged_kernel(const LinearParams p, int64_t rows_per_cta) {
+__global__ void __launch_bounds__(kStagedThreads, 2) gemv_staged_kernel(const LinearParams p, int64_t rows_per_cta) {
     extern __shared__ __align__(128) uint4 s_w[];
     __shared__ __align__(8) uint64_t s_bar;
-    __shared__ unsigned long long s_best[kWarps];
-    __shared__ int s_last;
     asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
 
     constexpr int kMats = mats_of<kEpi>();
@@ -366,6 +368,15 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_staged_kernel(const LinearPa
 
     const int64_t pos = p.position != nullptr ? static_cast<int64_t>(*p.position) : 0;
     const bf16* xrow = input_row(p, 0, pos);
+    // The residual values this warp's rows add are read now, in parallel with the input row.
+    float res_pre[kEpi == LinearEpilogue::kResidual ? kStagedRowIters : 1];
+    if constexpr (kEpi == LinearEpilogue::kResidual) {
+#pragma unroll
+        for (int k = 0; k < kStagedRowIters; ++k) {
+            const int64_t r = warp + static_cast<int64_t>(k) * kStagedWarps;
+            res_pre[k] = (lane == 0 && r < nrows) ? Vec16<bf16>::load1(p.residual, r0 + r) : 0.0f;
+        }
+    }
     uint4 xv[kHoldX ? kC : 1];
     if constexpr (kHoldX) {
 #pragma unroll
@@ -420,10 +431,14 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_staged_kernel(const LinearPa
         return;
     }
 
-    // Each warp takes rows warp, warp + 8, ... of the slice, one at a time (measured on B200: interleaving four
+    // Each warp takes rows warp, warp + 16, ... of the slice, one at a time (measured on B200: interleaving four
     // rows per warp was slower).
-    unsigned long long best = 0ull;
-    for (int64_t r = warp; r < nrows; r += kWarps) {
+#pragma unroll
+    for (int k = 0; k < kStagedRowIters; ++k) {
+        const int64_t r = warp + static_cast<int64_t>(k) * kStagedWarps;
+        if (r >= nrows) {
+            break;
+        }
         float acc[kMats];
 #pragma unroll
         for (int mat = 0; mat < kMats; ++mat) {
@@ -446,10 +461,18 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_staged_kernel(const LinearPa
         for (int mat = 0; mat < kMats; ++mat) {
             acc[mat] = group_sum<32>(acc[mat]);
         }
-        gemv_epilogue<kEpi, 1>(p, r0 + r, acc, lane, pos, best);
-    }
-    if constexpr (kEpi == LinearEpilogue::kArgmax) {
-        argmax_finish(p, best, s_best, &s_last);
+        if (lane == 0) {
+            const int64_t n = r0 + r;
+            if constexpr (kEpi == LinearEpilogue::kStore) {
+                store_segment(p, 0, n, acc[0], pos);
+            } else if constexpr (kEpi == LinearEpilogue::kResidual) {
+                Vec16<bf16>::store1(p.out[0], n, res_pre[k] + round_to_bf16(acc[0]));
+            } else {
+                const float gate = round_to_bf16(acc[0]);
+                const float up = round_to_bf16(acc[1]);
+                Vec16<bf16>::store1(p.out[0], n, round_to_bf16(silu_pexp(gate)) * up);
+            }
+        }
     }
 }
 
@@ -712,11 +735,11 @@ GemvPlan plan_gemv(const LinearParams& p, int mats) {
         const int64_t r = kLoads / (mats * (per_lane < 1 ? 1 : per_lane));
         plan.rows = r >= 4 ? 4 : (r >= 2 ? 2 : 1);
     }
-    if (plan.fast && p.error != nullptr && p.N > 0) {
+    if (plan.fast && p.error != nullptr && p.N > 0 && p.epilogue != LinearEpilogue::kArgmax) {
         const int64_t sms = runtime::sm_count();
         const int64_t rpc = (p.N + sms - 1) / sms;
         const std::size_t bytes = static_cast<std::size_t>(rpc) * mats * p.K * 2;
-        if (bytes <= kMaxStagedBytes) {
+        if (bytes <= kMaxStagedBytes && rpc <= kStagedWarps * kStagedRowIters) {
             plan.staged = true;
             plan.rows_per_cta = rpc;
             plan.smem = bytes;
@@ -748,7 +771,7 @@ cudaError_t launch_fast_rows(const LinearParams& p, const GemvPlan& plan, cudaSt
                 return err;
             }
         }
-        return runtime::launch_smem(kernel, dim3(plan.grid), dim3(kThreads), plan.smem, s, 1u, p,
+        return runtime::launch_smem(kernel, dim3(plan.grid), dim3(kStagedThreads), plan.smem, s, 1u, p,
                                     plan.rows_per_cta);
     }
     constexpr int kMats = mats_of<kEpi>();
