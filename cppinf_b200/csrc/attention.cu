@@ -8,13 +8,15 @@
 // restates it (oracle_decoder_attention):
 //  - score: the head vector is cut into 8 segments of D / 8 dims, each summed in order by one lane, the 8 partials
 //    combined by a butterfly over lane distances 4, 2, 1; x_j = score * (1 / sqrt(D));
-//  - max over all parts (DSMEM exchange); e_j = exp(x_j - max) with the portable exp of pexp.cuh;
-//  - part sum: thread i adds e_j for j = lo + i, lo + i + 128, ... in order; warp butterfly; the 4 warp sums in
-//    order; then the 8 part sums in order (every CTA reads all 8 over DSMEM and gets the same total);
-//  - p_j = bf16(e_j / total);
-//  - context: warp w adds p_j v_j for j = lo + w, lo + w + 4, ... in order; the 4 warp sums in order; the 8 part
-//    sums in order (CTA c finishes dims [cD/8, (c+1)D/8)); stored in bf16.
-// Nothing but DSMEM carries partial results, so the kernel needs no global scratch.
+//  - per part: m_c = max x_j; S_c: thread i adds exp(x_j - m_c) for j = lo + i, lo + i + 128, ... in order, warp
+//    butterfly, the 4 warp sums in order (exp is the portable exp of pexp.cuh);
+//  - every part pushes (m_c, S_c) into every CTA's shared memory (DSMEM stores), one cluster barrier, then
+//    M = max m_c and total = sum over c in order of S_c * exp(m_c - M);
+//  - p_j = bf16(exp(x_j - M) / total);
+//  - context: warp w adds p_j v_j for j = lo + w, lo + w + 4, ... in order; the 4 warp sums in order; each part
+//    pushes its partial of dims [cD/8, (c+1)D/8) to CTA c, one cluster barrier, CTA c adds the 8 partials in order;
+//    stored in bf16.
+// Only DSMEM stores carry partial results (no remote loads, no global scratch); two cluster barriers in all.
 //
 // Roofline: HBM/L2-bound on the cache reads (2 * L * D * 2 bytes per query head, shared by the 2 heads of a group
 // through L2); the decode step reads every cached key and value once per layer.
@@ -141,10 +143,11 @@ __global__ void __launch_bounds__(kThreads) decoder_attention_kernel(const Atten
     // cached key and value rows.
     extern __shared__ __align__(16) float s_e[];
     __shared__ float s_red[kWarps];
-    __shared__ float s_max;
-    __shared__ float s_sum;
+    __shared__ float s_local;             // this part's max
+    __shared__ float s_m[kParts];         // every part's max and exp sum, pushed here by each part
+    __shared__ float s_s[kParts];
     __shared__ float s_acc[kWarps][kD];
-    __shared__ float s_part[kD];
+    __shared__ float s_recv[kParts][kFinal];  // the parts' P·V partials of the dims this CTA finishes
     __shared__ __align__(16) bf16 s_q[kFused ? kD : 8];
     __shared__ __align__(16) bf16 s_knew[kFused ? kD : 8];
     __shared__ __align__(8) uint64_t s_bar;
@@ -168,6 +171,9 @@ __global__ void __launch_bounds__(kThreads) decoder_attention_kernel(const Atten
         }
         return;  // the whole cluster leaves together (same t); no DSMEM access happens
     }
+    // Every CTA of the cluster has started once this barrier phase completes (waited on before the first DSMEM
+    // store below).
+    asm volatile("barrier.cluster.arrive.relaxed.aligned;" ::: "memory");
     const int64_t L = pos + 1;
     const int64_t P = (L + kParts - 1) / kParts;
     const int64_t lo = rank * P < L ? rank * P : L;
@@ -294,7 +300,7 @@ __global__ void __launch_bounds__(kThreads) decoder_attention_kernel(const Atten
     }
     __syncthreads();
 
-    // Maximum over all parts.
+    // This part's maximum and its sum of exp(x - max) (slot order, warp butterfly, warps in order).
     float mx = -INFINITY;
     for (int64_t i = threadIdx.x; i < n; i += kThreads) {
         mx = fmaxf(mx, s_e[i]);
@@ -310,44 +316,46 @@ __global__ void __launch_bounds__(kThreads) decoder_attention_kernel(const Atten
         for (int w = 1; w < kWarps; ++w) {
             m = fmaxf(m, s_red[w]);
         }
-        s_max = m;
+        s_local = m;
     }
-    cluster.sync();
-    float gmax = *cluster.map_shared_rank(&s_max, 0);
-#pragma unroll
-    for (int r = 1; r < kParts; ++r) {
-        gmax = fmaxf(gmax, *cluster.map_shared_rank(&s_max, r));
-    }
-
-    // exp and the part sum.
+    __syncthreads();
+    const float local_max = s_local;
     float sum = 0.0f;
     for (int64_t i = threadIdx.x; i < n; i += kThreads) {
-        const float e = pexp(s_e[i] - gmax);
-        s_e[i] = e;
-        sum = sum + e;
+        sum = sum + pexp(s_e[i] - local_max);
     }
     sum = group_sum<32>(sum);
+    __syncthreads();  // s_red is reused
     if (lane == 0) {
         s_red[warp] = sum;
     }
     __syncthreads();
-    if (threadIdx.x == 0) {
-        float s = s_red[0];
+    asm volatile("barrier.cluster.wait.aligned;" ::: "memory");  // every CTA has started: DSMEM is usable
+    if (threadIdx.x < kParts) {
+        float part_sum = s_red[0];
 #pragma unroll
         for (int w = 1; w < kWarps; ++w) {
-            s = s + s_red[w];
+            part_sum = part_sum + s_red[w];
         }
-        s_sum = s;
+        // Push (max, sum) of this part to every CTA of the cluster, this one included.
+        *cluster.map_shared_rank(&s_m[rank], static_cast<int>(threadIdx.x)) = local_max;
+        *cluster.map_shared_rank(&s_s[rank], static_cast<int>(threadIdx.x)) = part_sum;
     }
     cluster.sync();
-    float total = *cluster.map_shared_rank(&s_sum, 0);
+    // Global max M and total = sum over parts (in order) of part_sum * exp(part_max - M).
+    float gmax = s_m[0];
 #pragma unroll
     for (int r = 1; r < kParts; ++r) {
-        total = total + *cluster.map_shared_rank(&s_sum, r);
+        gmax = fmaxf(gmax, s_m[r]);
+    }
+    float total = s_s[0] * pexp(s_m[0] - gmax);
+#pragma unroll
+    for (int r = 1; r < kParts; ++r) {
+        total = total + s_s[r] * pexp(s_m[r] - gmax);
     }
 
     for (int64_t i = threadIdx.x; i < n; i += kThreads) {
-        s_e[i] = round_to_bf16(s_e[i] / total);
+        s_e[i] = round_to_bf16(pexp(s_e[i] - gmax) / total);
     }
     __syncthreads();
 
@@ -392,25 +400,23 @@ __global__ void __launch_bounds__(kThreads) decoder_attention_kernel(const Atten
     }
     __syncthreads();
     for (int d = threadIdx.x; d < kD; d += kThreads) {
-        float s = s_acc[0][d];
+        float part = s_acc[0][d];
 #pragma unroll
         for (int w = 1; w < kWarps; ++w) {
-            s = s + s_acc[w][d];
+            part = part + s_acc[w][d];
         }
-        s_part[d] = s;
+        // Push the partial of dim d to the CTA that finishes it.
+        *cluster.map_shared_rank(&s_recv[rank][d % kFinal], d / kFinal) = part;
     }
-    cluster.sync();
+    cluster.sync();  // after this no CTA touches another's shared memory
     if (threadIdx.x < kFinal) {
-        const int d = rank * kFinal + threadIdx.x;
-        float c = *cluster.map_shared_rank(&s_part[d], 0);
+        float c = s_recv[0][threadIdx.x];
 #pragma unroll
         for (int r = 1; r < kParts; ++r) {
-            c = c + *cluster.map_shared_rank(&s_part[d], r);
+            c = c + s_recv[r][threadIdx.x];
         }
-        Vec16<bf16>::store1(p.ctx, (t * p.q_heads + h) * kD + d, c);
+        Vec16<bf16>::store1(p.ctx, (t * p.q_heads + h) * kD + rank * kFinal + threadIdx.x, c);
     }
-    // Keep every CTA's shared memory alive until the others have read it.
-    cluster.sync();
     if (kStage && stage_failed) {
         mbar_wait_bounded(&s_bar, 0);  // no bulk copy may land after this CTA has left
     }

@@ -564,11 +564,12 @@ void oracle_linear_canonical(const uint16_t* x, int64_t x_stride, const uint16_t
  * Per (t, h), with L visible keys:
  *  - score s_j: the head vector is cut into G segments of D / G consecutive dims (G = 8, 4, 2 or 1, the largest
  *    dividing D), each summed in order from +0, the G partials combined by a butterfly over distances G/2 .. 1;
- *  - x_j = s_j * scale, scale = 1 / sqrt(D); M = max_j x_j; e_j = pexp(x_j - M) (qwen_attention.cpp:205-222);
+ *  - x_j = s_j * scale, scale = 1 / sqrt(D) (qwen_attention.cpp:205-222 scales then takes the max);
  *  - the keys are split into 8 parts of P = ceil(L / 8) consecutive keys (part c: [cP, min(L, cP + P)));
- *  - sum: in each part, slot i (0..127) adds e_j for j = lo + i, lo + i + 128, ... in order; slots 32w .. 32w+31 are
- *    combined by a butterfly; the 4 results, then the 8 part sums, are added in order;
- *  - p_j = bf16(e_j / sum) (the probabilities' bf16 cast, qwen_attention.cpp:321-327);
+ *  - part c: m_c = max of its x_j (-inf when empty); S_c: slot i (0..127) adds pexp(x_j - m_c) for j = lo + i,
+ *    lo + i + 128, ... in order, slots 32w .. 32w+31 are combined by a butterfly, the 4 results added in order;
+ *  - M = max_c m_c; sum = S_0 pexp(m_0 - M) + S_1 pexp(m_1 - M) + ... + S_7 pexp(m_7 - M), added in order;
+ *  - p_j = bf16(pexp(x_j - M) / sum) (the probabilities' bf16 cast, qwen_attention.cpp:321-327);
  *  - ctx_d: in each part, group w (0..3) adds p_j v_jd for j = lo + w, lo + w + 4, ... in order; the 4 group sums,
  *    then the 8 part sums, are added in order; stored in bf16. */
 void oracle_decoder_attention(const uint16_t* q, const uint16_t* kc, const uint16_t* vc, uint16_t* ctx, int64_t T,
@@ -588,7 +589,6 @@ void oracle_decoder_attention(const uint16_t* q, const uint16_t* kc, const uint1
         float* e = (float*)malloc(sizeof(float) * (size_t)L);
         float* acc = (float*)calloc((size_t)D, sizeof(float));
         float* grp = (float*)malloc(sizeof(float) * (size_t)D * WARPS);
-        float mx = -INFINITY;
         for (int64_t j = 0; j < L; ++j) {
             const uint16_t* kv = kc + (j * hkv + kvh) * D;
             float partial[8];
@@ -607,21 +607,23 @@ void oracle_decoder_attention(const uint16_t* q, const uint16_t* kc, const uint1
                 memcpy(partial, next, sizeof next);
             }
             e[j] = partial[0] * scale;
-            mx = e[j] > mx ? e[j] : mx;
-        }
-        for (int64_t j = 0; j < L; ++j) {
-            e[j] = oracle_pexp(e[j] - mx);
         }
         const int64_t P = (L + PARTS - 1) / PARTS;
-        float sum = 0.0f;
+        float part_max[PARTS];
+        float part_sum[PARTS];
+        float mx = -INFINITY;
         for (int c = 0; c < PARTS; ++c) {
             const int64_t lo = c * P < L ? c * P : L;
             const int64_t hi = lo + P < L ? lo + P : L;
+            float m = -INFINITY;
+            for (int64_t j = lo; j < hi; ++j) {
+                m = e[j] > m ? e[j] : m;
+            }
             float slots[SLOTS];
             for (int i = 0; i < SLOTS; ++i) {
                 float s = 0.0f;
                 for (int64_t j = lo + i; j < hi; j += SLOTS) {
-                    s = s + e[j];
+                    s = s + oracle_pexp(e[j] - m);
                 }
                 slots[i] = s;
             }
@@ -630,7 +632,17 @@ void oracle_decoder_attention(const uint16_t* q, const uint16_t* kc, const uint1
                 butterfly32(slots + 32 * w);
                 part = w == 0 ? slots[0] : part + slots[32 * w];
             }
-            sum = c == 0 ? part : sum + part;
+            part_max[c] = m;
+            part_sum[c] = part;
+            mx = m > mx ? m : mx;
+        }
+        float sum = 0.0f;
+        for (int c = 0; c < PARTS; ++c) {
+            const float term = part_sum[c] * oracle_pexp(part_max[c] - mx);
+            sum = c == 0 ? term : sum + term;
+        }
+        for (int64_t j = 0; j < L; ++j) {
+            e[j] = oracle_pexp(e[j] - mx);
         }
         for (int64_t j = 0; j < L; ++j) {
             e[j] = bf16_to_f32(f32_to_bf16(e[j] / sum));
