@@ -74,6 +74,8 @@ _SIGNATURES = {
     "cppinf_qk_norm_rope": [
         _int, _ptr, _ptr, _ptr, _ptr, _ptr, _ptr, _i64, _i64, _i64, _i64, _i64, _f32, _ptr, _i64, _ptr,
     ],
+    "cppinf_matmul": [_int, _ptr, ctypes.POINTER(_i64), _int, _ptr, ctypes.POINTER(_i64), _int, _ptr, _i64, _i64, _i64,
+                      _i64, _ptr],
     "cppinf_linear": [_ptr, _i64, _ptr, _ptr, _i64, _i64, _i64, _ptr],
     "cppinf_linear_residual": [_ptr, _i64, _ptr, _ptr, _ptr, _i64, _i64, _i64, _ptr],
     "cppinf_linear_silu_mul": [_ptr, _i64, _ptr, _ptr, _ptr, _i64, _i64, _i64, _ptr],

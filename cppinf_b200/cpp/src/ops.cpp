@@ -14,6 +14,7 @@
 #include <limits>
 #include <map>
 #include <mutex>
+#include <array>
 #include <optional>
 #include <stdexcept>
 #include <string_view>
@@ -26,6 +27,7 @@
 #include "nn/rope.h"
 #include "ops/elementwise_ops.h"
 #include "ops/nn_ops.h"
+#include "ops/matmul.h"
 #include "ops/tensor_ops.h"
 #include "tensors/tensor_utils.h"
 
@@ -443,6 +445,107 @@ std::vector<std::int64_t> row_argmax(const tensors::TensorView& logits) {
     cuda::check(cudaStreamSynchronize(cuda::current_stream()), "cudaStreamSynchronize");
     return out;
 }
+
+// ---- matmul.h ----------------------------------------------------------------------------------------------------
+
+namespace {
+
+// resolve_output_dtype and validate_matmul_inputs, src/ops/matmul.cpp:13-60
+tensors::DType resolve_matmul_dtype(const TensorView& lhs, const TensorView& rhs, const MatmulOptions& options) {
+    if (options.output_dtype.has_value()) {
+        return *options.output_dtype;
+    }
+    if (lhs.tensor_info().dtype == rhs.tensor_info().dtype) {
+        return lhs.tensor_info().dtype;
+    }
+    return DType::F32;
+}
+
+void validate_matmul(const TensorView& lhs, const TensorView& rhs, DType output_dtype) {
+    validate_supported_float_dtype(lhs.tensor_info().dtype, "matmul");
+    validate_supported_float_dtype(rhs.tensor_info().dtype, "matmul");
+    validate_supported_float_dtype(output_dtype, "matmul");
+    if (lhs.tensor_info().dtype == rhs.tensor_info().dtype) {
+        if (output_dtype != lhs.tensor_info().dtype &&
+            (lhs.tensor_info().dtype != DType::BF16 || output_dtype != DType::F32)) {
+            throw std::invalid_argument(
+                "matmul output dtype must match the input dtype, except BF16 inputs may request an F32 result.");
+        }
+    } else if (output_dtype != DType::F32) {
+        throw std::invalid_argument("matmul requires an F32 result when input dtypes differ.");
+    }
+    const auto& ls = lhs.tensor_info().shape;
+    const auto& rs = rhs.tensor_info().shape;
+    if (ls.rank() != rs.rank()) {
+        throw std::invalid_argument("matmul requires tensors with matching rank.");
+    }
+    if (ls.rank() != 2 && ls.rank() != 3) {
+        throw std::invalid_argument("matmul requires rank-2 or rank-3 tensors.");
+    }
+    if (ls.rank() == 3 && ls.dims()[0] != rs.dims()[0]) {
+        throw std::invalid_argument("matmul requires matching batch dimensions.");
+    }
+    if (ls.dims().back() != rs.dims()[rs.rank() - 2]) {
+        throw std::invalid_argument("matmul inner dimensions must match.");
+    }
+}
+
+// A matmul operand on the op's GPU with its element strides {batch, row, column}: device views are read in place,
+// host tensors are staged dense.
+struct MatmulOperand {
+    std::optional<DeviceOperand> staged;
+    const void* ptr = nullptr;
+    std::array<std::int64_t, 3> strides{};
+};
+
+MatmulOperand matmul_operand(const TensorView& view, const Device& device) {
+    MatmulOperand op;
+    const auto rank = view.tensor_info().shape.rank();
+    std::vector<std::int64_t> s;
+    if (view.device().is_cuda()) {
+        op.ptr = view.data().data();
+        const auto element = tensors::element_size_bytes(view.tensor_info().dtype);
+        for (const auto b : view.strides_bytes()) {
+            s.push_back(static_cast<std::int64_t>(b / element));
+        }
+    } else {
+        op.staged.emplace(view, device);
+        op.ptr = op.staged->get();
+        s = operand_strides(view);
+    }
+    op.strides = rank == 3 ? std::array<std::int64_t, 3>{s[0], s[1], s[2]} : std::array<std::int64_t, 3>{0, s[0], s[1]};
+    return op;
+}
+
+} // namespace
+
+tensors::Tensor matmul(const tensors::TensorView& lhs, const tensors::TensorView& rhs, MatmulOptions options) {
+    const auto output_dtype = resolve_matmul_dtype(lhs, rhs, options);
+    validate_matmul(lhs, rhs, output_dtype);
+    const auto placement = place({&lhs, &rhs}, "matmul");
+    DeviceScope scope(placement.device);
+    const auto& ld = lhs.tensor_info().shape.dims();
+    const auto& rd = rhs.tensor_info().shape.dims();
+    const bool batched = ld.size() == 3;
+    const std::int64_t batch = batched ? ld[0] : 1;
+    const std::int64_t m = ld[ld.size() - 2];
+    const std::int64_t k = ld.back();
+    const std::int64_t n = rd.back();
+    const auto shape = batched ? tensors::Shape({batch, m, n}) : tensors::Shape({m, n});
+    auto result = Tensor::empty(tensors::make_result_tensor_info("matmul_result", output_dtype, shape),
+                                placement.device);
+    if (batch * m * n != 0) {
+        const auto x = matmul_operand(lhs, placement.device);
+        const auto w = matmul_operand(rhs, placement.device);
+        cuda::check_status(cppinf_matmul(abi_dtype(lhs.tensor_info().dtype), x.ptr, x.strides.data(),
+                                         abi_dtype(rhs.tensor_info().dtype), w.ptr, w.strides.data(),
+                                         abi_dtype(output_dtype), out_ptr(result), batch, m, k, n,
+                                         cuda::current_stream()),
+                           "matmul");
+    }
+    return finish(std::move(result), placement);
+}
+
 
 // ---- tensor_ops.h ------------------------------------------------------------------------------------------------
 

@@ -12,6 +12,7 @@
 
 #include "nn/rope.h"
 #include "ops/elementwise_ops.h"
+#include "ops/matmul.h"
 #include "ops/nn_ops.h"
 #include "ops/tensor_ops.h"
 #include "tensors/bfloat16.h"
@@ -383,4 +384,106 @@ TEST(TensorTest, GivenHostTensor_WhenRoundTrippingThroughDevice_ThenBytesAreUnch
 
 int main(int argc, char** argv) {
     return test_harness::run_all(argc, argv);
+}
+
+// ---- ops::matmul: tests/ops/ops_test.cpp:63-110, 219-257, 341-357 ------------------------------------------------
+
+TEST(OpsTest, GivenCompatibleMatrices_WhenMultiplying_ThenMatmulResultIsReturned) {
+    const auto lhs = f32("lhs", {2, 3}, {1.0f, 2.0f, 3.0f, 4.0f, 5.0f, 6.0f});
+    const auto rhs = f32("rhs", {3, 2}, {7.0f, 8.0f, 9.0f, 10.0f, 11.0f, 12.0f});
+    EXPECT_TRUE(f32("matmul_result", {2, 2}, {58.0f, 64.0f, 139.0f, 154.0f}) ==
+                cppinf::ops::matmul(lhs.view(), rhs.view()));
+}
+
+TEST(OpsTest, GivenCompatibleBatchedMatrices_WhenMultiplying_ThenBatchedMatmulResultIsReturned) {
+    const auto lhs = f32("lhs", {2, 2, 3}, {1.0f, 2.0f, 3.0f, 4.0f, 5.0f, 6.0f, -1.0f, 0.5f, 2.0f, 3.0f, -2.0f, 1.0f});
+    const auto rhs =
+        f32("rhs", {2, 3, 2}, {7.0f, 8.0f, 9.0f, 10.0f, 11.0f, 12.0f, 2.0f, -1.0f, 0.25f, 3.5f, -4.0f, 1.5f});
+    EXPECT_TRUE(f32("matmul_result", {2, 2, 2}, {58.0f, 64.0f, 139.0f, 154.0f, -9.875f, 5.75f, 1.5f, -8.5f}) ==
+                cppinf::ops::matmul(lhs.view(), rhs.view()));
+}
+
+TEST(OpsTest, GivenCompatibleBatchedBf16Matrices_WhenMultiplyingToF32_ThenF32MatmulResultIsReturned) {
+    const auto lhs =
+        bf16("lhs", {2, 2, 3}, {1.0f, 2.0f, 3.0f, 4.0f, 5.0f, 6.0f, -1.0f, 0.5f, 2.0f, 3.0f, -2.0f, 1.0f});
+    const auto rhs =
+        bf16("rhs", {2, 3, 2}, {7.0f, 8.0f, 9.0f, 10.0f, 11.0f, 12.0f, 2.0f, -1.0f, 0.25f, 3.5f, -4.0f, 1.5f});
+    const auto result =
+        cppinf::ops::matmul(lhs.view(), rhs.view(), cppinf::ops::MatmulOptions{.output_dtype = DType::F32});
+    EXPECT_EQ(std::string("matmul_result"), result.tensor_info().name);
+    EXPECT_TRUE(result.tensor_info().dtype == DType::F32);
+    EXPECT_TRUE(result.tensor_info().shape == shape({2, 2, 2}));
+    expect_values_near(result, {58.0f, 64.0f, 139.0f, 154.0f, -9.875f, 5.75f, 1.5f, -8.5f}, 0.0f);
+}
+
+TEST(OpsTest, GivenF32AndBf16Matrices_WhenMultiplying_ThenF32MatmulResultIsReturned) {
+    const auto lhs = f32("lhs", {2, 3}, {1.0f, -2.5f, 3.25f, 4.5f, 0.5f, -1.75f});
+    const auto rhs = bf16("rhs", {3, 2}, {2.0f, -1.0f, 0.25f, 3.5f, -4.0f, 1.5f});
+    EXPECT_TRUE(f32("matmul_result", {2, 2}, {-11.625f, -4.875f, 16.125f, -5.375f}) ==
+                cppinf::ops::matmul(lhs.view(), rhs.view()));
+}
+
+TEST(OpsTest, GivenBf16AndF32Matrices_WhenMultiplying_ThenF32MatmulResultIsReturned) {
+    const auto lhs = bf16("lhs", {2, 3}, {1.0f, -2.5f, 3.25f, 4.5f, 0.5f, -1.75f});
+    const auto rhs = f32("rhs", {3, 2}, {2.0f, -1.0f, 0.25f, 3.5f, -4.0f, 1.5f});
+    EXPECT_TRUE(f32("matmul_result", {2, 2}, {-11.625f, -4.875f, 16.125f, -5.375f}) ==
+                cppinf::ops::matmul(lhs.view(), rhs.view()));
+}
+
+TEST(OpsTest, GivenStridedTensorView_WhenMultiplying_ThenMatmulUsesLogicalLayout) {
+    const auto input = f32("input", {2, 4}, {1.0f, 2.0f, 3.0f, 4.0f, 5.0f, 6.0f, 7.0f, 8.0f});
+    const auto rhs = f32("rhs", {2, 1}, {2.0f, -1.0f});
+    const auto reshaped = cppinf::ops::reshape(input.view(), shape({2, 2, 2}));
+    const auto strided_lhs = cppinf::ops::squeeze(cppinf::ops::narrow(reshaped, 1, 1, 1), 1);
+    EXPECT_TRUE(f32("matmul_result", {2, 1}, {2.0f, 6.0f}) == cppinf::ops::matmul(strided_lhs, rhs.view()));
+}
+
+TEST(OpsTest, GivenCompatibleBf16Matrices_WhenMultiplying_ThenMatmulResultIsReturned) {
+    const auto lhs = bf16("lhs", {2, 3}, {1.0f, 2.0f, 3.0f, 4.0f, 5.0f, 6.0f});
+    const auto rhs = bf16("rhs", {3, 2}, {7.0f, 8.0f, 9.0f, 10.0f, 11.0f, 12.0f});
+    EXPECT_TRUE(bf16("matmul_result", {2, 2}, {58.0f, 64.0f, 139.0f, 154.0f}) ==
+                cppinf::ops::matmul(lhs.view(), rhs.view()));
+}
+
+TEST(OpsTest, GivenTorchOracleBf16Matrices_WhenMultiplying_ThenExpectedResultIsReturned) {
+    const auto lhs = bf16("lhs", {2, 3}, {1.0f, -2.5f, 3.25f, 4.5f, 0.5f, -1.75f});
+    const auto rhs = bf16("rhs", {3, 2}, {2.0f, -1.0f, 0.25f, 3.5f, -4.0f, 1.5f});
+    EXPECT_TRUE(bf16("matmul_result", {2, 2}, {-11.625f, -4.875f, 16.125f, -5.375f}) ==
+                cppinf::ops::matmul(lhs.view(), rhs.view()));
+}
+
+TEST(DeviceOpsTest, GivenDeviceTransposedWeightView_WhenMultiplying_ThenVectorPathMatchesHostPath) {
+    // linear_project's use (src/nn/qwen_common.cpp:15-37): hidden [3, 16] times transpose_2d(weight [8, 16]).
+    std::vector<float> xs(3 * 16);
+    std::vector<float> ws(8 * 16);
+    for (std::size_t i = 0; i < xs.size(); ++i) {
+        xs[i] = static_cast<float>(static_cast<int>(i % 7) - 3) * 0.5f;
+    }
+    for (std::size_t i = 0; i < ws.size(); ++i) {
+        ws[i] = static_cast<float>(static_cast<int>(i % 5) - 2) * 0.25f;
+    }
+    const auto x = cppinf::tensors::make_bf16_tensor("x", shape({3, 16}), xs);
+    const auto w = cppinf::tensors::make_bf16_tensor("w", shape({8, 16}), ws);
+    const auto host = cppinf::ops::matmul(x.view(), cppinf::ops::transpose_2d(w.view()).view());
+    const auto dx = x.to(Device::cuda(0));
+    const auto dw = w.to(Device::cuda(0));
+    const auto dwt = TensorView(TensorInfo{"w_t", DType::BF16, shape({16, 8})}, dw.view().data(), {2, 32}, 0,
+                                Device::cuda(0));
+    const auto dev = cppinf::ops::matmul(dx.view(), dwt);
+    EXPECT_TRUE(dev.device().is_cuda());
+    EXPECT_TRUE(host == dev.to(Device::host()));
+}
+
+HOST_TEST(OpsTest, GivenMismatchedBatchDimensions_WhenMultiplying_ThenMatmulThrows) {
+    const auto lhs = f32("lhs", {2, 2, 3}, {1.0f, 2.0f, 3.0f, 4.0f, 5.0f, 6.0f, -1.0f, 0.5f, 2.0f, 3.0f, -2.0f, 1.0f});
+    const auto rhs = f32("rhs", {3, 3, 2}, {7.0f, 8.0f, 9.0f, 10.0f, 11.0f, 12.0f, 2.0f, -1.0f, 0.25f, 3.5f, -4.0f, 1.5f,
+                                            0.5f, 1.5f, -2.0f, 0.25f, 3.0f, -0.5f});
+    EXPECT_THROW(cppinf::ops::matmul(lhs.view(), rhs.view()), std::invalid_argument);
+}
+
+HOST_TEST(OpsTest, GivenF32InputsAndBf16OutputRequest_WhenMultiplying_ThenMatmulThrows) {
+    const auto lhs = f32("lhs", {2, 3}, {1.0f, 2.0f, 3.0f, 4.0f, 5.0f, 6.0f});
+    const auto rhs = f32("rhs", {3, 2}, {7.0f, 8.0f, 9.0f, 10.0f, 11.0f, 12.0f});
+    EXPECT_THROW(cppinf::ops::matmul(lhs.view(), rhs.view(), cppinf::ops::MatmulOptions{.output_dtype = DType::BF16}),
+                 std::invalid_argument);
 }

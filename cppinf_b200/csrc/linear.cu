@@ -689,6 +689,48 @@ __global__ void __launch_bounds__(kThreads) linear_rows_kernel(const LinearParam
     }
 }
 
+// ops::matmul for any operand types and strides: one warp per output element, the canonical lane order with chunks
+// of 8 when K % 8 == 0 and of 1 otherwise (the same order as the vector kernels, so a bf16 layout they accept gives
+// the same bits either way). Used for shapes and layouts the vector kernels do not take.
+struct MatmulArgs {
+    const void* x;
+    int64_t xs[3];
+    const void* w;
+    int64_t ws[3];
+    void* y;
+    int64_t batch;
+    int64_t m;
+    int64_t k;
+    int64_t n;
+};
+
+template <typename Tx, typename Tw, typename Ty>
+__global__ void __launch_bounds__(kThreads) matmul_generic_kernel(const MatmulArgs a) {
+    grid_dependency_begin();
+    const int lane = threadIdx.x & 31;
+    const int64_t total = a.batch * a.m * a.n;
+    const int64_t chunk = a.k % 8 == 0 ? 8 : 1;
+    const int64_t nchunks = a.k / chunk;
+    for (int64_t idx = (static_cast<int64_t>(blockIdx.x) * kThreads + threadIdx.x) / 32; idx < total;
+         idx += static_cast<int64_t>(gridDim.x) * kWarps) {
+        const int64_t b = idx / (a.m * a.n);
+        const int64_t i = (idx / a.n) % a.m;
+        const int64_t j = idx % a.n;
+        const int64_t xrow = b * a.xs[0] + i * a.xs[1];
+        const int64_t wcol = b * a.ws[0] + j * a.ws[2];
+        float acc = 0.0f;
+        for (int64_t c = lane; c < nchunks; c += 32) {
+            for (int64_t e = c * chunk; e < (c + 1) * chunk; ++e) {
+                acc = acc + Vec16<Tx>::load1(a.x, xrow + e * a.xs[2]) * Vec16<Tw>::load1(a.w, wcol + e * a.ws[1]);
+            }
+        }
+        acc = group_sum<32>(acc);
+        if (lane == 0) {
+            Vec16<Ty>::store1(a.y, idx, acc);
+        }
+    }
+}
+
 __global__ void __launch_bounds__(kThreads) embedding_kernel(const bf16* table, int64_t vocab, int64_t hidden,
                                                              const int64_t* tokens, int64_t count, bf16* out) {
     grid_dependency_begin();
@@ -851,6 +893,20 @@ cudaError_t launch_rows_epi(const LinearParams& p, cudaStream_t s) {
                                 dim3(kThreads), smem, s, 1u, p);
 }
 
+template <typename Tx, typename Tw>
+cudaError_t launch_matmul_w(const MatmulArgs& a, cppinf_dtype y_dtype, unsigned grid, cudaStream_t s) {
+    return y_dtype == CPPINF_DTYPE_BF16
+               ? runtime::launch(matmul_generic_kernel<Tx, Tw, bf16>, dim3(grid), dim3(kThreads), s, 1u, a)
+               : runtime::launch(matmul_generic_kernel<Tx, Tw, float>, dim3(grid), dim3(kThreads), s, 1u, a);
+}
+
+template <typename Tx>
+cudaError_t launch_matmul_x(const MatmulArgs& a, cppinf_dtype w_dtype, cppinf_dtype y_dtype, unsigned grid,
+                            cudaStream_t s) {
+    return w_dtype == CPPINF_DTYPE_BF16 ? launch_matmul_w<Tx, bf16>(a, y_dtype, grid, s)
+                                        : launch_matmul_w<Tx, float>(a, y_dtype, grid, s);
+}
+
 }  // namespace
 
 int gemv_grid(const LinearParams& p) {
@@ -979,6 +1035,50 @@ int run_linear(const LinearParams& p, void* stream, const char* name) {
 }  // namespace
 
 extern "C" {
+
+int cppinf_matmul(cppinf_dtype x_dtype, const void* x, const int64_t* x_strides, cppinf_dtype w_dtype, const void* w,
+                  const int64_t* w_strides, cppinf_dtype y_dtype, void* y, int64_t batch, int64_t m, int64_t k,
+                  int64_t n, void* stream) {
+    CPPINF_REQUIRE(rt::valid_dtype(x_dtype) && rt::valid_dtype(w_dtype) && rt::valid_dtype(y_dtype),
+                   CPPINF_ERR_INVALID_ARGUMENT, "matmul received an unsupported dtype.");
+    CPPINF_REQUIRE(batch >= 0 && m >= 0 && k >= 0 && n >= 0, CPPINF_ERR_INVALID_ARGUMENT,
+                   "matmul requires non-negative dimensions.");
+    CPPINF_REQUIRE(batch * m * n < (int64_t{1} << 40), CPPINF_ERR_OVERFLOW, "matmul result is too large.");
+    if (batch == 0 || m == 0 || n == 0) {
+        return rt::ok();
+    }
+    CPPINF_REQUIRE(x_strides && w_strides && x && w && y, CPPINF_ERR_INVALID_ARGUMENT,
+                   "matmul received a null pointer.");
+    const auto s = rt::as_stream(stream);
+    // Vector path: bf16 throughout, dense input rows, weight columns of rhs [k, n] contiguous in k (rhs is the
+    // transposed view of a row-major [n, k] weight), aligned rows, k a multiple of 8.
+    const bool bf16s = x_dtype == CPPINF_DTYPE_BF16 && w_dtype == CPPINF_DTYPE_BF16 && y_dtype == CPPINF_DTYPE_BF16;
+    const bool layout = x_strides[2] == 1 && w_strides[1] == 1 && w_strides[2] == k && k % 8 == 0 && k > 0 &&
+                        (m == 1 || (x_strides[1] % 8 == 0 && x_strides[1] >= k)) && rt::aligned16(x) &&
+                        rt::aligned16(w) && (batch == 1 || (x_strides[0] % 8 == 0 && w_strides[0] % 8 == 0)) &&
+                        k <= (m > 1 ? 6144 : 65536);
+    if (bf16s && layout) {
+        for (int64_t b = 0; b < batch; ++b) {
+            LinearParams p = linear_params(LinearEpilogue::kStore, static_cast<const bf16*>(x) + b * x_strides[0],
+                                           x_strides[1], static_cast<const bf16*>(w) + b * w_strides[0], nullptr,
+                                           static_cast<bf16*>(y) + b * m * n, m, k, n);
+            const int st = run_linear(p, stream, "matmul");
+            if (st != CPPINF_OK) {
+                return st;
+            }
+        }
+        return rt::ok();
+    }
+    MatmulArgs a{x, {x_strides[0], x_strides[1], x_strides[2]}, w, {w_strides[0], w_strides[1], w_strides[2]},
+                 y, batch, m, k, n};
+    const int64_t warps = batch * m * n;
+    const int64_t want = (warps + kWarps - 1) / kWarps;
+    const int64_t cap = static_cast<int64_t>(rt::sm_count()) * 8;
+    const auto grid = static_cast<unsigned>(want < cap ? want : cap);
+    const cudaError_t err = x_dtype == CPPINF_DTYPE_BF16 ? launch_matmul_x<bf16>(a, w_dtype, y_dtype, grid, s)
+                                                         : launch_matmul_x<float>(a, w_dtype, y_dtype, grid, s);
+    return rt::launched(err, "matmul");
+}
 
 int cppinf_linear(const void* x, int64_t x_row_stride, const void* weight, void* y, int64_t rows, int64_t in_features,
                   int64_t out_features, void* stream) {

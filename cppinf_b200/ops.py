@@ -327,6 +327,39 @@ def qk_norm_rope(q: torch.Tensor, k: torch.Tensor, q_weight: torch.Tensor, k_wei
 # ---- decoder: projections and attention ---------------------------------------------------------------------------
 
 
+def matmul(lhs: torch.Tensor, rhs: torch.Tensor, output_dtype: torch.dtype | None = None) -> torch.Tensor:
+    """ops::matmul, src/ops/matmul.cpp:85-114: rank-2 [m, k] x [k, n] or rank-3 [b, m, k] x [b, k, n], f32/bf16, any
+    strides (views are read in place). Output dtype as the reference resolves it (:14-24) and validated as
+    :26-60."""
+    code_l = _dtype_code(lhs, "matmul")
+    code_r = _dtype_code(rhs, "matmul")
+    out = output_dtype if output_dtype is not None else (lhs.dtype if lhs.dtype == rhs.dtype else torch.float32)
+    code_o = _dtype_code(torch.empty(0, dtype=out), "matmul")
+    if lhs.dtype == rhs.dtype:
+        if out != lhs.dtype and (lhs.dtype != torch.bfloat16 or out != torch.float32):
+            raise ValueError("matmul output dtype must match the input dtype, except BF16 inputs may request an F32 "
+                             "result.")
+    elif out != torch.float32:
+        raise ValueError("matmul requires an F32 result when input dtypes differ.")
+    if lhs.dim() != rhs.dim():
+        raise ValueError("matmul requires tensors with matching rank.")
+    if lhs.dim() not in (2, 3):
+        raise ValueError("matmul requires rank-2 or rank-3 tensors.")
+    if lhs.dim() == 3 and lhs.shape[0] != rhs.shape[0]:
+        raise ValueError("matmul requires matching batch dimensions.")
+    if lhs.shape[-1] != rhs.shape[-2]:
+        raise ValueError("matmul inner dimensions must match.")
+    _require_cuda(lhs, rhs)
+    l3 = lhs if lhs.dim() == 3 else lhs.unsqueeze(0)
+    r3 = rhs if rhs.dim() == 3 else rhs.unsqueeze(0)
+    b, m, k = l3.shape
+    n = r3.shape[2]
+    y = torch.empty(b, m, n, dtype=out, device=lhs.device)
+    capi.call("cppinf_matmul", code_l, l3.data_ptr(), capi.i64_array(l3.stride()), code_r, r3.data_ptr(),
+              capi.i64_array(r3.stride()), code_o, y.data_ptr(), b, m, k, n, _stream())
+    return y if lhs.dim() == 3 else y[0]
+
+
 def _validate_linear(input: torch.Tensor, weight: torch.Tensor, op: str) -> tuple[torch.Tensor, int, int, int]:
     # validate_projection_weight, src/nn/qwen_common.cpp:39-49, and matmul's dtype rules, src/ops/matmul.cpp:28-45
     if input.dtype != torch.bfloat16 or weight.dtype != torch.bfloat16:

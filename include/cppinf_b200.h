@@ -174,6 +174,17 @@ CPPINF_API int cppinf_qk_norm_rope(cppinf_dtype dtype, const void* q, const void
  * it within a bf16 ulp per op, not bit for bit.
  * ------------------------------------------------------------------------------------------------------------- */
 
+/* ops::matmul (src/ops/matmul.cpp:85-114, decl src/ops/matmul.h): y[b, i, j] = sum_p x[b, i, p] * w[b, p, j] for
+ * x [batch, m, k] and w [batch, k, n] of any f32/bf16 types with element strides {batch, row, column} (HOST
+ * arrays of 3), every element read as f32, the sum in the fixed lane order above (chunks of 8 when k % 8 == 0, of 1
+ * otherwise), stored once in y_dtype; y dense [batch, m, n]. (The reference's dtype rules -- same-dtype inputs keep
+ * it, bf16 inputs may ask for f32, mixed inputs give f32 -- are applied by its callers and by the C++ drop-in.)
+ * bf16 operands with w the transposed view of a row-major [n, k] weight take the vector kernels; any other layout
+ * a warp-per-output kernel with the same order. */
+CPPINF_API int cppinf_matmul(cppinf_dtype x_dtype, const void* x, const int64_t* x_strides, cppinf_dtype w_dtype,
+                             const void* w, const int64_t* w_strides, cppinf_dtype y_dtype, void* y, int64_t batch,
+                             int64_t m, int64_t k, int64_t n, void* stream);
+
 /* y[rows, out] = bf16(x[rows, in] * weight[out, in]^T): nn::detail::linear_project (src/nn/qwen_common.cpp:15-37)
  * over ops::matmul with bf16 operands and result (src/ops/matmul.cpp:85-114). Row r of x starts at r * x_row_stride;
  * y is dense. x, weight and x_row_stride * 2 bytes must be 16-byte aligned. */

@@ -678,3 +678,33 @@ void oracle_decoder_attention(const uint16_t* q, const uint16_t* kc, const uint1
         free(grp);
     }
 }
+
+/* ops::matmul (src/ops/matmul.cpp:85-114) in the device library's order for any operand types: lhs [batch, m, k]
+ * and rhs [batch, k, n] with element strides (batch, row, column), every element read as f32 (bf16 widened
+ * exactly), y[b, i, j] = sum_p lhs[b, i, p] rhs[b, p, j] in the canonical lane order (chunk 8 when k % 8 == 0, else
+ * 1; lane l adds chunks l, l+32, ... in element order from +0; butterfly over lane distances 16..1), stored once in
+ * y_dtype, y dense [batch, m, n]. Separately rounded multiply and add (-ffp-contract=off), as on the device. */
+void oracle_matmul_canonical(int x_dtype, const void* x, const int64_t* xs, int w_dtype, const void* w,
+                             const int64_t* ws, int y_dtype, void* y, int64_t batch, int64_t m, int64_t k,
+                             int64_t n) {
+    const int64_t chunk = k % 8 == 0 ? 8 : 1;
+    const int64_t nchunks = k / chunk;
+#pragma omp parallel for schedule(static)
+    for (int64_t idx = 0; idx < batch * m * n; ++idx) {
+        const int64_t b = idx / (m * n);
+        const int64_t i = (idx / n) % m;
+        const int64_t j = idx % n;
+        float partial[32] = {0};
+        for (int64_t c = 0; c < nchunks; ++c) {
+            float a = partial[c & 31];
+            for (int64_t e = c * chunk; e < (c + 1) * chunk; ++e) {
+                const float xv = load(x_dtype, x, b * xs[0] + i * xs[1] + e * xs[2]);
+                const float wv = load(w_dtype, w, b * ws[0] + e * ws[1] + j * ws[2]);
+                a = a + xv * wv;
+            }
+            partial[c & 31] = a;
+        }
+        butterfly32(partial);
+        store(y_dtype, y, idx, partial[0]);
+    }
+}

@@ -106,6 +106,7 @@ class Oracle:
             "oracle_silu_mul_pexp": [_p, _p, _p, _l],
             "oracle_linear_canonical": [_p, _l, _p, _l, _l, _l, _p, _p],
             "oracle_decoder_attention": [_p, _p, _p, _p, _l, _l, _l, _l, _l],
+            "oracle_matmul_canonical": [_i, _p, _p, _i, _p, _p, _i, _p, _l, _l, _l, _l],
         }
         for name, args in sig.items():
             fn = getattr(self.lib, name)
@@ -262,6 +263,22 @@ class Oracle:
         self.lib.oracle_linear_canonical(_ptr(x), k, _ptr(weight), m, k, n, None if f32_out else _ptr(out),
                                          _ptr(out) if f32_out else None)
         return out
+
+    def matmul(self, lhs, rhs, out_dtype=None):
+        """ops::matmul in the device order: lhs [.., m, k], rhs [.., k, n] numpy arrays of any strides (uint16 = bf16,
+        float32 = f32); out_dtype np.uint16 / np.float32 (default: the reference's rule)."""
+        if out_dtype is None:
+            out_dtype = lhs.dtype if lhs.dtype == rhs.dtype else np.float32
+        l3 = lhs if lhs.ndim == 3 else lhs[None]
+        r3 = rhs if rhs.ndim == 3 else rhs[None]
+        b, m, k = l3.shape
+        n = r3.shape[2]
+        xs = _i64([st // l3.itemsize for st in l3.strides])
+        ws = _i64([st // r3.itemsize for st in r3.strides])
+        out = np.empty((b, m, n), dtype=out_dtype)
+        self.lib.oracle_matmul_canonical(dtype_code(l3), l3.ctypes.data_as(_p), xs, dtype_code(r3), r3.ctypes.data_as(_p),
+                                         ws, dtype_code(out), _ptr(out), b, m, k, n)
+        return out if lhs.ndim == 3 else out[0]
 
     def decoder_attention(self, q, k_cache, v_cache, pos0: int):
         """q [T, Hq, D], caches [cap, Hkv, D] (bf16); query t at position pos0 + t. Returns ctx [T, Hq, D]."""

@@ -261,3 +261,64 @@ def test_qwen3_0_6b_greedy_tokens_bit_exact(cuda, oracle):
     model.close()
     want = OracleQwen3(cfg, w, 512 + steps, oracle).generate(prompt, steps)
     assert got == want
+
+
+# ---------------------------------------------------------------------------------------------------------------
+# ops::matmul
+# ---------------------------------------------------------------------------------------------------------------
+
+
+def test_matmul_reference_kats(ops):
+    # tests/ops/ops_test.cpp:63-110, 219-257: exact small-integer and quarter-step products
+    f32 = lambda a: to_dev(np.asarray(a, np.float32))  # noqa: E731
+    b16 = lambda a: to_dev(f32_to_bf16(np.asarray(a, np.float32)))  # noqa: E731
+    lhs, rhs = [[1, 2, 3], [4, 5, 6]], [[7, 8], [9, 10], [11, 12]]
+    assert to_host(ops.matmul(f32(lhs), f32(rhs))).tolist() == [[58, 64], [139, 154]]
+    got = ops.matmul(b16(lhs), b16(rhs))
+    assert got.dtype == torch.bfloat16 and bf16_to_f32(to_host(got)).tolist() == [[58, 64], [139, 154]]
+    bl = [[[1, 2, 3], [4, 5, 6]], [[-1, 0.5, 2], [3, -2, 1]]]
+    br = [[[7, 8], [9, 10], [11, 12]], [[2, -1], [0.25, 3.5], [-4, 1.5]]]
+    want = [[[58, 64], [139, 154]], [[-9.875, 5.75], [1.5, -8.5]]]
+    assert to_host(ops.matmul(f32(bl), f32(br))).tolist() == want
+    got = ops.matmul(b16(bl), b16(br), output_dtype=torch.float32)
+    assert got.dtype == torch.float32 and to_host(got).tolist() == want
+    ml, mr = [[1, -2.5, 3.25], [4.5, 0.5, -1.75]], [[2, -1], [0.25, 3.5], [-4, 1.5]]
+    mw = [[-11.625, -4.875], [16.125, -5.375]]
+    assert to_host(ops.matmul(f32(ml), b16(mr))).tolist() == mw
+    assert to_host(ops.matmul(b16(ml), f32(mr))).tolist() == mw
+    assert bf16_to_f32(to_host(ops.matmul(b16(ml), b16(mr)))).tolist() == mw
+    strided = f32([[1, 2, 3, 4], [5, 6, 7, 8]]).reshape(2, 2, 2)[:, 1, :]  # narrow + squeeze view
+    assert to_host(ops.matmul(strided, f32([[2], [-1]]))).tolist() == [[2], [6]]
+    with pytest.raises(ValueError):
+        ops.matmul(f32(bl), f32(np.zeros((3, 3, 2))))
+    with pytest.raises(ValueError):
+        ops.matmul(f32(lhs), f32(rhs), output_dtype=torch.bfloat16)
+
+
+@pytest.mark.parametrize("b,m,k,n,dx,dw,dy,rhs_layout", [
+    (1, 7, 1024, 96, "bf16", "bf16", "bf16", "weight_t"),   # vector path: rhs = transposed weight view
+    (1, 1, 2048, 333, "bf16", "bf16", "bf16", "weight_t"),
+    (2, 5, 64, 40, "bf16", "bf16", "bf16", "dense"),        # generic path, dense rhs [k, n]
+    (3, 4, 13, 6, "f32", "f32", "f32", "dense"),            # k not a multiple of 8
+    (1, 9, 200, 17, "f32", "bf16", "f32", "weight_t"),
+    (2, 3, 48, 5, "bf16", "f32", "f32", "dense"),
+    (4, 16, 128, 33, "bf16", "bf16", "f32", "dense"),       # attention-style scores in f32
+])
+def test_matmul_bit_exact(ops, oracle, b, m, k, n, dx, dw, dy, rhs_layout):
+    rng = np.random.default_rng(b * 1000 + m + k + n)
+    def make(shape, dt):
+        a = rng.standard_normal(shape).astype(np.float32)
+        return f32_to_bf16(a) if dt == "bf16" else a
+    lhs = make((b, m, k), dx)
+    if rhs_layout == "weight_t":
+        w = make((b, n, k), dw)
+        rhs_np = np.swapaxes(w, 1, 2)
+        rhs_dev = to_dev(w).transpose(1, 2)
+    else:
+        rhs_np = make((b, k, n), dw)
+        rhs_dev = to_dev(rhs_np)
+    out_dtype = torch.bfloat16 if dy == "bf16" else torch.float32
+    got = to_host(ops.matmul(to_dev(lhs), rhs_dev, output_dtype=out_dtype))
+    want = oracle.matmul(lhs, np.ascontiguousarray(rhs_np), np.uint16 if dy == "bf16" else np.float32)
+    assert got.shape == want.shape and got.dtype == want.dtype
+    assert (got.view(np.uint32 if dy == "f32" else np.uint16) == want.view(np.uint32 if dy == "f32" else np.uint16)).all()
