@@ -89,6 +89,8 @@ _SIGNATURES = {
     "cppinf_qwen3_set_weight": [_ptr, ctypes.c_char_p, _ptr, _i64, _int],
     "cppinf_qwen3_forward": [_ptr, ctypes.POINTER(_i64), _i64, _ptr, _int, ctypes.POINTER(_i64), _ptr],
     "cppinf_qwen3_decode": [_ptr, _i64, ctypes.POINTER(_i64), _ptr],
+    "cppinf_qwen3_load_safetensors": [_ptr, ctypes.c_char_p, ctypes.POINTER(_i64)],
+    "cppinf_safetensors_info": [ctypes.c_char_p, ctypes.POINTER(_i64), ctypes.POINTER(_i64)],
     "cppinf_qwen3_reset": [_ptr, _ptr],
     "cppinf_qwen3_length": [_ptr],
     "cppinf_qwen3_step_launches": [_ptr],
@@ -187,3 +189,11 @@ def rope_table(base: float, head_dim: int, positions: int):
     call("cppinf_rope_table", float(base), int(head_dim), int(positions),
          table.ctypes.data_as(ctypes.POINTER(_f32)))
     return table
+
+
+def safetensors_info(path) -> tuple[int, int]:
+    """(tensor count, data offset) of a safetensors file, parsed by the library (cppinf_safetensors_info)."""
+    count = _i64(0)
+    offset = _i64(0)
+    call("cppinf_safetensors_info", str(path).encode(), ctypes.byref(count), ctypes.byref(offset))
+    return int(count.value), int(offset.value)

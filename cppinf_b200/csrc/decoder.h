@@ -6,6 +6,9 @@
 #include <cuda_runtime.h>
 
 #include <cstdint>
+#include <string>
+
+#include "cppinf_b200.h"
 
 namespace cppinf::device {
 
@@ -110,5 +113,10 @@ cudaError_t launch_qk_norm_rope_at(const __nv_bfloat16* q, const __nv_bfloat16* 
 // Embedding lookup (src/models/qwen3/qwen3_model.cpp:132-165): out[t] = table[tokens[t]], ids clamped into range.
 cudaError_t launch_embedding(const __nv_bfloat16* table, int64_t vocab, int64_t hidden, const int64_t* tokens,
                              int64_t count, __nv_bfloat16* out, cudaStream_t s);
+
+// Host side of the model (qwen3.cu): bytes of the named checkpoint tensor the model uses (-1 if it does not use it),
+// and how many tensors it uses.
+int64_t qwen3_tensor_bytes(const cppinf_qwen3* model, const std::string& name);
+int64_t qwen3_tensor_count(const cppinf_qwen3* model);
 
 }  // namespace cppinf::device

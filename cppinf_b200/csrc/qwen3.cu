@@ -327,6 +327,26 @@ void release(cppinf_qwen3* m) {
 
 }  // namespace
 
+namespace cppinf::device {
+
+int64_t qwen3_tensor_bytes(const cppinf_qwen3* model, const std::string& name) {
+    WeightSlot slot{};
+    // find_weight records an error message for unknown names; this probe must not disturb the caller's.
+    const std::string saved = cppinf_last_error();
+    const int st = find_weight(const_cast<cppinf_qwen3*>(model), name, &slot);
+    if (st != CPPINF_OK) {
+        rt::fail(CPPINF_ERR_INVALID_ARGUMENT, saved);
+        return -1;
+    }
+    return slot.elements * 2;
+}
+
+int64_t qwen3_tensor_count(const cppinf_qwen3* model) {
+    return 11 * model->c.num_hidden_layers + 2;
+}
+
+}  // namespace cppinf::device
+
 extern "C" {
 
 int cppinf_qwen3_create(const cppinf_qwen3_config* config, int64_t max_sequence_length, cppinf_qwen3** model) {

@@ -101,6 +101,32 @@ def random_weights(config: Qwen3Config, seed: int = 0, std: float = 0.02) -> dic
     return out
 
 
+def write_safetensors(path, tensors: dict[str, np.ndarray], metadata: dict[str, str] | None = None) -> None:
+    """Writes numpy arrays (uint16 = bf16 bits, float32 = f32) as a safetensors file: 8-byte little-endian header
+    length, JSON header (padded with spaces to a multiple of 8), tensor bytes in order."""
+    import json
+    import struct
+
+    header: dict = {}
+    if metadata:
+        header["__metadata__"] = dict(metadata)
+    offset = 0
+    blobs = []
+    for name, arr in tensors.items():
+        arr = np.ascontiguousarray(arr)
+        dtype = {np.dtype(np.uint16): "BF16", np.dtype(np.float32): "F32"}[arr.dtype]
+        header[name] = {"dtype": dtype, "shape": list(arr.shape), "data_offsets": [offset, offset + arr.nbytes]}
+        blobs.append(arr.tobytes())
+        offset += arr.nbytes
+    text = json.dumps(header, separators=(",", ":")).encode()
+    text += b" " * (-len(text) % 8)
+    with open(path, "wb") as f:
+        f.write(struct.pack("<Q", len(text)))
+        f.write(text)
+        for b in blobs:
+            f.write(b)
+
+
 class Qwen3Model:
     """Device-resident Qwen3 with one cached sequence (libcppinf_b200.so, cppinf_qwen3_*).
 
@@ -167,6 +193,18 @@ class Qwen3Model:
                     self._capi.call("cppinf_qwen3_set_weight", self._handle, name.encode(), t.data_ptr(),
                                     t.numel() * 2, 1 if t.is_cuda else 0)
             torch.cuda.synchronize(self.device)
+
+    def load_safetensors(self, path) -> int:
+        """Loads a safetensors checkpoint straight from the mapped file into the model (cppinf_qwen3_load_safetensors);
+        returns the number of tensors copied."""
+        import ctypes
+
+        import torch
+
+        n = ctypes.c_int64(0)
+        with torch.cuda.device(self.device):
+            self._capi.call("cppinf_qwen3_load_safetensors", self._handle, str(path).encode(), ctypes.byref(n))
+        return int(n.value)
 
     @property
     def length(self) -> int:

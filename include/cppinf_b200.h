@@ -267,6 +267,18 @@ CPPINF_API void cppinf_qwen3_destroy(cppinf_qwen3* model);
 CPPINF_API int cppinf_qwen3_set_weight(cppinf_qwen3* model, const char* name, const void* data, int64_t bytes,
                                        int on_device);
 
+/* Loads a safetensors checkpoint (the format of src/files/safetensors_file.cpp: 8-byte little-endian header length,
+ * JSON header of {dtype, shape, data_offsets} per tensor, tensor bytes) into the model: the file is memory-mapped and
+ * each tensor the model uses is copied from the mapping to its device slot, so no host copy of the file is made.
+ * The header is checked as the reference does (same messages); every tensor the model uses must be present and bf16
+ * (validate_required_tensors, qwen3_model.cpp:63-90); tensors it does not use are skipped. `loaded` (HOST, may be
+ * NULL) receives the number of tensors copied. */
+CPPINF_API int cppinf_qwen3_load_safetensors(cppinf_qwen3* model, const char* path, int64_t* loaded);
+
+/* Host-only check of a safetensors file's header (the same parse and checks as cppinf_qwen3_load_safetensors):
+ * number of tensors and byte offset of the tensor data. */
+CPPINF_API int cppinf_safetensors_info(const char* path, int64_t* tensor_count, int64_t* data_offset);
+
 /* Qwen3Model::forward_cached (qwen3_model.cpp:275-311): appends `count` HOST token ids to the cached sequence.
  * logits (DEVICE bf16, may be NULL) receives [count, vocab] when all_rows != 0, else the last row [vocab].
  * next_token (HOST, may be NULL) receives the greedy token of the last row (cli_app.cpp:72-94); the call then

@@ -322,3 +322,36 @@ def test_matmul_bit_exact(ops, oracle, b, m, k, n, dx, dw, dy, rhs_layout):
     want = oracle.matmul(lhs, np.ascontiguousarray(rhs_np), np.uint16 if dy == "bf16" else np.float32)
     assert got.shape == want.shape and got.dtype == want.dtype
     assert (got.view(np.uint32 if dy == "f32" else np.uint16) == want.view(np.uint32 if dy == "f32" else np.uint16)).all()
+
+
+# ---------------------------------------------------------------------------------------------------------------
+# Safetensors checkpoints straight to the device
+# ---------------------------------------------------------------------------------------------------------------
+
+
+def test_load_safetensors_matches_set_weight(cuda, tmp_path):
+    from cppinf_b200.qwen3 import Qwen3Model, random_weights, write_safetensors
+
+    cfg = small_config()
+    w = random_weights(cfg, seed=21, std=0.05)
+    extra = dict(w)
+    extra["lm_head.weight"] = w["model.embed_tokens.weight"]          # a tied checkpoint's copy: skipped
+    extra["model.rotary_emb.inv_freq"] = np.ones(64, np.float32)      # a tensor the model does not use: skipped
+    path = tmp_path / "model.safetensors"
+    write_safetensors(path, extra, {"format": "pt"})
+    tokens = np.random.default_rng(4).integers(0, cfg.vocab_size, 20)
+    from_file = Qwen3Model(cfg, 64)
+    assert from_file.load_safetensors(path) == 11 * cfg.num_hidden_layers + 2
+    want = to_host(Qwen3Model(cfg, 64, w).forward(tokens))
+    assert_bits_equal(to_host(from_file.forward(tokens)), want, "safetensors-loaded logits")
+
+    missing = dict(w)
+    del missing["model.layers.1.mlp.down_proj.weight"]
+    write_safetensors(tmp_path / "missing.safetensors", missing)
+    with pytest.raises(IndexError):
+        Qwen3Model(cfg, 64).load_safetensors(tmp_path / "missing.safetensors")
+    wrong = dict(w)
+    wrong["model.norm.weight"] = np.ones(cfg.hidden_size, np.float32)
+    write_safetensors(tmp_path / "wrong.safetensors", wrong)
+    with pytest.raises(ValueError):
+        Qwen3Model(cfg, 64).load_safetensors(tmp_path / "wrong.safetensors")
