@@ -3,8 +3,9 @@
 // cast to bf16, probabilities times V in bf16) for one sequence, query t at position pos0 + t seeing keys
 // 0 .. pos0 + t, query head h reading key/value head h / (Hq / Hkv) (the repeat_interleave of :290-291).
 //
-// One thread-block cluster of 8 CTAs (128 threads each) per (query, head); CTA c owns the c-th of 8 parts of the
-// visible keys (P = ceil(L / 8) consecutive keys each). The order of every sum is fixed, and the CPU oracle
+// One thread-block cluster of 8 CTAs (128 threads each) per (query, head) -- for a prompt, per (run of consecutive
+// queries, head), the queries taken one after another; CTA c owns the c-th of 8 parts of the visible keys
+// (P = ceil(L / 8) consecutive keys each). The order of every sum is fixed, and the CPU oracle
 // restates it (oracle_decoder_attention):
 //  - score: the head vector is cut into 8 segments of D / 8 dims, each summed in order by one lane, the 8 partials
 //    combined by a butterfly over lane distances 4, 2, 1; x_j = score * (1 / sqrt(D));
@@ -157,268 +158,282 @@ __global__ void __launch_bounds__(kThreads) decoder_attention_kernel(const Atten
     const int lane = threadIdx.x & 31;
     const int warp = threadIdx.x >> 5;
     const int64_t unit = blockIdx.x / kParts;
-    const int64_t t = unit / p.q_heads;
-    const int h = static_cast<int>(unit - t * p.q_heads);
+    const int64_t tb = unit / p.q_heads;
+    const int h = static_cast<int>(unit - tb * p.q_heads);
+    const int64_t t_begin = tb * p.queries_per_cluster;
+    const int64_t t_end = t_begin + p.queries_per_cluster < p.T ? t_begin + p.queries_per_cluster : p.T;
     const int group = p.q_heads / p.kv_heads;
     const int kvh = h / group;
     if constexpr (!kStage) {
         grid_dependency_begin();
     }
-    const int64_t pos = p.pos0 + (p.position != nullptr ? static_cast<int64_t>(*p.position) : 0) + t;
-    if (pos >= p.capacity) {
-        if constexpr (kStage) {
-            grid_dependency_begin();
-        }
-        return;  // the whole cluster leaves together (same t); no DSMEM access happens
-    }
     // Every CTA of the cluster has started once this barrier phase completes (waited on before the first DSMEM
     // store below).
     asm volatile("barrier.cluster.arrive.relaxed.aligned;" ::: "memory");
-    const int64_t L = pos + 1;
-    const int64_t P = (L + kParts - 1) / kParts;
-    const int64_t lo = rank * P < L ? rank * P : L;
-    const int64_t hi = lo + P < L ? lo + P : L;
-    const int64_t n = hi - lo;
-    const int64_t kv_row = static_cast<int64_t>(p.kv_heads) * kD;
-    const float scale = 1.0f / sqrtf(static_cast<float>(kD));
-
-    // kStage: rows [lo, staged_hi) (every cached row of this part before the new token) go to shared memory now;
-    // the previous kernel in the stream writes neither them nor the sequence length.
-    bf16* s_kt = reinterpret_cast<bf16*>(s_e + ((max_part + 3) / 4) * 4);
-    bf16* s_vt = s_kt + max_part * kD;
-    const int64_t staged_hi = hi < pos ? hi : pos;
-    const int64_t staged = staged_hi > lo ? staged_hi - lo : 0;
-    float c_rope[kFused ? 8 : 1];
-    float s_rope[kFused ? 8 : 1];
-    uint4 wq_a, wq_b, wk_a, wk_b;
-    if constexpr (kStage) {
-        if (threadIdx.x == 0) {
-            mbar_init(&s_bar, 1);
-            mbar_arrive_expect_tx(&s_bar, static_cast<uint32_t>(staged * kD * 2 * 2));
+    bool started = false;
+    // The cluster takes queries t_begin .. t_end - 1 of head h one after another, each with the same arithmetic.
+    // Between two queries every CTA has passed the previous query's last cluster barrier, so no DSMEM store of the
+    // next query lands in shared memory that is still being read.
+    for (int64_t t = t_begin; t < t_end; ++t) {
+        const int64_t pos = p.pos0 + (p.position != nullptr ? static_cast<int64_t>(*p.position) : 0) + t;
+        if (pos >= p.capacity) {
+            if constexpr (kStage) {
+                grid_dependency_begin();
+            }
+            break;  // the whole cluster leaves together (same t, later queries lie further out)
         }
-        __syncthreads();
-        if (warp == 0) {
-            for (int64_t r = lane; r < staged; r += 32) {
-                const int64_t off = (lo + r) * kv_row + kvh * kD;
-                bulk_copy_g2s(s_kt + r * kD, p.k_cache + off, kD * 2, &s_bar);
-                bulk_copy_g2s(s_vt + r * kD, p.v_cache + off, kD * 2, &s_bar);
+        const int64_t L = pos + 1;
+        const int64_t P = (L + kParts - 1) / kParts;
+        const int64_t lo = rank * P < L ? rank * P : L;
+        const int64_t hi = lo + P < L ? lo + P : L;
+        const int64_t n = hi - lo;
+        const int64_t kv_row = static_cast<int64_t>(p.kv_heads) * kD;
+        const float scale = 1.0f / sqrtf(static_cast<float>(kD));
+
+        // kStage: rows [lo, staged_hi) (every cached row of this part before the new token) go to shared memory now;
+        // the previous kernel in the stream writes neither them nor the sequence length.
+        bf16* s_kt = reinterpret_cast<bf16*>(s_e + ((max_part + 3) / 4) * 4);
+        bf16* s_vt = s_kt + max_part * kD;
+        const int64_t staged_hi = hi < pos ? hi : pos;
+        const int64_t staged = staged_hi > lo ? staged_hi - lo : 0;
+        float c_rope[kFused ? 8 : 1];
+        float s_rope[kFused ? 8 : 1];
+        uint4 wq_a, wq_b, wk_a, wk_b;
+        if constexpr (kStage) {
+            if (threadIdx.x == 0) {
+                mbar_init(&s_bar, 1);
+                mbar_arrive_expect_tx(&s_bar, static_cast<uint32_t>(staged * kD * 2 * 2));
+            }
+            __syncthreads();
+            if (warp == 0) {
+                for (int64_t r = lane; r < staged; r += 32) {
+                    const int64_t off = (lo + r) * kv_row + kvh * kD;
+                    bulk_copy_g2s(s_kt + r * kD, p.k_cache + off, kD * 2, &s_bar);
+                    bulk_copy_g2s(s_vt + r * kD, p.v_cache + off, kD * 2, &s_bar);
+                }
             }
         }
-    }
-    if constexpr (kFused) {
-        // RoPE angles of this position and the q/k norm weights: constants, read before the wait.
-        constexpr int kLanes = kD / 16;
-        const int hl = lane % kLanes;
-        const float* trow = p.rope_table + pos * kD;
-#pragma unroll
-        for (int j = 0; j < 8; ++j) {
-            c_rope[j] = trow[hl * 8 + j];
-            s_rope[j] = trow[kD / 2 + hl * 8 + j];
-        }
-        wq_a = ld_cached(p.q_norm + hl * 8);
-        wq_b = ld_cached(p.q_norm + kD / 2 + hl * 8);
-        wk_a = ld_cached(p.k_norm + hl * 8);
-        wk_b = ld_cached(p.k_norm + kD / 2 + hl * 8);
-    }
-    if constexpr (kStage) {
-        grid_dependency_begin();
-    }
-
-    if constexpr (kFused) {
-        // q-norm + RoPE of this head and k-norm + RoPE of the new key (computed by every CTA that needs them).
-        if (warp == 0) {
-            norm_rope_head<kD>(p.q + (t * p.q_heads + h) * kD, wq_a, wq_b, c_rope, s_rope, p.eps, s_q, lane);
-        } else if (warp == 1) {
-            norm_rope_head<kD>(p.k_new + (t * p.kv_heads + kvh) * kD, wk_a, wk_b, c_rope, s_rope, p.eps, s_knew,
-                               lane);
-        }
-        __syncthreads();
-        if (rank == 0 && h % group == 0 && threadIdx.x < kD / 8) {
-            // One CTA per key/value head stores the new key row; nobody reads that row in this launch.
-            st_v4(const_cast<bf16*>(p.k_cache) + pos * kv_row + kvh * kD + threadIdx.x * 8,
-                  *reinterpret_cast<const uint4*>(s_knew + threadIdx.x * 8));
-        }
-    }
-    bool stage_failed = false;
-    if constexpr (kStage) {
-        const bool arrived = mbar_wait_bounded(&s_bar, 0);
-        // On a timeout the kernel still runs every cluster barrier below (with meaningless values), so no CTA of
-        // the cluster is left waiting; the host sees the error flag.
-        stage_failed = __syncthreads_or(arrived ? 0 : 1) != 0;
-        if (stage_failed && threadIdx.x == 0) {
-            atomicOr(p.error, 1u);
-        }
-    }
-
-    // Scores: 4 keys per warp iteration, 8 lanes per key; kScoreBatch iterations' loads in flight.
-    const int sub = lane % kSegments;
-    const int slot = lane / kSegments;
-    uint4 qv[kSegChunks];
-#pragma unroll
-    for (int c = 0; c < kSegChunks; ++c) {
         if constexpr (kFused) {
-            qv[c] = *reinterpret_cast<const uint4*>(s_q + sub * kSeg + c * 8);
-        } else {
-            qv[c] = ld_cached(p.q + (t * p.q_heads + h) * kD + sub * kSeg + c * 8);
+            // RoPE angles of this position and the q/k norm weights: constants, read before the wait.
+            constexpr int kLanes = kD / 16;
+            const int hl = lane % kLanes;
+            const float* trow = p.rope_table + pos * kD;
+    #pragma unroll
+            for (int j = 0; j < 8; ++j) {
+                c_rope[j] = trow[hl * 8 + j];
+                s_rope[j] = trow[kD / 2 + hl * 8 + j];
+            }
+            wq_a = ld_cached(p.q_norm + hl * 8);
+            wq_b = ld_cached(p.q_norm + kD / 2 + hl * 8);
+            wk_a = ld_cached(p.k_norm + hl * 8);
+            wk_b = ld_cached(p.k_norm + kD / 2 + hl * 8);
         }
-    }
-    constexpr int kIterKeys = kWarps * kKeysPerIter;
-    for (int64_t j0 = lo + warp * kKeysPerIter; j0 < hi; j0 += kIterKeys * kScoreBatch) {
-        uint4 kv[kScoreBatch][kSegChunks];
-#pragma unroll
-        for (int u = 0; u < kScoreBatch; ++u) {
-            const int64_t j = j0 + u * kIterKeys + slot;
-#pragma unroll
-            for (int c = 0; c < kSegChunks; ++c) {
-                if (j >= hi) {
-                    kv[u][c] = make_uint4(0u, 0u, 0u, 0u);
-                } else if (kFused && j == L - 1) {
-                    kv[u][c] = *reinterpret_cast<const uint4*>(s_knew + sub * kSeg + c * 8);
-                } else if (kStage) {
-                    kv[u][c] = *reinterpret_cast<const uint4*>(s_kt + (j - lo) * kD + sub * kSeg + c * 8);
-                } else {
-                    kv[u][c] = ld_cached(p.k_cache + j * kv_row + kvh * kD + sub * kSeg + c * 8);
+        if constexpr (kStage) {
+            grid_dependency_begin();
+        }
+
+        if constexpr (kFused) {
+            // q-norm + RoPE of this head and k-norm + RoPE of the new key (computed by every CTA that needs them).
+            if (warp == 0) {
+                norm_rope_head<kD>(p.q + (t * p.q_heads + h) * kD, wq_a, wq_b, c_rope, s_rope, p.eps, s_q, lane);
+            } else if (warp == 1) {
+                norm_rope_head<kD>(p.k_new + (t * p.kv_heads + kvh) * kD, wk_a, wk_b, c_rope, s_rope, p.eps, s_knew,
+                                   lane);
+            }
+            __syncthreads();
+            if (rank == 0 && h % group == 0 && threadIdx.x < kD / 8) {
+                // One CTA per key/value head stores the new key row; nobody reads that row in this launch.
+                st_v4(const_cast<bf16*>(p.k_cache) + pos * kv_row + kvh * kD + threadIdx.x * 8,
+                      *reinterpret_cast<const uint4*>(s_knew + threadIdx.x * 8));
+            }
+        }
+        bool stage_failed = false;
+        if constexpr (kStage) {
+            const bool arrived = mbar_wait_bounded(&s_bar, 0);
+            // On a timeout the kernel still runs every cluster barrier below (with meaningless values), so no CTA of
+            // the cluster is left waiting; the host sees the error flag.
+            stage_failed = __syncthreads_or(arrived ? 0 : 1) != 0;
+            if (stage_failed && threadIdx.x == 0) {
+                atomicOr(p.error, 1u);
+            }
+        }
+
+        // Scores: 4 keys per warp iteration, 8 lanes per key; kScoreBatch iterations' loads in flight.
+        const int sub = lane % kSegments;
+        const int slot = lane / kSegments;
+        uint4 qv[kSegChunks];
+    #pragma unroll
+        for (int c = 0; c < kSegChunks; ++c) {
+            if constexpr (kFused) {
+                qv[c] = *reinterpret_cast<const uint4*>(s_q + sub * kSeg + c * 8);
+            } else {
+                qv[c] = ld_cached(p.q + (t * p.q_heads + h) * kD + sub * kSeg + c * 8);
+            }
+        }
+        constexpr int kIterKeys = kWarps * kKeysPerIter;
+        for (int64_t j0 = lo + warp * kKeysPerIter; j0 < hi; j0 += kIterKeys * kScoreBatch) {
+            uint4 kv[kScoreBatch][kSegChunks];
+    #pragma unroll
+            for (int u = 0; u < kScoreBatch; ++u) {
+                const int64_t j = j0 + u * kIterKeys + slot;
+    #pragma unroll
+                for (int c = 0; c < kSegChunks; ++c) {
+                    if (j >= hi) {
+                        kv[u][c] = make_uint4(0u, 0u, 0u, 0u);
+                    } else if (kFused && j == L - 1) {
+                        kv[u][c] = *reinterpret_cast<const uint4*>(s_knew + sub * kSeg + c * 8);
+                    } else if (kStage) {
+                        kv[u][c] = *reinterpret_cast<const uint4*>(s_kt + (j - lo) * kD + sub * kSeg + c * 8);
+                    } else {
+                        kv[u][c] = ld_cached(p.k_cache + j * kv_row + kvh * kD + sub * kSeg + c * 8);
+                    }
+                }
+            }
+    #pragma unroll
+            for (int u = 0; u < kScoreBatch; ++u) {
+                const int64_t j = j0 + u * kIterKeys + slot;
+                float s = 0.0f;
+    #pragma unroll
+                for (int c = 0; c < kSegChunks; ++c) {
+                    s = dot8(qv[c], kv[u][c], s);
+                }
+    #pragma unroll
+                for (int offset = kSegments / 2; offset > 0; offset >>= 1) {
+                    s = s + __shfl_xor_sync(0xffffffffu, s, offset);
+                }
+                if (j < hi && sub == 0) {
+                    s_e[j - lo] = s * scale;
                 }
             }
         }
-#pragma unroll
-        for (int u = 0; u < kScoreBatch; ++u) {
-            const int64_t j = j0 + u * kIterKeys + slot;
-            float s = 0.0f;
-#pragma unroll
-            for (int c = 0; c < kSegChunks; ++c) {
-                s = dot8(qv[c], kv[u][c], s);
-            }
-#pragma unroll
-            for (int offset = kSegments / 2; offset > 0; offset >>= 1) {
-                s = s + __shfl_xor_sync(0xffffffffu, s, offset);
-            }
-            if (j < hi && sub == 0) {
-                s_e[j - lo] = s * scale;
-            }
-        }
-    }
-    __syncthreads();
+        __syncthreads();
 
-    // This part's maximum and its sum of exp(x - max) (slot order, warp butterfly, warps in order).
-    float mx = -INFINITY;
-    for (int64_t i = threadIdx.x; i < n; i += kThreads) {
-        mx = fmaxf(mx, s_e[i]);
-    }
-    mx = group_max<32>(mx);
-    if (lane == 0) {
-        s_red[warp] = mx;
-    }
-    __syncthreads();
-    if (threadIdx.x == 0) {
-        float m = s_red[0];
-#pragma unroll
-        for (int w = 1; w < kWarps; ++w) {
-            m = fmaxf(m, s_red[w]);
+        // This part's maximum and its sum of exp(x - max) (slot order, warp butterfly, warps in order).
+        float mx = -INFINITY;
+        for (int64_t i = threadIdx.x; i < n; i += kThreads) {
+            mx = fmaxf(mx, s_e[i]);
         }
-        s_local = m;
-    }
-    __syncthreads();
-    const float local_max = s_local;
-    float sum = 0.0f;
-    for (int64_t i = threadIdx.x; i < n; i += kThreads) {
-        sum = sum + pexp(s_e[i] - local_max);
-    }
-    sum = group_sum<32>(sum);
-    __syncthreads();  // s_red is reused
-    if (lane == 0) {
-        s_red[warp] = sum;
-    }
-    __syncthreads();
-    asm volatile("barrier.cluster.wait.aligned;" ::: "memory");  // every CTA has started: DSMEM is usable
-    if (threadIdx.x < kParts) {
-        float part_sum = s_red[0];
-#pragma unroll
-        for (int w = 1; w < kWarps; ++w) {
-            part_sum = part_sum + s_red[w];
+        mx = group_max<32>(mx);
+        if (lane == 0) {
+            s_red[warp] = mx;
         }
-        // Push (max, sum) of this part to every CTA of the cluster, this one included.
-        *cluster.map_shared_rank(&s_m[rank], static_cast<int>(threadIdx.x)) = local_max;
-        *cluster.map_shared_rank(&s_s[rank], static_cast<int>(threadIdx.x)) = part_sum;
-    }
-    cluster.sync();
-    // Global max M and total = sum over parts (in order) of part_sum * exp(part_max - M).
-    float gmax = s_m[0];
-#pragma unroll
-    for (int r = 1; r < kParts; ++r) {
-        gmax = fmaxf(gmax, s_m[r]);
-    }
-    float total = s_s[0] * pexp(s_m[0] - gmax);
-#pragma unroll
-    for (int r = 1; r < kParts; ++r) {
-        total = total + s_s[r] * pexp(s_m[r] - gmax);
-    }
-
-    for (int64_t i = threadIdx.x; i < n; i += kThreads) {
-        s_e[i] = round_to_bf16(pexp(s_e[i] - gmax) / total);
-    }
-    __syncthreads();
-
-    // Probabilities times V: warp w takes keys lo + w, lo + w + 4, ..., kValueBatch rows in flight.
-    float a[kDimsPerLane];
-#pragma unroll
-    for (int d = 0; d < kDimsPerLane; ++d) {
-        a[d] = 0.0f;
-    }
-    const bf16* vbase = p.v_cache + kvh * kD + lane * kDimsPerLane;
-    for (int64_t j0 = lo + warp; j0 < hi; j0 += kWarps * kValueBatch) {
-        typename VRow<kD>::Raw raw[kValueBatch];
-#pragma unroll
-        for (int u = 0; u < kValueBatch; ++u) {
-            const int64_t j = j0 + u * kWarps;
-            if (j < hi) {
-                if (kStage && j < staged_hi) {
-                    raw[u] = *reinterpret_cast<const typename VRow<kD>::Raw*>(s_vt + (j - lo) * kD +
-                                                                             lane * kDimsPerLane);
-                } else {
-                    raw[u] = VRow<kD>::load(vbase + j * kv_row);
-                }
+        __syncthreads();
+        if (threadIdx.x == 0) {
+            float m = s_red[0];
+    #pragma unroll
+            for (int w = 1; w < kWarps; ++w) {
+                m = fmaxf(m, s_red[w]);
             }
+            s_local = m;
         }
-#pragma unroll
-        for (int u = 0; u < kValueBatch; ++u) {
-            const int64_t j = j0 + u * kWarps;
-            if (j < hi) {
-                const float pj = s_e[j - lo];
-                float v[kDimsPerLane];
-                VRow<kD>::unpack(raw[u], v);
-#pragma unroll
-                for (int d = 0; d < kDimsPerLane; ++d) {
-                    a[d] = a[d] + pj * v[d];
-                }
+        __syncthreads();
+        const float local_max = s_local;
+        float sum = 0.0f;
+        for (int64_t i = threadIdx.x; i < n; i += kThreads) {
+            sum = sum + pexp(s_e[i] - local_max);
+        }
+        sum = group_sum<32>(sum);
+        __syncthreads();  // s_red is reused
+        if (lane == 0) {
+            s_red[warp] = sum;
+        }
+        __syncthreads();
+        if (!started) {
+            asm volatile("barrier.cluster.wait.aligned;" ::: "memory");  // every CTA has started: DSMEM is usable
+            started = true;
+        }
+        if (threadIdx.x < kParts) {
+            float part_sum = s_red[0];
+    #pragma unroll
+            for (int w = 1; w < kWarps; ++w) {
+                part_sum = part_sum + s_red[w];
             }
+            // Push (max, sum) of this part to every CTA of the cluster, this one included.
+            *cluster.map_shared_rank(&s_m[rank], static_cast<int>(threadIdx.x)) = local_max;
+            *cluster.map_shared_rank(&s_s[rank], static_cast<int>(threadIdx.x)) = part_sum;
         }
-    }
-#pragma unroll
-    for (int d = 0; d < kDimsPerLane; ++d) {
-        s_acc[warp][lane * kDimsPerLane + d] = a[d];
-    }
-    __syncthreads();
-    for (int d = threadIdx.x; d < kD; d += kThreads) {
-        float part = s_acc[0][d];
-#pragma unroll
-        for (int w = 1; w < kWarps; ++w) {
-            part = part + s_acc[w][d];
-        }
-        // Push the partial of dim d to the CTA that finishes it.
-        *cluster.map_shared_rank(&s_recv[rank][d % kFinal], d / kFinal) = part;
-    }
-    cluster.sync();  // after this no CTA touches another's shared memory
-    if (threadIdx.x < kFinal) {
-        float c = s_recv[0][threadIdx.x];
-#pragma unroll
+        cluster.sync();
+        // Global max M and total = sum over parts (in order) of part_sum * exp(part_max - M).
+        float gmax = s_m[0];
+    #pragma unroll
         for (int r = 1; r < kParts; ++r) {
-            c = c + s_recv[r][threadIdx.x];
+            gmax = fmaxf(gmax, s_m[r]);
         }
-        Vec16<bf16>::store1(p.ctx, (t * p.q_heads + h) * kD + rank * kFinal + threadIdx.x, c);
+        float total = s_s[0] * pexp(s_m[0] - gmax);
+    #pragma unroll
+        for (int r = 1; r < kParts; ++r) {
+            total = total + s_s[r] * pexp(s_m[r] - gmax);
+        }
+
+        for (int64_t i = threadIdx.x; i < n; i += kThreads) {
+            s_e[i] = round_to_bf16(pexp(s_e[i] - gmax) / total);
+        }
+        __syncthreads();
+
+        // Probabilities times V: warp w takes keys lo + w, lo + w + 4, ..., kValueBatch rows in flight.
+        float a[kDimsPerLane];
+    #pragma unroll
+        for (int d = 0; d < kDimsPerLane; ++d) {
+            a[d] = 0.0f;
+        }
+        const bf16* vbase = p.v_cache + kvh * kD + lane * kDimsPerLane;
+        for (int64_t j0 = lo + warp; j0 < hi; j0 += kWarps * kValueBatch) {
+            typename VRow<kD>::Raw raw[kValueBatch];
+    #pragma unroll
+            for (int u = 0; u < kValueBatch; ++u) {
+                const int64_t j = j0 + u * kWarps;
+                if (j < hi) {
+                    if (kStage && j < staged_hi) {
+                        raw[u] = *reinterpret_cast<const typename VRow<kD>::Raw*>(s_vt + (j - lo) * kD +
+                                                                                 lane * kDimsPerLane);
+                    } else {
+                        raw[u] = VRow<kD>::load(vbase + j * kv_row);
+                    }
+                }
+            }
+    #pragma unroll
+            for (int u = 0; u < kValueBatch; ++u) {
+                const int64_t j = j0 + u * kWarps;
+                if (j < hi) {
+                    const float pj = s_e[j - lo];
+                    float v[kDimsPerLane];
+                    VRow<kD>::unpack(raw[u], v);
+    #pragma unroll
+                    for (int d = 0; d < kDimsPerLane; ++d) {
+                        a[d] = a[d] + pj * v[d];
+                    }
+                }
+            }
+        }
+    #pragma unroll
+        for (int d = 0; d < kDimsPerLane; ++d) {
+            s_acc[warp][lane * kDimsPerLane + d] = a[d];
+        }
+        __syncthreads();
+        for (int d = threadIdx.x; d < kD; d += kThreads) {
+            float part = s_acc[0][d];
+    #pragma unroll
+            for (int w = 1; w < kWarps; ++w) {
+                part = part + s_acc[w][d];
+            }
+            // Push the partial of dim d to the CTA that finishes it.
+            *cluster.map_shared_rank(&s_recv[rank][d % kFinal], d / kFinal) = part;
+        }
+        cluster.sync();  // after this no CTA touches another's shared memory
+        if (threadIdx.x < kFinal) {
+            float c = s_recv[0][threadIdx.x];
+    #pragma unroll
+            for (int r = 1; r < kParts; ++r) {
+                c = c + s_recv[r][threadIdx.x];
+            }
+            Vec16<bf16>::store1(p.ctx, (t * p.q_heads + h) * kD + rank * kFinal + threadIdx.x, c);
+        }
+        if (kStage && stage_failed) {
+            mbar_wait_bounded(&s_bar, 0);  // no bulk copy may land after this CTA has left
+        }
     }
-    if (kStage && stage_failed) {
-        mbar_wait_bounded(&s_bar, 0);  // no bulk copy may land after this CTA has left
+    if (!started) {
+        asm volatile("barrier.cluster.wait.aligned;" ::: "memory");
     }
 }
 
@@ -435,9 +450,19 @@ cudaError_t launch_attention_variant(const AttentionParams& p, int64_t max_part,
             return err;
         }
     }
-    const int64_t blocks = p.T * p.q_heads * kParts;
+    const int64_t blocks = (p.T + p.queries_per_cluster - 1) / p.queries_per_cluster * p.q_heads * kParts;
     return runtime::launch_smem(kernel, dim3(static_cast<unsigned>(blocks)), dim3(kThreads), smem, s,
                                 static_cast<unsigned>(kParts), p, max_part);
+}
+
+// Prefill: a cluster takes several consecutive queries of one head in turn, so that a long prompt launches a few
+// waves of clusters instead of one short-lived cluster per (query, head).
+constexpr int64_t kTargetClusters = 1024;
+constexpr int64_t kMaxQueriesPerCluster = 16;
+
+int64_t queries_per_cluster(int64_t tokens, int64_t heads) {
+    const int64_t q = tokens * heads / kTargetClusters;
+    return q < 1 ? 1 : (q > kMaxQueriesPerCluster ? kMaxQueriesPerCluster : q);
 }
 
 template <int kD>
@@ -452,7 +477,9 @@ cudaError_t launch_attention_dim(const AttentionParams& p, int64_t max_keys, cud
         }
         return launch_attention_variant<kD, true, false>(p, max_part, score_bytes, s);
     }
-    return launch_attention_variant<kD, false, false>(p, max_part, score_bytes, s);
+    AttentionParams walk = p;
+    walk.queries_per_cluster = queries_per_cluster(p.T, p.q_heads);
+    return launch_attention_variant<kD, false, false>(walk, max_part, score_bytes, s);
 }
 
 }  // namespace

@@ -98,6 +98,7 @@ struct AttentionParams {
     // then read before the wait too, so the preceding kernel must not write it); a bounded wait that runs out
     // sets *error to 1.
     unsigned int* error;
+    int64_t queries_per_cluster = 1;  // consecutive queries one cluster takes in turn (prefill)
 };
 
 // Causal GQA attention of one sequence in the fixed partition order (see attention.cu). head_dim 64, 128 or 256.

@@ -689,6 +689,130 @@ __global__ void __launch_bounds__(kThreads) linear_rows_kernel(const LinearParam
     }
 }
 
+// Prefill projection with the 16-row input tile staged in shared memory as f32 (two planes: elements 0-3 and 4-7 of
+// every chunk, so a lane's 16-byte reads are conflict-free), and two weight rows (or the gate and up rows of one
+// output) per warp, so each staged input chunk feeds 16 multiply-adds. Same per-output order as the other kernels.
+template <LinearEpilogue kEpi>
+__global__ void __launch_bounds__(kThreads, 2) linear_rows_f32x_kernel(const LinearParams p) {
+    extern __shared__ float4 smem_xf[];  // [2 planes][kTileRows][K / 8]
+    grid_dependency_begin();
+    constexpr int kMats = mats_of<kEpi>();
+    constexpr int kSlots = 2;                      // weight rows a warp multiplies together
+    constexpr int kRowsPerWarp = kSlots / kMats;   // outputs a warp finishes per pass
+    constexpr int kBatch = 2;
+    const int lane = threadIdx.x & 31;
+    const int warp = threadIdx.x >> 5;
+    const int64_t nchunks = p.K / 8;
+    const int64_t plane = kTileRows * nchunks;
+    const int64_t m0 = static_cast<int64_t>(blockIdx.y) * kTileRows;
+    const int64_t mt = p.M - m0 < kTileRows ? p.M - m0 : kTileRows;
+    const int64_t row_bytes = p.K * 2;
+
+    for (int64_t i = threadIdx.x; i < plane; i += kThreads) {
+        const int64_t m = i / nchunks;
+        const int64_t c = i - m * nchunks;
+        float f[8] = {0.0f, 0.0f, 0.0f, 0.0f, 0.0f, 0.0f, 0.0f, 0.0f};
+        if (m < mt) {
+            Vec16<bf16>::unpack(ld_cached(input_row(p, m0 + m, 0) + c * 8), f);
+        }
+        smem_xf[i] = make_float4(f[0], f[1], f[2], f[3]);
+        smem_xf[plane + i] = make_float4(f[4], f[5], f[6], f[7]);
+    }
+    __syncthreads();
+
+    const int64_t step = static_cast<int64_t>(gridDim.x) * kWarps * kRowsPerWarp;
+    for (int64_t n0 = (static_cast<int64_t>(blockIdx.x) * kWarps + warp) * kRowsPerWarp; n0 < p.N; n0 += step) {
+        const char* wrows[kSlots];
+        bool valid[kSlots];
+#pragma unroll
+        for (int sl = 0; sl < kSlots; ++sl) {
+            const int mat = kMats == 2 ? sl : 0;
+            const int64_t n = kMats == 2 ? n0 : n0 + sl;
+            valid[sl] = n < p.N;
+            wrows[sl] = reinterpret_cast<const char*>(mat == 0 ? p.w0 : p.w1) + (valid[sl] ? n : 0) * row_bytes;
+        }
+        float acc[kSlots][kTileRows];
+#pragma unroll
+        for (int sl = 0; sl < kSlots; ++sl) {
+#pragma unroll
+            for (int m = 0; m < kTileRows; ++m) {
+                acc[sl][m] = 0.0f;
+            }
+        }
+        for (int64_t i0 = 0; lane + 32 * i0 < nchunks; i0 += kBatch) {
+            uint4 wraw[kSlots][kBatch];
+#pragma unroll
+            for (int sl = 0; sl < kSlots; ++sl) {
+#pragma unroll
+                for (int b = 0; b < kBatch; ++b) {
+                    const int64_t c = lane + 32 * (i0 + b);
+                    wraw[sl][b] = (valid[sl] && c < nchunks) ? ld_stream(wrows[sl] + c * 16) : make_uint4(0u, 0u, 0u, 0u);
+                }
+            }
+#pragma unroll
+            for (int b = 0; b < kBatch; ++b) {
+                const int64_t c = lane + 32 * (i0 + b);
+                if (c < nchunks) {
+                    float w[kSlots][8];
+#pragma unroll
+                    for (int sl = 0; sl < kSlots; ++sl) {
+                        Vec16<bf16>::unpack(wraw[sl][b], w[sl]);
+                    }
+#pragma unroll
+                    for (int m = 0; m < kTileRows; ++m) {
+                        const float4 xa = smem_xf[m * nchunks + c];
+                        const float4 xb = smem_xf[plane + m * nchunks + c];
+#pragma unroll
+                        for (int sl = 0; sl < kSlots; ++sl) {
+                            float a = acc[sl][m];
+                            a = a + xa.x * w[sl][0];
+                            a = a + xa.y * w[sl][1];
+                            a = a + xa.z * w[sl][2];
+                            a = a + xa.w * w[sl][3];
+                            a = a + xb.x * w[sl][4];
+                            a = a + xb.y * w[sl][5];
+                            a = a + xb.z * w[sl][6];
+                            a = a + xb.w * w[sl][7];
+                            acc[sl][m] = a;
+                        }
+                    }
+                }
+            }
+        }
+#pragma unroll
+        for (int sl = 0; sl < kSlots; ++sl) {
+#pragma unroll
+            for (int m = 0; m < kTileRows; ++m) {
+                acc[sl][m] = group_sum<32>(acc[sl][m]);
+            }
+        }
+#pragma unroll
+        for (int m = 0; m < kTileRows; ++m) {
+            if (lane == m && m < mt) {
+                const int64_t row = m0 + m;
+                if constexpr (kEpi == LinearEpilogue::kSiluMul) {
+                    const float gate = round_to_bf16(acc[0][m]);
+                    const float up = round_to_bf16(acc[1][m]);
+                    Vec16<bf16>::store1(p.out[0], row * p.ld[0] + n0, round_to_bf16(silu_pexp(gate)) * up);
+                } else {
+#pragma unroll
+                    for (int sl = 0; sl < kSlots; ++sl) {
+                        const int64_t n = n0 + sl;
+                        if (valid[sl]) {
+                            if constexpr (kEpi == LinearEpilogue::kStore) {
+                                store_segment(p, row, n, acc[sl][m], 0);
+                            } else {
+                                const float res = Vec16<bf16>::load1(p.residual, row * p.res_ld + n);
+                                Vec16<bf16>::store1(p.out[0], row * p.ld[0] + n, res + round_to_bf16(acc[sl][m]));
+                            }
+                        }
+                    }
+                }
+            }
+        }
+    }
+}
+
 // ops::matmul for any operand types and strides: one warp per output element, the canonical lane order with chunks
 // of 8 when K % 8 == 0 and of 1 otherwise (the same order as the vector kernels, so a bf16 layout they accept gives
 // the same bits either way). Used for shapes and layouts the vector kernels do not take.
@@ -876,8 +1000,10 @@ cudaError_t launch_gemv_epi(const LinearParams& p, cudaStream_t s) {
 
 template <LinearEpilogue kEpi>
 cudaError_t launch_rows_epi(const LinearParams& p, cudaStream_t s) {
-    const std::size_t smem = static_cast<std::size_t>(kTileRows) * p.K * 2;
-    auto kernel = linear_rows_kernel<kEpi>;
+    // f32 staging while the tile fits an SM's shared memory (K <= 3584), bf16 staging beyond.
+    const bool f32x = static_cast<std::size_t>(kTileRows) * p.K * 4 <= 224 * 1024;
+    const std::size_t smem = static_cast<std::size_t>(kTileRows) * p.K * (f32x ? 4 : 2);
+    auto kernel = f32x ? linear_rows_f32x_kernel<kEpi> : linear_rows_kernel<kEpi>;
     if (smem > 48 * 1024) {
         const cudaError_t err =
             cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));

@@ -145,6 +145,9 @@ def test_embedding(ops):
     (33, 5, 16, 8, 128),    # prefill chunk after a cached prefix
     (64, 0, 4, 4, 64),
     (9, 300, 8, 2, 256),
+    (301, 20, 16, 8, 128),  # prompt: clusters take runs of consecutive queries, the last run shorter
+    (512, 0, 16, 8, 128),
+    (200, 440, 32, 4, 64),
 ])
 def test_decoder_attention_bit_exact(ops, oracle, t, pos, hq, hkv, d):
     rng = np.random.default_rng(t * 1000 + pos + d)
