@@ -99,6 +99,18 @@ __device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t* bar, uint32_t by
                  : "memory");
 }
 
+// Per-thread asynchronous 16-byte copy global -> shared (L2 only, no L1 allocation, 256-byte L2 prefetch). The
+// data lands in shared memory without passing through registers; cp_async_wait_all() waits for the calling
+// thread's copies (a hardware wait, like a load's scoreboard), after which a __syncwarp()/__syncthreads() makes
+// them visible to the other threads.
+__device__ __forceinline__ void cp_async16(void* dst, const void* src) {
+    asm volatile("cp.async.cg.shared.global.L2::256B [%0], [%1], 16;" ::"r"(smem_addr(dst)), "l"(src) : "memory");
+}
+
+__device__ __forceinline__ void cp_async_wait_all() {
+    asm volatile("cp.async.wait_all;" ::: "memory");
+}
+
 __device__ __forceinline__ void bulk_copy_g2s(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
     asm volatile(
         "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(

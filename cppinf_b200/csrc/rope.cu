@@ -55,10 +55,21 @@ struct QkParams {
     int64_t table_positions;
 };
 
+// Shared-memory slot of one warp: the unit's raw head vectors (lane-major, each lane reads back what it copied),
+// the token's angle row and the two norm weight vectors.
+template <typename T, int kLanes, int kIters>
+struct QkSlot {
+    static constexpr int kDim = 2 * kLanes * Vec16<T>::kVec;
+    static constexpr int kWeightChunks = kDim * static_cast<int>(sizeof(T)) / 16;
+    uint4 data[kIters][2][32];
+    __align__(16) float table[kDim];
+    uint4 weights[2][kWeightChunks];
+};
+
 template <typename T, int kLanes, int kIters>
 __global__ void __launch_bounds__(kQkThreads) qk_norm_rope_kernel(QkParams p) {
-    grid_dependency_begin();
     using V = Vec16<T>;
+    using Slot = QkSlot<T, kLanes, kIters>;
     constexpr int kVec = V::kVec;
     constexpr int kHalf = kLanes * kVec;  // D / 2
     constexpr int kDim = 2 * kHalf;
@@ -66,7 +77,11 @@ __global__ void __launch_bounds__(kQkThreads) qk_norm_rope_kernel(QkParams p) {
     constexpr int kHeadsPerUnit = kHeadsPerIter * kIters;
     constexpr int64_t kHeadBytes = kDim * static_cast<int64_t>(sizeof(T));
     constexpr int kHalfBytes = kHalf * static_cast<int>(sizeof(T));
+    constexpr int kTableChunks = kDim * 4 / 16;
+    constexpr int kWeightChunks = Slot::kWeightChunks;
+    __shared__ Slot s_slot[kQkWarps];
 
+    grid_dependency_begin();
     const int lane = threadIdx.x & 31;
     const int hl = lane % kLanes;  // lane within the head
     const int slot = lane / kLanes;
@@ -81,10 +96,10 @@ __global__ void __launch_bounds__(kQkThreads) qk_norm_rope_kernel(QkParams p) {
     if (p.position != nullptr && p.position_offset + shift + t >= p.table_positions) {
         return;
     }
+    Slot& w = s_slot[threadIdx.x / 32];
 
-    // All loads of the unit first: kIters x 2 vectors per lane in flight.
-    uint4 first_raw[kIters];
-    uint4 second_raw[kIters];
+    // Every load of the unit is issued as an asynchronous copy into the warp's slot before any arithmetic: the
+    // values wait in shared memory rather than in registers, which keeps the kernel at more resident warps per SM.
 #pragma unroll
     for (int i = 0; i < kIters; ++i) {
         const int h = h0 + i * kHeadsPerIter + slot;
@@ -92,32 +107,22 @@ __global__ void __launch_bounds__(kQkThreads) qk_norm_rope_kernel(QkParams p) {
             const char* src = h < p.q_heads
                                   ? static_cast<const char*>(p.q) + (t * p.q_heads + h) * kHeadBytes
                                   : static_cast<const char*>(p.k) + (t * p.k_heads + (h - p.q_heads)) * kHeadBytes;
-            first_raw[i] = ld_stream(src + hl * 16);
-            second_raw[i] = ld_stream(src + kHalfBytes + hl * 16);
+            cp_async16(&w.data[i][0][lane], src + hl * 16);
+            cp_async16(&w.data[i][1][lane], src + kHalfBytes + hl * 16);
         }
     }
-
-    // cos / sin of pairs hl*kVec .. hl*kVec + kVec - 1 at this token's position.
-    const float* row = p.table + (p.position_offset + shift + t) * kDim + hl * kVec;
-    float c[kVec];
-    float s[kVec];
-#pragma unroll
-    for (int j = 0; j < kVec; j += 4) {
-        const float4 cv = ld_cached_f4(row + j);
-        const float4 sv = ld_cached_f4(row + kHalf + j);
-        c[j] = cv.x;
-        c[j + 1] = cv.y;
-        c[j + 2] = cv.z;
-        c[j + 3] = cv.w;
-        s[j] = sv.x;
-        s[j + 1] = sv.y;
-        s[j + 2] = sv.z;
-        s[j + 3] = sv.w;
+    // cos in [0, D/2) and sin in [D/2, D) of this token's position, then the q and k norm weights.
+    const char* row = reinterpret_cast<const char*>(p.table + (p.position_offset + shift + t) * kDim);
+    for (int c = lane; c < kTableChunks; c += 32) {
+        cp_async16(&w.table[c * 4], row + c * 16);
     }
-    const uint4 qw_first = ld_cached(static_cast<const char*>(p.qw) + hl * 16);
-    const uint4 qw_second = ld_cached(static_cast<const char*>(p.qw) + kHalfBytes + hl * 16);
-    const uint4 kw_first = ld_cached(static_cast<const char*>(p.kw) + hl * 16);
-    const uint4 kw_second = ld_cached(static_cast<const char*>(p.kw) + kHalfBytes + hl * 16);
+    for (int c = lane; c < 2 * kWeightChunks; c += 32) {
+        const bool is_q = c < kWeightChunks;
+        const int chunk = is_q ? c : c - kWeightChunks;
+        cp_async16(&w.weights[is_q ? 0 : 1][chunk], static_cast<const char*>(is_q ? p.qw : p.kw) + chunk * 16);
+    }
+    cp_async_wait_all();
+    __syncwarp();
 
 #pragma unroll
     for (int i = 0; i < kIters; ++i) {
@@ -126,8 +131,8 @@ __global__ void __launch_bounds__(kQkThreads) qk_norm_rope_kernel(QkParams p) {
         float a[kVec];
         float b[kVec];
         if (active) {
-            V::unpack(first_raw[i], a);
-            V::unpack(second_raw[i], b);
+            V::unpack(w.data[i][0][lane], a);
+            V::unpack(w.data[i][1][lane], b);
         } else {
 #pragma unroll
             for (int j = 0; j < kVec; ++j) {
@@ -151,11 +156,26 @@ __global__ void __launch_bounds__(kQkThreads) qk_norm_rope_kernel(QkParams p) {
         const float rms = sqrtf(mean + p.eps);
         const float inv = 1.0f / rms;
         if (active) {
-            const bool is_q = h < p.q_heads;
+            const int which = h < p.q_heads ? 0 : 1;
             float wa[kVec];
             float wb[kVec];
-            V::unpack(is_q ? qw_first : kw_first, wa);
-            V::unpack(is_q ? qw_second : kw_second, wb);
+            V::unpack(w.weights[which][hl], wa);
+            V::unpack(w.weights[which][kLanes + hl], wb);
+            float c[kVec];
+            float s[kVec];
+#pragma unroll
+            for (int j = 0; j < kVec; j += 4) {
+                const float4 cv = *reinterpret_cast<const float4*>(&w.table[hl * kVec + j]);
+                const float4 sv = *reinterpret_cast<const float4*>(&w.table[kHalf + hl * kVec + j]);
+                c[j] = cv.x;
+                c[j + 1] = cv.y;
+                c[j + 2] = cv.z;
+                c[j + 3] = cv.w;
+                s[j] = sv.x;
+                s[j + 1] = sv.y;
+                s[j + 2] = sv.z;
+                s[j + 3] = sv.w;
+            }
             float out_a[kVec];
             float out_b[kVec];
 #pragma unroll
