@@ -190,6 +190,11 @@ struct Vec16<bf16> {
     }
     // Value as stored: rounds f32 to bf16 and back.
     __device__ __forceinline__ static float quantize(float v) { return round_to_bf16(v); }
+    // Two values as stored (one rounding instruction for both).
+    __device__ __forceinline__ static float2 quantize2(float x, float y) {
+        const uint32_t w = pack_bf16x2(x, y);
+        return make_float2(bf16_lo(w), bf16_hi(w));
+    }
     __device__ __forceinline__ static float load1(const void* base, int64_t i) {
         const uint16_t bits = __ldg(reinterpret_cast<const unsigned short*>(base) + i);
         return __uint_as_float(static_cast<uint32_t>(bits) << 16);
@@ -212,6 +217,7 @@ struct Vec16<float> {
         return make_uint4(__float_as_uint(f[0]), __float_as_uint(f[1]), __float_as_uint(f[2]), __float_as_uint(f[3]));
     }
     __device__ __forceinline__ static float quantize(float v) { return v; }
+    __device__ __forceinline__ static float2 quantize2(float x, float y) { return make_float2(x, y); }
     __device__ __forceinline__ static float load1(const void* base, int64_t i) {
         return __ldg(reinterpret_cast<const float*>(base) + i);
     }

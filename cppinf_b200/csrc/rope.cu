@@ -140,15 +140,17 @@ __global__ void __launch_bounds__(kQkThreads) qk_norm_rope_kernel(QkParams p) {
                 b[j] = 0.0f;
             }
         }
+        // Squares as packed f32x2 products, summed by scalar adds in element order (sa = sa + a*a). The adds stay
+        // scalar on purpose: a packed product feeding a packed add is contracted into a fused multiply-add by the
+        // code generator, which rounds once and changes the result.
         float sa = 0.0f;
         float sb = 0.0f;
 #pragma unroll
         for (int j = 0; j < kVec; ++j) {
-            sa = sa + a[j] * a[j];
-        }
-#pragma unroll
-        for (int j = 0; j < kVec; ++j) {
-            sb = sb + b[j] * b[j];
+            const float2 v = make_float2(a[j], b[j]);
+            const float2 sq = __fmul2_rn(v, v);
+            sa = sa + sq.x;
+            sb = sb + sq.y;
         }
         // Every lane of the warp takes part; offsets below kLanes never leave the head's lane group.
         const float ss = group_sum<kLanes>(sa + sb);
@@ -161,30 +163,35 @@ __global__ void __launch_bounds__(kQkThreads) qk_norm_rope_kernel(QkParams p) {
             float wb[kVec];
             V::unpack(w.weights[which][hl], wa);
             V::unpack(w.weights[which][kLanes + hl], wb);
-            float c[kVec];
-            float s[kVec];
+            const float2 inv2 = make_float2(inv, inv);
+            float x[kVec];
+            float y[kVec];
 #pragma unroll
-            for (int j = 0; j < kVec; j += 4) {
-                const float4 cv = *reinterpret_cast<const float4*>(&w.table[hl * kVec + j]);
-                const float4 sv = *reinterpret_cast<const float4*>(&w.table[kHalf + hl * kVec + j]);
-                c[j] = cv.x;
-                c[j + 1] = cv.y;
-                c[j + 2] = cv.z;
-                c[j + 3] = cv.w;
-                s[j] = sv.x;
-                s[j + 1] = sv.y;
-                s[j + 2] = sv.z;
-                s[j + 3] = sv.w;
+            for (int j = 0; j < kVec; ++j) {
+                // (first * inv) * w and (second * inv) * w, separately rounded
+                const float2 n = __fmul2_rn(__fmul2_rn(make_float2(a[j], b[j]), inv2), make_float2(wa[j], wb[j]));
+                x[j] = n.x;
+                y[j] = n.y;
             }
             float out_a[kVec];
             float out_b[kVec];
 #pragma unroll
-            for (int j = 0; j < kVec; ++j) {
+            for (int j = 0; j < kVec; j += 2) {
+                const float4 cv = *reinterpret_cast<const float4*>(&w.table[hl * kVec + (j & ~3)]);
+                const float4 sv = *reinterpret_cast<const float4*>(&w.table[kHalf + hl * kVec + (j & ~3)]);
+                const float2 c = (j & 3) == 0 ? make_float2(cv.x, cv.y) : make_float2(cv.z, cv.w);
+                const float2 s = (j & 3) == 0 ? make_float2(sv.x, sv.y) : make_float2(sv.z, sv.w);
                 // The reference's rms_norm returns a tensor of the model dtype; RoPE reads those rounded values.
-                const float n1 = V::quantize((a[j] * inv) * wa[j]);
-                const float n2 = V::quantize((b[j] * inv) * wb[j]);
-                out_a[j] = n1 * c[j] - n2 * s[j];  // first  * cos - second * sin  (src/nn/rope.cpp:115-116)
-                out_b[j] = n2 * c[j] + n1 * s[j];  // second * cos + first  * sin  (src/nn/rope.cpp:117-118)
+                const float2 n1 = V::quantize2(x[j], x[j + 1]);  // first-half elements j, j + 1
+                const float2 n2 = V::quantize2(y[j], y[j + 1]);  // second-half elements j, j + 1
+                const float2 n1c = __fmul2_rn(n1, c);
+                const float2 n2s = __fmul2_rn(n2, s);
+                const float2 n2c = __fmul2_rn(n2, c);
+                const float2 n1s = __fmul2_rn(n1, s);
+                out_a[j] = n1c.x - n2s.x;  // first  * cos - second * sin  (src/nn/rope.cpp:115-116)
+                out_a[j + 1] = n1c.y - n2s.y;
+                out_b[j] = n2c.x + n1s.x;  // second * cos + first  * sin  (src/nn/rope.cpp:117-118)
+                out_b[j + 1] = n2c.y + n1s.y;
             }
             char* dst = h < p.q_heads ? static_cast<char*>(p.q_out) + (t * p.q_heads + h) * kHeadBytes
                                       : static_cast<char*>(p.k_out) +
