@@ -11,10 +11,12 @@
 // yields 0.
 //
 // Layout: a row is split across a thread-block cluster of up to 8 CTAs of 256 threads, each CTA scanning a
-// contiguous column range with 16-byte loads (scalar loads when the rows are not aligned for them), a thread's five
-// loads issued together (measured on B200 against 32-byte loads, other batch sizes and a parallel DSMEM combine:
-// none faster). CTA partials are combined through distributed shared memory (cluster rank 0 reads
-// the other CTAs' shared slots), so no global scratch and no second launch are needed.
+// contiguous column range (scalar loads when the rows are not aligned for 16-byte vectors). The range streams through
+// shared memory by per-thread asynchronous copies, all of a chunk requested before any is read; each 16-byte vector
+// is first reduced with packed max instructions and searched for its index only when it would replace the thread's
+// running maximum. (Measured on B200 against register loads in batches of 5, 32-byte loads and clusters of 16:
+// slower.) CTA partials are combined through distributed shared memory (cluster rank 0 reads the other CTAs' shared
+// slots), so no global scratch and no second launch are needed.
 //
 // Roofline: HBM-bound. Algorithmic bytes per row: cols * size read + 8 bytes written.
 #include <cooperative_groups.h>
@@ -29,7 +31,7 @@ namespace {
 
 constexpr int kThreads = 256;
 constexpr int kWarps = kThreads / 32;
-constexpr int kUnroll = 5;
+constexpr int kStaged = 10;  // 16-byte vectors per thread per shared-memory chunk (40 KB per CTA)
 constexpr int kMaxCluster = 8;
 
 __device__ __forceinline__ unsigned long long argmax_key(float v, uint32_t index) {
@@ -64,6 +66,46 @@ struct Running {
     __device__ __forceinline__ unsigned long long key() const {
         return index < 0 ? 0ull : argmax_key(value, static_cast<uint32_t>(index));
     }
+
+    // The kVec elements first .. first + kVec - 1 of one 16-byte vector, with the same result as visiting them one
+    // by one: m = the vector's largest non-NaN value (packed max instructions: NaN loses to any number, and an
+    // all-NaN vector gives NaN, which is never taken); when m would be taken, the index is the vector's first
+    // element equal to m (+0 and -0 compare equal, as under strict '>').
+    template <typename T>
+    __device__ __forceinline__ void visit_vector(uint4 r, int first) {
+        float m;
+        if constexpr (sizeof(T) == 2) {
+            const __nv_bfloat162 m01 = __hmax2(as_bf162(r.x), as_bf162(r.y));
+            const __nv_bfloat162 m23 = __hmax2(as_bf162(r.z), as_bf162(r.w));
+            const uint32_t mw = bf162_bits(__hmax2(m01, m23));
+            m = fmaxf(bf16_lo(mw), bf16_hi(mw));
+        } else {
+            m = fmaxf(fmaxf(__uint_as_float(r.x), __uint_as_float(r.y)),
+                      fmaxf(__uint_as_float(r.z), __uint_as_float(r.w)));
+        }
+        if (m > value || (index < 0 && m == m)) {
+            float v[Vec16<T>::kVec];
+            Vec16<T>::unpack(r, v);
+            int j = Vec16<T>::kVec - 1;
+#pragma unroll
+            for (int k = Vec16<T>::kVec - 2; k >= 0; --k) {
+                j = v[k] == m ? k : j;
+            }
+            value = m;
+            index = first + j;
+        }
+    }
+
+    __device__ __forceinline__ static __nv_bfloat162 as_bf162(uint32_t w) {
+        __nv_bfloat162 h;
+        memcpy(&h, &w, sizeof(w));
+        return h;
+    }
+    __device__ __forceinline__ static uint32_t bf162_bits(__nv_bfloat162 h) {
+        uint32_t w;
+        memcpy(&w, &h, sizeof(w));
+        return w;
+    }
 };
 
 // kBytes: 32 or 16 for vector loads of the row, 0 for element loads.
@@ -89,44 +131,27 @@ __global__ void __launch_bounds__(kThreads) row_argmax_kernel(const void* __rest
     // Each thread visits its elements in increasing index order (vectors v, v + kThreads, ...; then the tail).
     Running run;
     if constexpr (kBytes > 0) {
-        constexpr int kWords = kBytes / 4;
         const int64_t nvec = lo < hi ? (hi - lo) / kVec : 0;
         const char* base = xr + lo * static_cast<int64_t>(sizeof(T));
-        for (int64_t v = threadIdx.x; v < nvec; v += kUnroll * kThreads) {
-            // Raw words of kUnroll vectors in flight; unpacked one element at a time while visiting.
-            uint32_t w[kUnroll][kWords];
+        // The slice streams through shared memory in chunks of kStaged vectors per thread: every vector of a chunk
+        // is requested by an asynchronous copy before the thread waits for any of them, so a whole chunk (the whole
+        // slice, for the 151936-column vocabulary) is in flight at once without holding registers. Each thread
+        // reads back only the slots it filled, so no block barrier is needed.
+        __shared__ uint4 staged[kStaged][kThreads];
+        for (int64_t c0 = 0; c0 < nvec; c0 += static_cast<int64_t>(kStaged) * kThreads) {
 #pragma unroll
-            for (int u = 0; u < kUnroll; ++u) {
-                if (v + u * kThreads < nvec) {
-                    const char* p = base + (v + u * kThreads) * kBytes;
-                    if constexpr (kBytes == 32) {
-                        const U8 r = ld_stream32(p);
-#pragma unroll
-                        for (int k = 0; k < 8; ++k) {
-                            w[u][k] = r.r[k];
-                        }
-                    } else {
-                        const uint4 r = ld_stream(p);
-                        w[u][0] = r.x;
-                        w[u][1] = r.y;
-                        w[u][2] = r.z;
-                        w[u][3] = r.w;
-                    }
+            for (int u = 0; u < kStaged; ++u) {
+                const int64_t v = c0 + u * kThreads + threadIdx.x;
+                if (v < nvec) {
+                    cp_async16(&staged[u][threadIdx.x], base + v * kBytes);
                 }
             }
+            cp_async_wait_all();
 #pragma unroll
-            for (int u = 0; u < kUnroll; ++u) {
-                if (v + u * kThreads < nvec) {
-                    const int first = static_cast<int>(lo + (v + u * kThreads) * kVec);
-#pragma unroll
-                    for (int k = 0; k < kWords; ++k) {
-                        if constexpr (sizeof(T) == 2) {
-                            run.visit(bf16_lo(w[u][k]), first + 2 * k);
-                            run.visit(bf16_hi(w[u][k]), first + 2 * k + 1);
-                        } else {
-                            run.visit(__uint_as_float(w[u][k]), first + k);
-                        }
-                    }
+            for (int u = 0; u < kStaged; ++u) {
+                const int64_t v = c0 + u * kThreads + threadIdx.x;
+                if (v < nvec) {
+                    run.visit_vector<T>(staged[u][threadIdx.x], static_cast<int>(lo + v * kVec));
                 }
             }
         }

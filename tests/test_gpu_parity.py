@@ -306,6 +306,23 @@ def test_silu_mul_faithful(ops, oracle, n, dtype):
         np.testing.assert_allclose(got, out, rtol=1e-6, atol=1e-30)
 
 
+@pytest.mark.parametrize("dtype", ["bf16", "f32"])
+def test_silu_extreme_inputs(ops, oracle, dtype):
+    # 1 + exp(-x) reaches 2^126 and beyond for x < -87.3 (the quotient is a tiny normal number there), overflows to
+    # inf below -88.7 (quotient -0) and is exactly 1 for large positive x.
+    x = np.concatenate([np.linspace(-104.0, -80.0, 4001), np.linspace(-20.0, 20.0, 4001), [88.0, 1e30, -1e30, 0.0]])
+    x = x.astype(np.float32)
+    if dtype == "bf16":
+        x = f32_to_bf16(x)
+    got = to_host(ops.silu(to_dev(x)))
+    want = oracle.silu(x)
+    if dtype == "bf16":
+        assert ulp_distance(got, want).max() <= 1
+    else:
+        np.testing.assert_allclose(got, want, rtol=1e-6, atol=0)
+        assert np.array_equal(np.signbit(got), np.signbit(want))
+
+
 def test_silu_mul_matches_torch_fixture(ops, oracle, golden):
     g = golden("torch_silu_mul")
     got = to_host(ops.silu_mul(to_dev(g["gate"]), to_dev(g["up"])))
@@ -385,6 +402,29 @@ def test_row_argmax_planted_ties_across_cluster_slices(ops, oracle):
     assert np.array_equal(got, oracle.row_argmax(x))
     xb = f32_to_bf16(x)
     assert np.array_equal(to_host(ops.row_argmax(to_dev(xb))), oracle.row_argmax(xb))
+
+
+@pytest.mark.parametrize("dtype", ["bf16", "f32"])
+def test_row_argmax_special_values(ops, oracle, dtype):
+    # Vectors of 8 (bf16) or 4 (f32) elements are reduced with packed max instructions first; these rows put NaNs,
+    # infinities and signed zeros at every position of a vector.
+    cols = 4096 + 13
+    rng = np.random.default_rng(23)
+    rows = []
+    rows.append(np.full(cols, -np.inf))
+    rows.append(np.full(cols, np.nan))
+    r = np.full(cols, np.nan); r[0] = -5.0; rows.append(r)
+    r = np.full(cols, np.nan); r[2049] = -np.inf; rows.append(r)
+    r = np.full(cols, -1.0); r[[100, 101, 3000]] = [-0.0, 0.0, -0.0]; rows.append(r)
+    r = np.full(cols, -1.0); r[[7, 8]] = [0.0, -0.0]; rows.append(r)
+    r = -np.abs(rng.standard_normal(cols)); r[::3] = np.nan; r[4100] = np.inf; r[17] = np.inf; rows.append(r)
+    r = rng.standard_normal(cols); r[0] = np.nan; rows.append(r)
+    for k in range(8):  # the maximum at each lane of a vector, tied with a later vector
+        r = np.full(cols, -2.0); r[16 + k] = 1.0; r[24 + (7 - k)] = 1.0; rows.append(r)
+    x = np.array(rows, np.float32)
+    if dtype == "bf16":
+        x = f32_to_bf16(x)
+    assert np.array_equal(to_host(ops.row_argmax(to_dev(x))), oracle.row_argmax(x))
 
 
 def test_row_argmax_row_strided_view(ops, oracle):
