@@ -96,8 +96,21 @@ __device__ __forceinline__ float apply_binary(float a, float b) {
 }
 
 // x / (1 + exp(-x)), oneDNN eltwise_swish with alpha = 1 as ops::silu configures it (src/ops/nn_ops.cpp:70-71).
+// The quotient uses the fast division (reciprocal approximation and one multiply, within 2 ulp): the IEEE division
+// sequence made the SiLU kernels issue-bound (the [4096, 3072] bf16 SiLU * up took 16.0 us with it, 13.2 us now).
+// Its reciprocal flushes to zero for divisors of 2^126 and above (x < -87.3), where the IEEE quotient is still a
+// tiny normal number, so there both operands are scaled by 1/4 first (exact: x is then below -87, d finite or inf).
 __device__ __forceinline__ float silu_f32(float x) {
-    return x / (1.0f + expf(-x));
+    const float d = 1.0f + expf(-x);
+    const float scale = d < 0x1p126f ? 1.0f : 0.25f;
+    return __fdividef(x * scale, d * scale);
+}
+
+// Two bf16 products, each rounded to nearest even (packed bf16 multiply).
+__device__ __forceinline__ uint32_t mul_bf16x2(uint32_t a, uint32_t b) {
+    uint32_t d;
+    asm("mul.rn.bf16x2 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b));
+    return d;
 }
 
 // Generic grid-stride driver. `Functor::load<kBytes>(i)` / `compute_store<kBytes>(i, loaded)` handle pack i,
@@ -203,15 +216,27 @@ struct SiluMulFunctor {
     }
     template <int kBytes>
     __device__ __forceinline__ void compute_store(int64_t i, const Loaded<kBytes>& l) const {
-        using P = PackOf<T, kBytes>;
-        float g[P::kElems], u[P::kElems];
-        P::unpack(l.g, g);
-        P::unpack(l.u, u);
+        if constexpr (sizeof(T) == 2) {
+            // bf16: the silu values are rounded to bf16 in pairs and multiplied by up as packed bf16. A product of
+            // two bf16 values is exact in f32, so one bf16 rounding of it equals the f32 product rounded to bf16.
+            Words<kBytes> o;
 #pragma unroll
-        for (int j = 0; j < P::kElems; ++j) {
-            g[j] = Vec16<T>::quantize(silu_f32(g[j])) * u[j];
+            for (int k = 0; k < Words<kBytes>::kCount; ++k) {
+                const uint32_t s = pack_bf16x2(silu_f32(bf16_lo(l.g.w[k])), silu_f32(bf16_hi(l.g.w[k])));
+                o.w[k] = mul_bf16x2(s, l.u.w[k]);
+            }
+            o.store(out + i * kBytes);
+        } else {
+            using P = PackOf<T, kBytes>;
+            float g[P::kElems], u[P::kElems];
+            P::unpack(l.g, g);
+            P::unpack(l.u, u);
+#pragma unroll
+            for (int j = 0; j < P::kElems; ++j) {
+                g[j] = silu_f32(g[j]) * u[j];
+            }
+            P::pack(g).store(out + i * kBytes);
         }
-        P::pack(g).store(out + i * kBytes);
     }
     __device__ __forceinline__ void scalar(int64_t e) const {
         const float s = Vec16<T>::quantize(silu_f32(Vec16<T>::load1(gate, e)));
