@@ -606,6 +606,44 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_kernel(const LinearParams p)
     }
 }
 
+// Sums kTileRows (16) per-lane partials over the warp in the canonical butterfly order -- partial[l] +
+// partial[l ^ d] for d = 16, 8, 4, 2, 1 -- and leaves the total of row (lane >> 1) in lanes 2r and 2r + 1. At each
+// distance a lane keeps half of its rows and trades the other half with its partner, so the 16 rows take 16
+// shuffles instead of 80, and the epilogue then runs on all lanes at once. Every addition is the same pair of
+// operands as in the plain butterfly (IEEE addition is commutative), so the bits are the same.
+__device__ __forceinline__ float reduce_rows16(const float (&acc)[kTileRows], int lane) {
+    static_assert(kTileRows == 16, "reduce_rows16 takes 16 rows");
+    float v8[8];
+    const bool b4 = (lane & 16) != 0;
+#pragma unroll
+    for (int k = 0; k < 8; ++k) {
+        const float keep = b4 ? acc[8 + k] : acc[k];
+        const float send = b4 ? acc[k] : acc[8 + k];
+        v8[k] = keep + __shfl_xor_sync(0xffffffffu, send, 16);
+    }
+    float v4[4];
+    const bool b3 = (lane & 8) != 0;
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+        const float keep = b3 ? v8[4 + k] : v8[k];
+        const float send = b3 ? v8[k] : v8[4 + k];
+        v4[k] = keep + __shfl_xor_sync(0xffffffffu, send, 8);
+    }
+    float v2[2];
+    const bool b2 = (lane & 4) != 0;
+#pragma unroll
+    for (int k = 0; k < 2; ++k) {
+        const float keep = b2 ? v4[2 + k] : v4[k];
+        const float send = b2 ? v4[k] : v4[2 + k];
+        v2[k] = keep + __shfl_xor_sync(0xffffffffu, send, 4);
+    }
+    const bool b1 = (lane & 2) != 0;
+    const float keep = b1 ? v2[1] : v2[0];
+    const float send = b1 ? v2[0] : v2[1];
+    const float v1 = keep + __shfl_xor_sync(0xffffffffu, send, 2);
+    return v1 + __shfl_xor_sync(0xffffffffu, v1, 1);
+}
+
 template <LinearEpilogue kEpi>
 __global__ void __launch_bounds__(kThreads) linear_rows_kernel(const LinearParams p) {
     extern __shared__ uint4 smem_x[];  // kTileRows rows of K / 8 chunks
@@ -663,27 +701,23 @@ __global__ void __launch_bounds__(kThreads) linear_rows_kernel(const LinearParam
                 }
             }
         }
+        float total[kMats];
 #pragma unroll
         for (int mat = 0; mat < kMats; ++mat) {
-#pragma unroll
-            for (int m = 0; m < kTileRows; ++m) {
-                acc[mat][m] = group_sum<32>(acc[mat][m]);
-            }
+            total[mat] = reduce_rows16(acc[mat], lane);
         }
-#pragma unroll
-        for (int m = 0; m < kTileRows; ++m) {
-            if (lane == m && m < mt) {
-                const int64_t row = m0 + m;
-                if constexpr (kEpi == LinearEpilogue::kStore) {
-                    store_segment(p, row, n, acc[0][m], 0);
-                } else if constexpr (kEpi == LinearEpilogue::kResidual) {
-                    const float res = Vec16<bf16>::load1(p.residual, row * p.res_ld + n);
-                    Vec16<bf16>::store1(p.out[0], row * p.ld[0] + n, res + round_to_bf16(acc[0][m]));
-                } else {
-                    const float gate = round_to_bf16(acc[0][m]);
-                    const float up = round_to_bf16(acc[1][m]);
-                    Vec16<bf16>::store1(p.out[0], row * p.ld[0] + n, round_to_bf16(silu_pexp(gate)) * up);
-                }
+        const int r = (lane >> 1) & (kTileRows - 1);
+        if ((lane & 1) == 0 && r < mt) {
+            const int64_t row = m0 + r;
+            if constexpr (kEpi == LinearEpilogue::kStore) {
+                store_segment(p, row, n, total[0], 0);
+            } else if constexpr (kEpi == LinearEpilogue::kResidual) {
+                const float res = Vec16<bf16>::load1(p.residual, row * p.res_ld + n);
+                Vec16<bf16>::store1(p.out[0], row * p.ld[0] + n, res + round_to_bf16(total[0]));
+            } else {
+                const float gate = round_to_bf16(total[0]);
+                const float up = round_to_bf16(total[1]);
+                Vec16<bf16>::store1(p.out[0], row * p.ld[0] + n, round_to_bf16(silu_pexp(gate)) * up);
             }
         }
     }
@@ -779,33 +813,29 @@ __global__ void __launch_bounds__(kThreads, 2) linear_rows_f32x_kernel(const Lin
                 }
             }
         }
-#pragma unroll
-        for (int sl = 0; sl < kSlots; ++sl) {
-#pragma unroll
-            for (int m = 0; m < kTileRows; ++m) {
-                acc[sl][m] = group_sum<32>(acc[sl][m]);
-            }
-        }
-#pragma unroll
-        for (int m = 0; m < kTileRows; ++m) {
-            if (lane == m && m < mt) {
-                const int64_t row = m0 + m;
-                if constexpr (kEpi == LinearEpilogue::kSiluMul) {
-                    const float gate = round_to_bf16(acc[0][m]);
-                    const float up = round_to_bf16(acc[1][m]);
+        const float total0 = reduce_rows16(acc[0], lane);
+        const float total1 = reduce_rows16(acc[1], lane);
+        // Lanes 2r and 2r + 1 hold row r: the even lane finishes slot 0, the odd lane slot 1 (SiLU * up: the even
+        // lane alone, from both).
+        const int r = (lane >> 1) & (kTileRows - 1);
+        const int sl = lane & 1;
+        if (r < mt) {
+            const int64_t row = m0 + r;
+            if constexpr (kEpi == LinearEpilogue::kSiluMul) {
+                if (sl == 0) {
+                    const float gate = round_to_bf16(total0);
+                    const float up = round_to_bf16(total1);
                     Vec16<bf16>::store1(p.out[0], row * p.ld[0] + n0, round_to_bf16(silu_pexp(gate)) * up);
-                } else {
-#pragma unroll
-                    for (int sl = 0; sl < kSlots; ++sl) {
-                        const int64_t n = n0 + sl;
-                        if (valid[sl]) {
-                            if constexpr (kEpi == LinearEpilogue::kStore) {
-                                store_segment(p, row, n, acc[sl][m], 0);
-                            } else {
-                                const float res = Vec16<bf16>::load1(p.residual, row * p.res_ld + n);
-                                Vec16<bf16>::store1(p.out[0], row * p.ld[0] + n, res + round_to_bf16(acc[sl][m]));
-                            }
-                        }
+                }
+            } else {
+                const int64_t n = n0 + sl;
+                if (valid[sl]) {
+                    const float v = sl == 0 ? total0 : total1;
+                    if constexpr (kEpi == LinearEpilogue::kStore) {
+                        store_segment(p, row, n, v, 0);
+                    } else {
+                        const float res = Vec16<bf16>::load1(p.residual, row * p.res_ld + n);
+                        Vec16<bf16>::store1(p.out[0], row * p.ld[0] + n, res + round_to_bf16(v));
                     }
                 }
             }
