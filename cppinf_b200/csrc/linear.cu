@@ -723,12 +723,15 @@ __global__ void __launch_bounds__(kThreads) linear_rows_kernel(const LinearParam
     }
 }
 
-// Prefill projection with the 16-row input tile staged in shared memory as f32 (two planes: elements 0-3 and 4-7 of
-// every chunk, so a lane's 16-byte reads are conflict-free), and two weight rows (or the gate and up rows of one
-// output) per warp, so each staged input chunk feeds 16 multiply-adds. Same per-output order as the other kernels.
+// Prefill projection with the 16-row input tile staged in shared memory as f32, interleaved by row pairs so that one
+// packed f32x2 product serves two rows, and two weight rows (or the gate and up rows of one output) per warp, so each
+// staged input chunk feeds 16 multiply-adds. Same per-output order as the other kernels.
 template <LinearEpilogue kEpi>
 __global__ void __launch_bounds__(kThreads, 2) linear_rows_f32x_kernel(const LinearParams p) {
-    extern __shared__ float4 smem_xf[];  // [2 planes][kTileRows][K / 8]
+    // [kTileRows / 2 row pairs][4 element pairs][K / 8 chunks]: float4 (x[2q][e], x[2q+1][e], x[2q][e+1],
+    // x[2q+1][e+1]) for e = 8 c + 2 k, so one 16-byte read gives two (row 2q, row 2q+1) pairs of one element each
+    // and a warp's reads of consecutive chunks are conflict-free.
+    extern __shared__ float4 smem_xf[];
     grid_dependency_begin();
     constexpr int kMats = mats_of<kEpi>();
     constexpr int kSlots = 2;                      // weight rows a warp multiplies together
@@ -737,20 +740,26 @@ __global__ void __launch_bounds__(kThreads, 2) linear_rows_f32x_kernel(const Lin
     const int lane = threadIdx.x & 31;
     const int warp = threadIdx.x >> 5;
     const int64_t nchunks = p.K / 8;
-    const int64_t plane = kTileRows * nchunks;
     const int64_t m0 = static_cast<int64_t>(blockIdx.y) * kTileRows;
     const int64_t mt = p.M - m0 < kTileRows ? p.M - m0 : kTileRows;
     const int64_t row_bytes = p.K * 2;
+    constexpr int kPairs = kTileRows / 2;
 
-    for (int64_t i = threadIdx.x; i < plane; i += kThreads) {
-        const int64_t m = i / nchunks;
-        const int64_t c = i - m * nchunks;
-        float f[8] = {0.0f, 0.0f, 0.0f, 0.0f, 0.0f, 0.0f, 0.0f, 0.0f};
-        if (m < mt) {
-            Vec16<bf16>::unpack(ld_cached(input_row(p, m0 + m, 0) + c * 8), f);
+    for (int64_t i = threadIdx.x; i < kPairs * nchunks; i += kThreads) {
+        const int64_t q = i / nchunks;
+        const int64_t c = i - q * nchunks;
+        float f0[8] = {0.0f, 0.0f, 0.0f, 0.0f, 0.0f, 0.0f, 0.0f, 0.0f};
+        float f1[8] = {0.0f, 0.0f, 0.0f, 0.0f, 0.0f, 0.0f, 0.0f, 0.0f};
+        if (2 * q < mt) {
+            Vec16<bf16>::unpack(ld_cached(input_row(p, m0 + 2 * q, 0) + c * 8), f0);
         }
-        smem_xf[i] = make_float4(f[0], f[1], f[2], f[3]);
-        smem_xf[plane + i] = make_float4(f[4], f[5], f[6], f[7]);
+        if (2 * q + 1 < mt) {
+            Vec16<bf16>::unpack(ld_cached(input_row(p, m0 + 2 * q + 1, 0) + c * 8), f1);
+        }
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+            smem_xf[(q * 4 + k) * nchunks + c] = make_float4(f0[2 * k], f1[2 * k], f0[2 * k + 1], f1[2 * k + 1]);
+        }
     }
     __syncthreads();
 
@@ -793,21 +802,29 @@ __global__ void __launch_bounds__(kThreads, 2) linear_rows_f32x_kernel(const Lin
                         Vec16<bf16>::unpack(wraw[sl][b], w[sl]);
                     }
 #pragma unroll
-                    for (int m = 0; m < kTileRows; ++m) {
-                        const float4 xa = smem_xf[m * nchunks + c];
-                        const float4 xb = smem_xf[plane + m * nchunks + c];
+                    for (int q = 0; q < kPairs; ++q) {
+                        // x[2q][e] * w[e] and x[2q+1][e] * w[e] as one packed product, then the two sums as scalar
+                        // adds in element order (a packed add after a packed product would be contracted into a
+                        // fused multiply-add by the code generator).
+                        float2 xp[8];
+#pragma unroll
+                        for (int k = 0; k < 4; ++k) {
+                            const float4 v = smem_xf[(q * 4 + k) * nchunks + c];
+                            xp[2 * k] = make_float2(v.x, v.y);
+                            xp[2 * k + 1] = make_float2(v.z, v.w);
+                        }
 #pragma unroll
                         for (int sl = 0; sl < kSlots; ++sl) {
-                            float a = acc[sl][m];
-                            a = a + xa.x * w[sl][0];
-                            a = a + xa.y * w[sl][1];
-                            a = a + xa.z * w[sl][2];
-                            a = a + xa.w * w[sl][3];
-                            a = a + xb.x * w[sl][4];
-                            a = a + xb.y * w[sl][5];
-                            a = a + xb.z * w[sl][6];
-                            a = a + xb.w * w[sl][7];
-                            acc[sl][m] = a;
+                            float a0 = acc[sl][2 * q];
+                            float a1 = acc[sl][2 * q + 1];
+#pragma unroll
+                            for (int e = 0; e < 8; ++e) {
+                                const float2 pr = __fmul2_rn(xp[e], make_float2(w[sl][e], w[sl][e]));
+                                a0 = a0 + pr.x;
+                                a1 = a1 + pr.y;
+                            }
+                            acc[sl][2 * q] = a0;
+                            acc[sl][2 * q + 1] = a1;
                         }
                     }
                 }
