@@ -1058,11 +1058,35 @@ cudaError_t launch_rows_epi(const LinearParams& p, cudaStream_t s) {
             return err;
         }
     }
+    // Every CTA stages one 16-row tile and walks its share of the N outputs, so CTAs are equal: size the grid to
+    // whole waves of resident CTAs (a partial last wave would run alone). The fewest waves that use at least 95% of
+    // the slots, up to 4; otherwise the best of those.
     const int64_t tiles = (p.M + kTileRows - 1) / kTileRows;
-    const int64_t want = (static_cast<int64_t>(runtime::sm_count()) * 4 + tiles - 1) / tiles;
+    int per_sm = 0;
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kernel, kThreads, smem) != cudaSuccess || per_sm < 1) {
+        per_sm = 1;
+    }
+    const int64_t slots = static_cast<int64_t>(per_sm) * runtime::sm_count();
     const int64_t row_blocks = (p.N + kWarps - 1) / kWarps;
-    const int64_t gx = want < row_blocks ? want : row_blocks;
-    return runtime::launch_smem(kernel, dim3(static_cast<unsigned>(gx < 1 ? 1 : gx), static_cast<unsigned>(tiles)),
+    int64_t gx = 1;
+    double best = 0.0;
+    for (int64_t waves = 1; waves <= 4; ++waves) {
+        int64_t g = waves * slots / tiles;
+        g = g < row_blocks ? g : row_blocks;
+        if (g < 1) {
+            continue;
+        }
+        const double used = static_cast<double>(g * tiles) /
+                            static_cast<double>(runtime::ceil_div(g * tiles, slots) * slots);
+        if (used > best + 1e-9) {
+            best = used;
+            gx = g;
+        }
+        if (used >= 0.95) {
+            break;
+        }
+    }
+    return runtime::launch_smem(kernel, dim3(static_cast<unsigned>(gx), static_cast<unsigned>(tiles)),
                                 dim3(kThreads), smem, s, 1u, p);
 }
 
