@@ -46,6 +46,8 @@ LINEAR_SHAPES = [
     (16, 512, 64),
     (37, 3072, 128),   # partial tile
     (512, 1024, 256),  # prefill
+    (21, 1024, 77),    # odd number of outputs: a warp's second weight row is past the end
+    (20, 4096, 33),    # K past the f32 tile: bf16 staging
 ]
 
 
@@ -66,7 +68,7 @@ def test_linear_strided_rows(ops, oracle):
     assert_bits_equal(got, oracle.linear_canonical(np.ascontiguousarray(big[:, 8:]), w), "strided linear")
 
 
-@pytest.mark.parametrize("m,k,n", [(1, 1024, 1024), (1, 3072, 1024), (19, 2048, 256)])
+@pytest.mark.parametrize("m,k,n", [(1, 1024, 1024), (1, 3072, 1024), (19, 2048, 256), (5, 1024, 131)])
 def test_linear_residual_bit_exact(ops, oracle, m, k, n):
     rng = np.random.default_rng(m * 7 + k)
     x = seeded_bf16(rng, (m, k))
