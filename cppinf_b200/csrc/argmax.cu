@@ -145,10 +145,12 @@ __global__ void __launch_bounds__(kThreads) row_argmax_kernel(const void* __rest
                 if (v < nvec) {
                     cp_async16(&staged[u][threadIdx.x], base + v * kBytes);
                 }
+                cp_async_commit();
             }
-            cp_async_wait_all();
+            // Vector u is visited as soon as its own copy group has landed (the later ones keep arriving).
 #pragma unroll
             for (int u = 0; u < kStaged; ++u) {
+                cp_async_wait_pending(kStaged - 1 - u);
                 const int64_t v = c0 + u * kThreads + threadIdx.x;
                 if (v < nvec) {
                     run.visit_vector<T>(staged[u][threadIdx.x], static_cast<int>(lo + v * kVec));

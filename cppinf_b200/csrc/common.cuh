@@ -111,6 +111,42 @@ __device__ __forceinline__ void cp_async_wait_all() {
     asm volatile("cp.async.wait_all;" ::: "memory");
 }
 
+// Closes the calling thread's current group of asynchronous copies.
+__device__ __forceinline__ void cp_async_commit() {
+    asm volatile("cp.async.commit_group;" ::: "memory");
+}
+
+// Waits until at most `pending` (0..15) of the calling thread's committed copy groups are still in flight; larger
+// values wait for all. In unrolled loops the switch folds to one instruction.
+__device__ __forceinline__ void cp_async_wait_pending(int pending) {
+    switch (pending) {
+#define CPPINF_WAIT_GROUP(n)                                       \
+    case n:                                                        \
+        asm volatile("cp.async.wait_group " #n ";" ::: "memory"); \
+        break;
+        CPPINF_WAIT_GROUP(0)
+        CPPINF_WAIT_GROUP(1)
+        CPPINF_WAIT_GROUP(2)
+        CPPINF_WAIT_GROUP(3)
+        CPPINF_WAIT_GROUP(4)
+        CPPINF_WAIT_GROUP(5)
+        CPPINF_WAIT_GROUP(6)
+        CPPINF_WAIT_GROUP(7)
+        CPPINF_WAIT_GROUP(8)
+        CPPINF_WAIT_GROUP(9)
+        CPPINF_WAIT_GROUP(10)
+        CPPINF_WAIT_GROUP(11)
+        CPPINF_WAIT_GROUP(12)
+        CPPINF_WAIT_GROUP(13)
+        CPPINF_WAIT_GROUP(14)
+        CPPINF_WAIT_GROUP(15)
+#undef CPPINF_WAIT_GROUP
+    default:
+        asm volatile("cp.async.wait_all;" ::: "memory");
+        break;
+    }
+}
+
 __device__ __forceinline__ void bulk_copy_g2s(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
     asm volatile(
         "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
