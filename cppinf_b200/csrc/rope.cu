@@ -100,6 +100,18 @@ __global__ void __launch_bounds__(kQkThreads) qk_norm_rope_kernel(QkParams p) {
 
     // Every load of the unit is issued as an asynchronous copy into the warp's slot before any arithmetic: the
     // values wait in shared memory rather than in registers, which keeps the kernel at more resident warps per SM.
+    // One copy group for the angle row and the weights, then one per iteration of heads, which is processed as soon
+    // as its own group has landed.
+    const char* row = reinterpret_cast<const char*>(p.table + (p.position_offset + shift + t) * kDim);
+    for (int c = lane; c < kTableChunks; c += 32) {
+        cp_async16(&w.table[c * 4], row + c * 16);  // cos in [0, D/2), sin in [D/2, D)
+    }
+    for (int c = lane; c < 2 * kWeightChunks; c += 32) {
+        const bool is_q = c < kWeightChunks;
+        const int chunk = is_q ? c : c - kWeightChunks;
+        cp_async16(&w.weights[is_q ? 0 : 1][chunk], static_cast<const char*>(is_q ? p.qw : p.kw) + chunk * 16);
+    }
+    cp_async_commit();
 #pragma unroll
     for (int i = 0; i < kIters; ++i) {
         const int h = h0 + i * kHeadsPerIter + slot;
@@ -110,22 +122,13 @@ __global__ void __launch_bounds__(kQkThreads) qk_norm_rope_kernel(QkParams p) {
             cp_async16(&w.data[i][0][lane], src + hl * 16);
             cp_async16(&w.data[i][1][lane], src + kHalfBytes + hl * 16);
         }
+        cp_async_commit();
     }
-    // cos in [0, D/2) and sin in [D/2, D) of this token's position, then the q and k norm weights.
-    const char* row = reinterpret_cast<const char*>(p.table + (p.position_offset + shift + t) * kDim);
-    for (int c = lane; c < kTableChunks; c += 32) {
-        cp_async16(&w.table[c * 4], row + c * 16);
-    }
-    for (int c = lane; c < 2 * kWeightChunks; c += 32) {
-        const bool is_q = c < kWeightChunks;
-        const int chunk = is_q ? c : c - kWeightChunks;
-        cp_async16(&w.weights[is_q ? 0 : 1][chunk], static_cast<const char*>(is_q ? p.qw : p.kw) + chunk * 16);
-    }
-    cp_async_wait_all();
-    __syncwarp();
 
 #pragma unroll
     for (int i = 0; i < kIters; ++i) {
+        cp_async_wait_pending(kIters - 1 - i);
+        __syncwarp();
         const int h = h0 + i * kHeadsPerIter + slot;
         const bool active = h < heads;
         float a[kVec];
