@@ -100,8 +100,21 @@ __global__ void __launch_bounds__(kQkThreads) qk_norm_rope_kernel(QkParams p) {
 
     // Every load of the unit is issued as an asynchronous copy into the warp's slot before any arithmetic: the
     // values wait in shared memory rather than in registers, which keeps the kernel at more resident warps per SM.
-    // One copy group for the angle row and the weights, then one per iteration of heads, which is processed as soon
-    // as its own group has landed.
+    // Copy groups: the first iteration's heads, then the angle row and the weights, then one group per further
+    // iteration. An iteration starts as soon as its heads have landed; the first one needs the angles and weights
+    // only after its norm statistics.
+    const auto copy_heads = [&](int i) {
+        const int h = h0 + i * kHeadsPerIter + slot;
+        if (h < heads) {
+            const char* src = h < p.q_heads
+                                  ? static_cast<const char*>(p.q) + (t * p.q_heads + h) * kHeadBytes
+                                  : static_cast<const char*>(p.k) + (t * p.k_heads + (h - p.q_heads)) * kHeadBytes;
+            cp_async16(&w.data[i][0][lane], src + hl * 16);
+            cp_async16(&w.data[i][1][lane], src + kHalfBytes + hl * 16);
+        }
+        cp_async_commit();
+    };
+    copy_heads(0);
     const char* row = reinterpret_cast<const char*>(p.table + (p.position_offset + shift + t) * kDim);
     for (int c = lane; c < kTableChunks; c += 32) {
         cp_async16(&w.table[c * 4], row + c * 16);  // cos in [0, D/2), sin in [D/2, D)
@@ -113,21 +126,13 @@ __global__ void __launch_bounds__(kQkThreads) qk_norm_rope_kernel(QkParams p) {
     }
     cp_async_commit();
 #pragma unroll
-    for (int i = 0; i < kIters; ++i) {
-        const int h = h0 + i * kHeadsPerIter + slot;
-        if (h < heads) {
-            const char* src = h < p.q_heads
-                                  ? static_cast<const char*>(p.q) + (t * p.q_heads + h) * kHeadBytes
-                                  : static_cast<const char*>(p.k) + (t * p.k_heads + (h - p.q_heads)) * kHeadBytes;
-            cp_async16(&w.data[i][0][lane], src + hl * 16);
-            cp_async16(&w.data[i][1][lane], src + kHalfBytes + hl * 16);
-        }
-        cp_async_commit();
+    for (int i = 1; i < kIters; ++i) {
+        copy_heads(i);
     }
 
 #pragma unroll
     for (int i = 0; i < kIters; ++i) {
-        cp_async_wait_pending(kIters - 1 - i);
+        cp_async_wait_pending(i == 0 ? kIters : kIters - 1 - i);
         __syncwarp();
         const int h = h0 + i * kHeadsPerIter + slot;
         const bool active = h < heads;
@@ -160,6 +165,10 @@ __global__ void __launch_bounds__(kQkThreads) qk_norm_rope_kernel(QkParams p) {
         const float mean = ss / static_cast<float>(kDim);
         const float rms = sqrtf(mean + p.eps);
         const float inv = 1.0f / rms;
+        if (i == 0) {
+            cp_async_wait_pending(kIters - 1);  // the angle row and the weights
+            __syncwarp();
+        }
         if (active) {
             const int which = h < p.q_heads ? 0 : 1;
             float wa[kVec];
