@@ -379,9 +379,15 @@ __global__ void __launch_bounds__(kStagedThreads, 2) gemv_staged_kernel(const Li
     }
     uint4 xv[kHoldX ? kC : 1];
     if constexpr (kHoldX) {
+        // With a norm, warp 0 alone loads and normalises the row and hands it to the other warps through shared
+        // memory (every warp doing it made the prologue issue-bound: 32 warps per SM repeating the same chain).
+        __shared__ uint4 s_xn[kC * 32];
+        const bool norm = p.norm_weight != nullptr;
+        if (!norm || warp == 0) {
 #pragma unroll
-        for (int i = 0; i < kC; ++i) {
-            xv[i] = ld_cached(xrow + (lane + 32 * i) * 8);
+            for (int i = 0; i < kC; ++i) {
+                xv[i] = ld_cached(xrow + (lane + 32 * i) * 8);
+            }
         }
         if (p.x_copy != nullptr && blockIdx.x == 0 && warp == 0) {
 #pragma unroll
@@ -389,7 +395,7 @@ __global__ void __launch_bounds__(kStagedThreads, 2) gemv_staged_kernel(const Li
                 st_v4(p.x_copy + (lane + 32 * i) * 8, xv[i]);
             }
         }
-        if (p.norm_weight != nullptr) {
+        if (norm && warp == 0) {
             // ops::rms_norm of the row: lane l's chunks are l, l + 32, ..., so its partial is the canonical one.
             float s = 0.0f;
 #pragma unroll
@@ -415,7 +421,14 @@ __global__ void __launch_bounds__(kStagedThreads, 2) gemv_staged_kernel(const Li
                 for (int e = 0; e < 8; ++e) {
                     f[e] = (f[e] * inv) * w[e];
                 }
-                xv[i] = Vec16<bf16>::pack(f);
+                s_xn[lane + 32 * i] = Vec16<bf16>::pack(f);
+            }
+        }
+        if (norm) {
+            __syncthreads();
+#pragma unroll
+            for (int i = 0; i < kC; ++i) {
+                xv[i] = s_xn[lane + 32 * i];
             }
         }
     }
