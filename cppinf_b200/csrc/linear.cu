@@ -364,7 +364,13 @@ __global__ void __launch_bounds__(kStagedThreads, 2) gemv_staged_kernel(const Li
         }
     }
 
-    asm volatile("griddepcontrol.wait;" ::: "memory");
+    // One warp waits for the previous grid; the others wait at the block barrier (which orders their reads after
+    // that wait), so warps of this CTA that are resident early do not compete for issue slots with the kernel
+    // still running on the SM.
+    if (warp == 0) {
+        asm volatile("griddepcontrol.wait;" ::: "memory");
+    }
+    __syncthreads();
 
     const int64_t pos = p.position != nullptr ? static_cast<int64_t>(*p.position) : 0;
     const bf16* xrow = input_row(p, 0, pos);
