@@ -211,10 +211,13 @@ CPPINF_API int cppinf_linear_argmax(const void* x, const void* weight, void* log
                                     int64_t out_features, int64_t* out_token, void* scratch, void* stream);
 CPPINF_API int64_t cppinf_linear_argmax_scratch_bytes(int64_t out_features, int64_t in_features);
 
-/* cppinf_linear_argmax without a caller-provided scratch: the per-CTA maxima and the arrival counter live in a
- * static device array of this library (one per device, zero-filled when the module loads; every call leaves the
- * counter at zero again). No device memory is allocated. This entry point has no counterpart in the reference (its
- * CLI argmax runs on host logits and needs no scratch). Limits: the launch must fit the static scratch (1024 CTAs,
+/* cppinf_linear_argmax without a caller-provided scratch, for callers that cannot allocate device memory: hosts
+ * whose allocator owns the whole device budget (a framework's caching allocator, a fixed memory plan) and FFI
+ * bindings that have no way to obtain a device buffer. The per-CTA maxima and the arrival counter live in a static
+ * device array of this library (one per device, held until the process exits, zero-filled when the module loads;
+ * every call leaves the counter at zero again). Nothing is allocated. The first call on a device looks up the array's
+ * device address (cudaGetSymbolAddress) with that device current; make that first call before any stream capture.
+ * This entry point has no counterpart in the reference (its CLI argmax runs on host logits and needs no scratch). Limits: the launch must fit the static scratch (1024 CTAs,
  * 8208 bytes; CPPINF_ERR_UNSUPPORTED with the sizes in the message otherwise). Calls on one device share the
  * scratch, so two calls that overlap in time -- on different streams, or from different threads without ordering
  * -- race and may return a wrong token; issue them on one stream or synchronise between them. */

@@ -1,5 +1,8 @@
 """cppinf_linear_argmax_noalloc (static device scratch) against cppinf_linear_argmax (caller-provided scratch).
 
+The no-alloc variant serves callers that cannot allocate device memory themselves (an allocator that owns the whole
+device budget, an FFI binding without device buffers); its output must equal the scratch version's bit for bit.
+
 Collected last on purpose: the static scratch is process-wide state on the device, so this file runs after every
 other GPU test. Two calls in a row check that each call leaves the static counter re-armed for the next one.
 """
