@@ -452,8 +452,8 @@ __global__ void __launch_bounds__(kStagedThreads, 2) gemv_staged_kernel(const Li
         return;
     }
 
-    // Each warp takes rows warp, warp + kStagedWarps, ... of the slice, one at a time (measured on B200: interleaving four
-    // rows per warp was slower).
+    // Each warp takes rows warp, warp + kStagedWarps, ... of the slice, one at a time (measured on B200:
+    // interleaving four rows per warp was slower).
 #pragma unroll
     for (int k = 0; k < kStagedRowIters; ++k) {
         const int64_t r = warp + static_cast<int64_t>(k) * kStagedWarps;
