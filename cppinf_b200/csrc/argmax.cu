@@ -10,7 +10,7 @@
 // (after folding -0 into +0): max(key) is the lowest index of the largest value. A row whose element 0 is NaN
 // yields 0.
 //
-// Layout: a row is split across a thread-block cluster of up to 8 CTAs of 256 threads, each CTA scanning a
+// Layout: a row is split across a thread-block cluster of up to 8 CTAs of 512 threads, each CTA scanning a
 // contiguous column range (scalar loads when the rows are not aligned for 16-byte vectors). The range streams through
 // shared memory by per-thread asynchronous copies, all of a chunk requested before any is read; each 16-byte vector
 // is first reduced with packed max instructions and searched for its index only when it would replace the thread's
@@ -29,9 +29,9 @@ namespace cg = cooperative_groups;
 namespace cppinf::device {
 namespace {
 
-constexpr int kThreads = 256;
+constexpr int kThreads = 512;  // measured on [64, 151936] bf16: 7.90 us against 8.37 with 256 and 10.98 with 128
 constexpr int kWarps = kThreads / 32;
-constexpr int kStaged = 10;  // 16-byte vectors per thread per shared-memory chunk (40 KB per CTA)
+constexpr int kStaged = 5;  // 16-byte vectors per thread per shared-memory chunk (40 KB per CTA)
 constexpr int kMaxCluster = 8;
 
 __device__ __forceinline__ unsigned long long argmax_key(float v, uint32_t index) {
