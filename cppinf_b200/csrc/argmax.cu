@@ -15,8 +15,9 @@
 // shared memory by per-thread asynchronous copies, all of a chunk requested before any is read; each 16-byte vector
 // is first reduced with packed max instructions and searched for its index only when it would replace the thread's
 // running maximum. (Measured on B200 against register loads in batches of 5, 32-byte loads and clusters of 16:
-// slower.) CTA partials are combined through distributed shared memory (cluster rank 0 reads the other CTAs' shared
-// slots), so no global scratch and no second launch are needed.
+// slower.) CTA partials are combined through distributed shared memory: each CTA stores its key into cluster rank
+// 0's shared array, one cluster barrier makes them visible, rank 0 combines them (measured: 7.67 -> 6.91 us against
+// rank 0 loading the other CTAs' slots between two barriers). No global scratch and no second launch are needed.
 //
 // Roofline: HBM-bound. Algorithmic bytes per row: cols * size read + 8 bytes written.
 #include <cooperative_groups.h>
@@ -113,9 +114,12 @@ template <typename T, int kBytes>
 __global__ void __launch_bounds__(kThreads) row_argmax_kernel(const void* __restrict__ x, int64_t cols,
                                                               int64_t row_stride, int64_t* __restrict__ out) {
     grid_dependency_begin();
+    // Every CTA of the cluster has started once this barrier phase completes; it is waited on right before the one
+    // DSMEM store below, long after every CTA has arrived.
+    asm volatile("barrier.cluster.arrive.relaxed.aligned;" ::: "memory");
     constexpr int kVec = kBytes == 0 ? 1 : kBytes / static_cast<int>(sizeof(T));
     __shared__ unsigned long long warp_best[kWarps];
-    __shared__ unsigned long long cta_best;
+    __shared__ unsigned long long cluster_best[kMaxCluster];  // rank 0's copy receives every CTA's key
 
     cg::cluster_group cluster = cg::this_cluster();
     const unsigned rank = cluster.block_rank();
@@ -176,20 +180,23 @@ __global__ void __launch_bounds__(kThreads) row_argmax_kernel(const void* __rest
         warp_best[warp] = best;
     }
     __syncthreads();
+    asm volatile("barrier.cluster.wait.aligned;" ::: "memory");  // every CTA has started: DSMEM is usable
     if (threadIdx.x == 0) {
         unsigned long long b = warp_best[0];
 #pragma unroll
         for (int w = 1; w < kWarps; ++w) {
             b = umax64(b, warp_best[w]);
         }
-        cta_best = b;
+        // Push this CTA's key into rank 0's shared memory (a remote store, no remote load).
+        *cluster.map_shared_rank(&cluster_best[rank], 0) = b;
     }
-    // Make every CTA's cta_best visible to the cluster, then let rank 0 combine them over DSMEM.
+    // The pushes are visible to rank 0 after this barrier; no CTA touches another's shared memory after it, so the
+    // other ranks may leave while rank 0 finishes.
     cluster.sync();
     if (rank == 0 && threadIdx.x == 0) {
-        unsigned long long b = cta_best;
+        unsigned long long b = cluster_best[0];
         for (unsigned r = 1; r < csize; ++r) {
-            b = umax64(b, *cluster.map_shared_rank(&cta_best, r));
+            b = umax64(b, cluster_best[r]);
         }
         const float first = Vec16<T>::load1(xr, 0);
         int64_t index = 0;
@@ -198,8 +205,6 @@ __global__ void __launch_bounds__(kThreads) row_argmax_kernel(const void* __rest
         }
         out[row] = index;
     }
-    // Keep every CTA (and its shared memory) alive until rank 0 has read it.
-    cluster.sync();
 }
 
 template <typename T>
