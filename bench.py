@@ -14,11 +14,16 @@ A step is one pass of one hot-path op over one batch of its configuration:
     row_argmax      logits bf16 [64, 151936] -> int64 [64]
 
 Metric: achieved HBM GB/s = algorithmic bytes (minimum read + write) / device time. Multi-GPU (torchrun, one process
-per GPU): every rank processes its own token rows of an N-times larger batch (weak scaling, RoPE positions stay
-global), no collective on the data path; time is the max over ranks.
+per GPU): the headline partitions one (2048 * N)-token batch into N token ranges (cppinf_b200/shard.py token_shard;
+RoPE positions stay global), 2048 rows per rank (weak scaling), with no collective on the data path; time is the max
+over ranks. The `sharded` object adds, for N > 1, one global batch of q/k (2048 * N and 2048 tokens), of the causal
+softmax (byte-balanced row ranges) and of the argmax (row ranges) partitioned across the ranks, each timed compute
+only and with the copy-back of every rank's output rows into one buffer on rank 0 (point-to-point over NCCL, i.e.
+NVLink peer copies).
 
 Timing: W eager warm-up steps, then K steps replayed from CUDA graphs of <= 1000 launches, bracketed by a barrier and
-a device synchronize, CUDA events on the launch stream. Consecutive steps rotate through buffer sets whose total is
+a device synchronize, CUDA events on the launch stream; `repeats` replays the same K steps 50 more times, each timed
+alone, for the median and the spread. Consecutive steps rotate through buffer sets whose total is
 more than three times the 126 MB L2, so every step reads cold data from HBM. `e2e` runs the same op through the
 public API from pinned host buffers (H2D, kernel, D2H pipelined over three streams) and reports the same metric.
 
@@ -85,6 +90,8 @@ def parse_args():
     p.add_argument("--cpu-seconds", type=float, default=8.0, help="CPU-baseline sample length")
     p.add_argument("--no-decode", action="store_true", help="skip the Qwen3-0.6B greedy-decode measurement")
     p.add_argument("--decode-runs", type=int, default=3, help="timed prefill + decode runs")
+    p.add_argument("--repeats", type=int, default=50, help="further timed replays of the headline steps (spread)")
+    p.add_argument("--copy-steps", type=int, default=100, help="steps of each multi-GPU copy-back measurement")
     return p.parse_args()
 
 
@@ -193,12 +200,18 @@ class ClockSampler:
 
 
 class Workload:
-    """Buffer sets plus a launch function for one op configuration on one GPU."""
+    """Buffer sets plus a launch function for one op configuration (or one rank's shard of it) on one GPU.
 
-    def __init__(self, name: str, rank: int, device):
+    Shards (cppinf_b200/shard.py): `tokens`/`position_offset` for qk_norm_rope (token rows keep their global RoPE
+    positions), `rows` for causal_softmax (a range of the flattened [16 * 2048] score rows, launched per matrix piece
+    at its query offset) and for row_argmax (a row count). Without a shard the whole configuration is built."""
+
+    def __init__(self, name: str, rank: int, device, tokens: int = 2048, position_offset: int | None = None,
+                 rows=None):
         import torch
 
         from cppinf_b200 import capi, ops
+        from cppinf_b200.shard import range_bytes, softmax_pieces
 
         self.name = name
         self.lib = capi.load()
@@ -211,7 +224,6 @@ class Workload:
             return (torch.randn(shape, generator=gen, device=device) * std + mean).to(dtype)
 
         bf16 = capi.DTYPE_BF16
-        self.resident_bytes = 0
         make_set = None
         if name == "rms_norm":
             w = randn(1024, 1.0, 0.1)
@@ -219,28 +231,29 @@ class Workload:
             def make_set():
                 x, y = randn((512, 1024)), torch.empty((512, 1024), dtype=torch.bfloat16, device=device)
                 return (x, y), lambda s: self.lib.cppinf_rms_norm(bf16, x.data_ptr(), 1024, w.data_ptr(),
-                                                                  y.data_ptr(), 512, 1024, 1e-6, s)
+                                                                  y.data_ptr(), 512, 1024, 1e-6, s), [y]
             set_bytes = 2 * 512 * 1024 * 2
         elif name == "qk_norm_rope":
-            tokens, hq, hk, d = 2048, 16, 8, 128
+            hq, hk, d = 16, 8, 128
+            offset = rank * tokens if position_offset is None else position_offset
             qw, kw = randn(d, 1.0, 0.1), randn(d, 1.0, 0.1)
-            offset = rank * tokens
             table = ops.rope_table(1e6, d, offset + tokens, device)
             self.table = table
+            self.bytes = qk_bytes(tokens)
 
             def make_set():
                 q, k = randn((tokens, hq, d)), randn((tokens, hk, d))
                 qo, ko = torch.empty_like(q), torch.empty_like(k)
                 return (q, k, qo, ko), lambda s: self.lib.cppinf_qk_norm_rope(
                     bf16, q.data_ptr(), k.data_ptr(), qw.data_ptr(), kw.data_ptr(), qo.data_ptr(), ko.data_ptr(),
-                    tokens, hq, hk, d, offset, 1e-6, table.data_ptr(), table.shape[0], s)
+                    tokens, hq, hk, d, offset, 1e-6, table.data_ptr(), table.shape[0], s), [qo, ko]
             set_bytes = 2 * tokens * (hq + hk) * d * 2
         elif name == "silu_mul":
             def make_set():
                 g, u = randn((4096, 3072)), randn((4096, 3072))
                 o = torch.empty_like(g)
                 return (g, u, o), lambda s: self.lib.cppinf_silu_mul(bf16, g.data_ptr(), u.data_ptr(), o.data_ptr(),
-                                                                     g.numel(), s)
+                                                                     g.numel(), s), [o]
             set_bytes = 3 * 4096 * 3072 * 2
         elif name == "add_rms_norm":
             w = randn(1024, 1.0, 0.1)
@@ -249,28 +262,64 @@ class Workload:
                 a, b = randn((4096, 1024)), randn((4096, 1024))
                 sm, y = torch.empty_like(a), torch.empty_like(a)
                 return (a, b, sm, y), lambda s: self.lib.cppinf_add_rms_norm(
-                    bf16, a.data_ptr(), b.data_ptr(), w.data_ptr(), sm.data_ptr(), y.data_ptr(), 4096, 1024, 1e-6, s)
+                    bf16, a.data_ptr(), b.data_ptr(), w.data_ptr(), sm.data_ptr(), y.data_ptr(), 4096, 1024, 1e-6,
+                    s), [sm, y]
             set_bytes = 4 * 4096 * 1024 * 2
         elif name == "causal_softmax":
             scale = 1.0 / math.sqrt(128.0)
+            matrices, n = 16, 2048
+            row_range = (0, matrices * n) if rows is None else rows
+            pieces = softmax_pieces(row_range, n)
+            nrows = row_range[1] - row_range[0]
+            self.bytes = range_bytes(row_range, n, n)
+            # Launches: consecutive whole matrices go to the square ops entry point in one call; a partial matrix
+            # goes to the position-aware one at its query offset.
+            launches = []
+            for pc in pieces:
+                whole = pc.query_start == 0 and pc.rows == n
+                if whole and launches and launches[-1][0] == "square":
+                    launches[-1][2] += 1
+                elif whole:
+                    launches.append(["square", None, 1])
+                else:
+                    launches.append(["piece", (capi.i64_array([pc.query_start]), capi.i64_array([pc.rows]),
+                                               capi.i64_array([n])), pc.rows])
 
             def make_set():
-                x = randn((16, 2048, 2048), 0.0, 2.0, torch.float32)
+                x = randn((nrows, n), 0.0, 2.0, torch.float32)
                 y = torch.empty_like(x)
-                return (x, y), lambda s: self.lib.cppinf_scaled_causal_softmax_f32(x.data_ptr(), y.data_ptr(), 16,
-                                                                                   2048, 2048, scale, s)
-            set_bytes = 2 * 16 * 2048 * 2048 * 4
+
+                def launch(s):
+                    r0 = 0
+                    for kind, arrs, count in launches:
+                        rows_here = count * n if kind == "square" else count
+                        xp, yp = x[r0:r0 + rows_here], y[r0:r0 + rows_here]
+                        if kind == "square":
+                            st = self.lib.cppinf_scaled_causal_softmax_f32(xp.data_ptr(), yp.data_ptr(), count, n,
+                                                                           n, scale, s)
+                        else:
+                            st = self.lib.cppinf_scaled_position_causal_softmax_f32(
+                                xp.data_ptr(), yp.data_ptr(), 1, 1, count, n, scale, arrs[0], arrs[1], arrs[2], s)
+                        if st != 0:
+                            return st
+                        r0 += rows_here
+                    return 0
+                return (x, y), launch, [y]
+            set_bytes = 2 * nrows * n * 4
         elif name == "row_argmax":
+            nrows = 64 if rows is None else rows
+            self.bytes = nrows * 151936 * 2 + nrows * 8
+
             def make_set():
-                x = randn((64, 151936), 0.0, 2.0)
-                o = torch.empty(64, dtype=torch.int64, device=device)
-                return (x, o), lambda s: self.lib.cppinf_row_argmax(bf16, x.data_ptr(), 64, 151936, 151936,
-                                                                    o.data_ptr(), s)
-            set_bytes = 64 * 151936 * 2
+                x = randn((nrows, 151936), 0.0, 2.0)
+                o = torch.empty(nrows, dtype=torch.int64, device=device)
+                return (x, o), lambda s: self.lib.cppinf_row_argmax(bf16, x.data_ptr(), nrows, 151936, 151936,
+                                                                    o.data_ptr(), s), [o]
+            set_bytes = nrows * 151936 * 2
         else:
             raise ValueError(name)
 
-        n_sets = max(1, math.ceil(3 * L2_BYTES / set_bytes))
+        n_sets = max(1, math.ceil(3 * L2_BYTES / max(set_bytes, 1)))
         self.sets = [make_set() for _ in range(n_sets)]
         self.resident_bytes = n_sets * set_bytes
         self.n_sets = n_sets
@@ -280,9 +329,14 @@ class Workload:
         if status != 0:
             self.capi.check(status, self.name)
 
+    def outputs(self, i: int) -> list:
+        return self.sets[i % self.n_sets][2]
 
-def time_device_steps(wl: Workload, steps: int, warmup: int, stream, barrier) -> tuple[float, int]:
-    """Times exactly `steps` launches (CUDA-graph replays) on `stream`; returns (ms, launches in timed region)."""
+
+def time_device_steps(wl: Workload, steps: int, warmup: int, stream, barrier,
+                      repeats: int = 0) -> tuple[float, int, list[float]]:
+    """Times exactly `steps` launches (CUDA-graph replays) on `stream`; returns (ms, launches in the timed region,
+    ms of each of `repeats` further timed replays of the same steps, for the spread)."""
     import torch
 
     h = stream.cuda_stream
@@ -309,21 +363,43 @@ def time_device_steps(wl: Workload, steps: int, warmup: int, stream, barrier) ->
         main_graph.replay()  # untimed: first replay uploads the graph
     torch.cuda.synchronize()
 
-    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    barrier()
-    torch.cuda.synchronize()
-    with torch.cuda.stream(stream):
-        start.record(stream)
-        for _ in range(replays):
-            main_graph.replay()
-        if tail_graph is not None:
-            tail_graph.replay()
-        end.record(stream)
-    torch.cuda.synchronize()
-    barrier()
+    def timed() -> float:
+        start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        barrier()
+        torch.cuda.synchronize()
+        with torch.cuda.stream(stream):
+            start.record(stream)
+            for _ in range(replays):
+                main_graph.replay()
+            if tail_graph is not None:
+                tail_graph.replay()
+            end.record(stream)
+        torch.cuda.synchronize()
+        barrier()
+        return start.elapsed_time(end)
+
+    ms = timed()
     launches = replays * main_launches + tail_launches
+    spread = [timed() for _ in range(repeats)]
     del main_graph, tail_graph
-    return start.elapsed_time(end), launches
+    return ms, launches, spread
+
+
+def time_single_launches(wl: Workload, count: int, stream) -> list[float]:
+    """Latency of isolated launches: each launch alone between two events, the stream drained in between."""
+    import torch
+
+    out = []
+    for i in range(count):
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        torch.cuda.synchronize()
+        with torch.cuda.stream(stream):
+            e0.record(stream)
+            wl.launch(i, stream.cuda_stream)
+            e1.record(stream)
+        torch.cuda.synchronize()
+        out.append(e0.elapsed_time(e1) * 1e3)
+    return out
 
 
 def time_e2e(wl_name: str, rank: int, device, steps: int) -> dict:
@@ -384,6 +460,100 @@ def time_e2e(wl_name: str, rank: int, device, steps: int) -> dict:
     ms = start.elapsed_time(end)
     in_bytes = host_q.numel() * 2 + host_k.numel() * 2
     return {"ms": ms, "steps": steps, "h2d_bytes_per_step": in_bytes, "d2h_bytes_per_step": in_bytes}
+
+
+def time_copy_back_steps(wl: Workload, steps: int, dsts: list, ranges: list, rank: int, stream, barrier) -> float:
+    """`steps` eager steps of the op followed by the copy-back of its outputs into `dsts` on rank 0
+    (shard.copy_back: point-to-point transfers over NCCL, i.e. NVLink peer traffic); CUDA events on `stream`, which
+    the transfers are ordered after and waited on by. Returns ms on this rank."""
+    import torch
+
+    from cppinf_b200.shard import copy_back
+
+    def step(i):
+        wl.launch(i, stream.cuda_stream)
+        for out, dst in zip(wl.outputs(i), dsts):
+            copy_back(out, dst, ranges, rank)
+
+    with torch.cuda.stream(stream):
+        for i in range(3):
+            step(i)
+    torch.cuda.synchronize()
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    barrier()
+    torch.cuda.synchronize()
+    with torch.cuda.stream(stream):
+        start.record(stream)
+        for i in range(steps):
+            step(i)
+        end.record(stream)
+    torch.cuda.synchronize()
+    barrier()
+    return start.elapsed_time(end)
+
+
+def sharded_legs(world: int, rank: int, device, stream, barrier, max_over_ranks, peak: float, steps: int,
+                 copy_steps: int) -> dict:
+    """Row partitioning of one global batch across the ranks (cppinf_b200/shard.py), compute only and with the
+    copy-back of every shard into one buffer on rank 0:
+
+    qk_norm_rope weak    global batch of 2048 * N tokens, 2048 per rank at their global RoPE positions
+    qk_norm_rope strong  the 2048-token configuration split into N token ranges
+    causal_softmax       the [16, 2048, 2048] configuration split into N byte-balanced row ranges
+    row_argmax           the [64, 151936] configuration split into N row ranges
+
+    Aggregate GB/s = the algorithmic bytes of the global batch / the max over ranks of the time; `frac` is that over
+    N x the measured peak. The copy-back moves the outputs (shard bytes `copy_bytes_per_step` in total, less rank 0's
+    own rows, which it copies locally) into rank 0's HBM."""
+    import torch
+
+    from cppinf_b200.shard import causal_row_ranges, range_bytes, row_ranges, token_shard
+
+    legs = {}
+    specs = [
+        ("qk_norm_rope_weak", "qk_norm_rope", 2048 * world),
+        ("qk_norm_rope_strong", "qk_norm_rope", 2048),
+        ("causal_softmax_strong", "causal_softmax", None),
+        ("row_argmax_strong", "row_argmax", None),
+    ]
+    for label, op, global_tokens in specs:
+        if op == "qk_norm_rope":
+            ranges = row_ranges(global_tokens, world)
+            sh = token_shard(global_tokens, world, rank)
+            wl = Workload(op, rank, device, tokens=sh.tokens, position_offset=sh.position_offset)
+            total = qk_bytes(global_tokens)
+            shapes = [((global_tokens, 16, 128), torch.bfloat16), ((global_tokens, 8, 128), torch.bfloat16)]
+            desc = f"q/k RMSNorm + RoPE, {global_tokens} tokens split into {world} token ranges"
+        elif op == "causal_softmax":
+            ranges = causal_row_ranges(16, 2048, 2048, world)
+            wl = Workload(op, rank, device, rows=ranges[rank])
+            total = sum(range_bytes(r, 2048, 2048) for r in ranges)
+            shapes = [((16 * 2048, 2048), torch.float32)]
+            desc = f"causal softmax [16, 2048, 2048], {world} byte-balanced row ranges"
+        else:
+            ranges = row_ranges(64, world)
+            wl = Workload(op, rank, device, rows=ranges[rank][1] - ranges[rank][0])
+            total = CONFIGS[op]["bytes"]
+            shapes = [((64,), torch.int64)]
+            desc = f"row argmax [64, 151936], {world} row ranges"
+        ms, _, _ = time_device_steps(wl, steps, 3, stream, barrier)
+        ms = max_over_ranks(ms)
+        gbs = total * steps / (ms * 1e-3) / 1e9
+        dsts = [torch.empty(shape, dtype=dt, device=device) if rank == 0 else None for shape, dt in shapes]
+        copy_bytes = sum(math.prod(shape) * torch.empty((), dtype=dt).element_size() for shape, dt in shapes)
+        cms = max_over_ranks(time_copy_back_steps(wl, copy_steps, dsts, ranges, rank, stream, barrier))
+        cgbs = total * copy_steps / (cms * 1e-3) / 1e9
+        legs[label] = {
+            "workload": desc, "bytes_per_step": total,
+            "compute": {"us_per_step": round(ms / steps * 1e3, 3), "gbs": round(gbs, 1),
+                        "frac_of_n_peak": round(gbs / (world * peak), 4), "steps": steps},
+            "with_copy_back": {"us_per_step": round(cms / copy_steps * 1e3, 3), "gbs": round(cgbs, 1),
+                               "frac_of_n_peak": round(cgbs / (world * peak), 4), "steps": copy_steps,
+                               "copy_bytes_per_step": copy_bytes},
+        }
+        del wl, dsts
+        torch.cuda.empty_cache()
+    return legs
 
 
 # ---------------------------------------------------------------------------------------------------------------
@@ -463,7 +633,7 @@ def measure_cpu(kind: str, seconds: float) -> dict:
             break
     cpu.close()
     gbs = n * qk_bytes(2048) / elapsed / 1e9
-    return {"value": round(gbs, 3), "unit": UNIT, "cores": cpu.threads, "kind": cpu.kind,
+    return {"value": round(gbs, 3), "unit": UNIT, "cores": cpu.threads, "cpu_model": cpu_model(), "kind": cpu.kind,
             "sample": f"{n} full 2048-token q/k steps in {elapsed:.1f} s: {cpu.describe()}"}
 
 
@@ -562,7 +732,8 @@ def measure_cpu_decode(seconds: float) -> dict:
         if time.perf_counter() - t0 >= seconds:
             break
     elapsed = time.perf_counter() - t0
-    return {"value": round(n / elapsed, 3), "unit": "tok/s", "cores": os.cpu_count(), "kind": "port",
+    return {"value": round(n / elapsed, 3), "unit": "tok/s", "cores": os.cpu_count(), "cpu_model": cpu_model(),
+            "kind": "port",
             "sample": f"{n} greedy decode steps after a 16-token prompt in {elapsed:.1f} s: the C restatement of "
                       "the decoder (oracle/qwen3.py, OpenMP over output rows)"}
 
@@ -570,6 +741,28 @@ def measure_cpu_decode(seconds: float) -> dict:
 # ---------------------------------------------------------------------------------------------------------------
 # Arms
 # ---------------------------------------------------------------------------------------------------------------
+
+
+def headline_config(workload: str, world: int) -> dict:
+    """The `config` of both arms' JSON lines (identical keys and values for the same workload and GPU count)."""
+    global_tokens = 2048 * world if workload == "qk_norm_rope" else None
+    return {
+        "workload": f"{workload}: {CONFIGS[workload]['desc']}",
+        "global_tokens": global_tokens,
+        "parallelism": (f"one {global_tokens}-token batch, token rows partitioned over {world} GPU(s) with global "
+                        "RoPE positions (cppinf_b200/shard.py token_shard), no data-path collective"
+                        if workload == "qk_norm_rope" else f"{world} GPU(s), one configuration per GPU"),
+    }
+
+
+def cpu_model() -> str:
+    try:
+        for line in Path("/proc/cpuinfo").read_text().splitlines():
+            if line.startswith("model name"):
+                return line.split(":", 1)[1].strip()
+    except OSError:
+        pass
+    return "unknown"
 
 
 def run_reference(args) -> None:
@@ -598,8 +791,9 @@ def run_reference(args) -> None:
         "warmup": args.warmup, "ms_per_step": round(elapsed / args.steps * 1e3, 4),
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
         "data": "synthetic (seeded N(0,1) q/k, N(1,0.1) norm weights)",
-        "config": {"workload": f"qk_norm_rope: {CONFIGS[HEADLINE]['desc']}", "tokens_per_step": tokens},
-        "cpu_baseline": {"value": value, "unit": UNIT, "cores": cpu.threads, "kind": cpu.kind, "sample": sample},
+        "config": headline_config(HEADLINE, world),
+        "cpu_baseline": {"value": value, "unit": UNIT, "cores": cpu.threads, "cpu_model": cpu_model(),
+                         "kind": cpu.kind, "sample": sample},
         "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     if not args.no_decode:
@@ -638,16 +832,32 @@ def run_ours(args) -> None:
     peak, peak_kind = read_peak_gbs()
     stream = torch.cuda.Stream(device)
 
-    wl = Workload(args.workload, rank, device)
+    if args.workload == "qk_norm_rope":
+        # This rank's token rows of one (2048 * N)-token batch, at their global RoPE positions.
+        from cppinf_b200.shard import token_shard
+
+        sh = token_shard(2048 * world, world, rank)
+        wl = Workload(args.workload, rank, device, tokens=sh.tokens, position_offset=sh.position_offset)
+    else:
+        wl = Workload(args.workload, rank, device)
     clocks = ClockSampler(local_rank)
     clocks.start()
-    ms, launches = time_device_steps(wl, args.steps, args.warmup, stream, barrier)
+    ms, launches, spread = time_device_steps(wl, args.steps, args.warmup, stream, barrier, repeats=args.repeats)
     clock_info = clocks.stop()
     ms_max = max_over_ranks(ms)
+    spread = [max_over_ranks(x) for x in spread]
     per_step_ms = ms_max / args.steps
     value = world * wl.bytes * args.steps / (ms_max * 1e-3) / 1e9
     achieved = wl.bytes / (ms / args.steps * 1e-3) / 1e9  # this rank's kernel: bytes per launch / launch time
     resident = wl.resident_bytes
+    repeats = None
+    if spread:
+        us = sorted(x / args.steps * 1e3 for x in spread)
+        med = statistics.median(us)
+        repeats = {"count": len(us), "us_per_step_median": round(med, 3), "us_per_step_min": round(us[0], 3),
+                   "us_per_step_max": round(us[-1], 3), "gbs_median": round(wl.bytes / (med * 1e-6) / 1e9, 1),
+                   "frac_median": round(wl.bytes / (med * 1e-6) / 1e9 / peak, 4),
+                   "how": f"the same {args.steps}-step graph replayed {len(us)} more times, each timed alone"}
     del wl
     torch.cuda.empty_cache()
 
@@ -661,19 +871,31 @@ def run_ours(args) -> None:
                     "how": "cppinf_b200.ops.qk_norm_rope from pinned host buffers; H2D, kernel and D2H on three "
                            "streams, double-buffered"}
 
+    # One GPU: every other configuration measured on its own. Several GPUs: one global batch per configuration
+    # partitioned across the ranks, with and without the copy-back to rank 0 (sharded_legs).
     per_op = {}
-    if not args.no_ops:
+    if not args.no_ops and world == 1:
         for name in CONFIGS:
             if name == args.workload:
                 continue
             w2 = Workload(name, rank, device)
-            op_ms, _ = time_device_steps(w2, args.op_steps, 3, stream, barrier)
+            op_ms, _, _ = time_device_steps(w2, args.op_steps, 3, stream, barrier)
             op_ms = max_over_ranks(op_ms)
             gbs = w2.bytes / (op_ms / args.op_steps * 1e-3) / 1e9
             per_op[name] = {"gbs": round(gbs, 1), "frac": round(gbs / peak, 4), "us_per_step":
-                            round(op_ms / args.op_steps * 1e3, 3), "bytes": w2.bytes}
+                            round(op_ms / args.op_steps * 1e3, 3), "bytes": w2.bytes,
+                            "traffic": read_traffic(name)}
+            if name == "rms_norm":
+                # [512, 1024] is launch-latency bound: the isolated single-launch time, beside the graph-batched one.
+                single = sorted(time_single_launches(w2, 50, stream))
+                per_op[name]["single_launch_us_median"] = round(statistics.median(single), 3)
+                per_op[name]["single_launch_gbs"] = round(w2.bytes / (statistics.median(single) * 1e-6) / 1e9, 1)
             del w2
             torch.cuda.empty_cache()
+    sharded = None
+    if not args.no_ops and world > 1:
+        sharded = sharded_legs(world, rank, device, stream, barrier, max_over_ranks, peak, args.op_steps,
+                               args.copy_steps)
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu:
@@ -716,21 +938,21 @@ def run_ours(args) -> None:
             "warmup": args.warmup, "ms_per_step": round(per_step_ms, 6), "higher_is_better": True,
             "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
             "data": "synthetic (seeded on device: N(0,1) activations, N(1,0.1) norm weights)",
-            "config": {
-                "workload": f"{args.workload}: {CONFIGS[args.workload]['desc']}",
-                "tokens_per_gpu": 2048 if args.workload == "qk_norm_rope" else None,
-                "parallelism": f"token rows sharded over {world} GPU(s), no data-path collective",
-                "l2": f"steps rotate through buffer sets totalling {resident / 2**20:.0f} MiB (> 3x the 126 MB L2)",
-                "timing": "CUDA graphs of <=1000 launches, CUDA events on the launch stream, max over ranks",
-            },
+            "config": headline_config(args.workload, world),
+            "l2": f"steps rotate through buffer sets totalling {resident / 2**20:.0f} MiB (> 3x the 126 MB L2)",
+            "timing": "CUDA graphs of <=1000 launches, CUDA events on the launch stream, max over ranks",
+            "repeats": repeats,
             "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": UNIT,
                          "frac": round(achieved / peak, 4), "peak_source": f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs)"
                          if peak_kind == "measured" else "fallback 6650 GB/s", "frac_of_8tbs": round(achieved / 8000, 4),
-                         "traffic": read_traffic(args.workload), "bytes_per_launch": CONFIGS[args.workload]["bytes"]},
+                         "traffic": read_traffic(args.workload), "bytes_per_launch": CONFIGS[args.workload]["bytes"],
+                         "traffic_source": "profiles/<op>.md: dram__bytes_read.sum + dram__bytes_write.sum per "
+                                           "launch, mean over launches in the middle of the bench's rotation"},
             "e2e": e2e_line,
             "gpu_launches": launches,
             "clocks": clock_info,
             "ops": per_op,
+            "sharded": sharded,
             "cpu_baseline": cpu,
             "decode": decode,
         }

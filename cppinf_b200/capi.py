@@ -54,6 +54,7 @@ _SIGNATURES = {
     "cppinf_last_error": [],
     "cppinf_status_name": [_int],
     "cppinf_launch_count": [],
+    "cppinf_set_wait_poll_limit": [ctypes.c_uint32],
     "cppinf_add": [_int, _ptr, _ptr, _ptr, _i64, _ptr],
     "cppinf_mul": [_int, _ptr, _ptr, _ptr, _i64, _ptr],
     "cppinf_silu": [_int, _ptr, _ptr, _i64, _ptr],
@@ -79,6 +80,7 @@ _SIGNATURES = {
     "cppinf_linear": [_ptr, _i64, _ptr, _ptr, _i64, _i64, _i64, _ptr],
     "cppinf_linear_residual": [_ptr, _i64, _ptr, _ptr, _ptr, _i64, _i64, _i64, _ptr],
     "cppinf_linear_silu_mul": [_ptr, _i64, _ptr, _ptr, _ptr, _i64, _i64, _i64, _ptr],
+    "cppinf_linear_tc": [_int, _ptr, _i64, _ptr, _ptr, _ptr, _ptr, _i64, _i64, _i64, _ptr, _ptr],
     "cppinf_linear_argmax": [_ptr, _ptr, _ptr, _i64, _i64, _ptr, _ptr, _ptr],
     "cppinf_linear_argmax_scratch_bytes": [_i64, _i64],
     "cppinf_linear_argmax_noalloc": [_ptr, _ptr, _ptr, _i64, _i64, _ptr, _ptr],
@@ -99,6 +101,7 @@ _RESTYPES = {
     "cppinf_last_error": ctypes.c_char_p,
     "cppinf_status_name": ctypes.c_char_p,
     "cppinf_launch_count": ctypes.c_uint64,
+    "cppinf_set_wait_poll_limit": ctypes.c_uint32,
     "cppinf_linear_argmax_scratch_bytes": _i64,
     "cppinf_qwen3_destroy": None,
     "cppinf_qwen3_length": _i64,
@@ -166,6 +169,14 @@ def check(status: int, what: str = "") -> None:
 
 def launch_count() -> int:
     return int(load().cppinf_launch_count())
+
+
+def set_wait_poll_limit(polls: int) -> int:
+    """Sets the process-wide poll limit of the kernels' first wait on staged copies; returns the previous one."""
+    return int(load().cppinf_set_wait_poll_limit(int(polls)))
+
+
+DEFAULT_POLL_LIMIT = 1 << 24
 
 
 def call(name: str, *args) -> None:

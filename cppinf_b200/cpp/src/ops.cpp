@@ -150,7 +150,7 @@ void validate_elementwise_inputs(const TensorView& lhs, const TensorView& rhs, s
     validate_supported_float_dtype(lhs.tensor_info().dtype, op_name);
 }
 
-// validate_last_dim_operation_input, src/ops/nn_ops.cpp:54-64
+// validate_last_dim_operation_input, src/ops/nn_ops.cpp:30-40
 void validate_last_dim_operation_input(const TensorView& input, std::string_view op_name) {
     validate_supported_float_dtype(input.tensor_info().dtype, op_name);
     if (input.tensor_info().shape.rank() == 0) {
@@ -162,7 +162,7 @@ void validate_last_dim_operation_input(const TensorView& input, std::string_view
     }
 }
 
-// Checks of src/ops/nn_ops.cpp:164-183.
+// Checks of src/ops/nn_ops.cpp:140-159.
 void validate_rms_norm(const TensorView& input, const TensorView& weight, float epsilon) {
     validate_last_dim_operation_input(input, "rms_norm");
     if (epsilon < 0.0f) {
@@ -305,7 +305,7 @@ tensors::Tensor softmax_last_dim(const tensors::TensorView& input) {
 }
 
 tensors::Tensor scaled_causal_softmax_last_dim(const tensors::TensorView& input, float scale) {
-    // src/ops/nn_ops.cpp:101-122
+    // src/ops/nn_ops.cpp:77-98
     validate_last_dim_operation_input(input, "scaled_causal_softmax_last_dim");
     if (input.tensor_info().shape.rank() < 2) {
         throw std::invalid_argument("scaled_causal_softmax_last_dim requires a tensor with rank at least 2.");
@@ -332,7 +332,7 @@ tensors::Tensor scaled_causal_softmax_last_dim(const tensors::TensorView& input,
     const void* x = staged.get();
     const auto count = static_cast<int64_t>(info.shape.num_elements());
     if (info.dtype != DType::F32) {
-        // maybe_cast_to_dtype(input, F32): the reference computes in f32 (src/ops/nn_ops.cpp:124-126).
+        // maybe_cast_to_dtype(input, F32): the reference computes in f32 (src/ops/nn_ops.cpp:100-102).
         f32_input = Tensor::empty(tensors::make_result_tensor_info("scaled_causal_softmax_last_dim_result",
                                                                    DType::F32, info.shape),
                                   placement.device);
@@ -726,7 +726,7 @@ namespace nn {
 
 tensors::Tensor apply_rope(const tensors::TensorView& input, std::size_t sequence_position_offset, float rope_base,
                            std::size_t sequence_dimension) {
-    // validate_rope_input, src/nn/rope.cpp:48-69
+    // validate_rope_input, src/nn/rope.cpp:33-54
     const auto& info = input.tensor_info();
     if (info.dtype != DType::BF16 && info.dtype != DType::F32) {
         throw std::invalid_argument("apply_rope received an unsupported dtype.");

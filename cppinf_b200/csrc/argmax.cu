@@ -13,11 +13,13 @@
 // Layout: a row is split across a thread-block cluster of up to 8 CTAs of 512 threads, each CTA scanning a
 // contiguous column range (scalar loads when the rows are not aligned for 16-byte vectors). The range streams through
 // shared memory by per-thread asynchronous copies, all of a chunk requested before any is read; each 16-byte vector
-// is first reduced with packed max instructions and searched for its index only when it would replace the thread's
-// running maximum. (Measured on B200 against register loads in batches of 5, 32-byte loads and clusters of 16:
-// slower.) CTA partials are combined through distributed shared memory: each CTA stores its key into cluster rank
-// 0's shared array, one cluster barrier makes them visible, rank 0 combines them (measured: 7.67 -> 6.91 us against
-// rank 0 loading the other CTAs' slots between two barriers). No global scratch and no second launch are needed.
+// is first reduced with packed max instructions; a vector that would replace the thread's running maximum is kept
+// whole and searched for its index once, after the last vector. Measured on B200 against register loads in batches
+// of 5, 32-byte loads, clusters of 16, and bulk copies (TMA) of 2-8 KB chunks per CTA on mbarriers (8.5-12.6 us
+// against 6.9: the single issuing thread and the spinning waiters cost more than per-thread copies): slower. CTA
+// partials are combined through distributed shared memory: each CTA stores its key into cluster rank 0's shared
+// array, one cluster barrier makes them visible, rank 0 combines them. No global scratch and no second launch are
+// needed, and no thread waits on a flag (the copy-group waits are hardware waits).
 //
 // Roofline: HBM-bound. Algorithmic bytes per row: cols * size read + 8 bytes written.
 #include <cooperative_groups.h>
@@ -53,14 +55,36 @@ __device__ __forceinline__ unsigned long long umax64(unsigned long long a, unsig
 
 // Per-thread running maximum over elements visited in increasing index order: strict '>' keeps the first of equal
 // values (+0 and -0 included) and never takes NaN; `index < 0` marks "no candidate yet" so a leading -inf counts.
+// A 16-byte vector that takes the maximum is kept whole (`vec`, with its first index in `index`) and searched for the
+// position of the maximum only once, at the end (`resolve`): later vectors replace it only with a strictly larger
+// value, so the first equal element of the kept vector is the answer, and the per-vector cost is a few packed max
+// instructions and one compare.
 struct Running {
     float value = -INFINITY;
     int index = -1;
+    bool pending = false;  // `index` is the first index of `vec`, not yet resolved to the element
+    uint4 vec = make_uint4(0u, 0u, 0u, 0u);
 
     __device__ __forceinline__ void visit(float v, int i) {
         if (v > value || (index < 0 && v == v)) {
             value = v;
             index = i;
+            pending = false;
+        }
+    }
+
+    template <typename T>
+    __device__ __forceinline__ void resolve() {
+        if (pending) {
+            float v[Vec16<T>::kVec];
+            Vec16<T>::unpack(vec, v);
+            int j = Vec16<T>::kVec - 1;
+#pragma unroll
+            for (int k = Vec16<T>::kVec - 2; k >= 0; --k) {
+                j = v[k] == value ? k : j;
+            }
+            index += j;
+            pending = false;
         }
     }
 
@@ -70,8 +94,7 @@ struct Running {
 
     // The kVec elements first .. first + kVec - 1 of one 16-byte vector, with the same result as visiting them one
     // by one: m = the vector's largest non-NaN value (packed max instructions: NaN loses to any number, and an
-    // all-NaN vector gives NaN, which is never taken); when m would be taken, the index is the vector's first
-    // element equal to m (+0 and -0 compare equal, as under strict '>').
+    // all-NaN vector gives NaN, which is never taken); when m is taken the vector is kept for `resolve`.
     template <typename T>
     __device__ __forceinline__ void visit_vector(uint4 r, int first) {
         float m;
@@ -85,15 +108,10 @@ struct Running {
                       fmaxf(__uint_as_float(r.z), __uint_as_float(r.w)));
         }
         if (m > value || (index < 0 && m == m)) {
-            float v[Vec16<T>::kVec];
-            Vec16<T>::unpack(r, v);
-            int j = Vec16<T>::kVec - 1;
-#pragma unroll
-            for (int k = Vec16<T>::kVec - 2; k >= 0; --k) {
-                j = v[k] == m ? k : j;
-            }
             value = m;
-            index = first + j;
+            index = first;
+            vec = r;
+            pending = true;
         }
     }
 
@@ -123,31 +141,34 @@ __global__ void __launch_bounds__(kThreads) row_argmax_kernel(const void* __rest
 
     cg::cluster_group cluster = cg::this_cluster();
     const unsigned rank = cluster.block_rank();
-    const unsigned csize = cluster.num_blocks();
-    const int64_t row = blockIdx.x / csize;
+    const unsigned csize = cluster.num_blocks();     // a power of two (1 .. 8)
+    const unsigned cshift = __ffs(csize) - 1;
+    const int64_t row = blockIdx.x >> cshift;
     const char* xr = static_cast<const char*>(x) + row * row_stride * static_cast<int64_t>(sizeof(T));
 
-    // Column range of this CTA, cut at vector boundaries so every vector load stays aligned.
-    const int64_t per_cta = ((cols + csize - 1) / csize + kVec - 1) / kVec * kVec;
-    const int64_t lo = per_cta * rank;
-    const int64_t hi = lo + per_cta < cols ? lo + per_cta : cols;
+    // Column range of this CTA, cut at vector boundaries so every vector load stays aligned (cols < 2^31, so the
+    // column arithmetic is 32-bit).
+    const int ncols = static_cast<int>(cols);
+    const int per_cta = ((((ncols - 1) >> cshift) + 1 + kVec - 1) / kVec) * kVec;
+    const int lo = per_cta * static_cast<int>(rank) < ncols ? per_cta * static_cast<int>(rank) : ncols;
+    const int hi = lo + per_cta < ncols ? lo + per_cta : ncols;
 
     // Each thread visits its elements in increasing index order (vectors v, v + kThreads, ...; then the tail).
     Running run;
     if constexpr (kBytes > 0) {
-        const int64_t nvec = lo < hi ? (hi - lo) / kVec : 0;
-        const char* base = xr + lo * static_cast<int64_t>(sizeof(T));
+        const int nvec = (hi - lo) / kVec;
+        const char* base = xr + static_cast<int64_t>(lo) * static_cast<int64_t>(sizeof(T));
         // The slice streams through shared memory in chunks of kStaged vectors per thread: every vector of a chunk
         // is requested by an asynchronous copy before the thread waits for any of them, so a whole chunk (the whole
         // slice, for the 151936-column vocabulary) is in flight at once without holding registers. Each thread
         // reads back only the slots it filled, so no block barrier is needed.
         __shared__ uint4 staged[kStaged][kThreads];
-        for (int64_t c0 = 0; c0 < nvec; c0 += static_cast<int64_t>(kStaged) * kThreads) {
+        for (int c0 = 0; c0 < nvec; c0 += kStaged * kThreads) {
 #pragma unroll
             for (int u = 0; u < kStaged; ++u) {
-                const int64_t v = c0 + u * kThreads + threadIdx.x;
+                const int v = c0 + u * kThreads + static_cast<int>(threadIdx.x);
                 if (v < nvec) {
-                    cp_async16(&staged[u][threadIdx.x], base + v * kBytes);
+                    cp_async16(&staged[u][threadIdx.x], base + static_cast<int64_t>(v) * kBytes);
                 }
                 cp_async_commit();
             }
@@ -155,18 +176,19 @@ __global__ void __launch_bounds__(kThreads) row_argmax_kernel(const void* __rest
 #pragma unroll
             for (int u = 0; u < kStaged; ++u) {
                 cp_async_wait_pending(kStaged - 1 - u);
-                const int64_t v = c0 + u * kThreads + threadIdx.x;
+                const int v = c0 + u * kThreads + static_cast<int>(threadIdx.x);
                 if (v < nvec) {
-                    run.visit_vector<T>(staged[u][threadIdx.x], static_cast<int>(lo + v * kVec));
+                    run.visit_vector<T>(staged[u][threadIdx.x], lo + v * kVec);
                 }
             }
         }
-        for (int64_t e = lo + nvec * kVec + threadIdx.x; e < hi; e += kThreads) {
-            run.visit(Vec16<T>::load1(xr, e), static_cast<int>(e));
+        run.resolve<T>();
+        for (int e = lo + nvec * kVec + static_cast<int>(threadIdx.x); e < hi; e += kThreads) {
+            run.visit(Vec16<T>::load1(xr, e), e);
         }
     } else {
-        for (int64_t e = lo + threadIdx.x; e < hi; e += kThreads) {
-            run.visit(Vec16<T>::load1(xr, e), static_cast<int>(e));
+        for (int e = lo + static_cast<int>(threadIdx.x); e < hi; e += kThreads) {
+            run.visit(Vec16<T>::load1(xr, e), e);
         }
     }
     unsigned long long best = run.key();

@@ -91,7 +91,7 @@ __device__ __forceinline__ float dot8(uint4 a, uint4 b, float acc) {
 // Per-head RMSNorm + RoPE of one raw head vector into shared memory, with exactly the arithmetic of
 // qk_norm_rope_kernel (rope.cu): kD / 16 lanes, lane hl holding dims [8 hl, 8 hl + 8) and the matching dims of the
 // second half; the sum of squares in the canonical lane order; normalised values rounded to bf16; then
-// (first * cos - second * sin, second * cos + first * sin) rounded to bf16 (src/nn/rope.cpp:115-118). The weights
+// (first * cos - second * sin, second * cos + first * sin) rounded to bf16 (src/nn/rope.cpp:100-103). The weights
 // (w_first, w_second) and the angles (c, s) of the lane's pairs are loaded by the caller.
 template <int kD>
 __device__ __forceinline__ void norm_rope_head(const bf16* src, uint4 w_first, uint4 w_second, const float (&c)[8],
@@ -256,7 +256,7 @@ __global__ void __launch_bounds__(kThreads) decoder_attention_kernel(const Atten
         }
         bool stage_failed = false;
         if constexpr (kStage) {
-            const bool arrived = mbar_wait_bounded(&s_bar, 0);
+            const bool arrived = mbar_wait_bounded(&s_bar, 0, p.poll_limit);
             // On a timeout the kernel still runs every cluster barrier below (with meaningless values), so no CTA of
             // the cluster is left waiting; the host sees the error flag.
             stage_failed = __syncthreads_or(arrived ? 0 : 1) != 0;

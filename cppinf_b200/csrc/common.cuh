@@ -169,12 +169,14 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t phase) {
     return done != 0;
 }
 
-// Waits for phase `phase` of `bar` with a bounded number of polls (each try_wait may itself suspend the thread for
-// a short, hardware-chosen time). Returns false if the limit ran out; the caller records the error and must not
-// use the copied data.
-__device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t phase) {
-    constexpr uint32_t kMaxPolls = 1u << 24;
-    for (uint32_t i = 0; i < kMaxPolls; ++i) {
+// Default poll limit of the bounded mbarrier waits: each try_wait may itself suspend the thread for a short,
+// hardware-chosen time, so 2^24 polls is far longer than any copy of this library takes.
+constexpr uint32_t kDefaultPollLimit = 1u << 24;
+
+// Waits for phase `phase` of `bar` with at most `max_polls` polls (0: give up at once). Returns false if the limit
+// ran out; the caller records the error and must not use the copied data.
+__device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t phase, uint32_t max_polls = kDefaultPollLimit) {
+    for (uint32_t i = 0; i < max_polls; ++i) {
         if (mbar_try_wait(bar, phase)) {
             return true;
         }
@@ -314,6 +316,27 @@ struct Chunk {
             return __float_as_uint(f[i]);
         }
     }
+};
+
+// ---- integer division by a launch-time constant ------------------------------------------------------------------
+
+// n / d for 0 <= n < 2^31 and 1 <= d < 2^31 by a multiply-high and a shift (Granlund-Montgomery round-up method):
+// with l = ceil(log2 d) and m = floor(2^32 (2^l - d) / d) + 1, n / d = (umulhi(n, m) + n) >> l, and the sum stays
+// below 2^32 because umulhi(n, m) <= n < 2^31. The host builds it once per launch; the device pays 3 instructions
+// instead of a 32- or 64-bit division routine.
+struct FastDiv {
+    uint32_t d = 1;
+    uint32_t m = 1;
+    uint32_t l = 0;
+
+    FastDiv() = default;
+    __host__ explicit FastDiv(uint32_t divisor) : d(divisor) {
+        while ((uint64_t{1} << l) < divisor) {
+            ++l;
+        }
+        m = static_cast<uint32_t>((((uint64_t{1} << 32) * ((uint64_t{1} << l) - divisor)) / divisor) + 1);
+    }
+    __device__ __forceinline__ uint32_t quot(uint32_t n) const { return (__umulhi(n, m) + n) >> l; }
 };
 
 // ---- warp reductions ---------------------------------------------------------------------------------------------

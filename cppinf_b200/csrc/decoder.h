@@ -7,6 +7,7 @@
 
 #include <cstdint>
 #include <string>
+#include <vector>
 
 #include "cppinf_b200.h"
 
@@ -60,6 +61,7 @@ struct LinearParams {
     // Single-row kernel only: when set, the CTA's slice of weight rows is staged in shared memory by bulk copies
     // issued before griddepcontrol.wait (if it fits), and a bounded wait that runs out sets *error to 1.
     unsigned int* error;
+    uint32_t poll_limit = 1u << 24;  // polls of that wait (cppinf_set_wait_poll_limit)
 };
 
 // Single-row (decode) linear: one warp per output row at a time, the weights streamed once. Supports every
@@ -72,6 +74,12 @@ int gemv_grid(const LinearParams& p);
 // Multi-row linear (prefill): tiles of up to 16 input rows staged in shared memory, kStore / kResidual / kSiluMul.
 // Requires K % 8 == 0 and 16-byte aligned rows.
 cudaError_t launch_linear_rows(const LinearParams& p, cudaStream_t s);
+
+// Multi-row linear on the tensor cores (gemm_tc.cu: tcgen05, tolerance parity, not the restated order):
+// kStore / kResidual / kSiluMul with N % 32 == 0, K % 8 == 0, segment starts multiples of 32, 16-byte aligned
+// operands, no embedding gather, RMSNorm prologue or device position. cudaErrorNotSupported otherwise.
+bool linear_tc_supported(const LinearParams& p);
+cudaError_t launch_linear_tc(const LinearParams& p, cudaStream_t s);
 
 struct AttentionParams {
     const __nv_bfloat16* q;        // [T, Hq, D]
@@ -99,17 +107,11 @@ struct AttentionParams {
     // sets *error to 1.
     unsigned int* error;
     int64_t queries_per_cluster = 1;  // consecutive queries one cluster takes in turn (prefill)
+    uint32_t poll_limit = 1u << 24;   // polls of the staging wait (cppinf_set_wait_poll_limit)
 };
 
 // Causal GQA attention of one sequence in the fixed partition order (see attention.cu). head_dim 64, 128 or 256.
 cudaError_t launch_decoder_attention(const AttentionParams& p, int64_t max_keys, cudaStream_t s);
-
-// q/k per-head RMSNorm + RoPE (rope.cu) at the device-side position: token t is rotated for position
-// *position + t and its k row is written to k_cache row *position + t; q_out is [tokens, q_heads, head_dim].
-cudaError_t launch_qk_norm_rope_at(const __nv_bfloat16* q, const __nv_bfloat16* k, const __nv_bfloat16* q_weight,
-                                   const __nv_bfloat16* k_weight, __nv_bfloat16* q_out, __nv_bfloat16* k_cache,
-                                   int64_t tokens, int q_heads, int k_heads, int head_dim, const int* position,
-                                   float eps, const float* table, int64_t table_positions, cudaStream_t s);
 
 // Embedding lookup (src/models/qwen3/qwen3_model.cpp:132-165): out[t] = table[tokens[t]], ids clamped into range.
 cudaError_t launch_embedding(const __nv_bfloat16* table, int64_t vocab, int64_t hidden, const int64_t* tokens,
@@ -118,6 +120,10 @@ cudaError_t launch_embedding(const __nv_bfloat16* table, int64_t vocab, int64_t 
 // Host side of the model (qwen3.cu): bytes of the named checkpoint tensor the model uses (-1 if it does not use it),
 // and how many tensors it uses.
 int64_t qwen3_tensor_bytes(const cppinf_qwen3* model, const std::string& name);
+
+// The shape the model expects for a checkpoint tensor it uses ([rows, cols] or [size]); false if it does not use it.
+bool qwen3_tensor_shape(const cppinf_qwen3* model, const std::string& name, std::vector<int64_t>* shape);
+int64_t qwen3_shape_elements(const std::vector<int64_t>& shape);
 int64_t qwen3_tensor_count(const cppinf_qwen3* model);
 
 }  // namespace cppinf::device

@@ -1,5 +1,5 @@
-// Streaming elementwise kernels: ops::add / ops::mul (src/ops/elementwise_ops.cpp:44-52), ops::silu
-// (src/ops/nn_ops.cpp:68-72), ops::cast (src/ops/tensor_ops.cpp:138-143), the fused silu*up product of the Qwen MLP
+// Streaming elementwise kernels: ops::add / ops::mul (src/ops/elementwise_ops.cpp:28-36), ops::silu
+// (src/ops/nn_ops.cpp:44-48), ops::cast (src/ops/tensor_ops.cpp:138-143), the fused silu*up product of the Qwen MLP
 // (src/nn/qwen_mlp.cpp:65-66) and the strided gather that materialises non-contiguous views.
 //
 // Every kernel is HBM-bound (<= 1 flop per byte). Layout: dense arrays walked in packs of 32 bytes (256-bit loads
@@ -95,7 +95,7 @@ __device__ __forceinline__ float apply_binary(float a, float b) {
     }
 }
 
-// x / (1 + exp(-x)), oneDNN eltwise_swish with alpha = 1 as ops::silu configures it (src/ops/nn_ops.cpp:70-71).
+// x / (1 + exp(-x)), oneDNN eltwise_swish with alpha = 1 as ops::silu configures it (src/ops/nn_ops.cpp:46-47).
 // The quotient uses the fast division (reciprocal approximation and one multiply, within 2 ulp): the IEEE division
 // sequence made the SiLU kernels issue-bound (the [4096, 3072] bf16 SiLU * up took 16.0 us with it, 13.2 us now).
 // Its reciprocal flushes to zero for divisors of 2^126 and above (x < -87.3), where the IEEE quotient is still a

@@ -441,7 +441,7 @@ __global__ void __launch_bounds__(kStagedThreads, 2) gemv_staged_kernel(const Li
         }
     }
 
-    const bool arrived = mbar_wait_bounded(&s_bar, 0);
+    const bool arrived = mbar_wait_bounded(&s_bar, 0, p.poll_limit);
     if (__syncthreads_or(arrived ? 0 : 1)) {
         // The copies did not complete within the poll limit: report it, give them one more bounded wait so no
         // copy lands in shared memory after this CTA has left, and produce nothing.

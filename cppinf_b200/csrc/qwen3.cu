@@ -86,6 +86,8 @@ struct cppinf_qwen3 {
     int64_t len = 0;
     cudaGraphExec_t step = nullptr;
     int64_t step_launches = 0;
+    uint32_t step_poll_limit = 0;  // the wait poll limit the decode-step graph was captured with
+    bool failed = false;           // a decode step reported a device error; cleared by cppinf_qwen3_reset
 };
 
 namespace {
@@ -120,6 +122,7 @@ LinearParams params_for(LinearEpilogue epi, const bf16* x, int64_t x_stride, con
     p.K = k;
     p.seg[0] = 0;
     p.seg[1] = p.seg[2] = p.seg[3] = n;
+    p.poll_limit = rt::wait_poll_limit();
     return p;
 }
 
@@ -179,6 +182,7 @@ int enqueue_step(cppinf_qwen3* m, cudaStream_t s, int64_t* launches) {
                            static_cast<int>(c.num_attention_heads), static_cast<int>(c.num_key_value_heads),
                            static_cast<int>(c.head_dim), 0, m->d_len, m->cap,
                            m->k, l.q_norm, l.k_norm, m->rope, c.rms_norm_eps, m->d_error};
+        ap.poll_limit = rt::wait_poll_limit();
         QWEN3_TRY(cppinf::device::launch_decoder_attention(ap, m->cap, s), "qwen3_attention");
         LinearParams o = params_for(LinearEpilogue::kResidual, m->ctx, m->q_dim, l.wo, nullptr, 1, H, m->q_dim);
         o.residual = m->h;
@@ -255,20 +259,23 @@ int enqueue_chunk(cppinf_qwen3* m, int64_t pos0, int64_t T, bf16* logits, cudaSt
     return CPPINF_OK;
 }
 
+// Where a checkpoint tensor goes and the shape the model expects: [rows, cols] for matrices, [rows] when cols == 0.
 struct WeightSlot {
     bf16* dst;
     int64_t elements;
+    int64_t rows;
+    int64_t cols;
 };
 
 int find_weight(cppinf_qwen3* m, const std::string& name, WeightSlot* slot) {
     const auto& c = m->c;
     const int64_t H = c.hidden_size;
     if (name == "model.embed_tokens.weight") {
-        *slot = {m->embed, c.vocab_size * H};
+        *slot = {m->embed, c.vocab_size * H, c.vocab_size, H};
         return CPPINF_OK;
     }
     if (name == "model.norm.weight") {
-        *slot = {m->final_norm, H};
+        *slot = {m->final_norm, H, H, 0};
         return CPPINF_OK;
     }
     const std::string prefix = "model.layers.";
@@ -286,27 +293,27 @@ int find_weight(cppinf_qwen3* m, const std::string& name, WeightSlot* slot) {
             const Layer& l = m->layers[static_cast<std::size_t>(layer)];
             const int64_t I = c.intermediate_size;
             if (field == "input_layernorm.weight") {
-                *slot = {l.in_norm, H};
+                *slot = {l.in_norm, H, H, 0};
             } else if (field == "post_attention_layernorm.weight") {
-                *slot = {l.post_norm, H};
+                *slot = {l.post_norm, H, H, 0};
             } else if (field == "self_attn.q_norm.weight") {
-                *slot = {l.q_norm, c.head_dim};
+                *slot = {l.q_norm, c.head_dim, c.head_dim, 0};
             } else if (field == "self_attn.k_norm.weight") {
-                *slot = {l.k_norm, c.head_dim};
+                *slot = {l.k_norm, c.head_dim, c.head_dim, 0};
             } else if (field == "self_attn.q_proj.weight") {
-                *slot = {l.wqkv, m->q_dim * H};
+                *slot = {l.wqkv, m->q_dim * H, m->q_dim, H};
             } else if (field == "self_attn.k_proj.weight") {
-                *slot = {l.wqkv + m->q_dim * H, m->kv_dim * H};
+                *slot = {l.wqkv + m->q_dim * H, m->kv_dim * H, m->kv_dim, H};
             } else if (field == "self_attn.v_proj.weight") {
-                *slot = {l.wqkv + (m->q_dim + m->kv_dim) * H, m->kv_dim * H};
+                *slot = {l.wqkv + (m->q_dim + m->kv_dim) * H, m->kv_dim * H, m->kv_dim, H};
             } else if (field == "self_attn.o_proj.weight") {
-                *slot = {l.wo, H * m->q_dim};
+                *slot = {l.wo, H * m->q_dim, H, m->q_dim};
             } else if (field == "mlp.gate_proj.weight") {
-                *slot = {l.wg, I * H};
+                *slot = {l.wg, I * H, I, H};
             } else if (field == "mlp.up_proj.weight") {
-                *slot = {l.wu, I * H};
+                *slot = {l.wu, I * H, I, H};
             } else if (field == "mlp.down_proj.weight") {
-                *slot = {l.wd, H * I};
+                *slot = {l.wd, H * I, H, I};
             } else {
                 return rt::fail(CPPINF_ERR_INVALID_ARGUMENT, "Qwen3Model does not use tensor '" + name + "'.");
             }
@@ -330,15 +337,29 @@ void release(cppinf_qwen3* m) {
 namespace cppinf::device {
 
 int64_t qwen3_tensor_bytes(const cppinf_qwen3* model, const std::string& name) {
+    std::vector<int64_t> shape;
+    return qwen3_tensor_shape(model, name, &shape) ? qwen3_shape_elements(shape) * 2 : -1;
+}
+
+bool qwen3_tensor_shape(const cppinf_qwen3* model, const std::string& name, std::vector<int64_t>* shape) {
     WeightSlot slot{};
     // find_weight records an error message for unknown names; this probe must not disturb the caller's.
     const std::string saved = cppinf_last_error();
     const int st = find_weight(const_cast<cppinf_qwen3*>(model), name, &slot);
     if (st != CPPINF_OK) {
         rt::fail(CPPINF_ERR_INVALID_ARGUMENT, saved);
-        return -1;
+        return false;
     }
-    return slot.elements * 2;
+    *shape = slot.cols == 0 ? std::vector<int64_t>{slot.rows} : std::vector<int64_t>{slot.rows, slot.cols};
+    return true;
+}
+
+int64_t qwen3_shape_elements(const std::vector<int64_t>& shape) {
+    int64_t n = 1;
+    for (const int64_t d : shape) {
+        n *= d;
+    }
+    return n;
 }
 
 int64_t qwen3_tensor_count(const cppinf_qwen3* model) {
@@ -525,7 +546,9 @@ int cppinf_qwen3_reset(cppinf_qwen3* model, void* stream) {
     const auto s = rt::as_stream(stream);
     CPPINF_CUDA_TRY(cudaMemsetAsync(model->cache, 0, model->cache_bytes, s));
     CPPINF_CUDA_TRY(cudaMemsetAsync(model->d_len, 0, sizeof(int), s));
+    CPPINF_CUDA_TRY(cudaMemsetAsync(model->d_error, 0, sizeof(unsigned int), s));
     model->len = 0;
+    model->failed = false;
     return rt::ok();
 }
 
@@ -542,6 +565,8 @@ int cppinf_qwen3_forward(cppinf_qwen3* model, const int64_t* token_ids, int64_t 
     CPPINF_REQUIRE(model && token_ids, CPPINF_ERR_INVALID_ARGUMENT, "qwen3_forward received a null pointer.");
     CPPINF_REQUIRE(count > 0, CPPINF_ERR_INVALID_ARGUMENT,
                    "Qwen3Model session forward requires at least one uncached token.");
+    CPPINF_REQUIRE(!model->failed, CPPINF_ERR_CUDA,
+                   "qwen3 model state is invalid after a device error; call qwen3_reset first.");
     CPPINF_REQUIRE(model->len + count <= model->cap, CPPINF_ERR_OUT_OF_RANGE,
                    "qwen_attention cache is too small for the new tokens.");
     for (int64_t i = 0; i < count; ++i) {
@@ -580,12 +605,21 @@ int cppinf_qwen3_decode(cppinf_qwen3* model, int64_t steps, int64_t* tokens, voi
         return rt::ok();
     }
     CPPINF_REQUIRE(tokens, CPPINF_ERR_INVALID_ARGUMENT, "qwen3_decode received a null pointer.");
+    CPPINF_REQUIRE(!model->failed, CPPINF_ERR_CUDA,
+                   "qwen3 model state is invalid after a device error; call qwen3_reset first.");
     CPPINF_REQUIRE(model->len > 0, CPPINF_ERR_INVALID_ARGUMENT,
                    "qwen3_decode needs a forward call first (the cache is empty).");
     CPPINF_REQUIRE(model->len + steps <= model->cap, CPPINF_ERR_OUT_OF_RANGE,
                    "qwen_attention cache is too small for the new tokens.");
     const auto s = rt::as_stream(stream);
+    if (model->step != nullptr && model->step_poll_limit != rt::wait_poll_limit()) {
+        // The wait poll limit changed since the step was captured: capture it again with the current one (an
+        // executable graph still in flight is freed when it completes).
+        cudaGraphExecDestroy(model->step);
+        model->step = nullptr;
+    }
     if (model->step == nullptr) {
+        model->step_poll_limit = rt::wait_poll_limit();
         cudaStream_t cap_stream = nullptr;
         CPPINF_CUDA_TRY(cudaStreamCreateWithFlags(&cap_stream, cudaStreamNonBlocking));
         cudaGraph_t graph = nullptr;
@@ -622,9 +656,14 @@ int cppinf_qwen3_decode(cppinf_qwen3* model, int64_t steps, int64_t* tokens, voi
                                     cudaMemcpyDeviceToHost, s));
     CPPINF_CUDA_TRY(cudaMemcpyAsync(&error, model->d_error, sizeof(error), cudaMemcpyDeviceToHost, s));
     CPPINF_CUDA_TRY(cudaStreamSynchronize(s));
+    if (error != 0) {
+        // The device advanced its sequence length but the tokens are not valid: the model needs a reset.
+        model->failed = true;
+        return rt::fail(CPPINF_ERR_CUDA,
+                        "qwen3_decode: a device wait for staged data ran out of its poll limit; results are invalid "
+                        "(call qwen3_reset).");
+    }
     model->len += steps;
-    CPPINF_REQUIRE(error == 0, CPPINF_ERR_CUDA,
-                   "qwen3_decode: a device wait for staged weights ran out of its poll limit; results are invalid.");
     return rt::ok();
 }
 

@@ -1,4 +1,4 @@
-// RMSNorm over the last dimension, ops::rms_norm (src/ops/nn_ops.cpp:164-225), and the residual add + RMSNorm pair
+// RMSNorm over the last dimension, ops::rms_norm (src/ops/nn_ops.cpp:140-201), and the residual add + RMSNorm pair
 // of the decoder block (src/nn/qwen_decoder_block.cpp:80-84 and :89 feeding the next layer's :73).
 //
 // The reference runs nine oneDNN passes: cast to f32, x*x, reduction_mean, +eps, sqrt, 1/rms, x*inv, *w, cast. Here

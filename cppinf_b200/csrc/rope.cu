@@ -1,4 +1,4 @@
-// Split-half RoPE, nn::apply_rope (src/nn/rope.cpp:73-124), and the fused per-head q/k RMSNorm + RoPE that the
+// Split-half RoPE, nn::apply_rope (src/nn/rope.cpp:58-109), and the fused per-head q/k RMSNorm + RoPE that the
 // attention block runs (src/nn/qwen_attention.cpp:383-390: ops::rms_norm on [B, T, H, D] head views, result rounded
 // to the model dtype, then apply_rope_batched at position cache_length + t).
 //
@@ -11,8 +11,14 @@
 // Fused kernel layout: q [T, Hq, D] and k [T, Hk, D] dense. A head vector is held by L = D / (2 * kVec) lanes; lane
 // l holds chunk l of the first half (elements l*kVec ..) and chunk l of the second half (D/2 + l*kVec ..), one 16-byte
 // vector each, so every RoPE pair (i, i + D/2) sits in one lane and no shuffle is needed for the rotation. One warp
-// unit covers kIters groups of 32/L heads of one token; all its loads are issued before any arithmetic. The token's
-// table row and the two weight vectors are read once per unit.
+// unit covers kIters groups of 32/L heads of one token, all q or all k heads (a token has ceil(Hq / unit) q units
+// then ceil(Hk / unit) k units), so the unit's rows are contiguous and share one norm weight vector and one angle
+// row: each lane holds the angles of its pairs in registers as f32 and the two weight chunks packed, for the whole
+// unit. The unit index is split into (token, unit of the token) by a multiply-high division (FastDiv). When every
+// unit is full (Hq and Hk multiples of the unit's heads: the Qwen3 shapes), the per-head bounds checks are compiled
+// out (kFull). Measured on B200 for [2048, 16 + 8, 128] bf16 against the layout whose units could mix q and k heads
+// and staged the angles and weights in shared memory: 6.43 -> 5.99 us; holding the weights as f32 (more registers,
+// fewer CTAs per SM) 6.36 us; fused multiply-adds in the sum of squares changed nothing.
 //
 // Reduction order: the sum of squares of a head equals the library's canonical order (lane c sums chunk c, then a
 // butterfly over lane distances 16, 8, ..., 1 over the D/kVec chunks): here a lane adds its first-half partial to its
@@ -32,7 +38,7 @@ namespace cppinf::device {
 namespace {
 
 constexpr int kThreads = 256;
-constexpr int kQkThreads = 64;  // two warp units per CTA (measured: 6.49 us against 6.52 with 4 and 6.74 with 8)
+constexpr int kQkThreads = 64;  // two warp units per CTA
 constexpr int kQkWarps = kQkThreads / 32;
 
 struct QkParams {
@@ -43,111 +49,84 @@ struct QkParams {
     void* q_out;
     void* k_out;
     const float* table;
-    int64_t tokens;
     int64_t position_offset;
+    uint32_t units;      // tokens * units_per_token (< 2^31)
+    FastDiv per_token;   // units_per_token = q_units + k_units
+    int q_units;         // ceil(q_heads / heads per unit): units [0, q_units) of a token hold q heads
     int q_heads;
     int k_heads;
-    int units_per_token;
     float eps;
-    // Decode steps: when set, *position is added to the RoPE position and to the k_out row (k_out is then the KV
-    // cache base), and tokens at or past table_positions are skipped.
-    const int* position;
-    int64_t table_positions;
 };
 
-// Shared-memory slot of one warp: the unit's raw head vectors (lane-major, each lane reads back what it copied),
-// the token's angle row and the two norm weight vectors.
-template <typename T, int kLanes, int kIters>
-struct QkSlot {
-    static constexpr int kDim = 2 * kLanes * Vec16<T>::kVec;
-    static constexpr int kWeightChunks = kDim * static_cast<int>(sizeof(T)) / 16;
-    uint4 data[kIters][2][32];
-    __align__(16) float table[kDim];
-    uint4 weights[2][kWeightChunks];
-};
-
-template <typename T, int kLanes, int kIters>
-__global__ void __launch_bounds__(kQkThreads) qk_norm_rope_kernel(QkParams p) {
+// A warp unit is kIters groups of 32/L heads, all q heads or all k heads of one token, so the unit's source rows
+// are one contiguous block and every head of the unit uses the same norm weights and the same angle row. Each lane
+// loads its weights and angles once per unit into registers; the head vectors arrive by asynchronous copies
+// into the warp's shared-memory slot (lane-major: each lane reads back exactly what it copied, no barrier but the
+// copy-group wait), one copy group per iteration, and each iteration starts as soon as its own group has landed.
+// At most 64 registers, so 16 CTAs fit an SM (measured 5.98 -> 5.93 us on [2048, 16 + 8, 128] bf16).
+template <typename T, int kLanes, int kIters, bool kFull>
+__global__ void __launch_bounds__(kQkThreads, 16) qk_norm_rope_kernel(const QkParams p) {
     using V = Vec16<T>;
-    using Slot = QkSlot<T, kLanes, kIters>;
     constexpr int kVec = V::kVec;
     constexpr int kHalf = kLanes * kVec;  // D / 2
     constexpr int kDim = 2 * kHalf;
     constexpr int kHeadsPerIter = 32 / kLanes;
     constexpr int kHeadsPerUnit = kHeadsPerIter * kIters;
-    constexpr int64_t kHeadBytes = kDim * static_cast<int64_t>(sizeof(T));
+    constexpr int kHeadBytes = kDim * static_cast<int>(sizeof(T));
     constexpr int kHalfBytes = kHalf * static_cast<int>(sizeof(T));
-    constexpr int kTableChunks = kDim * 4 / 16;
-    constexpr int kWeightChunks = Slot::kWeightChunks;
-    __shared__ Slot s_slot[kQkWarps];
+    __shared__ uint4 s_data[kQkWarps][kIters][2][32];
 
-    grid_dependency_begin();
     const int lane = threadIdx.x & 31;
     const int hl = lane % kLanes;  // lane within the head
     const int slot = lane / kLanes;
-    const int heads = p.q_heads + p.k_heads;
-    const int64_t unit = static_cast<int64_t>(blockIdx.x) * kQkWarps + threadIdx.x / 32;
-    if (unit >= p.tokens * p.units_per_token) {
+    const uint32_t unit = blockIdx.x * kQkWarps + threadIdx.x / 32;
+    if (unit >= p.units) {
+        grid_dependency_begin();
         return;  // the whole warp leaves together
     }
-    const int64_t t = unit / p.units_per_token;
-    const int h0 = static_cast<int>(unit - t * p.units_per_token) * kHeadsPerUnit;
-    const int64_t shift = p.position != nullptr ? static_cast<int64_t>(*p.position) : 0;
-    if (p.position != nullptr && p.position_offset + shift + t >= p.table_positions) {
-        return;
-    }
-    Slot& w = s_slot[threadIdx.x / 32];
+    const uint32_t t = p.per_token.quot(unit);
+    const int u = static_cast<int>(unit - t * p.per_token.d);
+    const bool is_q = u < p.q_units;
+    const int heads = is_q ? p.q_heads : p.k_heads;
+    const int h0 = (is_q ? u : u - p.q_units) * kHeadsPerUnit;
+    const int64_t row0 = static_cast<int64_t>(t) * heads + h0;  // first head row of the unit
+    const char* src = static_cast<const char*>(is_q ? p.q : p.k) + row0 * kHeadBytes + hl * 16;
+    char* dst = static_cast<char*>(is_q ? p.q_out : p.k_out) + row0 * kHeadBytes + hl * 16;
+    const char* wsrc = static_cast<const char*>(is_q ? p.qw : p.kw) + hl * 16;
+    const float* trow = p.table + (p.position_offset + t) * kDim + hl * kVec;
 
-    // Every load of the unit is issued as an asynchronous copy into the warp's slot before any arithmetic: the
-    // values wait in shared memory rather than in registers, which keeps the kernel at more resident warps per SM.
-    // Copy groups: the first iteration's heads, then the angle row and the weights, then one group per further
-    // iteration. An iteration starts as soon as its heads have landed; the first one needs the angles and weights
-    // only after its norm statistics.
-    const auto copy_heads = [&](int i) {
-        const int h = h0 + i * kHeadsPerIter + slot;
-        if (h < heads) {
-            const char* src = h < p.q_heads
-                                  ? static_cast<const char*>(p.q) + (t * p.q_heads + h) * kHeadBytes
-                                  : static_cast<const char*>(p.k) + (t * p.k_heads + (h - p.q_heads)) * kHeadBytes;
-            cp_async16(&w.data[i][0][lane], src + hl * 16);
-            cp_async16(&w.data[i][1][lane], src + kHalfBytes + hl * 16);
+    // Everything below reads memory, so it follows the dependency wait: the op does not know which of its inputs
+    // the previous kernel of the stream wrote.
+    grid_dependency_begin();
+#pragma unroll
+    for (int i = 0; i < kIters; ++i) {
+        if (kFull || h0 + i * kHeadsPerIter + slot < heads) {
+            const char* s = src + (i * kHeadsPerIter + slot) * kHeadBytes;
+            cp_async16(&s_data[threadIdx.x / 32][i][0][lane], s);
+            cp_async16(&s_data[threadIdx.x / 32][i][1][lane], s + kHalfBytes);
         }
         cp_async_commit();
-    };
-    copy_heads(0);
-    const char* row = reinterpret_cast<const char*>(p.table + (p.position_offset + shift + t) * kDim);
-    for (int c = lane; c < kTableChunks; c += 32) {
-        cp_async16(&w.table[c * 4], row + c * 16);  // cos in [0, D/2), sin in [D/2, D)
     }
-    for (int c = lane; c < 2 * kWeightChunks; c += 32) {
-        const bool is_q = c < kWeightChunks;
-        const int chunk = is_q ? c : c - kWeightChunks;
-        cp_async16(&w.weights[is_q ? 0 : 1][chunk], static_cast<const char*>(is_q ? p.qw : p.kw) + chunk * 16);
-    }
-    cp_async_commit();
+    const uint4 wpa = ld_cached(wsrc);
+    const uint4 wpb = ld_cached(wsrc + kHalfBytes);
+    float cs[kVec];
+    float sn[kVec];
 #pragma unroll
-    for (int i = 1; i < kIters; ++i) {
-        copy_heads(i);
+    for (int j = 0; j < kVec; j += 4) {
+        const float4 c4 = ld_cached_f4(trow + j);
+        const float4 s4 = ld_cached_f4(trow + kHalf + j);
+        cs[j] = c4.x, cs[j + 1] = c4.y, cs[j + 2] = c4.z, cs[j + 3] = c4.w;
+        sn[j] = s4.x, sn[j + 1] = s4.y, sn[j + 2] = s4.z, sn[j + 3] = s4.w;
     }
 
 #pragma unroll
     for (int i = 0; i < kIters; ++i) {
-        cp_async_wait_pending(i == 0 ? kIters : kIters - 1 - i);
-        __syncwarp();
-        const int h = h0 + i * kHeadsPerIter + slot;
-        const bool active = h < heads;
+        cp_async_wait_pending(kIters - 1 - i);
+        const bool active = h0 + i * kHeadsPerIter + slot < heads;
         float a[kVec];
         float b[kVec];
-        if (active) {
-            V::unpack(w.data[i][0][lane], a);
-            V::unpack(w.data[i][1][lane], b);
-        } else {
-#pragma unroll
-            for (int j = 0; j < kVec; ++j) {
-                a[j] = 0.0f;
-                b[j] = 0.0f;
-            }
-        }
+        V::unpack(s_data[threadIdx.x / 32][i][0][lane], a);  // inactive lanes read stale bytes and store nothing
+        V::unpack(s_data[threadIdx.x / 32][i][1][lane], b);
         // Squares as packed f32x2 products, summed by scalar adds in element order (sa = sa + a*a). The adds stay
         // scalar on purpose: a packed product feeding a packed add is contracted into a fused multiply-add by the
         // code generator, which rounds once and changes the result.
@@ -165,51 +144,36 @@ __global__ void __launch_bounds__(kQkThreads) qk_norm_rope_kernel(QkParams p) {
         const float mean = ss / static_cast<float>(kDim);
         const float rms = sqrtf(mean + p.eps);
         const float inv = 1.0f / rms;
-        if (i == 0) {
-            cp_async_wait_pending(kIters - 1);  // the angle row and the weights
-            __syncwarp();
+        const float2 inv2 = make_float2(inv, inv);
+        float wa[kVec];
+        float wb[kVec];
+        V::unpack(wpa, wa);
+        V::unpack(wpb, wb);
+        float out_a[kVec];
+        float out_b[kVec];
+#pragma unroll
+        for (int j = 0; j < kVec; j += 2) {
+            // (x * inv) * w, separately rounded, then stored in the model dtype: the reference's rms_norm returns a
+            // tensor of the input dtype and RoPE reads those rounded values.
+            const float2 x = __fmul2_rn(__fmul2_rn(make_float2(a[j], a[j + 1]), inv2), make_float2(wa[j], wa[j + 1]));
+            const float2 y = __fmul2_rn(__fmul2_rn(make_float2(b[j], b[j + 1]), inv2), make_float2(wb[j], wb[j + 1]));
+            const float2 n1 = V::quantize2(x.x, x.y);  // first-half elements j, j + 1
+            const float2 n2 = V::quantize2(y.x, y.y);  // second-half elements j, j + 1
+            const float2 c = make_float2(cs[j], cs[j + 1]);
+            const float2 s = make_float2(sn[j], sn[j + 1]);
+            const float2 n1c = __fmul2_rn(n1, c);
+            const float2 n2s = __fmul2_rn(n2, s);
+            const float2 n2c = __fmul2_rn(n2, c);
+            const float2 n1s = __fmul2_rn(n1, s);
+            out_a[j] = n1c.x - n2s.x;  // first  * cos - second * sin  (src/nn/rope.cpp:100-101)
+            out_a[j + 1] = n1c.y - n2s.y;
+            out_b[j] = n2c.x + n1s.x;  // second * cos + first  * sin  (src/nn/rope.cpp:102-103)
+            out_b[j + 1] = n2c.y + n1s.y;
         }
-        if (active) {
-            const int which = h < p.q_heads ? 0 : 1;
-            float wa[kVec];
-            float wb[kVec];
-            V::unpack(w.weights[which][hl], wa);
-            V::unpack(w.weights[which][kLanes + hl], wb);
-            const float2 inv2 = make_float2(inv, inv);
-            float x[kVec];
-            float y[kVec];
-#pragma unroll
-            for (int j = 0; j < kVec; ++j) {
-                // (first * inv) * w and (second * inv) * w, separately rounded
-                const float2 n = __fmul2_rn(__fmul2_rn(make_float2(a[j], b[j]), inv2), make_float2(wa[j], wb[j]));
-                x[j] = n.x;
-                y[j] = n.y;
-            }
-            float out_a[kVec];
-            float out_b[kVec];
-#pragma unroll
-            for (int j = 0; j < kVec; j += 2) {
-                const float4 cv = *reinterpret_cast<const float4*>(&w.table[hl * kVec + (j & ~3)]);
-                const float4 sv = *reinterpret_cast<const float4*>(&w.table[kHalf + hl * kVec + (j & ~3)]);
-                const float2 c = (j & 3) == 0 ? make_float2(cv.x, cv.y) : make_float2(cv.z, cv.w);
-                const float2 s = (j & 3) == 0 ? make_float2(sv.x, sv.y) : make_float2(sv.z, sv.w);
-                // The reference's rms_norm returns a tensor of the model dtype; RoPE reads those rounded values.
-                const float2 n1 = V::quantize2(x[j], x[j + 1]);  // first-half elements j, j + 1
-                const float2 n2 = V::quantize2(y[j], y[j + 1]);  // second-half elements j, j + 1
-                const float2 n1c = __fmul2_rn(n1, c);
-                const float2 n2s = __fmul2_rn(n2, s);
-                const float2 n2c = __fmul2_rn(n2, c);
-                const float2 n1s = __fmul2_rn(n1, s);
-                out_a[j] = n1c.x - n2s.x;  // first  * cos - second * sin  (src/nn/rope.cpp:115-116)
-                out_a[j + 1] = n1c.y - n2s.y;
-                out_b[j] = n2c.x + n1s.x;  // second * cos + first  * sin  (src/nn/rope.cpp:117-118)
-                out_b[j + 1] = n2c.y + n1s.y;
-            }
-            char* dst = h < p.q_heads ? static_cast<char*>(p.q_out) + (t * p.q_heads + h) * kHeadBytes
-                                      : static_cast<char*>(p.k_out) +
-                                            ((shift + t) * p.k_heads + (h - p.q_heads)) * kHeadBytes;
-            st_stream(dst + hl * 16, V::pack(out_a));
-            st_stream(dst + kHalfBytes + hl * 16, V::pack(out_b));
+        if (kFull || active) {
+            char* d = dst + (i * kHeadsPerIter + slot) * kHeadBytes;
+            st_stream(d, V::pack(out_a));
+            st_stream(d + kHalfBytes, V::pack(out_b));
         }
     }
 }
@@ -252,56 +216,52 @@ __global__ void __launch_bounds__(kThreads) rope_kernel(RopeParams p, int64_t to
 }
 
 template <typename T, int kLanes, int kIters>
-cudaError_t launch_qk_units(QkParams p, cudaStream_t s) {
+cudaError_t launch_qk_units(QkParams p, int64_t tokens, cudaStream_t s) {
     constexpr int kHeadsPerUnit = (32 / kLanes) * kIters;
-    const int heads = p.q_heads + p.k_heads;
-    p.units_per_token = (heads + kHeadsPerUnit - 1) / kHeadsPerUnit;
-    const int64_t units = p.tokens * p.units_per_token;
+    p.q_units = (p.q_heads + kHeadsPerUnit - 1) / kHeadsPerUnit;
+    const int per_token = p.q_units + (p.k_heads + kHeadsPerUnit - 1) / kHeadsPerUnit;
+    const int64_t units = tokens * per_token;
+    if (units >= (int64_t{1} << 31)) {
+        return cudaErrorInvalidConfiguration;  // the entry point rejects such sizes before this
+    }
+    p.units = static_cast<uint32_t>(units);
+    p.per_token = FastDiv(static_cast<uint32_t>(per_token));
     const auto blocks = static_cast<unsigned>(runtime::ceil_div(units, kQkWarps));
-    return ::cppinf::runtime::launch(qk_norm_rope_kernel<T, kLanes, kIters>, dim3(blocks), dim3(kQkThreads), s, 1u, p);
+    if (p.q_heads % kHeadsPerUnit == 0 && p.k_heads % kHeadsPerUnit == 0) {
+        return ::cppinf::runtime::launch(qk_norm_rope_kernel<T, kLanes, kIters, true>, dim3(blocks), dim3(kQkThreads),
+                                         s, 1u, p);
+    }
+    return ::cppinf::runtime::launch(qk_norm_rope_kernel<T, kLanes, kIters, false>, dim3(blocks), dim3(kQkThreads), s,
+                                     1u, p);
 }
 
-// A warp unit covers 8 heads of one token (two iterations of 4 heads at D = 128 bf16): measured on B200 against
-// units of 4, 12 and 24 heads for the [2048, 16 + 8, 128] configuration, it balances loads in flight per warp against
-// warps per SM best.
+// A warp unit covers 8 heads (two iterations of 4 heads at D = 128 bf16): measured on B200 against units of 4, 12
+// and 24 heads for the [2048, 16 + 8, 128] configuration, it balances loads in flight per warp against warps per SM
+// best.
 template <typename T, int kLanes>
-cudaError_t launch_qk(const QkParams& p, cudaStream_t s) {
+cudaError_t launch_qk(const QkParams& p, int64_t tokens, cudaStream_t s) {
     constexpr int kHeadsPerIter = 32 / kLanes;
     constexpr int kIters = kHeadsPerIter >= 8 ? 1 : 8 / kHeadsPerIter;
-    return launch_qk_units<T, kLanes, kIters>(p, s);
+    return launch_qk_units<T, kLanes, kIters>(p, tokens, s);
 }
 
 template <typename T>
-cudaError_t dispatch_qk(const QkParams& p, int lanes, cudaStream_t s) {
+cudaError_t dispatch_qk(const QkParams& p, int64_t tokens, int lanes, cudaStream_t s) {
     switch (lanes) {
     case 1:
-        return launch_qk<T, 1>(p, s);
+        return launch_qk<T, 1>(p, tokens, s);
     case 2:
-        return launch_qk<T, 2>(p, s);
+        return launch_qk<T, 2>(p, tokens, s);
     case 4:
-        return launch_qk<T, 4>(p, s);
+        return launch_qk<T, 4>(p, tokens, s);
     case 8:
-        return launch_qk<T, 8>(p, s);
+        return launch_qk<T, 8>(p, tokens, s);
     default:
-        return launch_qk<T, 16>(p, s);
+        return launch_qk<T, 16>(p, tokens, s);
     }
 }
 
 }  // namespace
-
-cudaError_t launch_qk_norm_rope_at(const bf16* q, const bf16* k, const bf16* q_weight, const bf16* k_weight,
-                                   bf16* q_out, bf16* k_cache, int64_t tokens, int q_heads, int k_heads,
-                                   int head_dim, const int* position, float eps, const float* table,
-                                   int64_t table_positions, cudaStream_t s) {
-    const int lanes = head_dim / 16;
-    if (head_dim % 16 != 0 || lanes < 1 || lanes > 16 || (lanes & (lanes - 1)) != 0) {
-        return cudaErrorInvalidValue;
-    }
-    QkParams p{q, k, q_weight, k_weight, q_out, k_cache, table, tokens, 0, q_heads, k_heads, 0, eps, position,
-               table_positions};
-    return dispatch_qk<bf16>(p, lanes, s);
-}
-
 }  // namespace cppinf::device
 
 using namespace cppinf::device;
@@ -317,7 +277,7 @@ int cppinf_rope_table(float base, int64_t head_dim, int64_t positions, float* ta
     CPPINF_REQUIRE(positions >= 0, CPPINF_ERR_INVALID_ARGUMENT, "rope table positions must be non-negative.");
     CPPINF_REQUIRE(positions == 0 || table, CPPINF_ERR_INVALID_ARGUMENT, "rope table received a null pointer.");
     const int64_t half = head_dim / 2;
-    // One inverse frequency per feature pair, as src/nn/rope.cpp:85-90 computes it.
+    // One inverse frequency per feature pair, as src/nn/rope.cpp:70-74 computes it.
     std::vector<float> inverse_frequencies(static_cast<std::size_t>(half));
     for (int64_t i = 0; i < half; ++i) {
         inverse_frequencies[static_cast<std::size_t>(i)] =
@@ -378,6 +338,8 @@ int cppinf_qk_norm_rope(cppinf_dtype dtype, const void* q, const void* k, const 
                    "qk_norm_rope requires non-negative sizes.");
     CPPINF_REQUIRE(q_heads + k_heads <= (int64_t{1} << 20), CPPINF_ERR_UNSUPPORTED,
                    "qk_norm_rope supports at most 2^20 heads.");
+    CPPINF_REQUIRE(tokens < (int64_t{1} << 31) / (q_heads + k_heads + 2), CPPINF_ERR_UNSUPPORTED,
+                   "qk_norm_rope supports fewer than 2^31 head vectors per call.");
     CPPINF_REQUIRE(head_dim > 0, CPPINF_ERR_INVALID_ARGUMENT, "rms_norm requires a non-empty last dimension.");
     CPPINF_REQUIRE(head_dim % 2 == 0, CPPINF_ERR_INVALID_ARGUMENT, "apply_rope requires an even head size.");
     CPPINF_REQUIRE(eps >= 0.0f, CPPINF_ERR_INVALID_ARGUMENT, "rms_norm requires a non-negative epsilon.");
@@ -398,14 +360,22 @@ int cppinf_qk_norm_rope(cppinf_dtype dtype, const void* q, const void* k, const 
                                                              rt::aligned16(q_out))) &&
                        (k_heads == 0 || (rt::aligned16(k) && rt::aligned16(k_weight) && rt::aligned16(k_out))),
                    CPPINF_ERR_UNSUPPORTED, "qk_norm_rope requires 16-byte aligned operands.");
-    // The kernel reads both weight vectors for every unit; a missing one is replaced by the other (never used).
-    const void* qw = q_heads == 0 ? k_weight : q_weight;
-    const void* kw = k_heads == 0 ? q_weight : k_weight;
-    QkParams p{q, k, qw, kw, q_out, k_out, table, tokens, position_offset, static_cast<int>(q_heads),
-               static_cast<int>(k_heads), 0, eps, nullptr, table_positions};
+    QkParams p{};
+    p.q = q;
+    p.k = k;
+    p.qw = q_weight;
+    p.kw = k_weight;
+    p.q_out = q_out;
+    p.k_out = k_out;
+    p.table = table;
+    p.position_offset = position_offset;
+    p.q_heads = static_cast<int>(q_heads);
+    p.k_heads = static_cast<int>(k_heads);
+    p.eps = eps;
     const auto s = rt::as_stream(stream);
-    const cudaError_t launch_err = dtype == CPPINF_DTYPE_BF16 ? dispatch_qk<bf16>(p, static_cast<int>(lanes), s)
-                                                              : dispatch_qk<float>(p, static_cast<int>(lanes), s);
+    const cudaError_t launch_err = dtype == CPPINF_DTYPE_BF16
+                                       ? dispatch_qk<bf16>(p, tokens, static_cast<int>(lanes), s)
+                                       : dispatch_qk<float>(p, tokens, static_cast<int>(lanes), s);
     return rt::launched(launch_err, "qk_norm_rope");
 }
 

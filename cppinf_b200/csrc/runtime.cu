@@ -10,6 +10,7 @@ namespace {
 
 thread_local std::string g_last_error;
 std::atomic<uint64_t> g_launches{0};
+std::atomic<uint32_t> g_poll_limit{1u << 24};
 
 struct DeviceProps {
     int sm_count = 0;
@@ -90,6 +91,10 @@ int max_threads_per_sm() {
     return props_for_current_device().max_threads_per_sm;
 }
 
+uint32_t wait_poll_limit() {
+    return g_poll_limit.load(std::memory_order_relaxed);
+}
+
 }  // namespace cppinf::runtime
 
 extern "C" {
@@ -123,6 +128,10 @@ const char* cppinf_status_name(int status) {
 
 uint64_t cppinf_launch_count(void) {
     return cppinf::runtime::g_launches.load(std::memory_order_relaxed);
+}
+
+uint32_t cppinf_set_wait_poll_limit(uint32_t polls) {
+    return cppinf::runtime::g_poll_limit.exchange(polls, std::memory_order_relaxed);
 }
 
 }  // extern "C"

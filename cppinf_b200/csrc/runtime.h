@@ -31,6 +31,10 @@ int sm_count();
 // Largest number of threads per SM of the current device (cached per device).
 int max_threads_per_sm();
 
+// Poll limit for the first wait on each bulk-copy barrier of the kernels launched from now on
+// (cppinf_set_wait_poll_limit).
+uint32_t wait_poll_limit();
+
 inline bool aligned16(const void* p) {
     return (reinterpret_cast<std::uintptr_t>(p) & 15u) == 0;
 }

@@ -494,11 +494,24 @@ int cppinf_qwen3_load_safetensors(cppinf_qwen3* model, const char* path, int64_t
     const int64_t required = cppinf::device::qwen3_tensor_count(model);
     int64_t count = 0;
     for (const auto& e : entries) {
-        if (cppinf::device::qwen3_tensor_bytes(model, e.name) < 0) {
+        std::vector<int64_t> want;
+        if (!cppinf::device::qwen3_tensor_shape(model, e.name, &want)) {
             continue;
         }
         CPPINF_REQUIRE(e.dtype == CPPINF_DTYPE_BF16, CPPINF_ERR_INVALID_ARGUMENT,
                        "Qwen3Model tensor '" + e.name + "' must be bf16.");
+        // The shape checks the reference's layers apply to their weights: validate_projection_weight
+        // (src/nn/qwen_common.cpp:38-49) for matrices, ops::rms_norm's weight checks (src/ops/nn_ops.cpp:150-159)
+        // for norm vectors. A transposed matrix has the right byte count, so the shape itself is compared.
+        if (want.size() == 2) {
+            CPPINF_REQUIRE(e.shape.size() == 2, CPPINF_ERR_INVALID_ARGUMENT, e.name + " must be rank-2.");
+            CPPINF_REQUIRE(e.shape == want, CPPINF_ERR_INVALID_ARGUMENT, e.name + " has an unexpected shape.");
+        } else {
+            CPPINF_REQUIRE(e.shape.size() == 1, CPPINF_ERR_INVALID_ARGUMENT,
+                           "rms_norm requires a rank-1 weight tensor.");
+            CPPINF_REQUIRE(e.shape == want, CPPINF_ERR_INVALID_ARGUMENT,
+                           "rms_norm weight size must match the input last dimension.");
+        }
         st = cppinf_qwen3_set_weight(model, e.name.c_str(), file.bytes() + offset + e.begin,
                                      static_cast<int64_t>(e.end - e.begin), 0);
         if (st != CPPINF_OK) {

@@ -1,6 +1,6 @@
 // Row softmax kernels:
-//  - ops::softmax_last_dim (src/ops/nn_ops.cpp:74-99, oneDNN softmax_accurate), bf16 or f32 in and out;
-//  - ops::scaled_causal_softmax_last_dim (src/ops/nn_ops.cpp:101-162), f32 [matrices, Q, K] with Q == K;
+//  - ops::softmax_last_dim (src/ops/nn_ops.cpp:50-75, oneDNN softmax_accurate), bf16 or f32 in and out;
+//  - ops::scaled_causal_softmax_last_dim (src/ops/nn_ops.cpp:77-138), f32 [matrices, Q, K] with Q == K;
 //  - the position-aware variant of attention, scaled_position_causal_softmax_last_dim
 //    (src/nn/qwen_attention.cpp:164-235), f32 [batch, heads, Qcap, Kcap] with per-batch offsets and lengths.
 //

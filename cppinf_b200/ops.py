@@ -119,7 +119,7 @@ def silu_mul(gate: torch.Tensor, up: torch.Tensor) -> torch.Tensor:
 
 
 def _validate_last_dim(input: torch.Tensor, op: str) -> int:
-    # validate_last_dim_operation_input, src/ops/nn_ops.cpp:54-64
+    # validate_last_dim_operation_input, src/ops/nn_ops.cpp:30-40
     code = _dtype_code(input, op)
     if input.dim() == 0:
         raise ValueError(f"{op} requires a tensor with rank at least 1.")
@@ -129,7 +129,7 @@ def _validate_last_dim(input: torch.Tensor, op: str) -> int:
 
 
 def _validate_rms(input: torch.Tensor, weight: torch.Tensor, epsilon: float) -> int:
-    # src/ops/nn_ops.cpp:164-183
+    # src/ops/nn_ops.cpp:140-159
     code = _validate_last_dim(input, "rms_norm")
     if epsilon < 0.0:
         raise ValueError("rms_norm requires a non-negative epsilon.")
@@ -277,7 +277,7 @@ def rope_table(rope_base: float, head_dim: int, positions: int, device: torch.de
 def apply_rope(input: torch.Tensor, sequence_position_offset: int = 0, rope_base: float = 1000000.0,
                sequence_dimension: int = 1) -> torch.Tensor:
     """nn::apply_rope, src/nn/rope.h:12-13, on a rank-3 tensor."""
-    # validate_rope_input, src/nn/rope.cpp:48-69
+    # validate_rope_input, src/nn/rope.cpp:33-54
     code = _dtype_code(input, "apply_rope")
     if input.dim() != 3:
         raise ValueError("apply_rope requires a rank-3 tensor.")

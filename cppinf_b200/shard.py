@@ -9,7 +9,10 @@ Every op on the path is row-independent, so ranks own disjoint row ranges and ex
   give unequal bytes; `causal_row_ranges` cuts the flattened rows where the cumulative algorithmic bytes reach
   rank / world of the total.
 
-The functions are pure host arithmetic; bench.py and the multi-rank tests (gloo on CPU) use them.
+`copy_back` is the one data movement between ranks: every rank's output rows land in one buffer on rank 0 by
+point-to-point transfers (NVLink peer traffic under NCCL, TCP under gloo). bench.py (`--gpus N`) partitions one global
+batch with these functions and times the ops with and without the copy-back; tests/test_sharding.py runs the same
+partition and copy-back on world-size-2 gloo ranks on the CPU.
 """
 
 from __future__ import annotations
@@ -99,3 +102,48 @@ def owner_of(row: int, ranges: list[tuple[int, int]]) -> int:
     if r < 0 or not (ranges[r][0] <= row < ranges[r][1]):
         raise IndexError(f"row {row} is outside the partition")
     return r
+
+
+@dataclass(frozen=True)
+class SoftmaxPiece:
+    """A run of consecutive rows of one [Q, K] score matrix: rows [query_start, query_start + rows) of `matrix`."""
+
+    matrix: int
+    query_start: int
+    rows: int
+
+
+def softmax_pieces(rng: tuple[int, int], query_len: int) -> list[SoftmaxPiece]:
+    """Splits a range of flattened [matrices * query_len] rows at matrix boundaries; each piece is one launch of the
+    position-aware causal softmax (query offset = query_start), whole matrices are pieces with query_start 0."""
+    start, end = rng
+    out = []
+    row = start
+    while row < end:
+        m, q = divmod(row, query_len)
+        n = min(end - row, query_len - q)
+        out.append(SoftmaxPiece(m, q, n))
+        row += n
+    return out
+
+
+def copy_back(local, dst, ranges: list[tuple[int, int]], rank: int, group=None) -> None:
+    """Gathers every rank's rows into `dst` on rank 0: rank r's `local` holds rows ranges[r] of the global tensor
+    (split along dim 0); rank 0 passes the global tensor as `dst` (others pass None). Rank 0 copies its own rows and
+    receives the others' directly into their rows of `dst` (one batch of concurrent point-to-point transfers, so
+    unequal shard sizes need no padding); the call returns once this rank's transfers are complete."""
+    import torch.distributed as dist
+
+    world = len(ranges)
+    if rank == 0:
+        s, e = ranges[0]
+        if e > s:
+            dst[s:e].copy_(local[: e - s])
+        ops = [dist.P2POp(dist.irecv, dst[ranges[r][0]:ranges[r][1]], r, group)
+               for r in range(1, world) if ranges[r][1] > ranges[r][0]]
+    else:
+        s, e = ranges[rank]
+        ops = [dist.P2POp(dist.isend, local[: e - s].contiguous(), 0, group)] if e > s else []
+    if ops:
+        for work in dist.batch_isend_irecv(ops):
+            work.wait()

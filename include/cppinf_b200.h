@@ -40,7 +40,7 @@ typedef enum cppinf_dtype {
 } cppinf_dtype;
 
 /* Status codes. The first three mirror the exception types the reference throws from the same checks
- * (src/common/checked.cpp:10-49, src/ops/nn_ops.cpp:54-64). */
+ * (src/common/checked.cpp:10-49, src/ops/nn_ops.cpp:30-40). */
 typedef enum cppinf_status {
     CPPINF_OK = 0,
     CPPINF_ERR_INVALID_ARGUMENT = -1, /* std::invalid_argument */
@@ -58,18 +58,28 @@ CPPINF_API const char* cppinf_status_name(int status);
 /* Number of kernel launches this library has issued from any thread since load (for launch accounting). */
 CPPINF_API uint64_t cppinf_launch_count(void);
 
+/* Failure detection (no counterpart in the reference, whose ops run on the CPU). The decoder's kernels that stage
+ * weights or cached rows by bulk copies wait on a shared-memory barrier for the copies to land; each such wait polls
+ * at most `polls` times (default 2^24, far longer than any copy takes) before the kernel gives up, sets the model's
+ * device error word (cppinf_qwen3_decode then returns CPPINF_ERR_CUDA) and, after a second wait with the default
+ * limit that lets its copies land, exits without using the data.
+ * The setting is process-wide and applies to kernels launched (or graphs captured) after the call; 0 makes every
+ * first wait give up at once, which is how the tests exercise the error path without a fault. Returns the previous
+ * limit. */
+CPPINF_API uint32_t cppinf_set_wait_poll_limit(uint32_t polls);
+
 /* ---------------------------------------------------------------------------------------------------------------
  * Elementwise ops.
  * ------------------------------------------------------------------------------------------------------------- */
 
-/* ops::add, src/ops/elementwise_ops.h:10 (impl src/ops/elementwise_ops.cpp:44-47 -> one_dnn_utils.cpp:125-149).
+/* ops::add, src/ops/elementwise_ops.h:10 (impl src/ops/elementwise_ops.cpp:28-31 -> one_dnn_utils.cpp:125-149).
  * out[i] = dtype(lhs[i] + rhs[i]) computed in f32, rounded to nearest-even for bf16. `out` may alias an input. */
 CPPINF_API int cppinf_add(cppinf_dtype dtype, const void* lhs, const void* rhs, void* out, int64_t count, void* stream);
 
-/* ops::mul, src/ops/elementwise_ops.h:14 (impl src/ops/elementwise_ops.cpp:49-52). Same rules as cppinf_add. */
+/* ops::mul, src/ops/elementwise_ops.h:14 (impl src/ops/elementwise_ops.cpp:33-36). Same rules as cppinf_add. */
 CPPINF_API int cppinf_mul(cppinf_dtype dtype, const void* lhs, const void* rhs, void* out, int64_t count, void* stream);
 
-/* ops::silu, src/ops/nn_ops.h:9 (impl src/ops/nn_ops.cpp:68-72, oneDNN eltwise_swish with alpha 1).
+/* ops::silu, src/ops/nn_ops.h:9 (impl src/ops/nn_ops.cpp:44-48, oneDNN eltwise_swish with alpha 1).
  * y[i] = dtype(x[i] / (1 + exp(-x[i]))). `y` may alias `x`. */
 CPPINF_API int cppinf_silu(cppinf_dtype dtype, const void* x, void* y, int64_t count, void* stream);
 
@@ -92,7 +102,7 @@ CPPINF_API int cppinf_strided_copy(cppinf_dtype dtype, const void* x, int64_t ra
  * Row reductions.
  * ------------------------------------------------------------------------------------------------------------- */
 
-/* ops::rms_norm, src/ops/nn_ops.h:22 (impl src/ops/nn_ops.cpp:164-225) over rows of `width` elements.
+/* ops::rms_norm, src/ops/nn_ops.h:22 (impl src/ops/nn_ops.cpp:140-201) over rows of `width` elements.
  * y[r, i] = dtype((x[r, i] * (1 / sqrt(mean_i(x[r, i]^2) + eps))) * w[i]), all in f32.
  * Row r of x starts at x + r * x_row_stride; y is dense [rows, width]. Requires eps >= 0. */
 CPPINF_API int cppinf_rms_norm(cppinf_dtype dtype, const void* x, int64_t x_row_stride, const void* weight, void* y,
@@ -104,11 +114,11 @@ CPPINF_API int cppinf_rms_norm(cppinf_dtype dtype, const void* x, int64_t x_row_
 CPPINF_API int cppinf_add_rms_norm(cppinf_dtype dtype, const void* a, const void* b, const void* weight, void* sum, void* y,
                         int64_t rows, int64_t width, float eps, void* stream);
 
-/* ops::softmax_last_dim, src/ops/nn_ops.h:13 (impl src/ops/nn_ops.cpp:74-99, oneDNN softmax_accurate).
+/* ops::softmax_last_dim, src/ops/nn_ops.h:13 (impl src/ops/nn_ops.cpp:50-75, oneDNN softmax_accurate).
  * Computed in f32, result rounded to `dtype`. x and y are dense [rows, width]. */
 CPPINF_API int cppinf_softmax_last_dim(cppinf_dtype dtype, const void* x, void* y, int64_t rows, int64_t width, void* stream);
 
-/* ops::scaled_causal_softmax_last_dim, src/ops/nn_ops.h:17 (impl src/ops/nn_ops.cpp:101-162).
+/* ops::scaled_causal_softmax_last_dim, src/ops/nn_ops.h:17 (impl src/ops/nn_ops.cpp:77-138).
  * x, y f32 dense [matrices, query_len, key_len] with query_len == key_len as the reference requires.
  * For row q: keys k <= q are visible, y = exp(x*scale - max) / sum over them, masked keys are written as 0. */
 CPPINF_API int cppinf_scaled_causal_softmax_f32(const float* x, float* y, int64_t matrices, int64_t query_len, int64_t key_len,
@@ -136,13 +146,13 @@ CPPINF_API int cppinf_row_argmax(cppinf_dtype dtype, const void* x, int64_t rows
  * ------------------------------------------------------------------------------------------------------------- */
 
 /* Host function: fills the HOST buffer `table` ([positions][head_dim] f32) with the split-half RoPE angles of
- * src/nn/rope.cpp:85-103: for pair i < head_dim/2 at position p,
+ * src/nn/rope.cpp:70-74, 84-88: for pair i < head_dim/2 at position p,
  *   inv_freq[i] = powf(base, -(float)i / (float)(head_dim/2)), angle = (float)p * inv_freq[i],
  *   table[p][i] = cosf(angle), table[p][head_dim/2 + i] = sinf(angle).
  * The same libm calls the reference makes, so device results match it bit for bit. */
 CPPINF_API int cppinf_rope_table(float base, int64_t head_dim, int64_t positions, float* table);
 
-/* nn::apply_rope, src/nn/rope.h:12 (impl src/nn/rope.cpp:73-124) on a rank-3 view [dim0, dim1, head_dim] with
+/* nn::apply_rope, src/nn/rope.h:12 (impl src/nn/rope.cpp:58-109) on a rank-3 view [dim0, dim1, head_dim] with
  * element strides (s0, s1, s2), sequence axis `seq_dim` (0 or 1), positions starting at `position_offset`.
  * `table` is a DEVICE copy of cppinf_rope_table(base, head_dim, >= position_offset + seq_len).
  * f32 math, result rounded to dtype; y is dense. */
@@ -200,6 +210,17 @@ CPPINF_API int cppinf_linear_residual(const void* x, int64_t x_row_stride, const
  * (gate_proj, up_proj, ops::silu, ops::mul), fused. gate and up are [out, in]. */
 CPPINF_API int cppinf_linear_silu_mul(const void* x, int64_t x_row_stride, const void* gate, const void* up, void* y,
                                       int64_t rows, int64_t in_features, int64_t out_features, void* stream);
+
+/* The three projections above on the tensor cores (tcgen05.mma, TMA-staged tiles, f32 accumulation in tensor memory):
+ * epilogue 0 = cppinf_linear (w1, residual unused), 1 = cppinf_linear_residual (y may alias residual),
+ * 2 = cppinf_linear_silu_mul (w0 = gate, w1 = up). Opt-in: the accumulation order inside the tensor cores is not
+ * the library's restated order, so results agree with cppinf_linear* to tolerance (a few bf16 ulps), not bit for
+ * bit. Needs out_features % 32 == 0, in_features and x_row_stride % 8 == 0 and 16-byte aligned operands
+ * (CPPINF_ERR_UNSUPPORTED otherwise). `error` (device, may be NULL) is set to 1 when a wait of the kernel ran out of
+ * its poll limit (cppinf_set_wait_poll_limit). */
+CPPINF_API int cppinf_linear_tc(int epilogue, const void* x, int64_t x_row_stride, const void* w0, const void* w1,
+                                const void* residual, void* y, int64_t rows, int64_t in_features,
+                                int64_t out_features, unsigned int* error, void* stream);
 
 /* Greedy token of one logits row computed on the fly: out_token (DEVICE int64) = argmax over n of
  * bf16(x * weight[n]^T), the LM head of src/models/qwen3/qwen3_model.cpp:306-311 followed by
@@ -292,10 +313,12 @@ CPPINF_API int cppinf_qwen3_forward(cppinf_qwen3* model, const int64_t* token_id
 /* Greedy decoding from the cached state: `steps` decode steps, each feeding the previous greedy token (the last
  * cppinf_qwen3_forward's, then each step's own). Writes the `steps` generated tokens to the HOST array `tokens` and
  * synchronises `stream`. One step is a captured CUDA graph of the whole decoder (the device-side sequence length
- * selects the cache row, the rotary position and the input token). */
+ * selects the cache row, the rotary position and the input token). Returns CPPINF_ERR_CUDA when a device wait ran
+ * out of its poll limit (cppinf_set_wait_poll_limit); the model then refuses forward/decode until
+ * cppinf_qwen3_reset. The step graph is captured again when the poll limit has changed since its capture. */
 CPPINF_API int cppinf_qwen3_decode(cppinf_qwen3* model, int64_t steps, int64_t* tokens, void* stream);
 
-/* Forgets the cached sequence (a fresh make_cache). */
+/* Forgets the cached sequence (a fresh make_cache) and clears a device error reported by cppinf_qwen3_decode. */
 CPPINF_API int cppinf_qwen3_reset(cppinf_qwen3* model, void* stream);
 
 /* Number of cached tokens. */

@@ -82,7 +82,7 @@ void oracle_cast(int src_dtype, const void* x, int dst_dtype, void* y, int64_t n
     }
 }
 
-/* ops::add / ops::mul, src/ops/elementwise_ops.cpp:44-52 -> binary_with_one_dnn, src/ops/one_dnn_utils.cpp:125-149:
+/* ops::add / ops::mul, src/ops/elementwise_ops.cpp:28-36 -> binary_with_one_dnn, src/ops/one_dnn_utils.cpp:125-149:
  * inputs already in the output dtype, f32 arithmetic, result stored in the output dtype. */
 void oracle_add(int dtype, const void* a, const void* b, void* out, int64_t n) {
 #pragma omp parallel for schedule(static)
@@ -98,7 +98,7 @@ void oracle_mul(int dtype, const void* a, const void* b, void* out, int64_t n) {
     }
 }
 
-/* ops::silu, src/ops/nn_ops.cpp:68-72: oneDNN eltwise_swish with alpha = 1, x / (1 + exp(-x)). */
+/* ops::silu, src/ops/nn_ops.cpp:44-48: oneDNN eltwise_swish with alpha = 1, x / (1 + exp(-x)). */
 static inline float silu_f32(float x) {
     return x / (1.0f + expf(-x));
 }
@@ -171,7 +171,7 @@ static float row_sum_squares(int dtype, const void* x, int64_t base, int64_t wid
     return partial[0];
 }
 
-/* ops::rms_norm, src/ops/nn_ops.cpp:164-225, per row of `width` elements:
+/* ops::rms_norm, src/ops/nn_ops.cpp:140-201, per row of `width` elements:
  * mean = sum(x^2) / width (reduction_mean), var = mean + eps, rms = sqrt(var), inv = 1 / rms, n = x * inv,
  * r = n * w, stored in the input dtype. Row r of x starts at r * x_row_stride; y is dense. */
 void oracle_rms_norm(int dtype, const void* x, int64_t x_row_stride, const void* w, void* y, int64_t rows,
@@ -198,7 +198,7 @@ void oracle_add_rms_norm(int dtype, const void* a, const void* b, const void* w,
     oracle_rms_norm(dtype, sum, width, w, y, rows, width, eps, chunk);
 }
 
-/* ops::softmax_last_dim, src/ops/nn_ops.cpp:74-99 (oneDNN softmax_accurate in the input dtype, computed in f32):
+/* ops::softmax_last_dim, src/ops/nn_ops.cpp:50-75 (oneDNN softmax_accurate in the input dtype, computed in f32):
  * y = exp(x - max) / sum. oneDNN's summation order is unspecified; the oracle sums the f32 exponentials in double
  * and rounds once, the order-free value every f32 order approximates. */
 void oracle_softmax_last_dim(int dtype, const void* x, void* y, int64_t rows, int64_t width) {
@@ -221,7 +221,7 @@ void oracle_softmax_last_dim(int dtype, const void* x, void* y, int64_t rows, in
     }
 }
 
-/* ops::scaled_causal_softmax_last_dim, src/ops/nn_ops.cpp:133-159, f32 [matrices, Q, K]. */
+/* ops::scaled_causal_softmax_last_dim, src/ops/nn_ops.cpp:77-138, f32 [matrices, Q, K]. */
 void oracle_scaled_causal_softmax(const float* x, float* y, int64_t matrices, int64_t query_len, int64_t key_len,
                                   float scale) {
 #pragma omp parallel for schedule(dynamic, 16)
@@ -282,7 +282,7 @@ void oracle_position_causal_softmax(const float* x, float* y, int64_t batch, int
     }
 }
 
-/* Angles of src/nn/rope.cpp:85-103 laid out [positions][head_dim]: cos in [0, D/2), sin in [D/2, D). */
+/* Angles of src/nn/rope.cpp:70-74, 84-88 laid out [positions][head_dim]: cos in [0, D/2), sin in [D/2, D). */
 void oracle_rope_table(float base, int64_t head_dim, int64_t positions, float* table) {
     const int64_t half = head_dim / 2;
     for (int64_t p = 0; p < positions; ++p) {
@@ -295,7 +295,7 @@ void oracle_rope_table(float base, int64_t head_dim, int64_t positions, float* t
     }
 }
 
-/* nn::apply_rope, src/nn/rope.cpp:73-124: rank-3 view [d0, d1, D] with element strides, sequence axis seq_dim,
+/* nn::apply_rope, src/nn/rope.cpp:58-109: rank-3 view [d0, d1, D] with element strides, sequence axis seq_dim,
  * positions from `offset`. f32 math, result stored in the input dtype (dense). */
 void oracle_rope(int dtype, const void* x, int64_t d0, int64_t d1, int64_t head_dim, int64_t s0, int64_t s1,
                  int64_t s2, int64_t seq_dim, int64_t offset, float base, void* y) {

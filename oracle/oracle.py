@@ -419,3 +419,16 @@ class Reference:
 
 def reference_available() -> bool:
     return REFERENCE_LIB.exists()
+
+
+def reference_tree() -> Path | None:
+    """The reference's source tree, when it is on this machine: $CPPINF_REFERENCE_DIR, else the directory that
+    oracle/Makefile compiled oracle/_ref from (recorded in oracle/_ref/reference_dir.txt). None when neither exists."""
+    candidates = [os.environ.get("CPPINF_REFERENCE_DIR")]
+    recorded = ORACLE_DIR / "_ref" / "reference_dir.txt"
+    if recorded.exists():
+        candidates.append(recorded.read_text().strip())
+    for c in candidates:
+        if c and (Path(c) / "src").is_dir():
+            return Path(c)
+    return None

@@ -93,7 +93,7 @@ void ref_f32_to_bf16(const float* x, uint16_t* y, int64_t n) {
     }
 }
 
-// ops::scaled_causal_softmax_last_dim, src/ops/nn_ops.cpp:101-162
+// ops::scaled_causal_softmax_last_dim, src/ops/nn_ops.cpp:77-138
 int ref_scaled_causal_softmax(const float* x, float* y, int64_t matrices, int64_t query_len, int64_t key_len,
                               float scale) {
     return guarded([&] {
@@ -115,7 +115,7 @@ int ref_position_causal_softmax(const float* x, float* y, int64_t batch, int64_t
     });
 }
 
-// nn::apply_rope, src/nn/rope.cpp:73-124, on a dense [d0, d1, head_dim] tensor.
+// nn::apply_rope, src/nn/rope.cpp:58-109, on a dense [d0, d1, head_dim] tensor.
 int ref_apply_rope(int dtype, const void* x, int64_t d0, int64_t d1, int64_t head_dim, int64_t offset, float base,
                    int64_t seq_dim, void* y) {
     return guarded([&] {
@@ -136,7 +136,7 @@ int ref_apply_rope_batched(int dtype, const void* x, int64_t batch, int64_t seq,
     });
 }
 
-// ops::add / ops::mul, src/ops/elementwise_ops.cpp:44-52
+// ops::add / ops::mul, src/ops/elementwise_ops.cpp:28-36
 int ref_add(int dtype, const void* a, const void* b, void* out, int64_t n) {
     return guarded([&] {
         const auto ta = make_input(dtype, {n}, a);
@@ -153,7 +153,7 @@ int ref_mul(int dtype, const void* a, const void* b, void* out, int64_t n) {
     });
 }
 
-// ops::silu, src/ops/nn_ops.cpp:68-72
+// ops::silu, src/ops/nn_ops.cpp:44-48
 int ref_silu(int dtype, const void* x, void* y, int64_t n) {
     return guarded([&] {
         const auto t = make_input(dtype, {n}, x);
@@ -179,7 +179,7 @@ int ref_cast(int src_dtype, const void* x, int dst_dtype, void* y, int64_t n) {
     });
 }
 
-// ops::rms_norm, src/ops/nn_ops.cpp:164-225. Needs oneDNN's reduction primitive: returns -6 here.
+// ops::rms_norm, src/ops/nn_ops.cpp:140-201. Needs oneDNN's reduction primitive: returns -6 here.
 int ref_rms_norm(int dtype, const void* x, const void* w, void* y, int64_t rows, int64_t width, float eps) {
     return guarded([&] {
         const auto tx = make_input(dtype, {rows, width}, x);

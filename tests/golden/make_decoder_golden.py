@@ -130,6 +130,12 @@ def make_hf_small() -> None:
 
 
 if __name__ == "__main__":
-    reference = Path(sys.argv[1]) if len(sys.argv) > 1 else Path("/root/reference")
+    # The reference tree: the first argument, else $CPPINF_REFERENCE_DIR, else where oracle/Makefile compiled it from.
+    sys.path.insert(0, str(HERE.parent.parent))
+    from oracle.oracle import reference_tree
+
+    reference = Path(sys.argv[1]) if len(sys.argv) > 1 else reference_tree()
+    if reference is None:
+        sys.exit("usage: make_decoder_golden.py <reference tree> (or set CPPINF_REFERENCE_DIR)")
     make_tiny(reference)
     make_hf_small()

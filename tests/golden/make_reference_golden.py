@@ -1,9 +1,9 @@
 """Generates tests/golden/ref_*.npz: golden vectors produced by the reference's OWN op code, compiled in place from
 the reference sources into oracle/_ref/libcppinf_ref.so (see oracle/Makefile), on seeded inputs:
 
-- ops::scaled_causal_softmax_last_dim          (src/ops/nn_ops.cpp:101-162)
+- ops::scaled_causal_softmax_last_dim          (src/ops/nn_ops.cpp:77-138)
 - scaled_position_causal_softmax_last_dim      (src/nn/qwen_attention.cpp:164-235), ragged offsets/lengths
-- nn::apply_rope, bf16 and f32, seq dim 0 and 1 (src/nn/rope.cpp:73-124)
+- nn::apply_rope, bf16 and f32, seq dim 0 and 1 (src/nn/rope.cpp:58-109)
 - apply_rope_batched                           (src/nn/qwen_attention.cpp:136-162)
 - ops::add / ops::mul / ops::cast              (src/ops/elementwise_ops.cpp, src/ops/tensor_ops.cpp)
 - ops::silu then ops::mul                      (src/nn/qwen_mlp.cpp:65-66)

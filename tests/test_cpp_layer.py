@@ -9,11 +9,15 @@ from pathlib import Path
 
 import pytest
 
-BINARY = Path(__file__).resolve().parent.parent / "cppinf_b200" / "_lib" / "cppinf_ops_tests"
+PACKAGE = Path(__file__).resolve().parent.parent / "cppinf_b200"
+BINARY = PACKAGE / "_lib" / "cppinf_ops_tests"
 
 
 def _run(*args: str) -> subprocess.CompletedProcess:
-    assert BINARY.exists(), f"{BINARY} not built (make -C cppinf_b200)"
+    # The binary is a build output (not in the repository): make brings it up to date with its sources first.
+    build = subprocess.run(["make", "-C", str(PACKAGE), "_lib/cppinf_ops_tests"], capture_output=True, text=True,
+                           timeout=900)
+    assert build.returncode == 0 and BINARY.exists(), f"building {BINARY} failed:\n{build.stdout}{build.stderr}"
     return subprocess.run([str(BINARY), *args], capture_output=True, text=True, timeout=600)
 
 

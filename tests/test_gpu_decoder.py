@@ -360,3 +360,30 @@ def test_load_safetensors_matches_set_weight(cuda, tmp_path):
     write_safetensors(tmp_path / "wrong.safetensors", wrong)
     with pytest.raises(ValueError):
         Qwen3Model(cfg, 64).load_safetensors(tmp_path / "wrong.safetensors")
+
+
+@pytest.mark.parametrize("name,make,message", [
+    # q_proj is [q_dim, hidden] = [512, 256]; its transpose has the same byte count
+    ("model.layers.0.self_attn.q_proj.weight", lambda a: np.ascontiguousarray(a.T), "has an unexpected shape"),
+    # gate_proj [512, 256] stored as [256, 512] (a swapped layout)
+    ("model.layers.1.mlp.gate_proj.weight", lambda a: a.reshape(256, 512), "has an unexpected shape"),
+    ("model.layers.0.self_attn.o_proj.weight", lambda a: a.reshape(-1), "must be rank-2"),
+    ("model.norm.weight", lambda a: a.reshape(16, 16), "requires a rank-1 weight tensor"),
+])
+def test_load_safetensors_rejects_wrong_shapes_with_same_bytes(cuda, tmp_path, name, make, message):
+    # validate_projection_weight (src/nn/qwen_common.cpp:38-49) and ops::rms_norm's weight checks
+    # (src/ops/nn_ops.cpp:150-159): a tensor with the right byte count but the wrong shape is rejected.
+    from cppinf_b200.qwen3 import Qwen3Model, random_weights, write_safetensors
+
+    cfg = small_config()
+    w = random_weights(cfg, seed=22, std=0.05)
+    bad = dict(w)
+    bad[name] = make(w[name])
+    assert bad[name].nbytes == w[name].nbytes
+    write_safetensors(tmp_path / "bad.safetensors", bad)
+    model = Qwen3Model(cfg, 64)
+    try:
+        with pytest.raises(ValueError, match=message):
+            model.load_safetensors(tmp_path / "bad.safetensors")
+    finally:
+        model.close()

@@ -306,6 +306,32 @@ def test_silu_mul_faithful(ops, oracle, n, dtype):
         np.testing.assert_allclose(got, out, rtol=1e-6, atol=1e-30)
 
 
+def test_silu_mul_full_configuration(ops, oracle):
+    # The SiLU(gate) * up configuration at its full size: gate, up bf16 [4096, 3072] ~N(0, 1), as a row-shaped call
+    # (src/nn/qwen_mlp.cpp:65-66). Faithful everywhere; the share of elements equal to the oracle's primary candidate
+    # (libm expf, IEEE division) is asserted too.
+    rng = np.random.default_rng(4096 * 3072)
+    g = f32_to_bf16(rng.standard_normal((4096, 3072)).astype(np.float32))
+    u = f32_to_bf16(rng.standard_normal((4096, 3072)).astype(np.float32))
+    got = to_host(ops.silu_mul(to_dev(g), to_dev(u)))
+    out, alt = oracle.silu_mul(g, u, with_alternative=True)
+    assert got.shape == (4096, 3072)
+    assert ((got == out) | (got == alt)).all()
+    assert (got == out).mean() > 0.9999
+
+
+def test_silu_mul_bench_tensors_equal_primary_candidate(ops, oracle):
+    # The exact tensors bench.py times for this configuration (seeded torch generator on the device, first buffer
+    # set): every element equals the oracle's primary candidate.
+    gen = torch.Generator(device="cuda").manual_seed(1000)
+    g = torch.randn((4096, 3072), generator=gen, device="cuda").to(torch.bfloat16)
+    u = torch.randn((4096, 3072), generator=gen, device="cuda").to(torch.bfloat16)
+    got = to_host(ops.silu_mul(g, u))
+    out, alt = oracle.silu_mul(to_host(g), to_host(u), with_alternative=True)
+    assert ((got == out) | (got == alt)).all()
+    assert (got == out).all(), f"{int((got != out).sum())} elements took the other faithful candidate"
+
+
 @pytest.mark.parametrize("dtype", ["bf16", "f32"])
 def test_silu_extreme_inputs(ops, oracle, dtype):
     # 1 + exp(-x) reaches 2^126 and beyond for x < -87.3 (the quotient is a tiny normal number there), overflows to
@@ -379,7 +405,9 @@ def test_row_argmax_fixture_with_ties_nans_and_signed_zeros(ops, golden):
     assert np.array_equal(to_host(ops.row_argmax(to_dev(g["x"]))), g["index"])
 
 
-@pytest.mark.parametrize("rows,cols", [(1, 1), (1, 151936), (64, 151936), (3, 7), (5, 100003), (200, 4096)])
+# (2, 1000000) and (1, 1000003): slices longer than the shared-memory ring, so stages are refilled
+@pytest.mark.parametrize("rows,cols", [(1, 1), (1, 151936), (64, 151936), (3, 7), (5, 100003), (200, 4096),
+                                       (2, 1000000), (1, 1000003)])
 @pytest.mark.parametrize("dtype", ["bf16", "f32"])
 def test_row_argmax_bit_exact(ops, oracle, rows, cols, dtype):
     rng = np.random.default_rng(rows * cols)

@@ -76,9 +76,12 @@ def test_writer_round_trip(tmp_path):
 def test_reference_real_logits_file():
     # The reference's own safetensors asset (tests/models/qwen3/qwen3_real_model_oracle.py writes it): one bf16
     # tensor of the 151,936 last-token logits.
-    path = Path("/root/reference/tests/models/qwen3/qwen3_real_last_token_logits.safetensors")
-    if not path.exists():
+    from oracle.oracle import reference_tree
+
+    tree = reference_tree()
+    if tree is None:
         pytest.skip("reference tree not present")
+    path = tree / "tests/models/qwen3/qwen3_real_last_token_logits.safetensors"
     count, offset = capi.safetensors_info(path)
     assert count == 1
     assert path.stat().st_size - offset == 151936 * 2

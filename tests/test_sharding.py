@@ -13,7 +13,7 @@ import torch.distributed as dist
 import torch.multiprocessing as mp
 
 from cppinf_b200.shard import (causal_row_bytes, causal_row_ranges, owner_of, range_bytes, row_ranges,
-                               token_shard)
+                               softmax_pieces, token_shard)
 
 
 @pytest.mark.parametrize("rows,world", [(2048, 1), (2048, 2), (2048, 8), (7, 3), (0, 4), (3, 8)])
@@ -50,6 +50,17 @@ def test_causal_row_ranges_single_matrix_split_is_not_equal_count():
     assert owner_of(0, ranges) == 0 and owner_of(999, ranges) == 1
 
 
+@pytest.mark.parametrize("world", [1, 2, 3, 8])
+def test_softmax_pieces_tile_each_rank_range(world):
+    for rng_ in causal_row_ranges(5, 64, 64, world):
+        pieces = softmax_pieces(rng_, 64)
+        assert sum(p.rows for p in pieces) == rng_[1] - rng_[0]
+        row = rng_[0]
+        for p in pieces:
+            assert p.matrix * 64 + p.query_start == row and 0 < p.rows and p.query_start + p.rows <= 64
+            row += p.rows
+
+
 def _free_port() -> int:
     with socket.socket() as s:
         s.bind(("127.0.0.1", 0))
@@ -64,7 +75,7 @@ def _worker(rank: int, world: int, port: int, result_path: str) -> None:
     sys.path.insert(0, str(repo))
     import torch
 
-    from cppinf_b200.shard import causal_row_ranges, row_ranges, token_shard
+    from cppinf_b200.shard import causal_row_ranges, copy_back, row_ranges, softmax_pieces, token_shard
     from oracle.oracle import Oracle, f32_to_bf16
 
     os.environ["OMP_NUM_THREADS"] = "1"
@@ -79,28 +90,49 @@ def _worker(rank: int, world: int, port: int, result_path: str) -> None:
     w = f32_to_bf16((1 + 0.1 * rng.standard_normal(256)).astype(np.float32))
     scores = (rng.standard_normal((3, 40, 40)) * 2).astype(np.float32)
 
+    # q/k: token rows with global RoPE positions
+    q_ranges = row_ranges(64, world)
     shard = token_shard(64, world, rank, position_offset=7)
+    assert (shard.start, shard.end) == q_ranges[rank]
     q_out, k_out = oracle.qk_norm_rope(q[shard.start:shard.end], k[shard.start:shard.end], qw, kw, 1e-6,
                                        shard.position_offset, 1e6)
-    s0, e0 = row_ranges(50, world)[rank]
+    # RMSNorm: equal row counts
+    x_ranges = row_ranges(50, world)
+    s0, e0 = x_ranges[rank]
     y = oracle.rms_norm(x[s0:e0], w, 1e-6)
-    cs, ce = causal_row_ranges(3, 40, 40, world)[rank]
+    # causal softmax: byte-balanced rows, computed per piece of one matrix at its query offset
+    c_ranges = causal_row_ranges(3, 40, 40, world)
     flat = scores.reshape(-1, 40)
-    probs = np.zeros((ce - cs, 40), np.float32)
-    for i, row in enumerate(range(cs, ce)):  # each row is a 1-row position-aware problem at query position row % 40
-        probs[i] = oracle.position_causal_softmax(flat[row][None, None, None, :], 0.125, [row % 40], [1], [40])[0, 0, 0]
+    parts = []
+    for piece in softmax_pieces(c_ranges[rank], 40):
+        rows = scores[piece.matrix, piece.query_start:piece.query_start + piece.rows]
+        parts.append(oracle.position_causal_softmax(rows[None, None], 0.125, [piece.query_start], [piece.rows],
+                                                    [40])[0, 0])
+    probs = np.concatenate(parts) if parts else np.zeros((0, 40), np.float32)
+    assert probs.shape[0] == c_ranges[rank][1] - c_ranges[rank][0]
 
-    gathered = [None] * world
-    dist.all_gather_object(gathered, (q_out, k_out, y, probs))
+    # copy-back of every rank's rows into one buffer on rank 0 (bench.py does the same over NCCL)
+    def bits(a):
+        return torch.from_numpy(np.ascontiguousarray(a).view(np.int16) if a.dtype == np.uint16 else a)
+
+    out = {}
+    for name, local, ranges, shape, dtype in (("q", q_out, q_ranges, q.shape, torch.int16),
+                                              ("k", k_out, q_ranges, k.shape, torch.int16),
+                                              ("y", y, x_ranges, x.shape, torch.int16),
+                                              ("p", probs, c_ranges, flat.shape, torch.float32)):
+        dst = torch.zeros(shape, dtype=dtype) if rank == 0 else None
+        copy_back(bits(local), dst, ranges, rank)
+        out[name] = dst
     t = torch.tensor([float(rank + 1)], dtype=torch.float64)
     dist.all_reduce(t, op=dist.ReduceOp.MAX)  # the max-over-ranks timing reduction bench.py uses
     if rank == 0:
         full_q, full_k = oracle.qk_norm_rope(q, k, qw, kw, 1e-6, 7, 1e6)
-        ok = (np.array_equal(np.concatenate([g[0] for g in gathered]), full_q)
-              and np.array_equal(np.concatenate([g[1] for g in gathered]), full_k)
-              and np.array_equal(np.concatenate([g[2] for g in gathered]), oracle.rms_norm(x, w, 1e-6))
-              and np.array_equal(np.concatenate([g[3] for g in gathered]),
-                                 oracle.scaled_causal_softmax(scores, 0.125).reshape(-1, 40))
+
+        def same(t_, a):
+            return np.array_equal(t_.numpy().view(np.uint16) if t_.dtype == torch.int16 else t_.numpy(), a)
+
+        ok = (same(out["q"], full_q) and same(out["k"], full_k) and same(out["y"], oracle.rms_norm(x, w, 1e-6))
+              and same(out["p"], oracle.scaled_causal_softmax(scores, 0.125).reshape(-1, 40))
               and t.item() == float(world))
         Path(result_path).write_text("ok" if ok else "mismatch")
     dist.barrier()
