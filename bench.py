@@ -40,6 +40,7 @@ Qwen3Model.generate with host token ids. Across GPUs decode runs one independent
 from __future__ import annotations
 
 import argparse
+import ctypes
 import json
 import math
 import os
@@ -462,33 +463,130 @@ def time_e2e(wl_name: str, rank: int, device, steps: int) -> dict:
     return {"ms": ms, "steps": steps, "h2d_bytes_per_step": in_bytes, "d2h_bytes_per_step": in_bytes}
 
 
-def time_copy_back_steps(wl: Workload, steps: int, dsts: list, ranges: list, rank: int, stream, barrier) -> float:
-    """`steps` eager steps of the op followed by the copy-back of its outputs into `dsts` on rank 0
-    (shard.copy_back: point-to-point transfers over NCCL, i.e. NVLink peer traffic); CUDA events on `stream`, which
-    the transfers are ordered after and waited on by. Returns ms on this rank."""
-    import torch
+class PeerOutputs:
+    """Rank 0's global output buffers (cudaMalloc) mapped into every rank through CUDA IPC handles sent over the
+    process group, opened on the rank's own device with lazy peer access, so each rank's copy engine writes its
+    output rows straight into rank 0's HBM over NVLink (one cudaMemcpyAsync per output, capturable in a graph).
+    Rank 0 copies its own rows locally. `path` is "nvlink peer copy" or, when a rank could not map the buffers
+    (every rank learns of it), "nccl send/recv" through shard.copy_back."""
 
-    from cppinf_b200.shard import copy_back
+    class _Handle(ctypes.Structure):  # cudaIpcMemHandle_t
+        _fields_ = [("reserved", ctypes.c_char * 64)]
+
+    def __init__(self, shapes: list, rank: int, device):
+        import torch
+        import torch.distributed as dist
+
+        self.rank = rank
+        self.device = device
+        self.shapes = shapes
+        self.row_bytes = [math.prod(shape[1:]) * torch.empty((), dtype=dt).element_size() for shape, dt in shapes]
+        self.nbytes = [shape[0] * rb for (shape, _), rb in zip(shapes, self.row_bytes)]
+        rt = ctypes.CDLL("libcudart.so.12")
+        self._rt = rt
+        rt.cudaMemcpyAsync.argtypes = [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_size_t, ctypes.c_int, ctypes.c_void_p]
+        self.ptrs, self.owned, self.dsts = [], [], None
+        ok = 1
+        try:
+            torch.cuda.set_device(device)
+            handles = None
+            if rank == 0:
+                handles = []
+                for n in self.nbytes:
+                    p = ctypes.c_void_p()
+                    if rt.cudaMalloc(ctypes.byref(p), ctypes.c_size_t(n)) != 0:
+                        raise RuntimeError("cudaMalloc")
+                    self.owned.append(p.value)
+                    h = PeerOutputs._Handle()
+                    if rt.cudaIpcGetMemHandle(ctypes.byref(h), ctypes.c_void_p(p.value)) != 0:
+                        raise RuntimeError("cudaIpcGetMemHandle")
+                    handles.append(bytes(h.reserved))
+                self.ptrs = list(self.owned)
+            box = [handles]
+            dist.broadcast_object_list(box, src=0)
+            if rank != 0:
+                rt.cudaIpcOpenMemHandle.argtypes = [ctypes.POINTER(ctypes.c_void_p), PeerOutputs._Handle, ctypes.c_uint]
+                for raw in box[0]:
+                    h = PeerOutputs._Handle()
+                    h.reserved = raw
+                    p = ctypes.c_void_p()
+                    if rt.cudaIpcOpenMemHandle(ctypes.byref(p), h, 1) != 0:  # cudaIpcMemLazyEnablePeerAccess
+                        raise RuntimeError("cudaIpcOpenMemHandle")
+                    self.ptrs.append(p.value)
+        except Exception:
+            ok = 0
+        flag = torch.tensor([ok], dtype=torch.int32, device=device)
+        dist.all_reduce(flag, op=dist.ReduceOp.MIN)
+        self.path = "nvlink peer copy" if int(flag.item()) == 1 else "nccl send/recv"
+        if self.path != "nvlink peer copy":
+            self.dsts = [torch.empty(shape, dtype=dt, device=device) if rank == 0 else None for shape, dt in shapes]
+
+    def copy(self, outputs: list, ranges: list, stream) -> None:
+        s, e = ranges[self.rank]
+        if e <= s:
+            return
+        if self.dsts is not None:
+            from cppinf_b200.shard import copy_back
+
+            for out, dst in zip(outputs, self.dsts):
+                copy_back(out, dst, ranges, self.rank)
+            return
+        for out, ptr, rb in zip(outputs, self.ptrs, self.row_bytes):
+            status = self._rt.cudaMemcpyAsync(ptr + s * rb, out.data_ptr(), (e - s) * rb, 4, stream.cuda_stream)
+            if status != 0:
+                raise RuntimeError(f"cudaMemcpyAsync (peer copy-back) failed with {status}")
+
+    def close(self) -> None:
+        """Unmaps the peers' views, then (after every rank has) frees rank 0's buffers."""
+        import torch
+        import torch.distributed as dist
+
+        torch.cuda.synchronize()
+        if self.rank != 0:
+            for p in self.ptrs:
+                self._rt.cudaIpcCloseMemHandle(ctypes.c_void_p(p))
+        dist.barrier()
+        for p in self.owned:
+            self._rt.cudaFree(ctypes.c_void_p(p))
+
+
+def time_copy_back_steps(wl: Workload, steps: int, peer: PeerOutputs, ranges: list, stream, barrier) -> float:
+    """`steps` steps of the op each followed by the copy of this rank's output rows into rank 0's buffers, timed with
+    CUDA events on `stream`. Peer copies are captured with the kernels in one CUDA graph; the NCCL fallback runs
+    eagerly. Returns ms on this rank: the time until its rows have landed in rank 0's HBM."""
+    import torch
 
     def step(i):
         wl.launch(i, stream.cuda_stream)
-        for out, dst in zip(wl.outputs(i), dsts):
-            copy_back(out, dst, ranges, rank)
+        peer.copy(wl.outputs(i), ranges, stream)
 
     with torch.cuda.stream(stream):
         for i in range(3):
             step(i)
     torch.cuda.synchronize()
+    g = None
+    if peer.dsts is None:
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g, stream=stream):
+            for i in range(steps):
+                step(i)
+        with torch.cuda.stream(stream):
+            g.replay()  # untimed: uploads the graph
+        torch.cuda.synchronize()
     start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     barrier()
     torch.cuda.synchronize()
     with torch.cuda.stream(stream):
         start.record(stream)
-        for i in range(steps):
-            step(i)
+        if g is not None:
+            g.replay()
+        else:
+            for i in range(steps):
+                step(i)
         end.record(stream)
     torch.cuda.synchronize()
     barrier()
+    del g
     return start.elapsed_time(end)
 
 
@@ -503,8 +601,9 @@ def sharded_legs(world: int, rank: int, device, stream, barrier, max_over_ranks,
     row_argmax           the [64, 151936] configuration split into N row ranges
 
     Aggregate GB/s = the algorithmic bytes of the global batch / the max over ranks of the time; `frac` is that over
-    N x the measured peak. The copy-back moves the outputs (shard bytes `copy_bytes_per_step` in total, less rank 0's
-    own rows, which it copies locally) into rank 0's HBM."""
+    N x the measured peak. The copy-back moves the outputs (`copy_bytes_per_step` in total; rank 0's own rows are a
+    local copy) into one set of buffers in rank 0's HBM by peer copies (PeerOutputs), captured with the kernels in
+    one CUDA graph per measurement."""
     import torch
 
     from cppinf_b200.shard import causal_row_ranges, range_bytes, row_ranges, token_shard
@@ -539,9 +638,9 @@ def sharded_legs(world: int, rank: int, device, stream, barrier, max_over_ranks,
         ms, _, _ = time_device_steps(wl, steps, 3, stream, barrier)
         ms = max_over_ranks(ms)
         gbs = total * steps / (ms * 1e-3) / 1e9
-        dsts = [torch.empty(shape, dtype=dt, device=device) if rank == 0 else None for shape, dt in shapes]
+        peer = PeerOutputs(shapes, rank, device)
         copy_bytes = sum(math.prod(shape) * torch.empty((), dtype=dt).element_size() for shape, dt in shapes)
-        cms = max_over_ranks(time_copy_back_steps(wl, copy_steps, dsts, ranges, rank, stream, barrier))
+        cms = max_over_ranks(time_copy_back_steps(wl, copy_steps, peer, ranges, stream, barrier))
         cgbs = total * copy_steps / (cms * 1e-3) / 1e9
         legs[label] = {
             "workload": desc, "bytes_per_step": total,
@@ -549,9 +648,10 @@ def sharded_legs(world: int, rank: int, device, stream, barrier, max_over_ranks,
                         "frac_of_n_peak": round(gbs / (world * peak), 4), "steps": steps},
             "with_copy_back": {"us_per_step": round(cms / copy_steps * 1e3, 3), "gbs": round(cgbs, 1),
                                "frac_of_n_peak": round(cgbs / (world * peak), 4), "steps": copy_steps,
-                               "copy_bytes_per_step": copy_bytes},
+                               "copy_bytes_per_step": copy_bytes, "path": peer.path},
         }
-        del wl, dsts
+        peer.close()
+        del wl, peer
         torch.cuda.empty_cache()
     return legs
 
@@ -703,9 +803,24 @@ def measure_decode(device, runs: int) -> dict:
     again = model.generate(prompt, DECODE_NEW)
     torch.cuda.synchronize(device)
     e2e_s = time.perf_counter() - t0
+    # The same prefill with the prompt projections on the tensor cores (opt-in, tolerance parity).
+    model.set_prefill("tensor_cores")
+    tc_ms = []
+    for i in range(runs + 1):
+        model.reset()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        torch.cuda.synchronize(device)
+        e0.record(stream)
+        tc_first, _ = model.forward_cached(prompt, logits=None)
+        e1.record(stream)
+        torch.cuda.synchronize(device)
+        if i > 0:  # the first run is a warm-up
+            tc_ms.append(e0.elapsed_time(e1))
+    model.set_prefill("cuda_cores")
     model.close()
     dec = statistics.median(decode_ms)
     return {"decode_ms": dec, "prefill_ms": statistics.median(prefill_ms), "e2e_s": e2e_s,
+            "prefill_tc_ms": statistics.median(tc_ms), "prefill_tc_first_token_same": tc_first == tokens[0],
             "launches_per_run": launches, "step_launches": 5 * cfg.num_hidden_layers + 1, "tokens": tokens,
             "deterministic": again == tokens, "cfg": cfg}
 
@@ -916,6 +1031,11 @@ def run_ours(args) -> None:
         decode = {
             "metric": "random-init Qwen3-0.6B greedy decode tok/s", "value": round(tok_s, 1), "unit": "tok/s",
             "ms_per_token": round(dec_ms / steps, 4), "prefill_ms": round(max_over_ranks(d["prefill_ms"]), 2),
+            "prefill_tensor_cores": {
+                "ms": round(max_over_ranks(d["prefill_tc_ms"]), 3),
+                "first_token_same": d["prefill_tc_first_token_same"],
+                "how": "Qwen3Model.set_prefill('tensor_cores'): the prompt projections on tcgen05 (tolerance parity); "
+                       "prefill_ms above is the default bit-exact CUDA-core path"},
             "config": {"model": "Qwen3-0.6B, random init N(0,0.02) bf16, unit norm weights, tied embeddings",
                        "prompt_tokens": DECODE_PROMPT, "generated_tokens": DECODE_NEW, "batch": 1,
                        "parallelism": f"{world} independent replica(s), one per GPU (decode does not shard)"},

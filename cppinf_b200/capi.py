@@ -94,6 +94,7 @@ _SIGNATURES = {
     "cppinf_qwen3_load_safetensors": [_ptr, ctypes.c_char_p, ctypes.POINTER(_i64)],
     "cppinf_safetensors_info": [ctypes.c_char_p, ctypes.POINTER(_i64), ctypes.POINTER(_i64)],
     "cppinf_qwen3_reset": [_ptr, _ptr],
+    "cppinf_qwen3_set_prefill": [_ptr, _int],
     "cppinf_qwen3_length": [_ptr],
     "cppinf_qwen3_step_launches": [_ptr],
 }

@@ -87,6 +87,7 @@ struct cppinf_qwen3 {
     cudaGraphExec_t step = nullptr;
     int64_t step_launches = 0;
     uint32_t step_poll_limit = 0;  // the wait poll limit the decode-step graph was captured with
+    int prefill_mode = 0;          // 0: CUDA-core projections (restated order), 1: tensor cores (tolerance parity)
     bool failed = false;           // a decode step reported a device error; cleared by cppinf_qwen3_reset
 };
 
@@ -213,6 +214,18 @@ int enqueue_step(cppinf_qwen3* m, cudaStream_t s, int64_t* launches) {
     return CPPINF_OK;
 }
 
+// A prompt-row projection: on the tensor cores when the model asks for them and the layout allows it, otherwise the
+// CUDA-core kernel with the restated order.
+cudaError_t launch_rows(const cppinf_qwen3* m, LinearParams p, cudaStream_t s) {
+    if (m->prefill_mode == 1) {
+        p.error = m->d_error;
+        if (cppinf::device::linear_tc_supported(p)) {
+            return cppinf::device::launch_linear_tc(p, s);
+        }
+    }
+    return cppinf::device::launch_linear_rows(p, s);
+}
+
 // Prompt rows [pos0, pos0 + T) whose ids are already in d_tokens; writes logits of all rows to `logits` when set.
 int enqueue_chunk(cppinf_qwen3* m, int64_t pos0, int64_t T, bf16* logits, cudaStream_t s) {
     const auto& c = m->c;
@@ -223,7 +236,7 @@ int enqueue_chunk(cppinf_qwen3* m, int64_t pos0, int64_t T, bf16* logits, cudaSt
         QWEN3_CHECK(cppinf_rms_norm(CPPINF_DTYPE_BF16, m->h, H, l.in_norm, m->xn, T, H, c.rms_norm_eps, s));
         LinearParams qkv = params_for(LinearEpilogue::kStore, m->xn, H, l.wqkv, nullptr, T, m->qkv_rows, H);
         set_qkv_outputs(m, l, qkv, pos0, nullptr);
-        QWEN3_TRY(cppinf::device::launch_linear_rows(qkv, s), "qwen3_qkv_rows");
+        QWEN3_TRY(launch_rows(m, qkv, s), "qwen3_qkv_rows");
         QWEN3_CHECK(cppinf_qk_norm_rope(CPPINF_DTYPE_BF16, m->q, m->k, l.q_norm, l.k_norm, m->qr,
                                         l.k_cache + pos0 * m->kv_dim, T, c.num_attention_heads,
                                         c.num_key_value_heads, c.head_dim, pos0, c.rms_norm_eps, m->rope, m->cap, s));
@@ -234,26 +247,26 @@ int enqueue_chunk(cppinf_qwen3* m, int64_t pos0, int64_t T, bf16* logits, cudaSt
         o.res_ld = H;
         o.out[0] = m->h;
         o.ld[0] = H;
-        QWEN3_TRY(cppinf::device::launch_linear_rows(o, s), "qwen3_o_proj_rows");
+        QWEN3_TRY(launch_rows(m, o, s), "qwen3_o_proj_rows");
         QWEN3_CHECK(cppinf_rms_norm(CPPINF_DTYPE_BF16, m->h, H, l.post_norm, m->xn, T, H, c.rms_norm_eps, s));
         LinearParams gu = params_for(LinearEpilogue::kSiluMul, m->xn, H, l.wg, l.wu, T, c.intermediate_size, H);
         gu.out[0] = m->act;
         gu.ld[0] = c.intermediate_size;
-        QWEN3_TRY(cppinf::device::launch_linear_rows(gu, s), "qwen3_gate_up_rows");
+        QWEN3_TRY(launch_rows(m, gu, s), "qwen3_gate_up_rows");
         LinearParams d = params_for(LinearEpilogue::kResidual, m->act, c.intermediate_size, l.wd, nullptr, T, H,
                                     c.intermediate_size);
         d.residual = m->h;
         d.res_ld = H;
         d.out[0] = m->h;
         d.ld[0] = H;
-        QWEN3_TRY(cppinf::device::launch_linear_rows(d, s), "qwen3_down_proj_rows");
+        QWEN3_TRY(launch_rows(m, d, s), "qwen3_down_proj_rows");
     }
     if (logits != nullptr) {
         QWEN3_CHECK(cppinf_rms_norm(CPPINF_DTYPE_BF16, m->h, H, m->final_norm, m->xn, T, H, c.rms_norm_eps, s));
         LinearParams lm = params_for(LinearEpilogue::kStore, m->xn, H, m->embed, nullptr, T, c.vocab_size, H);
         lm.out[0] = logits;
         lm.ld[0] = c.vocab_size;
-        QWEN3_TRY(T == 1 ? cppinf::device::launch_gemv(lm, s) : cppinf::device::launch_linear_rows(lm, s),
+        QWEN3_TRY(T == 1 ? cppinf::device::launch_gemv(lm, s) : launch_rows(m, lm, s),
                   "qwen3_lm_head_rows");
     }
     return CPPINF_OK;
@@ -549,6 +562,14 @@ int cppinf_qwen3_reset(cppinf_qwen3* model, void* stream) {
     CPPINF_CUDA_TRY(cudaMemsetAsync(model->d_error, 0, sizeof(unsigned int), s));
     model->len = 0;
     model->failed = false;
+    return rt::ok();
+}
+
+int cppinf_qwen3_set_prefill(cppinf_qwen3* model, int mode) {
+    CPPINF_REQUIRE(model, CPPINF_ERR_INVALID_ARGUMENT, "qwen3_set_prefill received a null pointer.");
+    CPPINF_REQUIRE(mode == 0 || mode == 1, CPPINF_ERR_INVALID_ARGUMENT,
+                   "qwen3_set_prefill mode must be 0 (CUDA cores) or 1 (tensor cores).");
+    model->prefill_mode = mode;
     return rt::ok();
 }
 

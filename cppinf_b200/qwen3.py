@@ -194,6 +194,14 @@ class Qwen3Model:
                                     t.numel() * 2, 1 if t.is_cuda else 0)
             torch.cuda.synchronize(self.device)
 
+    def set_prefill(self, mode: str) -> None:
+        """Prompt-row projections on "cuda_cores" (default: bit-exact to the oracle) or "tensor_cores" (tcgen05,
+        tolerance parity)."""
+        modes = {"cuda_cores": 0, "tensor_cores": 1}
+        if mode not in modes:
+            raise ValueError(f"prefill mode must be one of {sorted(modes)}")
+        self._capi.call("cppinf_qwen3_set_prefill", self._handle, modes[mode])
+
     def load_safetensors(self, path) -> int:
         """Loads a safetensors checkpoint straight from the mapped file into the model (cppinf_qwen3_load_safetensors);
         returns the number of tensors copied."""

@@ -321,6 +321,12 @@ CPPINF_API int cppinf_qwen3_decode(cppinf_qwen3* model, int64_t steps, int64_t* 
 /* Forgets the cached sequence (a fresh make_cache) and clears a device error reported by cppinf_qwen3_decode. */
 CPPINF_API int cppinf_qwen3_reset(cppinf_qwen3* model, void* stream);
 
+/* Projections of prompt rows (cppinf_qwen3_forward): mode 0 (default) runs them on the CUDA cores in the library's
+ * restated accumulation order, so logits and greedy tokens equal the CPU oracle's bit for bit; mode 1 runs the
+ * eligible ones on the tensor cores (cppinf_linear_tc), several times faster, with logits that agree to tolerance.
+ * Decode steps are unaffected. No counterpart in the reference (its matmul is one oneDNN path). */
+CPPINF_API int cppinf_qwen3_set_prefill(cppinf_qwen3* model, int mode);
+
 /* Number of cached tokens. */
 CPPINF_API int64_t cppinf_qwen3_length(const cppinf_qwen3* model);
 
