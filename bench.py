@@ -22,7 +22,8 @@ only and with the copy-back of every rank's output rows into one buffer on rank 
 NVLink peer copies).
 
 Timing: W eager warm-up steps, then K steps replayed from CUDA graphs of <= 1000 launches, bracketed by a barrier and
-a device synchronize, CUDA events on the launch stream; `repeats` replays the same K steps 50 more times, each timed
+a device synchronize, CUDA events on the launch stream (a ~100 us device spin queued before the start event hides the
+host's graph submission, which would otherwise sit inside a short timed region); `repeats` replays the same K steps 50 more times, each timed
 alone, for the median and the spread. Consecutive steps rotate through buffer sets whose total is
 more than three times the 126 MB L2, so every step reads cold data from HBM. `e2e` runs the same op through the
 public API from pinned host buffers (H2D, kernel, D2H pipelined over three streams) and reports the same metric.
@@ -56,6 +57,7 @@ REPO = Path(__file__).resolve().parent
 sys.path.insert(0, str(REPO))
 
 L2_BYTES = 126 * 1024 * 1024
+SPACER_CYCLES = 200_000  # ~100 us of device spin before a timed region (see time_device_steps)
 FALLBACK_HBM_GBS = 6650.0
 METRIC = "achieved HBM GB/s per op vs ~8 TB/s"
 UNIT = "GB/s"
@@ -73,6 +75,10 @@ CONFIGS = {
     "causal_softmax": dict(bytes=16 * (2048 * 2049 // 2) * 4 + 16 * 2048 * 2048 * 4,
                            desc="causal scaled softmax f32 [16,2048,2048] ~N(0,4), scale 1/sqrt(128)"),
     "row_argmax": dict(bytes=64 * 151936 * 2 + 64 * 8, desc="row argmax logits bf16 [64,151936] ~N(0,2)"),
+    # Tensor-bound: reported in TFLOP/s against the measured dense bf16 peak as well.
+    "linear_tc": dict(bytes=(512 * 1024 + 2 * 3072 * 1024 + 512 * 3072) * 2, flops=2 * 2 * 512 * 3072 * 1024,
+                      desc="tensor-core prefill gate/up projection with SiLU*up: x bf16 [512,1024] ~N(0,1), "
+                           "gate/up [3072,1024] ~N(0,0.02) (cppinf_linear_tc)"),
 }
 HEADLINE = "qk_norm_rope"
 
@@ -103,6 +109,14 @@ def read_peak_gbs() -> tuple[float, str]:
         return float(peaks["hbm_gbs"]), "measured"
     except (OSError, KeyError, ValueError):
         return FALLBACK_HBM_GBS, "fallback"
+
+
+def read_peak_tflops() -> tuple[float, str]:
+    """Dense bf16 peak for a kernel timed alone: MEASURED_PEAKS.json bf16_tflops (burst), else the fallback."""
+    try:
+        return float(json.loads((REPO / "MEASURED_PEAKS.json").read_text())["bf16_tflops"]), "measured (burst)"
+    except (OSError, KeyError, ValueError):
+        return 1590.0, "fallback"
 
 
 def read_traffic(workload: str) -> float | None:
@@ -307,6 +321,15 @@ class Workload:
                     return 0
                 return (x, y), launch, [y]
             set_bytes = 2 * nrows * n * 4
+        elif name == "linear_tc":
+            wg, wu = randn((3072, 1024), 0.0, 0.02), randn((3072, 1024), 0.0, 0.02)
+
+            def make_set():
+                x = randn((512, 1024))
+                y = torch.empty((512, 3072), dtype=torch.bfloat16, device=device)
+                return (x, y), lambda s: self.lib.cppinf_linear_tc(2, x.data_ptr(), 1024, wg.data_ptr(), wu.data_ptr(),
+                                                                   0, y.data_ptr(), 512, 1024, 3072, 0, s), [y]
+            set_bytes = (512 * 1024 + 512 * 3072) * 2
         elif name == "row_argmax":
             nrows = 64 if rows is None else rows
             self.bytes = nrows * 151936 * 2 + nrows * 8
@@ -369,6 +392,9 @@ def time_device_steps(wl: Workload, steps: int, warmup: int, stream, barrier,
         barrier()
         torch.cuda.synchronize()
         with torch.cuda.stream(stream):
+            # A ~100 us spin queued ahead of the start event keeps the device busy while the host submits the
+            # graph, so the timed region holds the K steps and not the submission latency.
+            torch.cuda._sleep(SPACER_CYCLES)
             start.record(stream)
             for _ in range(replays):
                 main_graph.replay()
@@ -1000,6 +1026,11 @@ def run_ours(args) -> None:
             per_op[name] = {"gbs": round(gbs, 1), "frac": round(gbs / peak, 4), "us_per_step":
                             round(op_ms / args.op_steps * 1e3, 3), "bytes": w2.bytes,
                             "traffic": read_traffic(name)}
+            if "flops" in CONFIGS[name]:
+                tflops = CONFIGS[name]["flops"] / (op_ms / args.op_steps * 1e-3) / 1e12
+                tpeak, tkind = read_peak_tflops()
+                per_op[name].update({"bound": "tensor", "tflops": round(tflops, 1), "tflops_peak": tpeak,
+                                     "tflops_frac": round(tflops / tpeak, 4), "tflops_peak_source": tkind})
             if name == "rms_norm":
                 # [512, 1024] is launch-latency bound: the isolated single-launch time, beside the graph-batched one.
                 single = sorted(time_single_launches(w2, 50, stream))
