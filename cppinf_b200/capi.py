@@ -85,6 +85,7 @@ _SIGNATURES = {
     "cppinf_linear_argmax_scratch_bytes": [_i64, _i64],
     "cppinf_linear_argmax_noalloc": [_ptr, _ptr, _ptr, _i64, _i64, _ptr, _ptr],
     "cppinf_decoder_attention": [_ptr, _ptr, _ptr, _ptr, _i64, _i64, _i64, _i64, _i64, _i64, _ptr],
+    "cppinf_decoder_attention_tc": [_ptr, _ptr, _ptr, _ptr, _i64, _i64, _i64, _i64, _i64, _i64, _ptr, _ptr],
     "cppinf_embedding": [_ptr, _i64, _i64, _ptr, _i64, _ptr, _ptr],
     "cppinf_qwen3_create": [ctypes.c_void_p, _i64, ctypes.POINTER(_ptr)],
     "cppinf_qwen3_destroy": [_ptr],

@@ -113,6 +113,11 @@ struct AttentionParams {
 // Causal GQA attention of one sequence in the fixed partition order (see attention.cu). head_dim 64, 128 or 256.
 cudaError_t launch_decoder_attention(const AttentionParams& p, int64_t max_keys, cudaStream_t s);
 
+// The same attention on the tensor cores for cached keys (attention_tc.cu: tcgen05, tolerance parity): head_dim 128,
+// no device position, no fused q/k norm. cudaErrorNotSupported otherwise.
+bool attention_tc_supported(const AttentionParams& p);
+cudaError_t launch_attention_tc(const AttentionParams& p, cudaStream_t s);
+
 // Embedding lookup (src/models/qwen3/qwen3_model.cpp:132-165): out[t] = table[tokens[t]], ids clamped into range.
 cudaError_t launch_embedding(const __nv_bfloat16* table, int64_t vocab, int64_t hidden, const int64_t* tokens,
                              int64_t count, __nv_bfloat16* out, cudaStream_t s);

@@ -240,8 +240,30 @@ int enqueue_chunk(cppinf_qwen3* m, int64_t pos0, int64_t T, bf16* logits, cudaSt
         QWEN3_CHECK(cppinf_qk_norm_rope(CPPINF_DTYPE_BF16, m->q, m->k, l.q_norm, l.k_norm, m->qr,
                                         l.k_cache + pos0 * m->kv_dim, T, c.num_attention_heads,
                                         c.num_key_value_heads, c.head_dim, pos0, c.rms_norm_eps, m->rope, m->cap, s));
-        QWEN3_CHECK(cppinf_decoder_attention(m->qr, l.k_cache, l.v_cache, m->ctx, T, c.num_attention_heads,
-                                             c.num_key_value_heads, c.head_dim, pos0, m->cap, s));
+        if (m->prefill_mode == 1) {
+            AttentionParams ap{};
+            ap.q = m->qr;
+            ap.k_cache = l.k_cache;
+            ap.v_cache = l.v_cache;
+            ap.ctx = m->ctx;
+            ap.T = T;
+            ap.q_heads = static_cast<int>(c.num_attention_heads);
+            ap.kv_heads = static_cast<int>(c.num_key_value_heads);
+            ap.head_dim = static_cast<int>(c.head_dim);
+            ap.pos0 = pos0;
+            ap.capacity = m->cap;
+            ap.error = m->d_error;
+            ap.poll_limit = rt::wait_poll_limit();
+            if (cppinf::device::attention_tc_supported(ap)) {
+                QWEN3_TRY(cppinf::device::launch_attention_tc(ap, s), "qwen3_attention_tc");
+            } else {
+                QWEN3_CHECK(cppinf_decoder_attention(m->qr, l.k_cache, l.v_cache, m->ctx, T, c.num_attention_heads,
+                                                     c.num_key_value_heads, c.head_dim, pos0, m->cap, s));
+            }
+        } else {
+            QWEN3_CHECK(cppinf_decoder_attention(m->qr, l.k_cache, l.v_cache, m->ctx, T, c.num_attention_heads,
+                                                 c.num_key_value_heads, c.head_dim, pos0, m->cap, s));
+        }
         LinearParams o = params_for(LinearEpilogue::kResidual, m->ctx, m->q_dim, l.wo, nullptr, T, H, m->q_dim);
         o.residual = m->h;
         o.res_ld = H;

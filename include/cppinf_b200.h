@@ -257,6 +257,16 @@ CPPINF_API int cppinf_decoder_attention(const void* q, const void* k_cache, cons
                                         int64_t tokens, int64_t q_heads, int64_t kv_heads, int64_t head_dim,
                                         int64_t position, int64_t capacity, void* stream);
 
+/* cppinf_decoder_attention on the tensor cores (tcgen05: S = Q K^T and P V as UMMAs with tensor-memory accumulators,
+ * the causal softmax with bf16 probabilities in between), for head_dim 128. Opt-in, like cppinf_linear_tc: contexts
+ * agree with cppinf_decoder_attention to tolerance (the running softmax sum and the tensor cores' accumulation order
+ * are not the restated order), not bit for bit. `error` (device, may be NULL) is set to 1 when a wait of the kernel
+ * ran out of its poll limit (cppinf_set_wait_poll_limit). No counterpart in the reference beyond the attention it
+ * computes (src/nn/qwen_attention.cpp:237-333). */
+CPPINF_API int cppinf_decoder_attention_tc(const void* q, const void* k_cache, const void* v_cache, void* ctx,
+                                           int64_t tokens, int64_t q_heads, int64_t kv_heads, int64_t head_dim,
+                                           int64_t position, int64_t capacity, unsigned int* error, void* stream);
+
 /* Embedding lookup (src/models/qwen3/qwen3_model.cpp:132-165): out[t] = table[token_ids[t]], table [vocab, hidden]
  * bf16, token_ids a DEVICE int64 array. Ids are validated on the host by the model; here they are clamped into
  * range. hidden must be a multiple of 8. */

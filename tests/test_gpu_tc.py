@@ -170,3 +170,55 @@ def test_model_prefill_on_tensor_cores_within_logit_tolerance(cuda, oracle):
             model.set_prefill("fp8")
     finally:
         model.close()
+
+
+def attention_inputs(rng, t, pos, cap, hq, hkv):
+    q = to_dev(seeded_bf16(rng, (t, hq, 128), 0, 1))
+    kc = to_dev(seeded_bf16(rng, (cap, hkv, 128), 0, 1))
+    vc = to_dev(seeded_bf16(rng, (cap, hkv, 128), 0, 1))
+    return q, kc, vc
+
+
+def run_attention(capi, name, q, kc, vc, t, pos, cap, hq, hkv, error=None):
+    ctx = torch.empty((t, hq, 128), dtype=torch.bfloat16, device="cuda")
+    args = [q.data_ptr(), kc.data_ptr(), vc.data_ptr(), ctx.data_ptr(), t, hq, hkv, 128, pos, cap]
+    if name == "cppinf_decoder_attention_tc":
+        args.append(0 if error is None else error.data_ptr())
+    capi.call(name, *args, torch.cuda.current_stream().cuda_stream)
+    return bf16_to_f32(to_host(ctx))
+
+
+# (queries, position of query 0, cache rows, q heads, kv heads): the 512-query prompt chunk of Qwen3-0.6B, the second
+# chunk of a 600-token prompt, one query, odd sizes across key tiles, and 4:1 grouped-query heads.
+ATTN_SHAPES = [(512, 0, 640, 16, 8), (88, 512, 640, 16, 8), (1, 100, 256, 16, 8), (130, 37, 300, 4, 2),
+               (200, 0, 200, 8, 2)]
+
+
+@pytest.mark.parametrize("t,pos,cap,hq,hkv", ATTN_SHAPES)
+def test_attention_tc_matches_restated_attention_within_tolerance(capi, t, pos, cap, hq, hkv):
+    # Contexts are weighted means of bf16 V rows; the tensor cores' score sums, the running softmax sum and bf16
+    # probabilities that round the other way move them by a few bf16 ulps at most. Bound: 0.02, the reference's own
+    # bf16 attention tolerance (tests/nn/qwen_attention_test.cpp:184-189), and a mean error far below it.
+    rng = np.random.default_rng(t * 31 + pos)
+    q, kc, vc = attention_inputs(rng, t, pos, cap, hq, hkv)
+    want = run_attention(capi, "cppinf_decoder_attention", q, kc, vc, t, pos, cap, hq, hkv)
+    got = run_attention(capi, "cppinf_decoder_attention_tc", q, kc, vc, t, pos, cap, hq, hkv)
+    assert np.isfinite(got).all()
+    err = np.abs(got - want)
+    assert err.max() <= 0.02, err.max()
+    assert err.mean() <= 2e-3, err.mean()
+
+
+def test_attention_tc_wait_that_runs_out_sets_error_and_completes(capi):
+    rng = np.random.default_rng(12)
+    q, kc, vc = attention_inputs(rng, 256, 0, 300, 8, 4)
+    error = torch.zeros(1, dtype=torch.int32, device="cuda")
+    want = run_attention(capi, "cppinf_decoder_attention", q, kc, vc, 256, 0, 300, 8, 4)
+    capi.set_wait_poll_limit(0)
+    try:
+        got = run_attention(capi, "cppinf_decoder_attention_tc", q, kc, vc, 256, 0, 300, 8, 4, error=error)
+    finally:
+        capi.set_wait_poll_limit(capi.DEFAULT_POLL_LIMIT)
+    assert int(error.item()) == 1
+    # every wait then waits again with the default limit, so the protocol completes and the result stands
+    assert np.abs(got - want).max() <= 0.02
