@@ -1065,8 +1065,8 @@ def run_ours(args) -> None:
             "prefill_tensor_cores": {
                 "ms": round(max_over_ranks(d["prefill_tc_ms"]), 3),
                 "first_token_same": d["prefill_tc_first_token_same"],
-                "how": "Qwen3Model.set_prefill('tensor_cores'): the prompt projections on tcgen05 (tolerance parity); "
-                       "prefill_ms above is the default bit-exact CUDA-core path"},
+                "how": "Qwen3Model.set_prefill('tensor_cores'): the prompt projections and attention on tcgen05 "
+                       "(tolerance parity); prefill_ms above is the default bit-exact CUDA-core path"},
             "config": {"model": "Qwen3-0.6B, random init N(0,0.02) bf16, unit norm weights, tied embeddings",
                        "prompt_tokens": DECODE_PROMPT, "generated_tokens": DECODE_NEW, "batch": 1,
                        "parallelism": f"{world} independent replica(s), one per GPU (decode does not shard)"},
