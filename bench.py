@@ -496,8 +496,8 @@ class PeerOutputs:
     Rank 0 copies its own rows locally. `path` is "nvlink peer copy" or, when a rank could not map the buffers
     (every rank learns of it), "nccl send/recv" through shard.copy_back."""
 
-    class _Handle(ctypes.Structure):  # cudaIpcMemHandle_t
-        _fields_ = [("reserved", ctypes.c_char * 64)]
+    class _Handle(ctypes.Structure):  # cudaIpcMemHandle_t (64 opaque bytes, NULs included)
+        _fields_ = [("reserved", ctypes.c_ubyte * 64)]
 
     def __init__(self, shapes: list, rank: int, device):
         import torch
@@ -526,7 +526,7 @@ class PeerOutputs:
                     h = PeerOutputs._Handle()
                     if rt.cudaIpcGetMemHandle(ctypes.byref(h), ctypes.c_void_p(p.value)) != 0:
                         raise RuntimeError("cudaIpcGetMemHandle")
-                    handles.append(bytes(h.reserved))
+                    handles.append(ctypes.string_at(ctypes.addressof(h), ctypes.sizeof(h)))
                 self.ptrs = list(self.owned)
             box = [handles]
             dist.broadcast_object_list(box, src=0)
@@ -534,13 +534,14 @@ class PeerOutputs:
                 rt.cudaIpcOpenMemHandle.argtypes = [ctypes.POINTER(ctypes.c_void_p), PeerOutputs._Handle, ctypes.c_uint]
                 for raw in box[0]:
                     h = PeerOutputs._Handle()
-                    h.reserved = raw
+                    ctypes.memmove(ctypes.addressof(h), raw, ctypes.sizeof(h))
                     p = ctypes.c_void_p()
                     if rt.cudaIpcOpenMemHandle(ctypes.byref(p), h, 1) != 0:  # cudaIpcMemLazyEnablePeerAccess
                         raise RuntimeError("cudaIpcOpenMemHandle")
                     self.ptrs.append(p.value)
         except Exception:
             ok = 0
+            rt.cudaGetLastError()  # a failed runtime call must not surface in a later launch check
         flag = torch.tensor([ok], dtype=torch.int32, device=device)
         dist.all_reduce(flag, op=dist.ReduceOp.MIN)
         self.path = "nvlink peer copy" if int(flag.item()) == 1 else "nccl send/recv"

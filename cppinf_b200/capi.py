@@ -98,6 +98,11 @@ _SIGNATURES = {
     "cppinf_qwen3_set_prefill": [_ptr, _int],
     "cppinf_qwen3_length": [_ptr],
     "cppinf_qwen3_step_launches": [_ptr],
+    "cppinf_qwen3_cache_create": [_ptr, _i64, _i64, ctypes.POINTER(_ptr)],
+    "cppinf_qwen3_cache_destroy": [_ptr],
+    "cppinf_qwen3_cache_batch": [_ptr],
+    "cppinf_qwen3_cache_lengths": [_ptr, ctypes.POINTER(_i64)],
+    "cppinf_qwen3_forward_batch": [_ptr, _ptr, ctypes.POINTER(_i64), ctypes.POINTER(_i64), _i64, _i64, _ptr, _ptr],
 }
 _RESTYPES = {
     "cppinf_last_error": ctypes.c_char_p,
@@ -108,6 +113,8 @@ _RESTYPES = {
     "cppinf_qwen3_destroy": None,
     "cppinf_qwen3_length": _i64,
     "cppinf_qwen3_step_launches": _i64,
+    "cppinf_qwen3_cache_destroy": None,
+    "cppinf_qwen3_cache_batch": _i64,
 }
 
 

@@ -294,6 +294,142 @@ int enqueue_chunk(cppinf_qwen3* m, int64_t pos0, int64_t T, bf16* logits, cudaSt
     return CPPINF_OK;
 }
 
+}  // namespace
+
+// A batch of cached sequences (Qwen3Cache of src/models/qwen3/qwen3_model.cpp:222-245): per layer and sequence a K
+// and a V cache [capacity, kv_heads, head_dim], and each sequence's length on the host.
+struct cppinf_qwen3_cache {
+    int64_t batch = 0;
+    int64_t cap = 0;
+    int64_t layers = 0;
+    int64_t kv_dim = 0;
+    std::size_t per_cache = 0;  // bytes of one K or V cache of one sequence and layer
+    char* mem = nullptr;
+    std::size_t bytes = 0;
+    int64_t* d_ids = nullptr;  // the token ids of one chunk of rows
+    std::vector<int64_t> lens;
+
+    bf16* k(int64_t layer, int64_t b) const {
+        return reinterpret_cast<bf16*>(mem + per_cache * static_cast<std::size_t>((layer * batch + b) * 2));
+    }
+    bf16* v(int64_t layer, int64_t b) const {
+        return reinterpret_cast<bf16*>(mem + per_cache * static_cast<std::size_t>((layer * batch + b) * 2 + 1));
+    }
+};
+
+namespace {
+
+// Rows [start, start + n) of sequence b, at rows [row, row + n) of a chunk.
+struct Piece {
+    int64_t b;
+    int64_t start;
+    int64_t n;
+    int64_t row;
+};
+
+// One chunk of a batched forward: the rows of `pieces` (at most the workspace's rows, one piece per sequence) go
+// through the decoder together -- embedding, norms, projections and the MLP over all rows at once, the q/k norm +
+// RoPE, the cache appends and the attention per sequence -- so each row is computed exactly as in a forward of its
+// own sequence. Logits of each piece go to logits[b, start .. start + n).
+int enqueue_batch_chunk(cppinf_qwen3* m, cppinf_qwen3_cache* kc, const std::vector<Piece>& pieces,
+                        const int64_t* host_ids, int64_t max_length, bf16* logits, cudaStream_t s) {
+    const auto& c = m->c;
+    const int64_t H = c.hidden_size;
+    const int64_t V = c.vocab_size;
+    const int64_t R = pieces.back().row + pieces.back().n;
+    std::vector<int64_t> ids(static_cast<std::size_t>(R));
+    for (const Piece& p : pieces) {
+        for (int64_t i = 0; i < p.n; ++i) {
+            ids[static_cast<std::size_t>(p.row + i)] = host_ids[p.b * max_length + p.start + i];
+        }
+    }
+    CPPINF_CUDA_TRY(cudaMemcpyAsync(kc->d_ids, ids.data(), static_cast<std::size_t>(R) * 8, cudaMemcpyHostToDevice,
+                                    s));
+    QWEN3_TRY(cppinf::device::launch_embedding(m->embed, V, H, kc->d_ids, R, m->h, s), "qwen3_embedding");
+    for (std::size_t li = 0; li < m->layers.size(); ++li) {
+        const Layer& l = m->layers[li];
+        const auto layer = static_cast<int64_t>(li);
+        QWEN3_CHECK(cppinf_rms_norm(CPPINF_DTYPE_BF16, m->h, H, l.in_norm, m->xn, R, H, c.rms_norm_eps, s));
+        LinearParams qkv = params_for(LinearEpilogue::kStore, m->xn, H, l.wqkv, nullptr, R, m->qkv_rows, H);
+        set_qkv_outputs(m, l, qkv, 0, nullptr);
+        qkv.out[2] = m->ctx;  // v rows [R, kv_dim] staged in the context buffer, then appended to each cache
+        QWEN3_TRY(launch_rows(m, qkv, s), "qwen3_qkv_rows");
+        for (const Piece& p : pieces) {
+            const int64_t pos = kc->lens[static_cast<std::size_t>(p.b)] + p.start;
+            CPPINF_CUDA_TRY(cudaMemcpyAsync(kc->v(layer, p.b) + pos * m->kv_dim, m->ctx + p.row * m->kv_dim,
+                                            static_cast<std::size_t>(p.n * m->kv_dim) * 2, cudaMemcpyDeviceToDevice,
+                                            s));
+        }
+        for (const Piece& p : pieces) {
+            const int64_t pos = kc->lens[static_cast<std::size_t>(p.b)] + p.start;
+            bf16* kcache = kc->k(layer, p.b);
+            bf16* vcache = kc->v(layer, p.b);
+            bf16* qr = m->qr + p.row * m->q_dim;
+            bf16* ctx = m->ctx + p.row * m->q_dim;
+            QWEN3_CHECK(cppinf_qk_norm_rope(CPPINF_DTYPE_BF16, m->q + p.row * m->q_dim, m->k + p.row * m->kv_dim,
+                                            l.q_norm, l.k_norm, qr, kcache + pos * m->kv_dim, p.n,
+                                            c.num_attention_heads, c.num_key_value_heads, c.head_dim, pos,
+                                            c.rms_norm_eps, m->rope, m->cap, s));
+            AttentionParams ap{};
+            ap.q = qr;
+            ap.k_cache = kcache;
+            ap.v_cache = vcache;
+            ap.ctx = ctx;
+            ap.T = p.n;
+            ap.q_heads = static_cast<int>(c.num_attention_heads);
+            ap.kv_heads = static_cast<int>(c.num_key_value_heads);
+            ap.head_dim = static_cast<int>(c.head_dim);
+            ap.pos0 = pos;
+            ap.capacity = kc->cap;
+            ap.error = m->d_error;
+            ap.poll_limit = rt::wait_poll_limit();
+            if (m->prefill_mode == 1 && cppinf::device::attention_tc_supported(ap)) {
+                QWEN3_TRY(cppinf::device::launch_attention_tc(ap, s), "qwen3_attention_tc");
+            } else {
+                QWEN3_CHECK(cppinf_decoder_attention(qr, kcache, vcache, ctx, p.n, c.num_attention_heads,
+                                                     c.num_key_value_heads, c.head_dim, pos, kc->cap, s));
+            }
+        }
+        LinearParams o = params_for(LinearEpilogue::kResidual, m->ctx, m->q_dim, l.wo, nullptr, R, H, m->q_dim);
+        o.residual = m->h;
+        o.res_ld = H;
+        o.out[0] = m->h;
+        o.ld[0] = H;
+        QWEN3_TRY(launch_rows(m, o, s), "qwen3_o_proj_rows");
+        QWEN3_CHECK(cppinf_rms_norm(CPPINF_DTYPE_BF16, m->h, H, l.post_norm, m->xn, R, H, c.rms_norm_eps, s));
+        LinearParams gu = params_for(LinearEpilogue::kSiluMul, m->xn, H, l.wg, l.wu, R, c.intermediate_size, H);
+        gu.out[0] = m->act;
+        gu.ld[0] = c.intermediate_size;
+        QWEN3_TRY(launch_rows(m, gu, s), "qwen3_gate_up_rows");
+        LinearParams d = params_for(LinearEpilogue::kResidual, m->act, c.intermediate_size, l.wd, nullptr, R, H,
+                                    c.intermediate_size);
+        d.residual = m->h;
+        d.res_ld = H;
+        d.out[0] = m->h;
+        d.ld[0] = H;
+        QWEN3_TRY(launch_rows(m, d, s), "qwen3_down_proj_rows");
+    }
+    QWEN3_CHECK(cppinf_rms_norm(CPPINF_DTYPE_BF16, m->h, H, m->final_norm, m->xn, R, H, c.rms_norm_eps, s));
+    // The LM head once per run of pieces that are consecutive in logits [batch, max_length, vocab].
+    std::size_t i = 0;
+    while (i < pieces.size()) {
+        std::size_t j = i + 1;
+        int64_t rows = pieces[i].n;
+        while (j < pieces.size() && pieces[j - 1].start + pieces[j - 1].n == max_length && pieces[j].start == 0 &&
+               pieces[j].b == pieces[j - 1].b + 1) {
+            rows += pieces[j].n;
+            ++j;
+        }
+        const Piece& first = pieces[i];
+        LinearParams lm = params_for(LinearEpilogue::kStore, m->xn + first.row * H, H, m->embed, nullptr, rows, V, H);
+        lm.out[0] = logits + (first.b * max_length + first.start) * V;
+        lm.ld[0] = V;
+        QWEN3_TRY(rows == 1 ? cppinf::device::launch_gemv(lm, s) : launch_rows(m, lm, s), "qwen3_lm_head_rows");
+        i = j;
+    }
+    return CPPINF_OK;
+}
+
 // Where a checkpoint tensor goes and the shape the model expects: [rows, cols] for matrices, [rows] when cols == 0.
 struct WeightSlot {
     bf16* dst;
@@ -637,6 +773,125 @@ int cppinf_qwen3_forward(cppinf_qwen3* model, const int64_t* token_ids, int64_t 
     if (next_token != nullptr) {
         CPPINF_CUDA_TRY(cudaMemcpyAsync(next_token, model->d_tokens + model->len, 8, cudaMemcpyDeviceToHost, s));
         CPPINF_CUDA_TRY(cudaStreamSynchronize(s));
+    }
+    return rt::ok();
+}
+
+int cppinf_qwen3_cache_create(const cppinf_qwen3* model, int64_t batch, int64_t capacity, cppinf_qwen3_cache** cache) {
+    CPPINF_REQUIRE(model && cache, CPPINF_ERR_INVALID_ARGUMENT, "qwen3_cache_create received a null pointer.");
+    *cache = nullptr;
+    CPPINF_REQUIRE(batch > 0 && capacity > 0, CPPINF_ERR_INVALID_ARGUMENT,
+                   "Qwen3Model cache requires non-zero batch and sequence dimensions.");
+    CPPINF_REQUIRE(capacity <= model->cap, CPPINF_ERR_UNSUPPORTED,
+                   "a batch cache may hold at most the model's max_sequence_length positions (its rotary table).");
+    auto* kc = new cppinf_qwen3_cache();
+    kc->batch = batch;
+    kc->cap = capacity;
+    kc->layers = model->c.num_hidden_layers;
+    kc->kv_dim = model->kv_dim;
+    kc->per_cache = align_up(static_cast<std::size_t>(capacity * model->kv_dim) * 2);
+    kc->bytes = kc->per_cache * 2 * static_cast<std::size_t>(batch * kc->layers);
+    kc->lens.assign(static_cast<std::size_t>(batch), 0);
+    cudaError_t err = cudaMalloc(&kc->mem, kc->bytes);
+    if (err == cudaSuccess) {
+        err = cudaMemset(kc->mem, 0, kc->bytes);
+    }
+    if (err == cudaSuccess) {
+        err = cudaMalloc(&kc->d_ids, static_cast<std::size_t>(kChunkRows) * 8);
+    }
+    if (err != cudaSuccess) {
+        cudaFree(kc->mem);
+        cudaFree(kc->d_ids);
+        delete kc;
+        return rt::cuda_fail(err, "qwen3_cache_create allocation");
+    }
+    *cache = kc;
+    return rt::ok();
+}
+
+void cppinf_qwen3_cache_destroy(cppinf_qwen3_cache* cache) {
+    if (cache != nullptr) {
+        cudaFree(cache->mem);
+        cudaFree(cache->d_ids);
+        delete cache;
+    }
+}
+
+int cppinf_qwen3_cache_lengths(const cppinf_qwen3_cache* cache, int64_t* lengths) {
+    CPPINF_REQUIRE(cache && lengths, CPPINF_ERR_INVALID_ARGUMENT, "qwen3_cache_lengths received a null pointer.");
+    std::memcpy(lengths, cache->lens.data(), cache->lens.size() * sizeof(int64_t));
+    return rt::ok();
+}
+
+int64_t cppinf_qwen3_cache_batch(const cppinf_qwen3_cache* cache) {
+    return cache != nullptr ? cache->batch : -1;
+}
+
+int cppinf_qwen3_forward_batch(cppinf_qwen3* model, cppinf_qwen3_cache* cache, const int64_t* token_ids,
+                               const int64_t* lengths, int64_t batch, int64_t max_length, void* logits,
+                               void* stream) {
+    CPPINF_REQUIRE(model && cache, CPPINF_ERR_INVALID_ARGUMENT, "qwen3_forward_batch received a null pointer.");
+    CPPINF_REQUIRE(batch > 0, CPPINF_ERR_INVALID_ARGUMENT,
+                   "Qwen3Model batched forward requires at least one sequence.");
+    CPPINF_REQUIRE(token_ids && lengths && logits, CPPINF_ERR_INVALID_ARGUMENT,
+                   "qwen3_forward_batch received a null pointer.");
+    CPPINF_REQUIRE(cache->layers == model->c.num_hidden_layers && cache->kv_dim == model->kv_dim,
+                   CPPINF_ERR_INVALID_ARGUMENT, "Qwen3Model cache must have one entry per decoder layer.");
+    CPPINF_REQUIRE(cache->batch == batch, CPPINF_ERR_INVALID_ARGUMENT,
+                   "Qwen3Model cache batch size must match the input batch size.");
+    CPPINF_REQUIRE(!model->failed, CPPINF_ERR_CUDA,
+                   "qwen3 model state is invalid after a device error; call qwen3_reset first.");
+    int64_t longest = 0;
+    for (int64_t b = 0; b < batch; ++b) {
+        CPPINF_REQUIRE(lengths[b] > 0, CPPINF_ERR_INVALID_ARGUMENT,
+                       "Qwen3Model batched forward requires each sequence to contain at least one token.");
+        longest = lengths[b] > longest ? lengths[b] : longest;
+    }
+    CPPINF_REQUIRE(longest <= max_length, CPPINF_ERR_INVALID_ARGUMENT,
+                   "qwen3_forward_batch: a sequence is longer than the padded length.");
+    for (int64_t b = 0; b < batch; ++b) {
+        CPPINF_REQUIRE(cache->lens[static_cast<std::size_t>(b)] + lengths[b] <= cache->cap, CPPINF_ERR_OUT_OF_RANGE,
+                       "qwen_attention cache is too small for the new tokens.");
+        for (int64_t i = 0; i < lengths[b]; ++i) {
+            const int64_t t = token_ids[b * max_length + i];
+            CPPINF_REQUIRE(t >= 0 && t < model->c.vocab_size, CPPINF_ERR_OUT_OF_RANGE,
+                           "Qwen3Model token id is out of vocabulary range.");
+        }
+    }
+    const auto s = rt::as_stream(stream);
+    const int64_t V = model->c.vocab_size;
+    bf16* out = static_cast<bf16*>(logits);
+    for (int64_t b = 0; b < batch; ++b) {
+        if (lengths[b] < max_length) {
+            // Right-padded positions: zero logits rows (only the sequences' own rows are results).
+            CPPINF_CUDA_TRY(cudaMemsetAsync(out + (b * max_length + lengths[b]) * V, 0,
+                                            static_cast<std::size_t>((max_length - lengths[b]) * V) * 2, s));
+        }
+    }
+    // Chunks of up to the workspace's rows, filled with the sequences' rows in order; a sequence longer than the
+    // room left continues in the next chunk (its later rows read the earlier ones from the cache).
+    const int64_t room = kChunkRows < model->cap ? kChunkRows : model->cap;
+    std::vector<Piece> pieces;
+    int64_t used = 0;
+    for (int64_t b = 0; b < batch; ++b) {
+        int64_t start = 0;
+        while (start < lengths[b]) {
+            const int64_t n = lengths[b] - start < room - used ? lengths[b] - start : room - used;
+            pieces.push_back({b, start, n, used});
+            start += n;
+            used += n;
+            if (used == room) {
+                QWEN3_CHECK(enqueue_batch_chunk(model, cache, pieces, token_ids, max_length, out, s));
+                pieces.clear();
+                used = 0;
+            }
+        }
+    }
+    if (!pieces.empty()) {
+        QWEN3_CHECK(enqueue_batch_chunk(model, cache, pieces, token_ids, max_length, out, s));
+    }
+    for (int64_t b = 0; b < batch; ++b) {
+        cache->lens[static_cast<std::size_t>(b)] += lengths[b];
     }
     return rt::ok();
 }

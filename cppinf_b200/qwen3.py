@@ -1,8 +1,10 @@
 """Qwen3 decoder on the device: configuration, seeded random weights and the model object.
 
 Mirrors the reference's model interface (src/models/qwen3/qwen3_model.h): ``Qwen3Model.forward(token_ids)`` returns
-bf16 logits [T, vocab]; ``make_cache(max_sequence_length)`` / ``forward_cached(token_ids, cache)`` run the cached
-path; ``generate`` is the greedy loop of src/cli/cli_app.cpp (temperature 0: argmax of the last logits row).
+bf16 logits [T, vocab]; ``forward_cached(token_ids)`` appends to the model's cached sequence;
+``make_cache(batch, max_sequence_length)`` / ``forward_cached_batch(token_id_batch, cache)`` run right-padded
+batches of cached sequences; ``generate`` is the greedy loop of src/cli/cli_app.cpp (temperature 0: argmax of the
+last logits row).
 The model itself lives in libcppinf_b200.so (cppinf_qwen3_* in include/cppinf_b200.h): weights, KV cache and
 activations stay in HBM, and one decode step is a captured CUDA graph whose kernels read the position and the
 previous token from device memory.
@@ -249,6 +251,31 @@ class Qwen3Model:
                             ctypes.byref(nxt), torch.cuda.current_stream().cuda_stream)
         return int(nxt.value), out
 
+    def make_cache(self, batch_size: int, max_sequence_length: int) -> "Qwen3Cache":
+        """Qwen3Model::make_cache(batch_size, max_sequence_length) (qwen3_model.cpp:222-245): a batch of empty cached
+        sequences for forward_cached_batch, separate from the model's own sequence."""
+        return Qwen3Cache(self, batch_size, max_sequence_length)
+
+    def forward_cached_batch(self, token_ids, cache: "Qwen3Cache"):
+        """Qwen3Model::forward_cached(TokenIdBatch, Qwen3Cache&) (qwen3_model.cpp:275-311): sequence b appends
+        token_ids[b] to its cached rows. Returns bf16 logits [batch, longest, vocab] on the device, right-padded rows
+        zero; each row equals the same row of a forward of that sequence alone, bit for bit."""
+        import torch
+
+        seqs = [[int(t) for t in seq] for seq in token_ids]
+        batch = len(seqs)
+        longest = max((len(q) for q in seqs), default=0)
+        packed = [0] * max(batch * longest, 1)
+        for b, q in enumerate(seqs):
+            packed[b * longest:b * longest + len(q)] = q
+        out = torch.empty(max(batch, 1), max(longest, 1), self.config.vocab_size, dtype=torch.bfloat16,
+                          device=self.device)
+        with torch.cuda.device(self.device):
+            self._capi.call("cppinf_qwen3_forward_batch", self._handle, cache._handle, self._capi.i64_array(packed),
+                            self._capi.i64_array([len(q) for q in seqs]), batch, longest, out.data_ptr(),
+                            torch.cuda.current_stream().cuda_stream)
+        return out
+
     def forward(self, token_ids):
         """Qwen3Model::forward: logits [T, vocab] of `token_ids` as a fresh sequence."""
         self.reset()
@@ -272,3 +299,43 @@ class Qwen3Model:
         self.reset()
         first, _ = self.forward_cached(prompt, logits=None)
         return [first] + self.decode(steps - 1)
+
+
+class Qwen3Cache:
+    """A batch of cached sequences on the model's device (cppinf_qwen3_cache_*): per layer and sequence K and V
+    [capacity, kv_heads, head_dim]; ``sequence_lengths`` mirrors Qwen3Cache::sequence_lengths."""
+
+    def __init__(self, model: Qwen3Model, batch_size: int, max_sequence_length: int):
+        import ctypes
+
+        import torch
+
+        self._capi = model._capi
+        handle = ctypes.c_void_p()
+        with torch.cuda.device(model.device):
+            self._capi.call("cppinf_qwen3_cache_create", model._handle, int(batch_size), int(max_sequence_length),
+                            ctypes.byref(handle))
+        self._handle = handle
+        self.capacity = int(max_sequence_length)
+
+    @property
+    def batch_size(self) -> int:
+        return int(self._capi.load().cppinf_qwen3_cache_batch(self._handle))
+
+    @property
+    def sequence_lengths(self) -> list[int]:
+        n = self.batch_size
+        arr = self._capi.i64_array([0] * n)
+        self._capi.call("cppinf_qwen3_cache_lengths", self._handle, arr)
+        return [int(arr[i]) for i in range(n)]
+
+    def close(self) -> None:
+        if getattr(self, "_handle", None) is not None and self._handle.value:
+            self._capi.load().cppinf_qwen3_cache_destroy(self._handle)
+            self._handle = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass

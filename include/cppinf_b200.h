@@ -328,6 +328,28 @@ CPPINF_API int cppinf_qwen3_forward(cppinf_qwen3* model, const int64_t* token_id
  * cppinf_qwen3_reset. The step graph is captured again when the poll limit has changed since its capture. */
 CPPINF_API int cppinf_qwen3_decode(cppinf_qwen3* model, int64_t steps, int64_t* tokens, void* stream);
 
+/* A batch of cached sequences: Qwen3Model::make_cache(batch_size, max_sequence_length) (qwen3_model.cpp:222-245),
+ * per layer and sequence a K and a V cache [capacity, kv_heads, head_dim] in device memory, every length 0.
+ * `capacity` may not exceed the model's max_sequence_length. Independent of the model's own cached sequence. */
+typedef struct cppinf_qwen3_cache cppinf_qwen3_cache;
+CPPINF_API int cppinf_qwen3_cache_create(const cppinf_qwen3* model, int64_t batch, int64_t capacity,
+                                         cppinf_qwen3_cache** cache);
+CPPINF_API void cppinf_qwen3_cache_destroy(cppinf_qwen3_cache* cache);
+CPPINF_API int64_t cppinf_qwen3_cache_batch(const cppinf_qwen3_cache* cache);
+/* Qwen3Cache::sequence_lengths: `lengths` (HOST, cppinf_qwen3_cache_batch entries). */
+CPPINF_API int cppinf_qwen3_cache_lengths(const cppinf_qwen3_cache* cache, int64_t* lengths);
+
+/* Qwen3Model::forward_cached(const TokenIdBatch&, Qwen3Cache&) (qwen3_model.cpp:275-311, the right-padded packing of
+ * pack_token_id_batch :104-130): sequence b appends its lengths[b] HOST token ids token_ids[b * max_length ..] to
+ * its cached rows. logits (DEVICE bf16 [batch, max_length, vocab]) receives each sequence's rows; right-padded rows
+ * are set to zero. Every row equals, bit for bit, the same row of a forward of that sequence alone (the reference's
+ * mixed-length batch test, qwen3_model_test.cpp:459-486): the projections and the MLP run over the rows of all
+ * sequences at once, the q/k norm + RoPE, cache appends and attention per sequence. Errors follow the reference
+ * (empty batch, empty sequence, cache batch mismatch, cache too small, token out of range). */
+CPPINF_API int cppinf_qwen3_forward_batch(cppinf_qwen3* model, cppinf_qwen3_cache* cache, const int64_t* token_ids,
+                                          const int64_t* lengths, int64_t batch, int64_t max_length, void* logits,
+                                          void* stream);
+
 /* Forgets the cached sequence (a fresh make_cache) and clears a device error reported by cppinf_qwen3_decode. */
 CPPINF_API int cppinf_qwen3_reset(cppinf_qwen3* model, void* stream);
 
