@@ -88,6 +88,32 @@ __device__ __forceinline__ float dot8(uint4 a, uint4 b, float acc) {
     return acc;
 }
 
+// dot8 with the query chunk already unpacked into f32 pairs (elements 2q, 2q + 1 of word q): one packed product
+// per key word, then the scalar adds in element order. bf16 x bf16 products are exact in f32, so the sum is the
+// same as dot8's bit for bit.
+__device__ __forceinline__ float dot8(const float2 (&a)[4], uint4 b, float acc) {
+    const float2 p0 = __fmul2_rn(a[0], make_float2(bf16_lo(b.x), bf16_hi(b.x)));
+    const float2 p1 = __fmul2_rn(a[1], make_float2(bf16_lo(b.y), bf16_hi(b.y)));
+    const float2 p2 = __fmul2_rn(a[2], make_float2(bf16_lo(b.z), bf16_hi(b.z)));
+    const float2 p3 = __fmul2_rn(a[3], make_float2(bf16_lo(b.w), bf16_hi(b.w)));
+    acc = acc + p0.x;
+    acc = acc + p0.y;
+    acc = acc + p1.x;
+    acc = acc + p1.y;
+    acc = acc + p2.x;
+    acc = acc + p2.y;
+    acc = acc + p3.x;
+    acc = acc + p3.y;
+    return acc;
+}
+
+__device__ __forceinline__ void unpack_pairs(uint4 x, float2 (&xp)[4]) {
+    xp[0] = make_float2(bf16_lo(x.x), bf16_hi(x.x));
+    xp[1] = make_float2(bf16_lo(x.y), bf16_hi(x.y));
+    xp[2] = make_float2(bf16_lo(x.z), bf16_hi(x.z));
+    xp[3] = make_float2(bf16_lo(x.w), bf16_hi(x.w));
+}
+
 // Per-head RMSNorm + RoPE of one raw head vector into shared memory, with exactly the arithmetic of
 // qk_norm_rope_kernel (rope.cu): kD / 16 lanes, lane hl holding dims [8 hl, 8 hl + 8) and the matching dims of the
 // second half; the sum of squares in the canonical lane order; normalised values rounded to bf16; then
@@ -268,13 +294,13 @@ __global__ void __launch_bounds__(kThreads) decoder_attention_kernel(const Atten
         // Scores: 4 keys per warp iteration, 8 lanes per key; kScoreBatch iterations' loads in flight.
         const int sub = lane % kSegments;
         const int slot = lane / kSegments;
-        uint4 qv[kSegChunks];
+        float2 qv[kSegChunks][4];
     #pragma unroll
         for (int c = 0; c < kSegChunks; ++c) {
             if constexpr (kFused) {
-                qv[c] = *reinterpret_cast<const uint4*>(s_q + sub * kSeg + c * 8);
+                unpack_pairs(*reinterpret_cast<const uint4*>(s_q + sub * kSeg + c * 8), qv[c]);
             } else {
-                qv[c] = ld_cached(p.q + (t * p.q_heads + h) * kD + sub * kSeg + c * 8);
+                unpack_pairs(ld_cached(p.q + (t * p.q_heads + h) * kD + sub * kSeg + c * 8), qv[c]);
             }
         }
         constexpr int kIterKeys = kWarps * kKeysPerIter;
@@ -366,10 +392,14 @@ __global__ void __launch_bounds__(kThreads) decoder_attention_kernel(const Atten
         for (int r = 1; r < kParts; ++r) {
             gmax = fmaxf(gmax, s_m[r]);
         }
-        float total = s_s[0] * pexp(s_m[0] - gmax);
+        // Lane r forms part r's term; every lane then adds the terms in part order from the shuffled values (one
+        // exponential per lane instead of kParts).
+        const int tr = lane % kParts;
+        const float term = s_s[tr] * pexp(s_m[tr] - gmax);
+        float total = __shfl_sync(0xffffffffu, term, 0);
     #pragma unroll
         for (int r = 1; r < kParts; ++r) {
-            total = total + s_s[r] * pexp(s_m[r] - gmax);
+            total = total + __shfl_sync(0xffffffffu, term, r);
         }
 
         for (int64_t i = threadIdx.x; i < n; i += kThreads) {
@@ -405,9 +435,12 @@ __global__ void __launch_bounds__(kThreads) decoder_attention_kernel(const Atten
                     const float pj = s_e[j - lo];
                     float v[kDimsPerLane];
                     VRow<kD>::unpack(raw[u], v);
+                    // p_j * v_j as packed products (exact: bf16 x bf16), added in dimension chains as before.
     #pragma unroll
-                    for (int d = 0; d < kDimsPerLane; ++d) {
-                        a[d] = a[d] + pj * v[d];
+                    for (int d = 0; d < kDimsPerLane; d += 2) {
+                        const float2 pv = __fmul2_rn(make_float2(pj, pj), make_float2(v[d], v[d + 1]));
+                        a[d] = a[d] + pv.x;
+                        a[d + 1] = a[d + 1] + pv.y;
                     }
                 }
             }

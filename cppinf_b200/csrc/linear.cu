@@ -60,6 +60,34 @@ __device__ __forceinline__ float dot_chunk(uint4 x, const float (&w)[8], float a
     return acc;
 }
 
+// An input chunk as f32 pairs: pair q holds elements 2q and 2q + 1 (the low and high halves of 32-bit word q).
+__device__ __forceinline__ void unpack_pairs(uint4 x, float2 (&xp)[4]) {
+    xp[0] = make_float2(bf16_lo(x.x), bf16_hi(x.x));
+    xp[1] = make_float2(bf16_lo(x.y), bf16_hi(x.y));
+    xp[2] = make_float2(bf16_lo(x.z), bf16_hi(x.z));
+    xp[3] = make_float2(bf16_lo(x.w), bf16_hi(x.w));
+}
+
+// dot_chunk with the input already unpacked into pairs: one packed product per weight word, then the two scalar
+// adds in element order. A product of two bf16 values is exact in f32, so the packed product equals the scalar one
+// and the sum is the canonical one bit for bit. (The adds stay scalar: a packed add fed by a packed product would be
+// contracted into a fused multiply-add.)
+__device__ __forceinline__ float dot_chunk(const float2 (&xp)[4], uint4 w, float acc) {
+    const float2 p0 = __fmul2_rn(xp[0], make_float2(bf16_lo(w.x), bf16_hi(w.x)));
+    const float2 p1 = __fmul2_rn(xp[1], make_float2(bf16_lo(w.y), bf16_hi(w.y)));
+    const float2 p2 = __fmul2_rn(xp[2], make_float2(bf16_lo(w.z), bf16_hi(w.z)));
+    const float2 p3 = __fmul2_rn(xp[3], make_float2(bf16_lo(w.w), bf16_hi(w.w)));
+    acc = acc + p0.x;
+    acc = acc + p0.y;
+    acc = acc + p1.x;
+    acc = acc + p1.y;
+    acc = acc + p2.x;
+    acc = acc + p2.y;
+    acc = acc + p3.x;
+    acc = acc + p3.y;
+    return acc;
+}
+
 __device__ __forceinline__ int64_t clamp_token(int64_t t, int64_t vocab) {
     return t < 0 ? 0 : (t >= vocab ? vocab - 1 : t);
 }
@@ -452,6 +480,16 @@ __global__ void __launch_bounds__(kStagedThreads, 2) gemv_staged_kernel(const Li
         return;
     }
 
+    // The held input row unpacked once into f32 pairs for every row of the slice (the step is issue-bound: the
+    // per-row unpacking of the input was a third of the body's instructions).
+    float2 xp[kHoldX ? kC : 1][4];
+    if constexpr (kHoldX) {
+#pragma unroll
+        for (int i = 0; i < kC; ++i) {
+            unpack_pairs(xv[i], xp[i]);
+        }
+    }
+
     // Each warp takes rows warp, warp + kStagedWarps, ... of the slice, one at a time (measured on B200:
     // interleaving four rows per warp was slower).
 #pragma unroll
@@ -467,15 +505,18 @@ __global__ void __launch_bounds__(kStagedThreads, 2) gemv_staged_kernel(const Li
         }
 #pragma unroll
         for (int i = 0; i < kC; ++i) {
-            uint4 x;
+            float2 xq[4];
             if constexpr (kHoldX) {
-                x = xv[i];
+#pragma unroll
+                for (int q = 0; q < 4; ++q) {
+                    xq[q] = xp[i][q];
+                }
             } else {
-                x = ld_cached(xrow + (lane + 32 * i) * 8);
+                unpack_pairs(ld_cached(xrow + (lane + 32 * i) * 8), xq);
             }
 #pragma unroll
             for (int mat = 0; mat < kMats; ++mat) {
-                acc[mat] = dot_chunk(x, s_w[(mat * rows_per_cta + r) * kRowChunks + lane + 32 * i], acc[mat]);
+                acc[mat] = dot_chunk(xq, s_w[(mat * rows_per_cta + r) * kRowChunks + lane + 32 * i], acc[mat]);
             }
         }
 #pragma unroll
