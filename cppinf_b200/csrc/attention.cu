@@ -219,7 +219,10 @@ __global__ void __launch_bounds__(kThreads) decoder_attention_kernel(const Atten
         const int64_t P = (L + kParts - 1) / kParts;
         const int64_t lo = rank * P < L ? rank * P : L;
         const int64_t hi = lo + P < L ? lo + P : L;
-        const int64_t n = hi - lo;
+        // Keys of this part are addressed by their 32-bit index i in [0, n), key j = lo + i (64-bit index math in
+        // these loops cost ~0.6 us per layer of the decode step, measured on B200).
+        const int n = static_cast<int>(hi - lo);
+        const int i_new = static_cast<int>(L - 1 - lo);  // the new token's key (outside [0, n) in other parts)
         const int64_t kv_row = static_cast<int64_t>(p.kv_heads) * kD;
         const float scale = 1.0f / sqrtf(static_cast<float>(kD));
 
@@ -272,6 +275,11 @@ __global__ void __launch_bounds__(kThreads) decoder_attention_kernel(const Atten
             } else if (warp == 1) {
                 norm_rope_head<kD>(p.k_new + (t * p.kv_heads + kvh) * kD, wk_a, wk_b, c_rope, s_rope, p.eps, s_knew,
                                    lane);
+            } else if (kStage && warp == 2 && i_new >= 0 && i_new < n && lane < kD / 8) {
+                // The new token's value row (written to the cache by the previous kernel) joins the staged rows, so
+                // the P·V loop reads shared memory only.
+                *reinterpret_cast<uint4*>(s_vt + i_new * kD + lane * 8) =
+                    ld_cached(p.v_cache + pos * kv_row + kvh * kD + lane * 8);
             }
             __syncthreads();
             if (rank == 0 && h % group == 0 && threadIdx.x < kD / 8) {
@@ -304,27 +312,27 @@ __global__ void __launch_bounds__(kThreads) decoder_attention_kernel(const Atten
             }
         }
         constexpr int kIterKeys = kWarps * kKeysPerIter;
-        for (int64_t j0 = lo + warp * kKeysPerIter; j0 < hi; j0 += kIterKeys * kScoreBatch) {
+        for (int i0 = warp * kKeysPerIter; i0 < n; i0 += kIterKeys * kScoreBatch) {
             uint4 kv[kScoreBatch][kSegChunks];
     #pragma unroll
             for (int u = 0; u < kScoreBatch; ++u) {
-                const int64_t j = j0 + u * kIterKeys + slot;
+                const int i = i0 + u * kIterKeys + slot;
     #pragma unroll
                 for (int c = 0; c < kSegChunks; ++c) {
-                    if (j >= hi) {
+                    if (i >= n) {
                         kv[u][c] = make_uint4(0u, 0u, 0u, 0u);
-                    } else if (kFused && j == L - 1) {
+                    } else if (kFused && i == i_new) {
                         kv[u][c] = *reinterpret_cast<const uint4*>(s_knew + sub * kSeg + c * 8);
                     } else if (kStage) {
-                        kv[u][c] = *reinterpret_cast<const uint4*>(s_kt + (j - lo) * kD + sub * kSeg + c * 8);
+                        kv[u][c] = *reinterpret_cast<const uint4*>(s_kt + i * kD + sub * kSeg + c * 8);
                     } else {
-                        kv[u][c] = ld_cached(p.k_cache + j * kv_row + kvh * kD + sub * kSeg + c * 8);
+                        kv[u][c] = ld_cached(p.k_cache + (lo + i) * kv_row + kvh * kD + sub * kSeg + c * 8);
                     }
                 }
             }
     #pragma unroll
             for (int u = 0; u < kScoreBatch; ++u) {
-                const int64_t j = j0 + u * kIterKeys + slot;
+                const int i = i0 + u * kIterKeys + slot;
                 float s = 0.0f;
     #pragma unroll
                 for (int c = 0; c < kSegChunks; ++c) {
@@ -334,8 +342,8 @@ __global__ void __launch_bounds__(kThreads) decoder_attention_kernel(const Atten
                 for (int offset = kSegments / 2; offset > 0; offset >>= 1) {
                     s = s + __shfl_xor_sync(0xffffffffu, s, offset);
                 }
-                if (j < hi && sub == 0) {
-                    s_e[j - lo] = s * scale;
+                if (i < n && sub == 0) {
+                    s_e[i] = s * scale;
                 }
             }
         }
@@ -343,7 +351,7 @@ __global__ void __launch_bounds__(kThreads) decoder_attention_kernel(const Atten
 
         // This part's maximum and its sum of exp(x - max) (slot order, warp butterfly, warps in order).
         float mx = -INFINITY;
-        for (int64_t i = threadIdx.x; i < n; i += kThreads) {
+        for (int i = threadIdx.x; i < n; i += kThreads) {
             mx = fmaxf(mx, s_e[i]);
         }
         mx = group_max<32>(mx);
@@ -362,7 +370,7 @@ __global__ void __launch_bounds__(kThreads) decoder_attention_kernel(const Atten
         __syncthreads();
         const float local_max = s_local;
         float sum = 0.0f;
-        for (int64_t i = threadIdx.x; i < n; i += kThreads) {
+        for (int i = threadIdx.x; i < n; i += kThreads) {
             sum = sum + pexp(s_e[i] - local_max);
         }
         sum = group_sum<32>(sum);
@@ -402,7 +410,7 @@ __global__ void __launch_bounds__(kThreads) decoder_attention_kernel(const Atten
             total = total + __shfl_sync(0xffffffffu, term, r);
         }
 
-        for (int64_t i = threadIdx.x; i < n; i += kThreads) {
+        for (int i = threadIdx.x; i < n; i += kThreads) {
             s_e[i] = round_to_bf16(pexp(s_e[i] - gmax) / total);
         }
         __syncthreads();
@@ -414,25 +422,25 @@ __global__ void __launch_bounds__(kThreads) decoder_attention_kernel(const Atten
             a[d] = 0.0f;
         }
         const bf16* vbase = p.v_cache + kvh * kD + lane * kDimsPerLane;
-        for (int64_t j0 = lo + warp; j0 < hi; j0 += kWarps * kValueBatch) {
+        for (int i0 = warp; i0 < n; i0 += kWarps * kValueBatch) {
             typename VRow<kD>::Raw raw[kValueBatch];
     #pragma unroll
             for (int u = 0; u < kValueBatch; ++u) {
-                const int64_t j = j0 + u * kWarps;
-                if (j < hi) {
-                    if (kStage && j < staged_hi) {
-                        raw[u] = *reinterpret_cast<const typename VRow<kD>::Raw*>(s_vt + (j - lo) * kD +
+                const int i = i0 + u * kWarps;
+                if (i < n) {
+                    if constexpr (kStage) {
+                        raw[u] = *reinterpret_cast<const typename VRow<kD>::Raw*>(s_vt + i * kD +
                                                                                  lane * kDimsPerLane);
                     } else {
-                        raw[u] = VRow<kD>::load(vbase + j * kv_row);
+                        raw[u] = VRow<kD>::load(vbase + (lo + i) * kv_row);
                     }
                 }
             }
     #pragma unroll
             for (int u = 0; u < kValueBatch; ++u) {
-                const int64_t j = j0 + u * kWarps;
-                if (j < hi) {
-                    const float pj = s_e[j - lo];
+                const int i = i0 + u * kWarps;
+                if (i < n) {
+                    const float pj = s_e[i];
                     float v[kDimsPerLane];
                     VRow<kD>::unpack(raw[u], v);
                     // p_j * v_j as packed products (exact: bf16 x bf16), added in dimension chains as before.

@@ -413,6 +413,15 @@ __global__ void __launch_bounds__(kStagedThreads, 2) gemv_staged_kernel(const Li
             res_pre[k] = (lane == 0 && r < nrows) ? Vec16<bf16>::load1(p.residual, r0 + r) : 0.0f;
         }
     }
+    // Without a held (and normalised) row, the whole input row is still loaded here, right after the wait, so its
+    // latency overlaps the residual load and the wait for the staged slice.
+    uint4 xraw[kHoldX ? 1 : kC];
+    if constexpr (!kHoldX) {
+#pragma unroll
+        for (int i = 0; i < kC; ++i) {
+            xraw[i] = ld_cached(xrow + (lane + 32 * i) * 8);
+        }
+    }
     uint4 xv[kHoldX ? kC : 1];
     if constexpr (kHoldX) {
         // With a norm, warp 0 alone loads and normalises the row and hands it to the other warps through shared
@@ -512,7 +521,7 @@ __global__ void __launch_bounds__(kStagedThreads, 2) gemv_staged_kernel(const Li
                     xq[q] = xp[i][q];
                 }
             } else {
-                unpack_pairs(ld_cached(xrow + (lane + 32 * i) * 8), xq);
+                unpack_pairs(xraw[i], xq);
             }
 #pragma unroll
             for (int mat = 0; mat < kMats; ++mat) {
