@@ -3,10 +3,11 @@
 // cast to bf16, probabilities times V in bf16) for one sequence, query t at position pos0 + t seeing keys
 // 0 .. pos0 + t, query head h reading key/value head h / (Hq / Hkv) (the repeat_interleave of :290-291).
 //
-// One thread-block cluster of 8 CTAs (128 threads each) per (query, head) -- for a prompt, per (run of consecutive
-// queries, head), the queries taken one after another; CTA c owns the c-th of 8 parts of the visible keys
-// (P = ceil(L / 8) consecutive keys each). The order of every sum is fixed, and the CPU oracle
-// restates it (oracle_decoder_attention):
+// One thread-block cluster of 8 CTAs per (query, head) -- for a prompt, per (run of consecutive queries, head), the
+// queries taken one after another; CTA c owns the c-th of 8 parts of the visible keys (P = ceil(L / 8) consecutive
+// keys each). The order of every sum is fixed in terms of 128 slots and 4 warp chains per part, and the CPU oracle
+// restates it (oracle_decoder_attention); a CTA runs it with 8 warps (the score loop over all of them, each warp
+// chain's P·V split into two halves of the dims):
 //  - score: the head vector is cut into 8 segments of D / 8 dims, each summed in order by one lane, the 8 partials
 //    combined by a butterfly over lane distances 4, 2, 1; x_j = score * (1 / sqrt(D));
 //  - per part: m_c = max x_j; S_c: thread i adds exp(x_j - m_c) for j = lo + i, lo + i + 128, ... in order, warp
@@ -42,6 +43,13 @@ constexpr int kParts = 8;
 constexpr int kThreads = 128;
 constexpr int kWarps = kThreads / 32;
 constexpr int kSegments = 8;  // lanes per key in the score dot product
+// The cluster kernel's CTA: 8 warps play the 128 slots and the 4 warp chains of a part (kThreads, kWarps above are
+// the restated order's), so each warp's share of the score and P·V loops is half as long.
+// Registers are capped at 3 CTAs per SM (80 per thread): the decode step's kernels become resident early under
+// programmatic dependent launch only while the neighbouring kernels' CTAs fit beside them (measured on the
+// Qwen3-0.6B decode step: uncapped, 118 registers, 1496 tok/s; capped 1657; capped at 4 CTAs, spilling, 1560).
+constexpr int kCtaThreads = 256;
+constexpr int kCtaWarps = kCtaThreads / 32;
 
 // A lane's kD / 32 values of one V row, loaded raw (so several rows can be in flight) and unpacked at use.
 template <int kD>
@@ -59,6 +67,39 @@ struct VRow<64> {
 
 template <>
 struct VRow<128> {
+    using Raw = uint2;
+    static __device__ __forceinline__ Raw load(const bf16* p) { return __ldg(reinterpret_cast<const uint2*>(p)); }
+    static __device__ __forceinline__ void unpack(Raw w, float (&v)[4]) {
+        v[0] = bf16_lo(w.x);
+        v[1] = bf16_hi(w.x);
+        v[2] = bf16_lo(w.y);
+        v[3] = bf16_hi(w.y);
+    }
+};
+
+// P·V with two hardware warps per warp chain: a lane's kD / 64 values of one V row (the chain's half of the dims).
+template <int kD>
+struct VHalf;
+
+template <>
+struct VHalf<64> {
+    using Raw = unsigned short;
+    static __device__ __forceinline__ Raw load(const bf16* p) { return __ldg(reinterpret_cast<const unsigned short*>(p)); }
+    static __device__ __forceinline__ void unpack(Raw w, float (&v)[1]) { v[0] = __uint_as_float(static_cast<uint32_t>(w) << 16); }
+};
+
+template <>
+struct VHalf<128> {
+    using Raw = uint32_t;
+    static __device__ __forceinline__ Raw load(const bf16* p) { return __ldg(reinterpret_cast<const unsigned int*>(p)); }
+    static __device__ __forceinline__ void unpack(Raw w, float (&v)[2]) {
+        v[0] = bf16_lo(w);
+        v[1] = bf16_hi(w);
+    }
+};
+
+template <>
+struct VHalf<256> {
     using Raw = uint2;
     static __device__ __forceinline__ Raw load(const bf16* p) { return __ldg(reinterpret_cast<const uint2*>(p)); }
     static __device__ __forceinline__ void unpack(Raw w, float (&v)[4]) {
@@ -163,11 +204,11 @@ __device__ __forceinline__ void norm_rope_head(const bf16* src, uint4 w_first, u
 }
 
 template <int kD, bool kFused, bool kStage>
-__global__ void __launch_bounds__(kThreads) decoder_attention_kernel(const AttentionParams p, int64_t max_part) {
+__global__ void __launch_bounds__(kCtaThreads, 3) decoder_attention_kernel(const AttentionParams p, int64_t max_part) {
     constexpr int kSeg = kD / kSegments;       // dims per score segment
     constexpr int kSegChunks = kSeg / 8;       // 16-byte chunks per segment
     constexpr int kKeysPerIter = 32 / kSegments;
-    constexpr int kDimsPerLane = kD / 32;
+    constexpr int kDimsPerLane = kD / 64;      // P·V: a lane's dims of its chain's half
     constexpr int kFinal = kD / kParts;        // context dims each CTA finishes
     // Loads issued together: warp iterations of score loads, and V rows per warp. Measured on the Qwen3-0.6B decode
     // step: 2 and 4 took 691 us per token, 4 and 8 took 699; 4 and 16, or 2 and 2, were slower still.
@@ -176,7 +217,7 @@ __global__ void __launch_bounds__(kThreads) decoder_attention_kernel(const Atten
     // Dynamic shared memory: this part's scores (then exp values, then probabilities), and with kStage the part's
     // cached key and value rows.
     extern __shared__ __align__(16) float s_e[];
-    __shared__ float s_red[kWarps];
+    __shared__ float s_red[kCtaWarps];
     __shared__ float s_local;             // this part's max
     __shared__ float s_m[kParts];         // every part's max and exp sum, pushed here by each part
     __shared__ float s_s[kParts];
@@ -299,7 +340,8 @@ __global__ void __launch_bounds__(kThreads) decoder_attention_kernel(const Atten
             }
         }
 
-        // Scores: 4 keys per warp iteration, 8 lanes per key; kScoreBatch iterations' loads in flight.
+        // Scores: 4 keys per warp iteration, 8 lanes per key, all warps of the CTA; kScoreBatch iterations' loads
+        // in flight.
         const int sub = lane % kSegments;
         const int slot = lane / kSegments;
         float2 qv[kSegChunks][4];
@@ -311,7 +353,7 @@ __global__ void __launch_bounds__(kThreads) decoder_attention_kernel(const Atten
                 unpack_pairs(ld_cached(p.q + (t * p.q_heads + h) * kD + sub * kSeg + c * 8), qv[c]);
             }
         }
-        constexpr int kIterKeys = kWarps * kKeysPerIter;
+        constexpr int kIterKeys = kCtaWarps * kKeysPerIter;
         for (int i0 = warp * kKeysPerIter; i0 < n; i0 += kIterKeys * kScoreBatch) {
             uint4 kv[kScoreBatch][kSegChunks];
     #pragma unroll
@@ -351,7 +393,7 @@ __global__ void __launch_bounds__(kThreads) decoder_attention_kernel(const Atten
 
         // This part's maximum and its sum of exp(x - max) (slot order, warp butterfly, warps in order).
         float mx = -INFINITY;
-        for (int i = threadIdx.x; i < n; i += kThreads) {
+        for (int i = threadIdx.x; i < n; i += kCtaThreads) {
             mx = fmaxf(mx, s_e[i]);
         }
         mx = group_max<32>(mx);
@@ -362,20 +404,23 @@ __global__ void __launch_bounds__(kThreads) decoder_attention_kernel(const Atten
         if (threadIdx.x == 0) {
             float m = s_red[0];
     #pragma unroll
-            for (int w = 1; w < kWarps; ++w) {
+            for (int w = 1; w < kCtaWarps; ++w) {
                 m = fmaxf(m, s_red[w]);
             }
             s_local = m;
         }
         __syncthreads();
         const float local_max = s_local;
+        // The 128 slot chains are the first 4 warps' lanes (the order restated by the oracle).
         float sum = 0.0f;
-        for (int i = threadIdx.x; i < n; i += kThreads) {
-            sum = sum + pexp(s_e[i] - local_max);
+        if (threadIdx.x < kThreads) {
+            for (int i = threadIdx.x; i < n; i += kThreads) {
+                sum = sum + pexp(s_e[i] - local_max);
+            }
         }
         sum = group_sum<32>(sum);
         __syncthreads();  // s_red is reused
-        if (lane == 0) {
+        if (lane == 0 && warp < kWarps) {
             s_red[warp] = sum;
         }
         __syncthreads();
@@ -410,29 +455,31 @@ __global__ void __launch_bounds__(kThreads) decoder_attention_kernel(const Atten
             total = total + __shfl_sync(0xffffffffu, term, r);
         }
 
-        for (int i = threadIdx.x; i < n; i += kThreads) {
+        for (int i = threadIdx.x; i < n; i += kCtaThreads) {
             s_e[i] = round_to_bf16(pexp(s_e[i] - gmax) / total);
         }
         __syncthreads();
 
-        // Probabilities times V: warp w takes keys lo + w, lo + w + 4, ..., kValueBatch rows in flight.
+        // Probabilities times V: warp chain w = warp % 4 takes keys lo + w, lo + w + 4, ... in order (the restated
+        // order); the two hardware warps of a chain take half of the dims each; kValueBatch rows in flight.
+        const int chain = warp % kWarps;
+        const int dim0 = (warp / kWarps) * (kD / 2) + lane * kDimsPerLane;
         float a[kDimsPerLane];
     #pragma unroll
         for (int d = 0; d < kDimsPerLane; ++d) {
             a[d] = 0.0f;
         }
-        const bf16* vbase = p.v_cache + kvh * kD + lane * kDimsPerLane;
-        for (int i0 = warp; i0 < n; i0 += kWarps * kValueBatch) {
-            typename VRow<kD>::Raw raw[kValueBatch];
+        const bf16* vbase = p.v_cache + kvh * kD + dim0;
+        for (int i0 = chain; i0 < n; i0 += kWarps * kValueBatch) {
+            typename VHalf<kD>::Raw raw[kValueBatch];
     #pragma unroll
             for (int u = 0; u < kValueBatch; ++u) {
                 const int i = i0 + u * kWarps;
                 if (i < n) {
                     if constexpr (kStage) {
-                        raw[u] = *reinterpret_cast<const typename VRow<kD>::Raw*>(s_vt + i * kD +
-                                                                                 lane * kDimsPerLane);
+                        raw[u] = *reinterpret_cast<const typename VHalf<kD>::Raw*>(s_vt + i * kD + dim0);
                     } else {
-                        raw[u] = VRow<kD>::load(vbase + (lo + i) * kv_row);
+                        raw[u] = VHalf<kD>::load(vbase + (lo + i) * kv_row);
                     }
                 }
             }
@@ -442,23 +489,27 @@ __global__ void __launch_bounds__(kThreads) decoder_attention_kernel(const Atten
                 if (i < n) {
                     const float pj = s_e[i];
                     float v[kDimsPerLane];
-                    VRow<kD>::unpack(raw[u], v);
-                    // p_j * v_j as packed products (exact: bf16 x bf16), added in dimension chains as before.
+                    VHalf<kD>::unpack(raw[u], v);
+                    if constexpr (kDimsPerLane >= 2) {
+                        // p_j * v_j as packed products (exact: bf16 x bf16), added in the dimension chains.
     #pragma unroll
-                    for (int d = 0; d < kDimsPerLane; d += 2) {
-                        const float2 pv = __fmul2_rn(make_float2(pj, pj), make_float2(v[d], v[d + 1]));
-                        a[d] = a[d] + pv.x;
-                        a[d + 1] = a[d + 1] + pv.y;
+                        for (int d = 0; d < kDimsPerLane; d += 2) {
+                            const float2 pv = __fmul2_rn(make_float2(pj, pj), make_float2(v[d], v[d + 1]));
+                            a[d] = a[d] + pv.x;
+                            a[d + 1] = a[d + 1] + pv.y;
+                        }
+                    } else {
+                        a[0] = a[0] + pj * v[0];
                     }
                 }
             }
         }
     #pragma unroll
         for (int d = 0; d < kDimsPerLane; ++d) {
-            s_acc[warp][lane * kDimsPerLane + d] = a[d];
+            s_acc[chain][dim0 + d] = a[d];
         }
         __syncthreads();
-        for (int d = threadIdx.x; d < kD; d += kThreads) {
+        for (int d = threadIdx.x; d < kD; d += kCtaThreads) {
             float part = s_acc[0][d];
     #pragma unroll
             for (int w = 1; w < kWarps; ++w) {
@@ -675,7 +726,7 @@ cudaError_t launch_attention_variant(const AttentionParams& p, int64_t max_part,
         }
     }
     const int64_t blocks = (p.T + p.queries_per_cluster - 1) / p.queries_per_cluster * p.q_heads * kParts;
-    return runtime::launch_smem(kernel, dim3(static_cast<unsigned>(blocks)), dim3(kThreads), smem, s,
+    return runtime::launch_smem(kernel, dim3(static_cast<unsigned>(blocks)), dim3(kCtaThreads), smem, s,
                                 static_cast<unsigned>(kParts), p, max_part);
 }
 

@@ -347,12 +347,14 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_fast_kernel(const LinearPara
 // as in gemv_fast_kernel and each warp takes rows r, r + kStagedWarps, ... of the slice from shared memory.
 // 8 warps per CTA: measured on the Qwen3-0.6B decode step, 670 us per token against 692 with 16 warps, 892 with 4
 // (8 rows per warp) and 759 with 32.
+// At most 85 registers (3 CTAs per SM): the decode step's next kernels must fit beside a staged CTA to become
+// resident early (Qwen3-0.6B decode: 1595 tok/s with 2 CTAs per SM, 1657 with 3; 4, spilling: 1640).
 constexpr int kStagedThreads = 256;
 constexpr int kStagedWarps = kStagedThreads / 32;
 constexpr int kStagedRowIters = 4;  // rows a warp may own: kStagedWarps * 4 rows per CTA at most
 
 template <LinearEpilogue kEpi, int kC>
-__global__ void __launch_bounds__(kStagedThreads, 2) gemv_staged_kernel(const LinearParams p, int64_t rows_per_cta) {
+__global__ void __launch_bounds__(kStagedThreads, 3) gemv_staged_kernel(const LinearParams p, int64_t rows_per_cta) {
     extern __shared__ __align__(128) uint4 s_w[];
     __shared__ __align__(8) uint64_t s_bar;
     asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
@@ -413,10 +415,11 @@ __global__ void __launch_bounds__(kStagedThreads, 2) gemv_staged_kernel(const Li
             res_pre[k] = (lane == 0 && r < nrows) ? Vec16<bf16>::load1(p.residual, r0 + r) : 0.0f;
         }
     }
-    // Without a held (and normalised) row, the whole input row is still loaded here, right after the wait, so its
-    // latency overlaps the residual load and the wait for the staged slice.
-    uint4 xraw[kHoldX ? 1 : kC];
-    if constexpr (!kHoldX) {
+    // Without a held (and normalised) row, the whole input row (up to K = 2048: more would double the registers
+    // of a CTA and keep the next kernels' CTAs from becoming resident early) is still loaded here, right after the
+    // wait, so its latency overlaps the residual load and the wait for the staged slice.
+    uint4 xraw[kHoldX || kC > 8 ? 1 : kC];
+    if constexpr (!kHoldX && kC <= 8) {
 #pragma unroll
         for (int i = 0; i < kC; ++i) {
             xraw[i] = ld_cached(xrow + (lane + 32 * i) * 8);
@@ -520,8 +523,10 @@ __global__ void __launch_bounds__(kStagedThreads, 2) gemv_staged_kernel(const Li
                 for (int q = 0; q < 4; ++q) {
                     xq[q] = xp[i][q];
                 }
-            } else {
+            } else if constexpr (kC <= 8) {
                 unpack_pairs(xraw[i], xq);
+            } else {
+                unpack_pairs(ld_cached(xrow + (lane + 32 * i) * 8), xq);
             }
 #pragma unroll
             for (int mat = 0; mat < kMats; ++mat) {
