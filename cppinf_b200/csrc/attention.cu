@@ -117,42 +117,9 @@ struct VRow<256> {
     static __device__ __forceinline__ void unpack(Raw w, float (&v)[8]) { Vec16<bf16>::unpack(w, v); }
 };
 
+// Eight elements of a score segment: fused multiply-adds in element order (fma_bf16x8, common.cuh).
 __device__ __forceinline__ float dot8(uint4 a, uint4 b, float acc) {
-    acc = acc + bf16_lo(a.x) * bf16_lo(b.x);
-    acc = acc + bf16_hi(a.x) * bf16_hi(b.x);
-    acc = acc + bf16_lo(a.y) * bf16_lo(b.y);
-    acc = acc + bf16_hi(a.y) * bf16_hi(b.y);
-    acc = acc + bf16_lo(a.z) * bf16_lo(b.z);
-    acc = acc + bf16_hi(a.z) * bf16_hi(b.z);
-    acc = acc + bf16_lo(a.w) * bf16_lo(b.w);
-    acc = acc + bf16_hi(a.w) * bf16_hi(b.w);
-    return acc;
-}
-
-// dot8 with the query chunk already unpacked into f32 pairs (elements 2q, 2q + 1 of word q): one packed product
-// per key word, then the scalar adds in element order. bf16 x bf16 products are exact in f32, so the sum is the
-// same as dot8's bit for bit.
-__device__ __forceinline__ float dot8(const float2 (&a)[4], uint4 b, float acc) {
-    const float2 p0 = __fmul2_rn(a[0], make_float2(bf16_lo(b.x), bf16_hi(b.x)));
-    const float2 p1 = __fmul2_rn(a[1], make_float2(bf16_lo(b.y), bf16_hi(b.y)));
-    const float2 p2 = __fmul2_rn(a[2], make_float2(bf16_lo(b.z), bf16_hi(b.z)));
-    const float2 p3 = __fmul2_rn(a[3], make_float2(bf16_lo(b.w), bf16_hi(b.w)));
-    acc = acc + p0.x;
-    acc = acc + p0.y;
-    acc = acc + p1.x;
-    acc = acc + p1.y;
-    acc = acc + p2.x;
-    acc = acc + p2.y;
-    acc = acc + p3.x;
-    acc = acc + p3.y;
-    return acc;
-}
-
-__device__ __forceinline__ void unpack_pairs(uint4 x, float2 (&xp)[4]) {
-    xp[0] = make_float2(bf16_lo(x.x), bf16_hi(x.x));
-    xp[1] = make_float2(bf16_lo(x.y), bf16_hi(x.y));
-    xp[2] = make_float2(bf16_lo(x.z), bf16_hi(x.z));
-    xp[3] = make_float2(bf16_lo(x.w), bf16_hi(x.w));
+    return fma_bf16x8(a, b, acc);
 }
 
 // Per-head RMSNorm + RoPE of one raw head vector into shared memory, with exactly the arithmetic of
@@ -344,13 +311,13 @@ __global__ void __launch_bounds__(kCtaThreads, 3) decoder_attention_kernel(const
         // in flight.
         const int sub = lane % kSegments;
         const int slot = lane / kSegments;
-        float2 qv[kSegChunks][4];
+        uint4 qv[kSegChunks];
     #pragma unroll
         for (int c = 0; c < kSegChunks; ++c) {
             if constexpr (kFused) {
-                unpack_pairs(*reinterpret_cast<const uint4*>(s_q + sub * kSeg + c * 8), qv[c]);
+                qv[c] = *reinterpret_cast<const uint4*>(s_q + sub * kSeg + c * 8);
             } else {
-                unpack_pairs(ld_cached(p.q + (t * p.q_heads + h) * kD + sub * kSeg + c * 8), qv[c]);
+                qv[c] = ld_cached(p.q + (t * p.q_heads + h) * kD + sub * kSeg + c * 8);
             }
         }
         constexpr int kIterKeys = kCtaWarps * kKeysPerIter;
@@ -490,16 +457,18 @@ __global__ void __launch_bounds__(kCtaThreads, 3) decoder_attention_kernel(const
                     const float pj = s_e[i];
                     float v[kDimsPerLane];
                     VHalf<kD>::unpack(raw[u], v);
+                    // a[d] = fma(p_j, v_j[d], a[d]) (p_j is a bf16 value, so each product is exact as in
+                    // fma_bf16x2); neighbouring dims are separate chains, advanced two at a time.
                     if constexpr (kDimsPerLane >= 2) {
-                        // p_j * v_j as packed products (exact: bf16 x bf16), added in the dimension chains.
     #pragma unroll
                         for (int d = 0; d < kDimsPerLane; d += 2) {
-                            const float2 pv = __fmul2_rn(make_float2(pj, pj), make_float2(v[d], v[d + 1]));
-                            a[d] = a[d] + pv.x;
-                            a[d + 1] = a[d + 1] + pv.y;
+                            const float2 r = __ffma2_rn(make_float2(pj, pj), make_float2(v[d], v[d + 1]),
+                                                        make_float2(a[d], a[d + 1]));
+                            a[d] = r.x;
+                            a[d + 1] = r.y;
                         }
                     } else {
-                        a[0] = a[0] + pj * v[0];
+                        a[0] = __fmaf_rn(pj, v[0], a[0]);
                     }
                 }
             }
@@ -683,7 +652,7 @@ __global__ void __launch_bounds__(kRowThreads, kD >= 256 ? 2 : 3) attention_rows
                 VRow<kD>::unpack(raw[u], v);
 #pragma unroll
                 for (int d = 0; d < kDimsPerLane; ++d) {
-                    a[u % kWarps][d] = a[u % kWarps][d] + pj * v[d];
+                    a[u % kWarps][d] = __fmaf_rn(pj, v[d], a[u % kWarps][d]);
                 }
             }
         }

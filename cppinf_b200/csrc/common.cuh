@@ -194,6 +194,27 @@ __device__ __forceinline__ float bf16_hi(uint32_t packed) {
     return __uint_as_float(packed & 0xffff0000u);
 }
 
+// Dot-product accumulation of bf16 operands: acc = fma(a, b, acc), rounded once. A product of two bf16 values has at
+// most 16 significant bits, so wherever it lies in the f32 normal range it is exact and the fused multiply-add equals
+// the separately rounded `acc + a * b`; the CPU oracle restates it with fmaf, which agrees for every operand.
+// Mixed-precision form (bf16 operands straight from the packed words, f32 accumulator): one instruction per element.
+__device__ __forceinline__ float fma_bf16x2(uint32_t a, uint32_t b, float acc) {  // low halves, then high halves
+    asm("{\n\t.reg .b16 al, ah, bl, bh;\n\tmov.b32 {al, ah}, %1;\n\tmov.b32 {bl, bh}, %2;\n\t"
+        "fma.rn.f32.bf16 %0, al, bl, %0;\n\tfma.rn.f32.bf16 %0, ah, bh, %0;\n\t}"
+        : "+f"(acc)
+        : "r"(a), "r"(b));
+    return acc;
+}
+
+// Eight elements of two 16-byte bf16 vectors, accumulated in element order.
+__device__ __forceinline__ float fma_bf16x8(uint4 a, uint4 b, float acc) {
+    acc = fma_bf16x2(a.x, b.x, acc);
+    acc = fma_bf16x2(a.y, b.y, acc);
+    acc = fma_bf16x2(a.z, b.z, acc);
+    acc = fma_bf16x2(a.w, b.w, acc);
+    return acc;
+}
+
 // Packs two f32 values into a bf16x2 word (lo in the low half), round-to-nearest-even.
 __device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
     uint32_t r;

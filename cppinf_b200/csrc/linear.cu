@@ -22,6 +22,8 @@
 #include <mutex>
 #include <string>
 
+#include <type_traits>
+
 #include "common.cuh"
 #include "decoder.h"
 #include "pexp.cuh"
@@ -35,56 +37,21 @@ constexpr int kWarps = kThreads / 32;
 constexpr int kLoads = 16;  // 16-byte weight loads a lane keeps in flight in the single-row kernel
 constexpr int kTileRows = 16;
 
+// One 16-byte chunk of the canonical dot product: 8 fused multiply-adds in element order (fma_bf16x8, common.cuh).
 __device__ __forceinline__ float dot_chunk(uint4 x, uint4 w, float acc) {
-    acc = acc + bf16_lo(x.x) * bf16_lo(w.x);
-    acc = acc + bf16_hi(x.x) * bf16_hi(w.x);
-    acc = acc + bf16_lo(x.y) * bf16_lo(w.y);
-    acc = acc + bf16_hi(x.y) * bf16_hi(w.y);
-    acc = acc + bf16_lo(x.z) * bf16_lo(w.z);
-    acc = acc + bf16_hi(x.z) * bf16_hi(w.z);
-    acc = acc + bf16_lo(x.w) * bf16_lo(w.w);
-    acc = acc + bf16_hi(x.w) * bf16_hi(w.w);
-    return acc;
+    return fma_bf16x8(x, w, acc);
 }
 
-// Same products with the weight chunk already unpacked.
+// Same products with the weight chunk already unpacked (exact f32 copies of bf16 values).
 __device__ __forceinline__ float dot_chunk(uint4 x, const float (&w)[8], float acc) {
-    acc = acc + bf16_lo(x.x) * w[0];
-    acc = acc + bf16_hi(x.x) * w[1];
-    acc = acc + bf16_lo(x.y) * w[2];
-    acc = acc + bf16_hi(x.y) * w[3];
-    acc = acc + bf16_lo(x.z) * w[4];
-    acc = acc + bf16_hi(x.z) * w[5];
-    acc = acc + bf16_lo(x.w) * w[6];
-    acc = acc + bf16_hi(x.w) * w[7];
-    return acc;
-}
-
-// An input chunk as f32 pairs: pair q holds elements 2q and 2q + 1 (the low and high halves of 32-bit word q).
-__device__ __forceinline__ void unpack_pairs(uint4 x, float2 (&xp)[4]) {
-    xp[0] = make_float2(bf16_lo(x.x), bf16_hi(x.x));
-    xp[1] = make_float2(bf16_lo(x.y), bf16_hi(x.y));
-    xp[2] = make_float2(bf16_lo(x.z), bf16_hi(x.z));
-    xp[3] = make_float2(bf16_lo(x.w), bf16_hi(x.w));
-}
-
-// dot_chunk with the input already unpacked into pairs: one packed product per weight word, then the two scalar
-// adds in element order. A product of two bf16 values is exact in f32, so the packed product equals the scalar one
-// and the sum is the canonical one bit for bit. (The adds stay scalar: a packed add fed by a packed product would be
-// contracted into a fused multiply-add.)
-__device__ __forceinline__ float dot_chunk(const float2 (&xp)[4], uint4 w, float acc) {
-    const float2 p0 = __fmul2_rn(xp[0], make_float2(bf16_lo(w.x), bf16_hi(w.x)));
-    const float2 p1 = __fmul2_rn(xp[1], make_float2(bf16_lo(w.y), bf16_hi(w.y)));
-    const float2 p2 = __fmul2_rn(xp[2], make_float2(bf16_lo(w.z), bf16_hi(w.z)));
-    const float2 p3 = __fmul2_rn(xp[3], make_float2(bf16_lo(w.w), bf16_hi(w.w)));
-    acc = acc + p0.x;
-    acc = acc + p0.y;
-    acc = acc + p1.x;
-    acc = acc + p1.y;
-    acc = acc + p2.x;
-    acc = acc + p2.y;
-    acc = acc + p3.x;
-    acc = acc + p3.y;
+    acc = __fmaf_rn(bf16_lo(x.x), w[0], acc);
+    acc = __fmaf_rn(bf16_hi(x.x), w[1], acc);
+    acc = __fmaf_rn(bf16_lo(x.y), w[2], acc);
+    acc = __fmaf_rn(bf16_hi(x.y), w[3], acc);
+    acc = __fmaf_rn(bf16_lo(x.z), w[4], acc);
+    acc = __fmaf_rn(bf16_hi(x.z), w[5], acc);
+    acc = __fmaf_rn(bf16_lo(x.w), w[6], acc);
+    acc = __fmaf_rn(bf16_hi(x.w), w[7], acc);
     return acc;
 }
 
@@ -492,16 +459,6 @@ __global__ void __launch_bounds__(kStagedThreads, 3) gemv_staged_kernel(const Li
         return;
     }
 
-    // The held input row unpacked once into f32 pairs for every row of the slice (the step is issue-bound: the
-    // per-row unpacking of the input was a third of the body's instructions).
-    float2 xp[kHoldX ? kC : 1][4];
-    if constexpr (kHoldX) {
-#pragma unroll
-        for (int i = 0; i < kC; ++i) {
-            unpack_pairs(xv[i], xp[i]);
-        }
-    }
-
     // Each warp takes rows warp, warp + kStagedWarps, ... of the slice, one at a time (measured on B200:
     // interleaving four rows per warp was slower).
 #pragma unroll
@@ -517,20 +474,17 @@ __global__ void __launch_bounds__(kStagedThreads, 3) gemv_staged_kernel(const Li
         }
 #pragma unroll
         for (int i = 0; i < kC; ++i) {
-            float2 xq[4];
+            uint4 xr;
             if constexpr (kHoldX) {
-#pragma unroll
-                for (int q = 0; q < 4; ++q) {
-                    xq[q] = xp[i][q];
-                }
+                xr = xv[i];
             } else if constexpr (kC <= 8) {
-                unpack_pairs(xraw[i], xq);
+                xr = xraw[i];
             } else {
-                unpack_pairs(ld_cached(xrow + (lane + 32 * i) * 8), xq);
+                xr = ld_cached(xrow + (lane + 32 * i) * 8);
             }
 #pragma unroll
             for (int mat = 0; mat < kMats; ++mat) {
-                acc[mat] = dot_chunk(xq, s_w[(mat * rows_per_cta + r) * kRowChunks + lane + 32 * i], acc[mat]);
+                acc[mat] = dot_chunk(xr, s_w[(mat * rows_per_cta + r) * kRowChunks + lane + 32 * i], acc[mat]);
             }
         }
 #pragma unroll
@@ -800,8 +754,8 @@ __global__ void __launch_bounds__(kThreads) linear_rows_kernel(const LinearParam
 }
 
 // Prefill projection with the 16-row input tile staged in shared memory as f32, interleaved by row pairs so that one
-// packed f32x2 product serves two rows, and two weight rows (or the gate and up rows of one output) per warp, so each
-// staged input chunk feeds 16 multiply-adds. Same per-output order as the other kernels.
+// packed f32x2 fused multiply-add advances two rows, and two weight rows (or the gate and up rows of one output) per
+// warp, so each staged input chunk feeds 16 multiply-adds. Same per-output order as the other kernels.
 template <LinearEpilogue kEpi>
 __global__ void __launch_bounds__(kThreads, 2) linear_rows_f32x_kernel(const LinearParams p) {
     // [kTileRows / 2 row pairs][4 element pairs][K / 8 chunks]: float4 (x[2q][e], x[2q+1][e], x[2q][e+1],
@@ -879,9 +833,6 @@ __global__ void __launch_bounds__(kThreads, 2) linear_rows_f32x_kernel(const Lin
                     }
 #pragma unroll
                     for (int q = 0; q < kPairs; ++q) {
-                        // x[2q][e] * w[e] and x[2q+1][e] * w[e] as one packed product, then the two sums as scalar
-                        // adds in element order (a packed add after a packed product would be contracted into a
-                        // fused multiply-add by the code generator).
                         float2 xp[8];
 #pragma unroll
                         for (int k = 0; k < 4; ++k) {
@@ -891,16 +842,15 @@ __global__ void __launch_bounds__(kThreads, 2) linear_rows_f32x_kernel(const Lin
                         }
 #pragma unroll
                         for (int sl = 0; sl < kSlots; ++sl) {
-                            float a0 = acc[sl][2 * q];
-                            float a1 = acc[sl][2 * q + 1];
+                            // Rows 2q and 2q + 1 are separate chains: one packed fused multiply-add advances
+                            // both, each rounded once (fma_bf16x2's arithmetic; the inputs are exact f32 copies).
+                            float2 a01 = make_float2(acc[sl][2 * q], acc[sl][2 * q + 1]);
 #pragma unroll
                             for (int e = 0; e < 8; ++e) {
-                                const float2 pr = __fmul2_rn(xp[e], make_float2(w[sl][e], w[sl][e]));
-                                a0 = a0 + pr.x;
-                                a1 = a1 + pr.y;
+                                a01 = __ffma2_rn(xp[e], make_float2(w[sl][e], w[sl][e]), a01);
                             }
-                            acc[sl][2 * q] = a0;
-                            acc[sl][2 * q + 1] = a1;
+                            acc[sl][2 * q] = a01.x;
+                            acc[sl][2 * q + 1] = a01.y;
                         }
                     }
                 }
@@ -968,7 +918,13 @@ __global__ void __launch_bounds__(kThreads) matmul_generic_kernel(const MatmulAr
         float acc = 0.0f;
         for (int64_t c = lane; c < nchunks; c += 32) {
             for (int64_t e = c * chunk; e < (c + 1) * chunk; ++e) {
-                acc = acc + Vec16<Tx>::load1(a.x, xrow + e * a.xs[2]) * Vec16<Tw>::load1(a.w, wcol + e * a.ws[1]);
+                const float xv = Vec16<Tx>::load1(a.x, xrow + e * a.xs[2]);
+                const float wv = Vec16<Tw>::load1(a.w, wcol + e * a.ws[1]);
+                if constexpr (std::is_same_v<Tx, bf16> && std::is_same_v<Tw, bf16>) {
+                    acc = __fmaf_rn(xv, wv, acc);  // bf16 operands: fused, as in the vector kernels
+                } else {
+                    acc = acc + xv * wv;  // an f32 operand: separately rounded product and sum
+                }
             }
         }
         acc = group_sum<32>(acc);

@@ -404,8 +404,10 @@ void oracle_linear(int dtype, const void* x, const void* weight, void* y, int64_
  *  - exp: the portable exponential below, in the attention softmax and in SiLU;
  *  - attention (qwen_attention.cpp:236-333 with the softmax of :164-235): the fixed partition order of
  *    oracle_decoder_attention.
- * A product of two bf16 values is exact in f32 (8 + 8 significant bits) unless it underflows, so accumulating
- * `acc + a * b` equals an FMA for every operand pair that occurs here. */
+ * Every product-accumulate of two bf16 values (a probability is a bf16 value too) is a fused multiply-add, fmaf,
+ * as on the device (fma.rn.f32.bf16). The product has at most 16 significant bits, so in the f32 normal range it is
+ * exact and the FMA equals `acc + a * b` with a separately rounded product; fmaf agrees with the device for every
+ * operand, subnormal products included. */
 
 /* Portable exp, written from the mathematics: Cody-Waite argument reduction x = n ln2 + r with ln2 split into a
  * 12-bit head (so n * head is exact for |n| <= 2^12) and an f32 tail, e^r by its Taylor polynomial to degree 7 in
@@ -501,7 +503,7 @@ void oracle_linear_canonical(const uint16_t* x, int64_t x_stride, const uint16_t
             for (int64_t c = 0; c < nchunks; ++c) {
                 float a = partial[c & 31];
                 for (int64_t e = c * chunk; e < (c + 1) * chunk; ++e) {
-                    a = a + xf[e] * bf16_to_f32(wr[e]);
+                    a = fmaf(xf[e], bf16_to_f32(wr[e]), a);
                 }
                 partial[c & 31] = a;
             }
@@ -535,7 +537,7 @@ void oracle_linear_canonical(const uint16_t* x, int64_t x_stride, const uint16_t
                     const float wv = bf16_to_f32(wr[e]);
                     const float* xk = xt + e * MB;
                     for (int mm = 0; mm < MB; ++mm) {
-                        a[mm] = a[mm] + xk[mm] * wv;
+                        a[mm] = fmaf(xk[mm], wv, a[mm]);
                     }
                 }
             }
@@ -595,7 +597,7 @@ void oracle_decoder_attention(const uint16_t* q, const uint16_t* kc, const uint1
             for (int64_t g = 0; g < G; ++g) {
                 float s = 0.0f;
                 for (int64_t d = g * seg; d < (g + 1) * seg; ++d) {
-                    s = s + bf16_to_f32(qv[d]) * bf16_to_f32(kv[d]);
+                    s = fmaf(bf16_to_f32(qv[d]), bf16_to_f32(kv[d]), s);
                 }
                 partial[g] = s;
             }
@@ -658,7 +660,7 @@ void oracle_decoder_attention(const uint16_t* q, const uint16_t* kc, const uint1
                 for (int64_t j = lo + w; j < hi; j += WARPS) {
                     const uint16_t* vv = vc + (j * hkv + kvh) * D;
                     for (int64_t d = 0; d < D; ++d) {
-                        a[d] = a[d] + e[j] * bf16_to_f32(vv[d]);
+                        a[d] = fmaf(e[j], bf16_to_f32(vv[d]), a[d]);
                     }
                 }
             }
@@ -683,12 +685,14 @@ void oracle_decoder_attention(const uint16_t* q, const uint16_t* kc, const uint1
  * and rhs [batch, k, n] with element strides (batch, row, column), every element read as f32 (bf16 widened
  * exactly), y[b, i, j] = sum_p lhs[b, i, p] rhs[b, p, j] in the canonical lane order (chunk 8 when k % 8 == 0, else
  * 1; lane l adds chunks l, l+32, ... in element order from +0; butterfly over lane distances 16..1), stored once in
- * y_dtype, y dense [batch, m, n]. Separately rounded multiply and add (-ffp-contract=off), as on the device. */
+ * y_dtype, y dense [batch, m, n]. Each step is a fused multiply-add when both operands are bf16 (their product is
+ * exact in f32 in the normal range; the device fuses it too), else a separately rounded multiply and add. */
 void oracle_matmul_canonical(int x_dtype, const void* x, const int64_t* xs, int w_dtype, const void* w,
                              const int64_t* ws, int y_dtype, void* y, int64_t batch, int64_t m, int64_t k,
                              int64_t n) {
     const int64_t chunk = k % 8 == 0 ? 8 : 1;
     const int64_t nchunks = k / chunk;
+    const int fused = x_dtype == DT_BF16 && w_dtype == DT_BF16;
 #pragma omp parallel for schedule(static)
     for (int64_t idx = 0; idx < batch * m * n; ++idx) {
         const int64_t b = idx / (m * n);
@@ -700,7 +704,7 @@ void oracle_matmul_canonical(int x_dtype, const void* x, const int64_t* xs, int 
             for (int64_t e = c * chunk; e < (c + 1) * chunk; ++e) {
                 const float xv = load(x_dtype, x, b * xs[0] + i * xs[1] + e * xs[2]);
                 const float wv = load(w_dtype, w, b * ws[0] + e * ws[1] + j * ws[2]);
-                a = a + xv * wv;
+                a = fused ? fmaf(xv, wv, a) : a + xv * wv;
             }
             partial[c & 31] = a;
         }

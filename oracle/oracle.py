@@ -76,6 +76,18 @@ def ulp_distance(a_bits: np.ndarray, b_bits: np.ndarray) -> np.ndarray:
     return np.abs(ordered(a_bits) - ordered(b_bits))
 
 
+def cpu_has_fma() -> bool:
+    """True when the host CPU has FMA3 (read from /proc/cpuinfo; assumed present where that file does not exist)."""
+    try:
+        with open("/proc/cpuinfo") as f:
+            for line in f:
+                if line.startswith("flags"):
+                    return "fma" in line.split()
+    except OSError:
+        return True
+    return True
+
+
 class Oracle:
     """The C restatement (oracle/oracle.c)."""
 
@@ -83,6 +95,8 @@ class Oracle:
         path = Path(path or os.environ.get("CPPINF_ORACLE_LIB", ORACLE_LIB))
         if not path.exists():
             raise RuntimeError(f"oracle library missing at {path}; build it with `make -C oracle`")
+        if not cpu_has_fma():
+            raise RuntimeError("the oracle is built with FMA3 instructions (its fmaf dot products); this CPU lacks them")
         self.lib = ctypes.CDLL(str(path))
         sig = {
             "oracle_f32_to_bf16": [_p, _p, _l],

@@ -60,6 +60,22 @@ def test_linear_bit_exact(ops, oracle, m, k, n):
     assert_bits_equal(got, oracle.linear_canonical(x, w), "linear")
 
 
+@pytest.mark.parametrize("m,k,n", [(1, 1024, 64), (16, 1024, 64), (1, 264, 9)])
+def test_linear_subnormal_products_bit_exact(ops, oracle, m, k, n):
+    # Operands scaled by 2^-70: every product lies near 2^-140, where a separately rounded product would lose bits
+    # and only the fused multiply-add keeps them. Device (fma.rn.f32.bf16) and oracle (fmaf) still agree bit for
+    # bit, in the bf16 projection and in the f32 output of the generic matmul.
+    rng = np.random.default_rng(31 + m + k)
+    scale = np.float32(2.0**-70)
+    x = f32_to_bf16(bf16_to_f32(seeded_bf16(rng, (m, k))) * scale)
+    w = f32_to_bf16(bf16_to_f32(seeded_bf16(rng, (n, k))) * scale)
+    assert_bits_equal(to_host(ops.linear(to_dev(x), to_dev(w))), oracle.linear_canonical(x, w), "tiny linear")
+    got = to_host(ops.matmul(to_dev(x), to_dev(w).t(), output_dtype=torch.float32))
+    want = oracle.linear_canonical(x, w, f32_out=True)
+    assert np.array_equal(got.view(np.uint32), want.view(np.uint32))
+    assert np.any(want != 0) and np.all(np.abs(want) < 2.0**-120)  # the case is really in the subnormal range
+
+
 def test_linear_strided_rows(ops, oracle):
     rng = np.random.default_rng(7)
     big = seeded_bf16(rng, (9, 1032))
