@@ -273,7 +273,13 @@ __global__ void __launch_bounds__(kCtaThreads, 3) decoder_attention_kernel(const
             wk_b = ld_cached(p.k_norm + kD / 2 + hl * 8);
         }
         if constexpr (kStage) {
-            grid_dependency_begin();
+            // One warp waits for the previous grid; the others wait at the block barrier, which orders their reads
+            // after that wait (waiting warps would otherwise take issue slots from the kernel still running).
+            if (warp == 0) {
+                asm volatile("griddepcontrol.wait;" ::: "memory");
+            }
+            __syncthreads();
+            asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
         }
 
         if constexpr (kFused) {
