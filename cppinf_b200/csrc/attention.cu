@@ -33,6 +33,7 @@
 #include "decoder.h"
 #include "pexp.cuh"
 #include "runtime.h"
+#include "tcgen05.cuh"
 
 namespace cg = cooperative_groups;
 
@@ -170,8 +171,16 @@ __device__ __forceinline__ void norm_rope_head(const bf16* src, uint4 w_first, u
     }
 }
 
+// The decode kernel's staging copies: TMA maps of the K and V caches, each a 3-D tensor [cap][Hkv][D] with a box of
+// {D, 1, rows} (one head's rows of a part, 2 KB apart in the cache, in one copy).
+struct StageMaps {
+    CUtensorMap k;
+    CUtensorMap v;
+};
+
 template <int kD, bool kFused, bool kStage>
-__global__ void __launch_bounds__(kCtaThreads, 3) decoder_attention_kernel(const AttentionParams p, int64_t max_part) {
+__global__ void __launch_bounds__(kCtaThreads, 3)
+    decoder_attention_kernel(const AttentionParams p, int64_t max_part, const __grid_constant__ StageMaps maps) {
     constexpr int kSeg = kD / kSegments;       // dims per score segment
     constexpr int kSegChunks = kSeg / 8;       // 16-byte chunks per segment
     constexpr int kKeysPerIter = 32 / kSegments;
@@ -236,26 +245,30 @@ __global__ void __launch_bounds__(kCtaThreads, 3) decoder_attention_kernel(const
 
         // kStage: rows [lo, staged_hi) (every cached row of this part before the new token) go to shared memory now;
         // the previous kernel in the stream writes neither them nor the sequence length.
-        bf16* s_kt = reinterpret_cast<bf16*>(s_e + ((max_part + 3) / 4) * 4);
+        // The staged tiles start on a 128-byte boundary (TMA destinations), after the scores.
+        char* const s_tiles = reinterpret_cast<char*>(s_e + ((max_part + 3) / 4) * 4);
+        bf16* s_kt = reinterpret_cast<bf16*>(s_tiles + ((128u - (smem_addr(s_tiles) & 127u)) & 127u));
         bf16* s_vt = s_kt + max_part * kD;
         const int64_t staged_hi = hi < pos ? hi : pos;
         const int64_t staged = staged_hi > lo ? staged_hi - lo : 0;
+        uint4 v_new = make_uint4(0u, 0u, 0u, 0u);
         float c_rope[kFused ? 8 : 1];
         float s_rope[kFused ? 8 : 1];
         uint4 wq_a, wq_b, wk_a, wk_b;
         if constexpr (kStage) {
+            // Two TMA copies of max_part rows each (the box), from row lo: rows past the part's cached ones (the new
+            // token's, later positions, or zeros past the cache) arrive too and are never read -- the new key comes
+            // from s_knew and the new value row is written over its slot after this wait. Measured on B200: one
+            // 256-byte bulk copy per row kept warp 0 issuing for ~6 us, past the end of the previous kernel.
             if (threadIdx.x == 0) {
                 mbar_init(&s_bar, 1);
-                mbar_arrive_expect_tx(&s_bar, static_cast<uint32_t>(staged * kD * 2 * 2));
-            }
-            __syncthreads();
-            if (warp == 0) {
-                for (int64_t r = lane; r < staged; r += 32) {
-                    const int64_t off = (lo + r) * kv_row + kvh * kD;
-                    bulk_copy_g2s(s_kt + r * kD, p.k_cache + off, kD * 2, &s_bar);
-                    bulk_copy_g2s(s_vt + r * kD, p.v_cache + off, kD * 2, &s_bar);
+                mbar_arrive_expect_tx(&s_bar, staged > 0 ? static_cast<uint32_t>(max_part * kD * 2 * 2) : 0u);
+                if (staged > 0) {
+                    tc::tma_load_3d(s_kt, &maps.k, 0, kvh, static_cast<int>(lo), &s_bar);
+                    tc::tma_load_3d(s_vt, &maps.v, 0, kvh, static_cast<int>(lo), &s_bar);
                 }
             }
+            __syncthreads();
         }
         if constexpr (kFused) {
             // RoPE angles of this position and the q/k norm weights: constants, read before the wait.
@@ -290,10 +303,9 @@ __global__ void __launch_bounds__(kCtaThreads, 3) decoder_attention_kernel(const
                 norm_rope_head<kD>(p.k_new + (t * p.kv_heads + kvh) * kD, wk_a, wk_b, c_rope, s_rope, p.eps, s_knew,
                                    lane);
             } else if (kStage && warp == 2 && i_new >= 0 && i_new < n && lane < kD / 8) {
-                // The new token's value row (written to the cache by the previous kernel) joins the staged rows, so
-                // the P·V loop reads shared memory only.
-                *reinterpret_cast<uint4*>(s_vt + i_new * kD + lane * 8) =
-                    ld_cached(p.v_cache + pos * kv_row + kvh * kD + lane * 8);
+                // The new token's value row (written to the cache by the previous kernel), stored into the staged
+                // tile after the copies have landed, so the P·V loop reads shared memory only.
+                v_new = ld_cached(p.v_cache + pos * kv_row + kvh * kD + lane * 8);
             }
             __syncthreads();
             if (rank == 0 && h % group == 0 && threadIdx.x < kD / 8) {
@@ -308,6 +320,9 @@ __global__ void __launch_bounds__(kCtaThreads, 3) decoder_attention_kernel(const
             // On a timeout the kernel still runs every cluster barrier below (with meaningless values), so no CTA of
             // the cluster is left waiting; the host sees the error flag.
             stage_failed = __syncthreads_or(arrived ? 0 : 1) != 0;
+            if (warp == 2 && i_new >= 0 && i_new < n && lane < kD / 8) {
+                *reinterpret_cast<uint4*>(s_vt + i_new * kD + lane * 8) = v_new;  // read after later barriers
+            }
             if (stage_failed && threadIdx.x == 0) {
                 atomicOr(p.error, 1u);
             }
@@ -691,7 +706,8 @@ constexpr std::size_t kMaxRowScoreBytes = 64 * 1024;
 constexpr std::size_t kMaxStagedBytes = 110 * 1024;
 
 template <int kD, bool kFused, bool kStage>
-cudaError_t launch_attention_variant(const AttentionParams& p, int64_t max_part, std::size_t smem, cudaStream_t s) {
+cudaError_t launch_attention_variant(const AttentionParams& p, int64_t max_part, std::size_t smem, cudaStream_t s,
+                                     const StageMaps& maps = StageMaps{}) {
     auto kernel = decoder_attention_kernel<kD, kFused, kStage>;
     if (smem > 48 * 1024) {
         const cudaError_t err =
@@ -702,7 +718,24 @@ cudaError_t launch_attention_variant(const AttentionParams& p, int64_t max_part,
     }
     const int64_t blocks = (p.T + p.queries_per_cluster - 1) / p.queries_per_cluster * p.q_heads * kParts;
     return runtime::launch_smem(kernel, dim3(static_cast<unsigned>(blocks)), dim3(kCtaThreads), smem, s,
-                                static_cast<unsigned>(kParts), p, max_part);
+                                static_cast<unsigned>(kParts), p, max_part, maps);
+}
+
+// TMA map of one cache [capacity][kv_heads][kD] with a box of one head's `rows` rows.
+template <int kD>
+bool make_stage_map(CUtensorMap* map, const bf16* cache, int64_t capacity, int kv_heads, int64_t rows) {
+    const tc::EncodeTiled encode = tc::encode_tiled();
+    if (encode == nullptr || (reinterpret_cast<uintptr_t>(cache) & 15u) != 0) {
+        return false;
+    }
+    const cuuint64_t dims[3] = {static_cast<cuuint64_t>(kD), static_cast<cuuint64_t>(kv_heads),
+                                static_cast<cuuint64_t>(capacity)};
+    const cuuint64_t strides[2] = {static_cast<cuuint64_t>(kD) * 2, static_cast<cuuint64_t>(kv_heads) * kD * 2};
+    const cuuint32_t box[3] = {static_cast<cuuint32_t>(kD), 1, static_cast<cuuint32_t>(rows)};
+    const cuuint32_t elem_strides[3] = {1, 1, 1};
+    return encode(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<bf16*>(cache), dims, strides, box,
+                  elem_strides, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
+                  CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
 // Prefill: a cluster takes several consecutive queries of one head in turn, so that a long prompt launches a few
@@ -720,10 +753,14 @@ cudaError_t launch_attention_dim(const AttentionParams& p, int64_t max_keys, cud
     const int64_t per_part = (max_keys + kParts - 1) / kParts;
     const int64_t max_part = per_part < 1 ? 1 : per_part;
     const std::size_t score_bytes = static_cast<std::size_t>((max_part + 3) / 4 * 4) * sizeof(float);
-    const std::size_t staged_bytes = score_bytes + static_cast<std::size_t>(max_part) * kD * 2 * 2;
+    // Staged tiles: 128 bytes of alignment slack after the scores, then max_part rows of K and of V.
+    const std::size_t staged_bytes = score_bytes + 128 + static_cast<std::size_t>(max_part) * kD * 2 * 2;
     if (p.q_norm != nullptr) {
-        if (p.error != nullptr && p.T == 1 && staged_bytes <= kMaxStagedBytes) {
-            return launch_attention_variant<kD, true, true>(p, max_part, staged_bytes, s);
+        StageMaps maps{};
+        if (p.error != nullptr && p.T == 1 && staged_bytes <= kMaxStagedBytes && max_part <= 256 &&
+            make_stage_map<kD>(&maps.k, p.k_cache, p.capacity, p.kv_heads, max_part) &&
+            make_stage_map<kD>(&maps.v, p.v_cache, p.capacity, p.kv_heads, max_part)) {
+            return launch_attention_variant<kD, true, true>(p, max_part, staged_bytes, s, maps);
         }
         return launch_attention_variant<kD, true, false>(p, max_part, score_bytes, s);
     }
