@@ -138,20 +138,22 @@ __device__ __forceinline__ void norm_rope_head(const bf16* src, uint4 w_first, u
     float b[8];
     Vec16<bf16>::unpack(ld_cached(src + hl * 8), a);
     Vec16<bf16>::unpack(ld_cached(src + kHalf + hl * 8), b);
+    // Products as packed f32x2 pairs (first-half element, second-half element), sums and differences scalar in the
+    // same order as rope.cu (a packed product feeding a packed add would be contracted into a fused multiply-add).
     float sa = 0.0f;
     float sb = 0.0f;
 #pragma unroll
     for (int j = 0; j < 8; ++j) {
-        sa = sa + a[j] * a[j];
-    }
-#pragma unroll
-    for (int j = 0; j < 8; ++j) {
-        sb = sb + b[j] * b[j];
+        const float2 v = make_float2(a[j], b[j]);
+        const float2 sq = __fmul2_rn(v, v);
+        sa = sa + sq.x;
+        sb = sb + sq.y;
     }
     const float ss = group_sum<kLanes>(sa + sb);
     const float mean = ss / static_cast<float>(kD);
     const float rms = sqrtf(mean + eps);
     const float inv = 1.0f / rms;
+    const float2 inv2 = make_float2(inv, inv);
     float wa[8];
     float wb[8];
     Vec16<bf16>::unpack(w_first, wa);
@@ -160,10 +162,13 @@ __device__ __forceinline__ void norm_rope_head(const bf16* src, uint4 w_first, u
     float out_b[8];
 #pragma unroll
     for (int j = 0; j < 8; ++j) {
-        const float n1 = round_to_bf16((a[j] * inv) * wa[j]);
-        const float n2 = round_to_bf16((b[j] * inv) * wb[j]);
-        out_a[j] = n1 * c[j] - n2 * s[j];
-        out_b[j] = n2 * c[j] + n1 * s[j];
+        const float2 x = __fmul2_rn(__fmul2_rn(make_float2(a[j], b[j]), inv2), make_float2(wa[j], wb[j]));
+        const float n1 = round_to_bf16(x.x);
+        const float n2 = round_to_bf16(x.y);
+        const float2 nc = __fmul2_rn(make_float2(n1, n2), make_float2(c[j], c[j]));  // n1 * c, n2 * c
+        const float2 ns = __fmul2_rn(make_float2(n2, n1), make_float2(s[j], s[j]));  // n2 * s, n1 * s
+        out_a[j] = nc.x - ns.x;
+        out_b[j] = nc.y + ns.y;
     }
     if (lane < kLanes) {
         *reinterpret_cast<uint4*>(dst + hl * 8) = Vec16<bf16>::pack(out_a);

@@ -950,7 +950,7 @@ __global__ void __launch_bounds__(kThreads) embedding_kernel(const bf16* table, 
 // Launch plan of the single-row kernels. K = 256 * c with c in {1, 2, 3, 4, 6, 8, 12} (c <= 4 with the RMSNorm
 // prologue or the input copy) takes the fast kernel with
 // kRows rows per warp (a lane's whole row group, kRows * mats * c 16-byte loads, in flight at once); other K take
-// the generic kernel. Grids: one CTA per SM, two for the vocabulary-sized argmax head.
+// the generic kernel. Grids: one CTA per SM, two for the vocabulary-sized argmax head and for the staged kernel.
 struct GemvPlan {
     bool fast;
     bool staged;            // gemv_staged_kernel: the CTA's weight rows staged in shared memory
@@ -981,8 +981,10 @@ GemvPlan plan_gemv(const LinearParams& p, int mats) {
         plan.rows = r >= 4 ? 4 : (r >= 2 ? 2 : 1);
     }
     if (plan.fast && p.error != nullptr && p.N > 0 && p.epilogue != LinearEpilogue::kArgmax) {
+        // Slices for two CTAs per SM: half as many rows per warp after the wait (Qwen3-0.6B decode, measured on
+        // B200: one CTA per SM 1884 tok/s, two 1909, three 1912, four 1609 -- past the register cap of three).
         const int64_t sms = runtime::sm_count();
-        const int64_t rpc = (p.N + sms - 1) / sms;
+        const int64_t rpc = (p.N + 2 * sms - 1) / (2 * sms);
         const std::size_t bytes = static_cast<std::size_t>(rpc) * mats * p.K * 2;
         if (bytes <= kMaxStagedBytes && rpc <= kStagedWarps * kStagedRowIters) {
             plan.staged = true;
