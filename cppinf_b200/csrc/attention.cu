@@ -212,16 +212,19 @@ __global__ void __launch_bounds__(kCtaThreads, 3)
     const int rank = static_cast<int>(cluster.block_rank());
     const int lane = threadIdx.x & 31;
     const int warp = threadIdx.x >> 5;
-    const int64_t unit = blockIdx.x / kParts;
-    const int64_t tb = unit / p.q_heads;
-    const int h = static_cast<int>(unit - tb * p.q_heads);
-    const int64_t t_begin = tb * p.queries_per_cluster;
-    const int64_t t_end = t_begin + p.queries_per_cluster < p.T ? t_begin + p.queries_per_cluster : p.T;
-    const int group = p.q_heads / p.kv_heads;
-    const int kvh = h / group;
     if constexpr (!kStage) {
         grid_dependency_begin();
     }
+    // The sequence position first (one memory round trip; the decode variant reads it before its wait, the previous
+    // kernel does not write it), then the index math in 32 bits while it is in flight (the grid has < 2^31 CTAs).
+    const int64_t pos_base = p.pos0 + (p.position != nullptr ? static_cast<int64_t>(*p.position) : 0);
+    const int unit = static_cast<int>(blockIdx.x / kParts);
+    const int tb = unit / p.q_heads;
+    const int h = unit - tb * p.q_heads;
+    const int64_t t_begin = static_cast<int64_t>(tb) * p.queries_per_cluster;
+    const int64_t t_end = t_begin + p.queries_per_cluster < p.T ? t_begin + p.queries_per_cluster : p.T;
+    const int group = p.q_heads / p.kv_heads;
+    const int kvh = h / group;
     // Every CTA of the cluster has started once this barrier phase completes (waited on before the first DSMEM
     // store below).
     asm volatile("barrier.cluster.arrive.relaxed.aligned;" ::: "memory");
@@ -230,7 +233,7 @@ __global__ void __launch_bounds__(kCtaThreads, 3)
     // Between two queries every CTA has passed the previous query's last cluster barrier, so no DSMEM store of the
     // next query lands in shared memory that is still being read.
     for (int64_t t = t_begin; t < t_end; ++t) {
-        const int64_t pos = p.pos0 + (p.position != nullptr ? static_cast<int64_t>(*p.position) : 0) + t;
+        const int64_t pos = pos_base + t;
         if (pos >= p.capacity) {
             if constexpr (kStage) {
                 grid_dependency_begin();
