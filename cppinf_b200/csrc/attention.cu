@@ -198,8 +198,8 @@ __global__ void __launch_bounds__(kCtaThreads, 3)
     // Dynamic shared memory: this part's scores (then exp values, then probabilities), and with kStage the part's
     // cached key and value rows.
     extern __shared__ __align__(16) float s_e[];
-    __shared__ float s_red[kCtaWarps];
-    __shared__ float s_local;             // this part's max
+    __shared__ float s_red[kCtaWarps];    // per-warp maxima of this part's scores
+    __shared__ float s_wsum[kWarps];      // per-warp exp sums of the 4 slot warps
     __shared__ float s_m[kParts];         // every part's max and exp sum, pushed here by each part
     __shared__ float s_s[kParts];
     __shared__ float s_acc[kWarps][kD];
@@ -397,16 +397,12 @@ __global__ void __launch_bounds__(kCtaThreads, 3)
             s_red[warp] = mx;
         }
         __syncthreads();
-        if (threadIdx.x == 0) {
-            float m = s_red[0];
+        // Every thread folds the warp maxima itself (the max is exact in any order; no second barrier).
+        float local_max = s_red[0];
     #pragma unroll
-            for (int w = 1; w < kCtaWarps; ++w) {
-                m = fmaxf(m, s_red[w]);
-            }
-            s_local = m;
+        for (int w = 1; w < kCtaWarps; ++w) {
+            local_max = fmaxf(local_max, s_red[w]);
         }
-        __syncthreads();
-        const float local_max = s_local;
         // The 128 slot chains are the first 4 warps' lanes (the order restated by the oracle).
         float sum = 0.0f;
         if (threadIdx.x < kThreads) {
@@ -415,9 +411,8 @@ __global__ void __launch_bounds__(kCtaThreads, 3)
             }
         }
         sum = group_sum<32>(sum);
-        __syncthreads();  // s_red is reused
         if (lane == 0 && warp < kWarps) {
-            s_red[warp] = sum;
+            s_wsum[warp] = sum;
         }
         __syncthreads();
         if (!started) {
@@ -425,10 +420,10 @@ __global__ void __launch_bounds__(kCtaThreads, 3)
             started = true;
         }
         if (threadIdx.x < kParts) {
-            float part_sum = s_red[0];
+            float part_sum = s_wsum[0];
     #pragma unroll
             for (int w = 1; w < kWarps; ++w) {
-                part_sum = part_sum + s_red[w];
+                part_sum = part_sum + s_wsum[w];
             }
             // Push (max, sum) of this part to every CTA of the cluster, this one included.
             *cluster.map_shared_rank(&s_m[rank], static_cast<int>(threadIdx.x)) = local_max;
