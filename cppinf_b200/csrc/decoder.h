@@ -102,9 +102,9 @@ struct AttentionParams {
     const float* rope_table;       // [capacity, D]
     float eps;
     // Decode steps: when set (and the part's rows fit in shared memory), the cached key/value rows before the new
-    // token are staged into shared memory by bulk copies issued before griddepcontrol.wait (the sequence length is
-    // then read before the wait too, so the preceding kernel must not write it); a bounded wait that runs out
-    // sets *error to 1.
+    // token are staged into shared memory by TMA tensor copies issued before griddepcontrol.wait (the sequence
+    // length is then read before the wait too, so the preceding kernel must not write it); a bounded wait that runs
+    // out sets *error to 1.
     unsigned int* error;
     int64_t queries_per_cluster = 1;  // consecutive queries one cluster takes in turn (prefill)
     uint32_t poll_limit = 1u << 24;   // polls of the staging wait (cppinf_set_wait_poll_limit)
