@@ -138,18 +138,15 @@ __device__ __forceinline__ void norm_rope_head(const bf16* src, uint4 w_first, u
     float b[8];
     Vec16<bf16>::unpack(ld_cached(src + hl * 8), a);
     Vec16<bf16>::unpack(ld_cached(src + kHalf + hl * 8), b);
-    // Products as packed f32x2 pairs (first-half element, second-half element), sums and differences scalar in the
-    // same order as rope.cu (a packed product feeding a packed add would be contracted into a fused multiply-add).
-    float sa = 0.0f;
-    float sb = 0.0f;
+    // Products as packed f32x2 pairs (first-half element, second-half element), the norm and rotation sums and
+    // differences scalar in the same order as rope.cu.
+    float2 s2 = make_float2(0.0f, 0.0f);  // the two halves' sums of squares as fused multiply-adds (rope.cu's bf16 path)
 #pragma unroll
     for (int j = 0; j < 8; ++j) {
         const float2 v = make_float2(a[j], b[j]);
-        const float2 sq = __fmul2_rn(v, v);
-        sa = sa + sq.x;
-        sb = sb + sq.y;
+        s2 = __ffma2_rn(v, v, s2);
     }
-    const float ss = group_sum<kLanes>(sa + sb);
+    const float ss = group_sum<kLanes>(s2.x + s2.y);
     const float mean = ss / static_cast<float>(kD);
     const float rms = sqrtf(mean + eps);
     const float inv = 1.0f / rms;

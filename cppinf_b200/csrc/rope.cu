@@ -18,7 +18,8 @@
 // unit is full (Hq and Hk multiples of the unit's heads: the Qwen3 shapes), the per-head bounds checks are compiled
 // out (kFull). Measured on B200 for [2048, 16 + 8, 128] bf16 against the layout whose units could mix q and k heads
 // and staged the angles and weights in shared memory: 6.43 -> 5.99 us; holding the weights as f32 (more registers,
-// fewer CTAs per SM) 6.36 us; fused multiply-adds in the sum of squares changed nothing.
+// fewer CTAs per SM) 6.36 us. Later, with the packed products below, packed fused multiply-adds for the bf16 sum
+// of squares: 5.92 -> 5.82 us.
 //
 // Reduction order: the sum of squares of a head equals the library's canonical order (lane c sums chunk c, then a
 // butterfly over lane distances 16, 8, ..., 1 over the D/kVec chunks): here a lane adds its first-half partial to its
@@ -29,6 +30,8 @@
 // (D * 4 bytes per position) and the two weight vectors are shared by all heads and come from L1/L2.
 #include <cmath>
 #include <vector>
+
+#include <type_traits>
 
 #include "common.cuh"
 #include "decoder.h"
@@ -127,17 +130,30 @@ __global__ void __launch_bounds__(kQkThreads, 16) qk_norm_rope_kernel(const QkPa
         float b[kVec];
         V::unpack(s_data[threadIdx.x / 32][i][0][lane], a);  // inactive lanes read stale bytes and store nothing
         V::unpack(s_data[threadIdx.x / 32][i][1][lane], b);
-        // Squares as packed f32x2 products, summed by scalar adds in element order (sa = sa + a*a). The adds stay
-        // scalar on purpose: a packed product feeding a packed add is contracted into a fused multiply-add by the
-        // code generator, which rounds once and changes the result.
+        // Sums of squares in element order, the two halves' chains side by side. bf16: one packed fused
+        // multiply-add advances both chains; the square of a bf16 value is exact in f32 wherever it is a normal
+        // number (|x| >= 2^-63), so this equals the separately rounded `sa + a*a` there (the oracle restates it with
+        // fmaf). f32: packed products then scalar adds (a packed product feeding a packed add would be contracted
+        // into a fused multiply-add by the code generator, which rounds once and changes the result).
         float sa = 0.0f;
         float sb = 0.0f;
+        if constexpr (std::is_same_v<T, bf16>) {
+            float2 s2 = make_float2(0.0f, 0.0f);
 #pragma unroll
-        for (int j = 0; j < kVec; ++j) {
-            const float2 v = make_float2(a[j], b[j]);
-            const float2 sq = __fmul2_rn(v, v);
-            sa = sa + sq.x;
-            sb = sb + sq.y;
+            for (int j = 0; j < kVec; ++j) {
+                const float2 v = make_float2(a[j], b[j]);
+                s2 = __ffma2_rn(v, v, s2);
+            }
+            sa = s2.x;
+            sb = s2.y;
+        } else {
+#pragma unroll
+            for (int j = 0; j < kVec; ++j) {
+                const float2 v = make_float2(a[j], b[j]);
+                const float2 sq = __fmul2_rn(v, v);
+                sa = sa + sq.x;
+                sb = sb + sq.y;
+            }
         }
         // Every lane of the warp takes part; offsets below kLanes never leave the head's lane group.
         const float ss = group_sum<kLanes>(sa + sb);

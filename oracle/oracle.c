@@ -139,8 +139,10 @@ void oracle_silu_mul(int dtype, const void* gate, const void* up, void* out, voi
 /* Sum of squares of one row in the device library's canonical order: the row is cut into chunks of `chunk`
  * consecutive elements; lane l (0..31) sums, in increasing element order, chunks l, l+32, l+64, ...; the 32 partials
  * are combined by a butterfly over lane distances 16, 8, 4, 2, 1 (partial[l] + partial[l ^ d]). chunk == 0 returns
- * the exactly rounded f32 of the double-precision sum instead. */
-static float row_sum_squares(int dtype, const void* x, int64_t base, int64_t width, int chunk) {
+ * the exactly rounded f32 of the double-precision sum instead. `fused`: each step is fmaf(v, v, s), as the fused
+ * q/k kernel does for bf16 (the square of a bf16 value is exact in f32 where it is normal, |v| >= 2^-63, so the two
+ * forms differ only below that); otherwise a separately rounded product and sum, as the reference's rms_norm. */
+static float row_sum_squares(int dtype, const void* x, int64_t base, int64_t width, int chunk, int fused) {
     if (chunk == 0) {
         double acc = 0.0;
         for (int64_t e = 0; e < width; ++e) {
@@ -157,7 +159,7 @@ static float row_sum_squares(int dtype, const void* x, int64_t base, int64_t wid
         for (int64_t c = lane; c < nchunks; c += 32) {
             for (int j = 0; j < chunk; ++j) {
                 const float v = load(dtype, x, base + c * chunk + j);
-                s = s + v * v;
+                s = fused ? fmaf(v, v, s) : s + v * v;
             }
         }
         partial[lane] = s;
@@ -179,7 +181,7 @@ void oracle_rms_norm(int dtype, const void* x, int64_t x_row_stride, const void*
 #pragma omp parallel for schedule(static)
     for (int64_t r = 0; r < rows; ++r) {
         const int64_t base = r * x_row_stride;
-        const float ss = row_sum_squares(dtype, x, base, width, chunk);
+        const float ss = row_sum_squares(dtype, x, base, width, chunk, 0);
         const float mean = ss / (float)width;
         const float var = mean + eps;
         const float rms = sqrtf(var);
@@ -341,7 +343,7 @@ void oracle_qk_norm_rope(int dtype, const void* q, const void* k, const void* qw
         const void* w = h < q_heads ? qw : kw;
         const int64_t base_idx = h < q_heads ? (t * q_heads + h) * head_dim : (t * k_heads + (h - q_heads)) * head_dim;
         float normed[8192];
-        const float ss = row_sum_squares(dtype, src, base_idx, head_dim, chunk);
+        const float ss = row_sum_squares(dtype, src, base_idx, head_dim, chunk, dtype == DT_BF16);
         const float mean = ss / (float)head_dim;
         const float var = mean + eps;
         const float rms = sqrtf(var);

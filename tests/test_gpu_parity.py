@@ -238,6 +238,22 @@ def test_qk_norm_rope_bit_exact(ops, oracle, tokens, hq, hk, d, offset):
     assert np.array_equal(to_host(k_out), want_k)
 
 
+def test_qk_norm_rope_bf16_subnormal_squares_bit_exact(ops, oracle):
+    # Head vectors scaled by 2^-66: the squares lie near 2^-132, below the f32 normal range, where a separately
+    # rounded square would lose bits. The kernel's fused sum of squares and the oracle's fmaf restatement agree.
+    rng = np.random.default_rng(77)
+    scale = np.float32(2.0**-66)
+    q = f32_to_bf16(bf16_to_f32(seeded_bf16(rng, (6, 16, 128))) * scale)
+    k = f32_to_bf16(bf16_to_f32(seeded_bf16(rng, (6, 8, 128))) * scale)
+    qw, kw = seeded_bf16(rng, (128,), 1.0, 0.1), seeded_bf16(rng, (128,), 1.0, 0.1)
+    assert np.abs(bf16_to_f32(q)).max() < 2.0**-63  # every square is subnormal
+    # eps 0, so the (subnormal) mean of squares alone sets the scale
+    q_out, k_out = ops.qk_norm_rope(to_dev(q), to_dev(k), to_dev(qw), to_dev(kw), 0.0, 5, 1e6)
+    want_q, want_k = oracle.qk_norm_rope(q, k, qw, kw, 0.0, 5, 1e6)
+    assert np.array_equal(to_host(q_out), want_q)
+    assert np.array_equal(to_host(k_out), want_k)
+
+
 def test_qk_norm_rope_f32(ops, oracle):
     rng = np.random.default_rng(14)
     q = rng.standard_normal((9, 4, 128)).astype(np.float32)
