@@ -231,6 +231,26 @@ def test_model_chunked_prefill_and_decode_tokens(small_pair):
     assert model.length == 600 + 24
 
 
+@pytest.mark.parametrize("head_dim,hq,hkv", [(64, 4, 2), (256, 2, 1)])
+def test_model_decode_tokens_other_head_dims(cuda, head_dim, hq, hkv):
+    # The decode step's kernels for head_dim 64 and 256 (the staged GEMVs and the 8-warp cluster attention with its
+    # TMA-staged K/V tiles and half-row P·V chains): greedy tokens of prefill + graph-replayed decode steps equal
+    # the oracle's.
+    from cppinf_b200.qwen3 import Qwen3Config, Qwen3Model, random_weights
+    from oracle.qwen3 import OracleQwen3
+
+    cfg = Qwen3Config(vocab_size=512, hidden_size=256, intermediate_size=512, num_hidden_layers=2,
+                      num_attention_heads=hq, num_key_value_heads=hkv, head_dim=head_dim)
+    w = random_weights(cfg, seed=21 + head_dim, std=0.05)
+    model = Qwen3Model(cfg, 200, w)
+    ref = OracleQwen3(cfg, w, 200)
+    prompt = np.random.default_rng(head_dim).integers(0, cfg.vocab_size, 70)
+    got = model.generate(prompt, 40)
+    ref.reset()
+    assert got == ref.generate(prompt, 40)
+    model.close()
+
+
 def test_model_cached_logits_match_full_forward(small_pair):
     cfg, model, ref = small_pair
     tokens = np.random.default_rng(3).integers(0, cfg.vocab_size, 12)
