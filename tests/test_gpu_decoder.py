@@ -251,6 +251,16 @@ def test_model_decode_tokens_other_head_dims(cuda, head_dim, hq, hkv):
     model.close()
 
 
+def test_model_decode_from_one_token_prompt(small_pair):
+    # Decode steps at contexts of 2 .. 41 keys: most of the 8 parts hold zero or one cached row, so some CTAs stage
+    # nothing and the new token's part may be the only non-empty one.
+    cfg, model, ref = small_pair
+    prompt = [int(np.random.default_rng(4).integers(0, cfg.vocab_size))]
+    got = model.generate(prompt, 41)
+    ref.reset()
+    assert got == ref.generate(prompt, 41)
+
+
 def test_model_cached_logits_match_full_forward(small_pair):
     cfg, model, ref = small_pair
     tokens = np.random.default_rng(3).integers(0, cfg.vocab_size, 12)
