@@ -128,7 +128,8 @@ __device__ __forceinline__ float dot8(uint4 a, uint4 b, float acc) {
 // second half; the sum of squares in the canonical lane order; normalised values rounded to bf16; then
 // (first * cos - second * sin, second * cos + first * sin) rounded to bf16 (src/nn/rope.cpp:100-103). The weights
 // (w_first, w_second) and the angles (c, s) of the lane's pairs are loaded by the caller.
-template <int kD>
+// kShared: `src` is in this CTA's shared memory (the fused projection's gathered rows) rather than global memory.
+template <int kD, bool kShared = false>
 __device__ __forceinline__ void norm_rope_head(const bf16* src, uint4 w_first, uint4 w_second, const float (&c)[8],
                                                const float (&s)[8], float eps, bf16* dst, int lane) {
     constexpr int kLanes = kD / 16;
@@ -136,8 +137,13 @@ __device__ __forceinline__ void norm_rope_head(const bf16* src, uint4 w_first, u
     const int hl = lane % kLanes;
     float a[8];
     float b[8];
-    Vec16<bf16>::unpack(ld_cached(src + hl * 8), a);
-    Vec16<bf16>::unpack(ld_cached(src + kHalf + hl * 8), b);
+    if constexpr (kShared) {
+        Vec16<bf16>::unpack(*reinterpret_cast<const uint4*>(src + hl * 8), a);
+        Vec16<bf16>::unpack(*reinterpret_cast<const uint4*>(src + kHalf + hl * 8), b);
+    } else {
+        Vec16<bf16>::unpack(ld_cached(src + hl * 8), a);
+        Vec16<bf16>::unpack(ld_cached(src + kHalf + hl * 8), b);
+    }
     // Products as packed f32x2 pairs (first-half element, second-half element), the norm and rotation sums and
     // differences scalar in the same order as rope.cu.
     float2 s2 = make_float2(0.0f, 0.0f);  // the two halves' sums of squares as fused multiply-adds (rope.cu's bf16 path)
@@ -173,6 +179,17 @@ __device__ __forceinline__ void norm_rope_head(const bf16* src, uint4 w_first, u
     }
 }
 
+// Row `row` of the fused q|k|v weight matrix's part m (0: W_q rows of head h, 1: W_k, 2: W_v rows of key/value head
+// kvh), counted from the head's first row.
+template <int kD>
+__device__ __forceinline__ const bf16* proj_row(const AttentionParams& p, int m, int h, int kvh, int row) {
+    const int64_t q_dim = static_cast<int64_t>(p.q_heads) * kD;
+    const int64_t kv_dim = static_cast<int64_t>(p.kv_heads) * kD;
+    const int64_t first = m == 0 ? static_cast<int64_t>(h) * kD
+                                 : (m == 1 ? q_dim : q_dim + kv_dim) + static_cast<int64_t>(kvh) * kD;
+    return p.wqkv + (first + row) * p.hidden;
+}
+
 // The decode kernel's staging copies: TMA maps of the K and V caches, each a 3-D tensor [cap][Hkv][D] with a box of
 // {D, 1, rows} (one head's rows of a part, 2 KB apart in the cache, in one copy).
 struct StageMaps {
@@ -180,9 +197,22 @@ struct StageMaps {
     CUtensorMap v;
 };
 
-template <int kD, bool kFused, bool kStage>
-__global__ void __launch_bounds__(kCtaThreads, 3)
+// kProjC > 0 (decode only, with kFused and kStage): the q|k|v projection of the new token is fused in, for a hidden
+// size of 256 * kProjC. CTA c of head h's cluster computes dims [c D/8, (c+1) D/8) of the head's q row and of its
+// key/value head's k and v rows: its D/8 rows of each weight matrix (contiguous in the fused matrix) are brought into
+// L2 before the dependency wait and into registers right after it, while warp 0 RMS-normalises the input row as the
+// staged projection does (same order); each of the 3 D/8 dot products runs in the canonical lane order on one warp,
+// and the slices are gathered into every CTA of the cluster through DSMEM behind one cluster barrier -- the
+// projection kernel, its launch boundary and the round trip of q and k through global memory are gone. (Staging the
+// rows in shared memory instead, 96 KB per CTA, kept the clusters from becoming resident beside the running
+// kernels: 1430 tok/s against 1930 unfused.)
+template <int kD, bool kFused, bool kStage, int kProjC = 0>
+__global__ void __launch_bounds__(kCtaThreads, kProjC > 0 ? 2 : 3)
     decoder_attention_kernel(const AttentionParams p, int64_t max_part, const __grid_constant__ StageMaps maps) {
+    constexpr bool kProj = kProjC > 0;
+    static_assert(!kProj || (kFused && kStage), "the fused projection runs in the staged decode kernel");
+    constexpr int kProjRows = kD / 8;          // rows of each of q, k, v a CTA computes
+    constexpr int kProjAll = 3 * kProjRows;
     constexpr int kSeg = kD / kSegments;       // dims per score segment
     constexpr int kSegChunks = kSeg / 8;       // 16-byte chunks per segment
     constexpr int kKeysPerIter = 32 / kSegments;
@@ -203,6 +233,11 @@ __global__ void __launch_bounds__(kCtaThreads, 3)
     __shared__ float s_recv[kParts][kFinal];  // the parts' P·V partials of the dims this CTA finishes
     __shared__ __align__(16) bf16 s_q[kFused ? kD : 8];
     __shared__ __align__(16) bf16 s_knew[kFused ? kD : 8];
+    __shared__ __align__(16) uint4 s_xn[kProj ? kProjC * 32 : 1];  // the normalised input row
+    __shared__ __align__(16) bf16 s_proj[kProj ? kProjAll : 8];    // this CTA's q, k, v values
+    __shared__ __align__(16) bf16 s_qraw[kProj ? kD : 8];          // the gathered raw q, k, v rows
+    __shared__ __align__(16) bf16 s_kraw[kProj ? kD : 8];
+    __shared__ __align__(16) bf16 s_vraw[kProj ? kD : 8];
     __shared__ __align__(8) uint64_t s_bar;
 
     cg::cluster_group cluster = cg::this_cluster();
@@ -272,14 +307,23 @@ __global__ void __launch_bounds__(kCtaThreads, 3)
                     tc::tma_load_3d(s_kt, &maps.k, 0, kvh, static_cast<int>(lo), &s_bar);
                     tc::tma_load_3d(s_vt, &maps.v, 0, kvh, static_cast<int>(lo), &s_bar);
                 }
+                if constexpr (kProj) {
+                    // This CTA's rows of W_q (head h), W_k and W_v (key/value head kvh), D/8 contiguous rows each,
+                    // brought into L2 while the previous kernel runs.
+    #pragma unroll
+                    for (int m = 0; m < 3; ++m) {
+                        bulk_prefetch_l2(proj_row<kD>(p, m, h, kvh, rank * kProjRows), kProjRows * p.hidden * 2);
+                    }
+                }
             }
             __syncthreads();
         }
-        if constexpr (kFused) {
-            // RoPE angles of this position and the q/k norm weights: constants, read before the wait.
-            constexpr int kLanes = kD / 16;
-            const int hl = lane % kLanes;
-            const float* trow = p.rope_table + pos * kD;
+        // RoPE angles of this position and the q/k norm weights: constants, read before the wait (with the fused
+        // projection only brought into L1 then, and read after the projection, which needs the registers).
+        constexpr int kLanes = kD / 16;
+        const int hl = lane % kLanes;
+        const float* trow = p.rope_table + pos * kD;
+        auto load_constants = [&]() {
     #pragma unroll
             for (int j = 0; j < 8; ++j) {
                 c_rope[j] = trow[hl * 8 + j];
@@ -289,6 +333,25 @@ __global__ void __launch_bounds__(kCtaThreads, 3)
             wq_b = ld_cached(p.q_norm + kD / 2 + hl * 8);
             wk_a = ld_cached(p.k_norm + hl * 8);
             wk_b = ld_cached(p.k_norm + kD / 2 + hl * 8);
+        };
+        if constexpr (kProj) {
+            if (warp < 2) {
+                asm volatile("prefetch.global.L1 [%0];" ::"l"(trow + hl * 8));
+                asm volatile("prefetch.global.L1 [%0];" ::"l"(trow + kD / 2 + hl * 8));
+                asm volatile("prefetch.global.L1 [%0];" ::"l"((warp == 0 ? p.q_norm : p.k_norm) + hl * 8));
+                asm volatile("prefetch.global.L1 [%0];" ::"l"((warp == 0 ? p.q_norm : p.k_norm) + kD / 2 + hl * 8));
+            }
+        } else if constexpr (kFused) {
+            load_constants();
+        }
+        uint4 nw[kProj ? kProjC : 1];  // kProj: warp 0's chunks of the input norm weight (a constant)
+        if constexpr (kProj) {
+            if (warp == 0) {
+    #pragma unroll
+                for (int i = 0; i < kProjC; ++i) {
+                    nw[i] = ld_cached(p.in_norm + (lane + 32 * i) * 8);
+                }
+            }
         }
         if constexpr (kStage) {
             // One warp waits for the previous grid; the others wait at the block barrier, which orders their reads
@@ -300,7 +363,143 @@ __global__ void __launch_bounds__(kCtaThreads, 3)
             asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
         }
 
-        if constexpr (kFused) {
+        bool stage_failed = false;
+        if constexpr (kProj) {
+            // The input row: warp 0 loads it (the embedding row of the token at this position in the first layer,
+            // which it also copies to the residual stream) and RMS-normalises it exactly as the staged projection
+            // does (lane l's chunks l, l + 32, ..., canonical order), for every warp through shared memory.
+            if (warp == 0) {
+                const bf16* xrow = p.x;
+                if (p.tokens != nullptr) {
+                    const int64_t tok = p.tokens[pos];
+                    xrow += (tok < 0 ? 0 : (tok >= p.vocab ? p.vocab - 1 : tok)) * p.hidden;
+                }
+                uint4 xv[kProjC];
+    #pragma unroll
+                for (int i = 0; i < kProjC; ++i) {
+                    xv[i] = ld_cached(xrow + (lane + 32 * i) * 8);
+                }
+                if (p.x_copy != nullptr && blockIdx.x == 0) {
+    #pragma unroll
+                    for (int i = 0; i < kProjC; ++i) {
+                        st_v4(p.x_copy + (lane + 32 * i) * 8, xv[i]);
+                    }
+                }
+                float ssq = 0.0f;
+    #pragma unroll
+                for (int i = 0; i < kProjC; ++i) {
+                    float f[8];
+                    Vec16<bf16>::unpack(xv[i], f);
+    #pragma unroll
+                    for (int e = 0; e < 8; ++e) {
+                        ssq = ssq + f[e] * f[e];
+                    }
+                }
+                ssq = group_sum<32>(ssq);
+                const float mean = ssq / static_cast<float>(kProjC * 256);
+                const float rms = sqrtf(mean + p.eps);
+                const float inv = 1.0f / rms;
+    #pragma unroll
+                for (int i = 0; i < kProjC; ++i) {
+                    float f[8];
+                    float w[8];
+                    Vec16<bf16>::unpack(xv[i], f);
+                    Vec16<bf16>::unpack(nw[i], w);
+    #pragma unroll
+                    for (int e = 0; e < 8; ++e) {
+                        f[e] = (f[e] * inv) * w[e];
+                    }
+                    s_xn[lane + 32 * i] = Vec16<bf16>::pack(f);
+                }
+            }
+            // Each warp takes rows warp, warp + 8, ... of the 3 D/8, two at a time in registers; its first two are
+            // requested before the barrier, so they arrive while warp 0 normalises the row.
+            constexpr int kRowsPerWarp = kProjAll / kCtaWarps;
+            static_assert(kProjAll % kCtaWarps == 0, "whole rows per warp");
+            constexpr int kBatch = kRowsPerWarp < 2 ? kRowsPerWarp : 2;
+            uint4 wreg[kBatch][kProjC];
+            auto load_rows = [&](int k0) {
+    #pragma unroll
+                for (int b = 0; b < kBatch; ++b) {
+                    if (k0 + b < kRowsPerWarp) {
+                        const int r = warp + (k0 + b) * kCtaWarps;
+                        const bf16* wrow = proj_row<kD>(p, r / kProjRows, h, kvh, rank * kProjRows + r % kProjRows);
+    #pragma unroll
+                        for (int i = 0; i < kProjC; ++i) {
+                            wreg[b][i] = ld_cached(wrow + (lane + 32 * i) * 8);
+                        }
+                    }
+                }
+            };
+            load_rows(0);
+            __syncthreads();
+            const bool arrived = mbar_wait_bounded(&s_bar, 0, p.poll_limit);
+            // On a timeout the kernel still runs every cluster barrier below (with meaningless values), so no CTA of
+            // the cluster is left waiting; the host sees the error flag.
+            stage_failed = __syncthreads_or(arrived ? 0 : 1) != 0;
+            if (stage_failed && threadIdx.x == 0) {
+                atomicOr(p.error, 1u);
+            }
+            // The 3 D/8 dot products, one warp each at a time: fused multiply-adds in the canonical lane order and a
+            // butterfly, rounded to bf16 once (the staged projection's arithmetic).
+    #pragma unroll
+            for (int k0 = 0; k0 < kRowsPerWarp; k0 += kBatch) {
+                if (k0 > 0) {
+                    load_rows(k0);
+                }
+    #pragma unroll
+                for (int b = 0; b < kBatch; ++b) {
+                    if (k0 + b < kRowsPerWarp) {
+                        float acc = 0.0f;
+    #pragma unroll
+                        for (int i = 0; i < kProjC; ++i) {
+                            acc = fma_bf16x8(s_xn[lane + 32 * i], wreg[b][i], acc);
+                        }
+                        acc = group_sum<32>(acc);
+                        if (lane == 0) {
+                            s_proj[warp + (k0 + b) * kCtaWarps] = __float2bfloat16_rn(acc);
+                        }
+                    }
+                }
+            }
+            __syncthreads();
+            if (!started) {
+                asm volatile("barrier.cluster.wait.aligned;" ::: "memory");  // every CTA has started: DSMEM is usable
+                started = true;
+            }
+            // Gather: value r of this CTA goes to dim rank * D/8 + r % (D/8) of the q, k or v row of every CTA.
+            for (int idx = threadIdx.x; idx < kProjAll * kParts; idx += kCtaThreads) {
+                const int r = idx / kParts;
+                const int m = r / kProjRows;
+                bf16* row = m == 0 ? s_qraw : (m == 1 ? s_kraw : s_vraw);
+                *cluster.map_shared_rank(row + rank * kProjRows + r % kProjRows, idx % kParts) = s_proj[r];
+            }
+            if (h % group == 0 && threadIdx.x < kProjRows) {
+                // One cluster per key/value head stores the new token's value row (for the steps that follow).
+                const_cast<bf16*>(p.v_cache)[pos * kv_row + kvh * kD + rank * kProjRows + threadIdx.x] =
+                    s_proj[2 * kProjRows + threadIdx.x];
+            }
+            cluster.sync();
+            // q-norm + RoPE of this head and k-norm + RoPE of the new key from the gathered rows; the new value row
+            // into the staged tile (the copies have landed).
+            if (warp < 2) {
+                load_constants();
+            }
+            if (warp == 0) {
+                norm_rope_head<kD, true>(s_qraw, wq_a, wq_b, c_rope, s_rope, p.eps, s_q, lane);
+            } else if (warp == 1) {
+                norm_rope_head<kD, true>(s_kraw, wk_a, wk_b, c_rope, s_rope, p.eps, s_knew, lane);
+            } else if (warp == 2 && i_new >= 0 && i_new < n && lane < kD / 8) {
+                *reinterpret_cast<uint4*>(s_vt + i_new * kD + lane * 8) =
+                    *reinterpret_cast<const uint4*>(s_vraw + lane * 8);
+            }
+            __syncthreads();
+            if (rank == 0 && h % group == 0 && threadIdx.x < kD / 8) {
+                // One CTA per key/value head stores the new key row; nobody reads that row in this launch.
+                st_v4(const_cast<bf16*>(p.k_cache) + pos * kv_row + kvh * kD + threadIdx.x * 8,
+                      *reinterpret_cast<const uint4*>(s_knew + threadIdx.x * 8));
+            }
+        } else if constexpr (kFused) {
             // q-norm + RoPE of this head and k-norm + RoPE of the new key (computed by every CTA that needs them).
             if (warp == 0) {
                 norm_rope_head<kD>(p.q + (t * p.q_heads + h) * kD, wq_a, wq_b, c_rope, s_rope, p.eps, s_q, lane);
@@ -319,8 +518,7 @@ __global__ void __launch_bounds__(kCtaThreads, 3)
                       *reinterpret_cast<const uint4*>(s_knew + threadIdx.x * 8));
             }
         }
-        bool stage_failed = false;
-        if constexpr (kStage) {
+        if constexpr (kStage && !kProj) {
             const bool arrived = mbar_wait_bounded(&s_bar, 0, p.poll_limit);
             // On a timeout the kernel still runs every cluster barrier below (with meaningless values), so no CTA of
             // the cluster is left waiting; the host sees the error flag.
@@ -705,16 +903,17 @@ constexpr std::size_t kMaxRowScoreBytes = 64 * 1024;
 // Staged parts up to this size leave room in the SM's shared memory for the neighbouring kernels' CTAs.
 constexpr std::size_t kMaxStagedBytes = 110 * 1024;
 
-template <int kD, bool kFused, bool kStage>
+
+
+template <int kD, bool kFused, bool kStage, int kProjC = 0>
 cudaError_t launch_attention_variant(const AttentionParams& p, int64_t max_part, std::size_t smem, cudaStream_t s,
                                      const StageMaps& maps = StageMaps{}) {
-    auto kernel = decoder_attention_kernel<kD, kFused, kStage>;
-    if (smem > 48 * 1024) {
-        const cudaError_t err =
-            cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
-        if (err != cudaSuccess) {
-            return err;
-        }
+    auto kernel = decoder_attention_kernel<kD, kFused, kStage, kProjC>;
+    // Opted in for every size: static and dynamic shared memory together may pass 48 KB before the dynamic part does.
+    const cudaError_t err =
+        cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
+    if (err != cudaSuccess) {
+        return err;
     }
     const int64_t blocks = (p.T + p.queries_per_cluster - 1) / p.queries_per_cluster * p.q_heads * kParts;
     return runtime::launch_smem(kernel, dim3(static_cast<unsigned>(blocks)), dim3(kCtaThreads), smem, s,
@@ -757,9 +956,29 @@ cudaError_t launch_attention_dim(const AttentionParams& p, int64_t max_keys, cud
     const std::size_t staged_bytes = score_bytes + 128 + static_cast<std::size_t>(max_part) * kD * 2 * 2;
     if (p.q_norm != nullptr) {
         StageMaps maps{};
-        if (p.error != nullptr && p.T == 1 && staged_bytes <= kMaxStagedBytes && max_part <= 256 &&
-            make_stage_map<kD>(&maps.k, p.k_cache, p.capacity, p.kv_heads, max_part) &&
-            make_stage_map<kD>(&maps.v, p.v_cache, p.capacity, p.kv_heads, max_part)) {
+        const bool maps_ok = p.error != nullptr && p.T == 1 && max_part <= 256 &&
+                             make_stage_map<kD>(&maps.k, p.k_cache, p.capacity, p.kv_heads, max_part) &&
+                             make_stage_map<kD>(&maps.v, p.v_cache, p.capacity, p.kv_heads, max_part);
+        if (p.wqkv != nullptr) {
+            // The caller left the projection to this kernel (decode_projection_fused): no fallback exists.
+            if constexpr (kD <= 128) {
+                const std::size_t bytes = staged_bytes;
+                if (maps_ok && bytes <= kMaxStagedBytes) {
+                    switch (p.hidden) {
+                    case 256:
+                        return launch_attention_variant<kD, true, true, 1>(p, max_part, bytes, s, maps);
+                    case 512:
+                        return launch_attention_variant<kD, true, true, 2>(p, max_part, bytes, s, maps);
+                    case 1024:
+                        return launch_attention_variant<kD, true, true, 4>(p, max_part, bytes, s, maps);
+                    default:
+                        break;
+                    }
+                }
+            }
+            return cudaErrorNotSupported;
+        }
+        if (maps_ok && staged_bytes <= kMaxStagedBytes) {
             return launch_attention_variant<kD, true, true>(p, max_part, staged_bytes, s, maps);
         }
         return launch_attention_variant<kD, true, false>(p, max_part, score_bytes, s);
@@ -783,6 +1002,17 @@ cudaError_t launch_attention_dim(const AttentionParams& p, int64_t max_keys, cud
 }
 
 }  // namespace
+
+bool decode_projection_fused(int64_t head_dim, int64_t hidden, int64_t capacity) {
+    if ((head_dim != 64 && head_dim != 128) || (hidden != 256 && hidden != 512 && hidden != 1024) || capacity < 1) {
+        return false;
+    }
+    // The same sizes launch_attention_dim checks for the staged decode kernel with max_keys = capacity.
+    const int64_t max_part = (capacity + kParts - 1) / kParts;
+    const std::size_t score_bytes = static_cast<std::size_t>((max_part + 3) / 4 * 4) * sizeof(float);
+    const std::size_t bytes = score_bytes + 128 + static_cast<std::size_t>(max_part) * head_dim * 2 * 2;
+    return max_part <= 256 && bytes <= kMaxStagedBytes && tc::encode_tiled() != nullptr;
+}
 
 cudaError_t launch_decoder_attention(const AttentionParams& p, int64_t max_keys, cudaStream_t s) {
     switch (p.head_dim) {

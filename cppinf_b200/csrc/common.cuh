@@ -147,6 +147,11 @@ __device__ __forceinline__ void cp_async_wait_pending(int pending) {
     }
 }
 
+// Brings `bytes` (a multiple of 16, 16-byte aligned) of global memory into L2 without waiting (no data returned).
+__device__ __forceinline__ void bulk_prefetch_l2(const void* src, uint32_t bytes) {
+    asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(src), "r"(bytes) : "memory");
+}
+
 __device__ __forceinline__ void bulk_copy_g2s(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
     asm volatile(
         "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(

@@ -108,7 +108,23 @@ struct AttentionParams {
     unsigned int* error;
     int64_t queries_per_cluster = 1;  // consecutive queries one cluster takes in turn (prefill)
     uint32_t poll_limit = 1u << 24;   // polls of the staging wait (cppinf_set_wait_poll_limit)
+    // Decode steps with the q|k|v projection fused in (when wqkv is set and decode_projection_fused() holds): the
+    // kernel RMS-normalises the input row x (or, when `tokens` is set, the embedding row tokens[*position], which
+    // it also copies to x_copy) with in_norm, and computes the new token's q, k and v rows from the fused
+    // [(Hq + 2 Hkv) D, hidden] weight matrix itself; q and k_new above are then unused, and the v row is written to
+    // v_cache at the position.
+    const __nv_bfloat16* x = nullptr;
+    const int64_t* tokens = nullptr;
+    int64_t vocab = 0;
+    __nv_bfloat16* x_copy = nullptr;
+    const __nv_bfloat16* in_norm = nullptr;
+    const __nv_bfloat16* wqkv = nullptr;
+    int hidden = 0;
 };
+
+// Whether the decode attention can take the q|k|v projection of a model with these sizes (head_dim 64 or 128,
+// hidden 256, 512 or 1024); otherwise the projection runs as its own kernel.
+bool decode_projection_fused(int64_t head_dim, int64_t hidden, int64_t capacity);
 
 // Causal GQA attention of one sequence in the fixed partition order (see attention.cu). head_dim 64, 128 or 256.
 cudaError_t launch_decoder_attention(const AttentionParams& p, int64_t max_keys, cudaStream_t s);

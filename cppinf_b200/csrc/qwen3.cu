@@ -12,11 +12,12 @@
 // projection (v rows written straight into the cache), fused q/k-norm + RoPE (k rows into the cache), attention,
 // o_proj with the residual add, rms_norm, gate/up with SiLU * up, down_proj with the residual add -- and finally
 // the last row's final norm + LM head + argmax in one kernel.
-// decode(): one step is 5 kernels per layer + 1 (QKV with the input norm and, in layer 0, the embedding gather;
-// attention with the q/k-norm + RoPE of the new token fused in; o_proj + residual; gate/up with the
-// post-attention norm and SiLU * up;
-// down_proj + residual; final norm + LM head + argmax), captured once as a CUDA graph. Every kernel reads the
-// sequence length from device memory, and the last one advances it, so the same graph is replayed for every step.
+// decode(): one step is 4 kernels per layer + 1 (attention with the input norm, the q|k|v projection -- in layer 0
+// after the embedding gather -- and the q/k-norm + RoPE of the new token fused in; o_proj + residual; gate/up with
+// the post-attention norm and SiLU * up; down_proj + residual; final norm + LM head + argmax), captured once as a
+// CUDA graph. Sizes the fused attention does not take (decode_projection_fused) run the projection as a fifth kernel
+// per layer. Every kernel reads the sequence length from device memory, and the last one advances it, so the same
+// graph is replayed for every step.
 #include <cstring>
 #include <string>
 #include <vector>
@@ -159,31 +160,50 @@ LinearParams lm_head_params(const cppinf_qwen3* m, const bf16* x, int64_t advanc
     return p;
 }
 
+// Whether the decode step's attention kernel takes the input norm and the q|k|v projection (decoder.h).
+bool projection_fused(const cppinf_qwen3* m) {
+    return cppinf::device::decode_projection_fused(m->c.head_dim, m->c.hidden_size, m->cap);
+}
+
 // One decode step at the device-side position (see the file comment). Returns the number of launches.
 int enqueue_step(cppinf_qwen3* m, cudaStream_t s, int64_t* launches) {
     const auto& c = m->c;
     const int64_t H = c.hidden_size;
+    const bool fused = projection_fused(m);
     int64_t n = 0;
     for (std::size_t i = 0; i < m->layers.size(); ++i) {
         const Layer& l = m->layers[i];
-        LinearParams qkv = params_for(LinearEpilogue::kStore, i == 0 ? m->embed : m->h, H, l.wqkv, nullptr, 1,
-                                      m->qkv_rows, H);
-        if (i == 0) {
-            qkv.tokens = m->d_tokens;
-            qkv.vocab = c.vocab_size;
-            qkv.x_copy = m->h;
+        if (!fused) {
+            LinearParams qkv = params_for(LinearEpilogue::kStore, i == 0 ? m->embed : m->h, H, l.wqkv, nullptr, 1,
+                                          m->qkv_rows, H);
+            if (i == 0) {
+                qkv.tokens = m->d_tokens;
+                qkv.vocab = c.vocab_size;
+                qkv.x_copy = m->h;
+            }
+            qkv.norm_weight = l.in_norm;
+            qkv.eps = c.rms_norm_eps;
+            set_qkv_outputs(m, l, qkv, 0, m->d_len);
+            qkv.error = m->d_error;
+            QWEN3_TRY(cppinf::device::launch_gemv(qkv, s), "qwen3_qkv");
+            ++n;
         }
-        qkv.norm_weight = l.in_norm;
-        qkv.eps = c.rms_norm_eps;
-        set_qkv_outputs(m, l, qkv, 0, m->d_len);
-        qkv.error = m->d_error;
-        QWEN3_TRY(cppinf::device::launch_gemv(qkv, s), "qwen3_qkv");
-        // q/k-norm + RoPE and the new key's cache row are fused into the attention kernel.
+        // q/k-norm + RoPE and the new key's cache row are fused into the attention kernel, and with `fused` the
+        // input norm and the q|k|v projection too (the first layer's embedding gather included).
         AttentionParams ap{m->q, l.k_cache, l.v_cache, m->ctx, 1,
                            static_cast<int>(c.num_attention_heads), static_cast<int>(c.num_key_value_heads),
                            static_cast<int>(c.head_dim), 0, m->d_len, m->cap,
                            m->k, l.q_norm, l.k_norm, m->rope, c.rms_norm_eps, m->d_error};
         ap.poll_limit = rt::wait_poll_limit();
+        if (fused) {
+            ap.x = i == 0 ? m->embed : m->h;
+            ap.tokens = i == 0 ? m->d_tokens : nullptr;
+            ap.vocab = c.vocab_size;
+            ap.x_copy = i == 0 ? m->h : nullptr;
+            ap.in_norm = l.in_norm;
+            ap.wqkv = l.wqkv;
+            ap.hidden = static_cast<int>(H);
+        }
         QWEN3_TRY(cppinf::device::launch_decoder_attention(ap, m->cap, s), "qwen3_attention");
         LinearParams o = params_for(LinearEpilogue::kResidual, m->ctx, m->q_dim, l.wo, nullptr, 1, H, m->q_dim);
         o.residual = m->h;
@@ -207,7 +227,7 @@ int enqueue_step(cppinf_qwen3* m, cudaStream_t s, int64_t* launches) {
         d.ld[0] = H;
         d.error = m->d_error;
         QWEN3_TRY(cppinf::device::launch_gemv(d, s), "qwen3_down_proj");
-        n += 5;
+        n += 4;
     }
     QWEN3_TRY(cppinf::device::launch_gemv(lm_head_params(m, m->h, 1, nullptr), s), "qwen3_lm_head_argmax");
     *launches = n + 1;
@@ -736,7 +756,10 @@ int64_t cppinf_qwen3_length(const cppinf_qwen3* model) {
 }
 
 int64_t cppinf_qwen3_step_launches(const cppinf_qwen3* model) {
-    return model != nullptr ? 5 * model->c.num_hidden_layers + 1 : 0;
+    if (model == nullptr) {
+        return 0;
+    }
+    return (projection_fused(model) ? 4 : 5) * model->c.num_hidden_layers + 1;
 }
 
 int cppinf_qwen3_forward(cppinf_qwen3* model, const int64_t* token_ids, int64_t count, void* logits, int all_rows,
