@@ -238,6 +238,9 @@ __global__ void __launch_bounds__(kCtaThreads, kProjC > 0 ? 2 : 3)
     __shared__ __align__(16) bf16 s_qraw[kProj ? kD : 8];          // the gathered raw q, k, v rows
     __shared__ __align__(16) bf16 s_kraw[kProj ? kD : 8];
     __shared__ __align__(16) bf16 s_vraw[kProj ? kD : 8];
+    __shared__ __align__(16) float s_angles[kProj ? kD : 4];       // kProj: the position's RoPE row (cos, sin)
+    __shared__ __align__(16) bf16 s_qnw[kProj ? kD : 8];           // kProj: the q and k norm weights
+    __shared__ __align__(16) bf16 s_knw[kProj ? kD : 8];
     __shared__ __align__(8) uint64_t s_bar;
 
     cg::cluster_group cluster = cg::this_cluster();
@@ -324,22 +327,34 @@ __global__ void __launch_bounds__(kCtaThreads, kProjC > 0 ? 2 : 3)
         const int hl = lane % kLanes;
         const float* trow = p.rope_table + pos * kD;
         auto load_constants = [&]() {
+            if constexpr (kProj) {
     #pragma unroll
-            for (int j = 0; j < 8; ++j) {
-                c_rope[j] = trow[hl * 8 + j];
-                s_rope[j] = trow[kD / 2 + hl * 8 + j];
+                for (int j = 0; j < 8; ++j) {
+                    c_rope[j] = s_angles[hl * 8 + j];
+                    s_rope[j] = s_angles[kD / 2 + hl * 8 + j];
+                }
+                wq_a = *reinterpret_cast<const uint4*>(s_qnw + hl * 8);
+                wq_b = *reinterpret_cast<const uint4*>(s_qnw + kD / 2 + hl * 8);
+                wk_a = *reinterpret_cast<const uint4*>(s_knw + hl * 8);
+                wk_b = *reinterpret_cast<const uint4*>(s_knw + kD / 2 + hl * 8);
+            } else {
+    #pragma unroll
+                for (int j = 0; j < 8; ++j) {
+                    c_rope[j] = trow[hl * 8 + j];
+                    s_rope[j] = trow[kD / 2 + hl * 8 + j];
+                }
+                wq_a = ld_cached(p.q_norm + hl * 8);
+                wq_b = ld_cached(p.q_norm + kD / 2 + hl * 8);
+                wk_a = ld_cached(p.k_norm + hl * 8);
+                wk_b = ld_cached(p.k_norm + kD / 2 + hl * 8);
             }
-            wq_a = ld_cached(p.q_norm + hl * 8);
-            wq_b = ld_cached(p.q_norm + kD / 2 + hl * 8);
-            wk_a = ld_cached(p.k_norm + hl * 8);
-            wk_b = ld_cached(p.k_norm + kD / 2 + hl * 8);
         };
         if constexpr (kProj) {
-            if (warp < 2) {
-                asm volatile("prefetch.global.L1 [%0];" ::"l"(trow + hl * 8));
-                asm volatile("prefetch.global.L1 [%0];" ::"l"(trow + kD / 2 + hl * 8));
-                asm volatile("prefetch.global.L1 [%0];" ::"l"((warp == 0 ? p.q_norm : p.k_norm) + hl * 8));
-                asm volatile("prefetch.global.L1 [%0];" ::"l"((warp == 0 ? p.q_norm : p.k_norm) + kD / 2 + hl * 8));
+            // Copied into shared memory before the wait (registers are short during the projection).
+            for (int i = threadIdx.x; i < kD; i += kCtaThreads) {
+                s_angles[i] = trow[i];
+                s_qnw[i] = p.q_norm[i];
+                s_knw[i] = p.k_norm[i];
             }
         } else if constexpr (kFused) {
             load_constants();
