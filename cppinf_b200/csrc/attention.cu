@@ -349,14 +349,7 @@ __global__ void __launch_bounds__(kCtaThreads, kProjC > 0 ? 2 : 3)
                 wk_b = ld_cached(p.k_norm + kD / 2 + hl * 8);
             }
         };
-        if constexpr (kProj) {
-            // Copied into shared memory before the wait (registers are short during the projection).
-            for (int i = threadIdx.x; i < kD; i += kCtaThreads) {
-                s_angles[i] = trow[i];
-                s_qnw[i] = p.q_norm[i];
-                s_knw[i] = p.k_norm[i];
-            }
-        } else if constexpr (kFused) {
+        if constexpr (kFused && !kProj) {
             load_constants();
         }
         uint4 nw[kProj ? kProjC : 1];  // kProj: warp 0's chunks of the input norm weight (a constant)
@@ -383,6 +376,15 @@ __global__ void __launch_bounds__(kCtaThreads, kProjC > 0 ? 2 : 3)
             // The input row: warp 0 loads it (the embedding row of the token at this position in the first layer,
             // which it also copies to the residual stream) and RMS-normalises it exactly as the staged projection
             // does (lane l's chunks l, l + 32, ..., canonical order), for every warp through shared memory.
+            if (warp != 0) {
+                // The RoPE row and the q/k norm weights into shared memory, for after the projection (registers
+                // are short during it); warps 1.. do it while warp 0 normalises the input row.
+                for (int i = threadIdx.x - 32; i < kD; i += kCtaThreads - 32) {
+                    s_angles[i] = trow[i];
+                    s_qnw[i] = p.q_norm[i];
+                    s_knw[i] = p.k_norm[i];
+                }
+            }
             if (warp == 0) {
                 const bf16* xrow = p.x;
                 if (p.tokens != nullptr) {
