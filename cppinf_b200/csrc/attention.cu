@@ -409,7 +409,7 @@ __global__ void __launch_bounds__(kCtaThreads, kProjC > 0 ? 2 : 3)
                     Vec16<bf16>::unpack(xv[i], f);
     #pragma unroll
                     for (int e = 0; e < 8; ++e) {
-                        ssq = ssq + f[e] * f[e];
+                        ssq = __fmaf_rn(f[e], f[e], ssq);  // a bf16 square: fused, as sum_square
                     }
                 }
                 ssq = group_sum<32>(ssq);

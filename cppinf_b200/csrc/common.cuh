@@ -199,6 +199,18 @@ __device__ __forceinline__ float bf16_hi(uint32_t packed) {
     return __uint_as_float(packed & 0xffff0000u);
 }
 
+// One step of an RMSNorm sum of squares: s + v * v, fused for bf16 inputs (the square of a bf16 value is exact in f32
+// wherever it is normal, |v| >= 2^-63, so this equals the separately rounded form there; the oracle restates it with
+// fmaf), separately rounded for f32 inputs (whose squares are not exact).
+template <typename T>
+__device__ __forceinline__ float sum_square(float s, float v) {
+    if constexpr (sizeof(T) == 2) {
+        return __fmaf_rn(v, v, s);
+    } else {
+        return s + v * v;
+    }
+}
+
 // Dot-product accumulation of bf16 operands: acc = fma(a, b, acc), rounded once. A product of two bf16 values has at
 // most 16 significant bits, so wherever it lies in the f32 normal range it is exact and the fused multiply-add equals
 // the separately rounded `acc + a * b`; the CPU oracle restates it with fmaf, which agrees for every operand.

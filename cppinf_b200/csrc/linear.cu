@@ -249,7 +249,7 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_fast_kernel(const LinearPara
                 Vec16<bf16>::unpack(xv[i], f);
 #pragma unroll
                 for (int e = 0; e < 8; ++e) {
-                    s = s + f[e] * f[e];
+                    s = __fmaf_rn(f[e], f[e], s);  // a bf16 square: fused, as sum_square
                 }
             }
             s = group_sum<32>(s);
@@ -419,7 +419,7 @@ __global__ void __launch_bounds__(kStagedThreads, 3) gemv_staged_kernel(const Li
                 Vec16<bf16>::unpack(xv[i], f);
 #pragma unroll
                 for (int e = 0; e < 8; ++e) {
-                    s = s + f[e] * f[e];
+                    s = __fmaf_rn(f[e], f[e], s);  // a bf16 square: fused, as sum_square
                 }
             }
             s = group_sum<32>(s);
@@ -574,7 +574,7 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_kernel(const LinearParams p)
                 Vec16<bf16>::unpack(smem_x[c], f);
 #pragma unroll
                 for (int e = 0; e < 8; ++e) {
-                    s = s + f[e] * f[e];
+                    s = __fmaf_rn(f[e], f[e], s);  // a bf16 square: fused, as sum_square
                 }
             }
             s = group_sum<32>(s);

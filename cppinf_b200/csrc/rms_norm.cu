@@ -82,7 +82,7 @@ __global__ void __launch_bounds__(kThreads) rms_norm_regs_kernel(RmsParams p) {
                 }
 #pragma unroll
                 for (int j = 0; j < kVec; ++j) {
-                    ss = ss + vals[i][j] * vals[i][j];
+                    ss = sum_square<T>(ss, vals[i][j]);
                 }
             }
         }
@@ -134,7 +134,7 @@ __global__ void __launch_bounds__(kThreads) rms_norm_stream_kernel(RmsParams p, 
                     v = V::quantize(v + V::load1(p.b, d_base + e));
                     V::store1(p.sum, d_base + e, v);
                 }
-                ss = ss + v * v;
+                ss = sum_square<T>(ss, v);
             }
         }
         ss = group_sum<32>(ss);

@@ -139,9 +139,10 @@ void oracle_silu_mul(int dtype, const void* gate, const void* up, void* out, voi
 /* Sum of squares of one row in the device library's canonical order: the row is cut into chunks of `chunk`
  * consecutive elements; lane l (0..31) sums, in increasing element order, chunks l, l+32, l+64, ...; the 32 partials
  * are combined by a butterfly over lane distances 16, 8, 4, 2, 1 (partial[l] + partial[l ^ d]). chunk == 0 returns
- * the exactly rounded f32 of the double-precision sum instead. `fused`: each step is fmaf(v, v, s), as the fused
- * q/k kernel does for bf16 (the square of a bf16 value is exact in f32 where it is normal, |v| >= 2^-63, so the two
- * forms differ only below that); otherwise a separately rounded product and sum, as the reference's rms_norm. */
+ * the exactly rounded f32 of the double-precision sum instead. `fused`: each step is fmaf(v, v, s), as every bf16
+ * RMSNorm and q/k-norm kernel of the device library does (the square of a bf16 value is exact in f32 where it is
+ * normal, |v| >= 2^-63, so the two forms differ only below that); otherwise (f32) a separately rounded product and
+ * sum, as the reference's rms_norm. */
 static float row_sum_squares(int dtype, const void* x, int64_t base, int64_t width, int chunk, int fused) {
     if (chunk == 0) {
         double acc = 0.0;
@@ -181,7 +182,7 @@ void oracle_rms_norm(int dtype, const void* x, int64_t x_row_stride, const void*
 #pragma omp parallel for schedule(static)
     for (int64_t r = 0; r < rows; ++r) {
         const int64_t base = r * x_row_stride;
-        const float ss = row_sum_squares(dtype, x, base, width, chunk, 0);
+        const float ss = row_sum_squares(dtype, x, base, width, chunk, dtype == DT_BF16);
         const float mean = ss / (float)width;
         const float var = mean + eps;
         const float rms = sqrtf(var);

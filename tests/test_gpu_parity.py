@@ -178,6 +178,23 @@ def test_rms_norm_bit_exact(ops, oracle, rows, width, dtype):
     assert np.array_equal(got, oracle.rms_norm(x, w, 1e-6))
 
 
+@pytest.mark.parametrize("rows,width", [(3, 1024), (5, 1001)])
+def test_rms_norm_bf16_subnormal_squares_bit_exact(ops, oracle, rows, width):
+    # Rows scaled by 2^-66 (squares near 2^-132, below the f32 normal range) and eps 0: the kernels' fused sums of
+    # squares (vector and scalar paths) and the oracle's fmaf restatement agree; so do the residual-add variant's.
+    rng = np.random.default_rng(rows + width)
+    scale = np.float32(2.0**-66)
+    x = f32_to_bf16(bf16_to_f32(seeded_bf16(rng, (rows, width))) * scale)
+    b = f32_to_bf16(bf16_to_f32(seeded_bf16(rng, (rows, width))) * scale)
+    w = seeded_bf16(rng, (width,), 1.0, 0.1)
+    assert np.abs(bf16_to_f32(x)).max() < 2.0**-63
+    assert np.array_equal(to_host(ops.rms_norm(to_dev(x), to_dev(w), 0.0)), oracle.rms_norm(x, w, 0.0))
+    s_out, y = ops.add_rms_norm(to_dev(x), to_dev(b), to_dev(w), 0.0)
+    want_s, want_y = oracle.add_rms_norm(x, b, w, 0.0)
+    assert np.array_equal(to_host(s_out), want_s)
+    assert np.array_equal(to_host(y), want_y)
+
+
 def test_rms_norm_row_strided_view(ops, oracle):
     rng = np.random.default_rng(11)
     base = seeded_bf16(rng, (64, 1536))
