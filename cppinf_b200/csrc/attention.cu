@@ -18,15 +18,19 @@
 //  - context: warp w adds p_j v_j for j = lo + w, lo + w + 4, ... in order; the 4 warp sums in order; each part
 //    pushes its partial of dims [cD/8, (c+1)D/8) to CTA c, one cluster barrier, CTA c adds the 8 partials in order;
 //    stored in bf16.
-// Only DSMEM stores carry partial results (no remote loads, no global scratch); two cluster barriers in all.
+// Only DSMEM stores carry partial results (no remote loads, no global scratch); two cluster barriers in all (three
+// with the fused projection below). Every product-accumulate (scores, P·V) is a fused multiply-add of bf16 values.
 //
 // Queries whose keys are all in the cache already (prompt chunks, the C ABI entry) with up to 16384 visible keys take
 // attention_rows_kernel instead: one CTA of 8 warps per (query, head), warp c playing part c with the same order of
 // every sum, and shared memory plus block barriers in place of the cluster (measured on B200: the 512-token prompt of
-// Qwen3-0.6B 45.2 -> 35.2 ms). The decode step keeps the cluster kernel, which also fuses the q/k norm and RoPE.
+// Qwen3-0.6B 45.2 -> 35.2 ms). The decode step keeps the cluster kernel: it stages each part's cached K/V rows with
+// two TMA tensor copies before its dependency wait, fuses the new token's q/k norm and RoPE, and (for the model's
+// common sizes) the input RMSNorm and the q|k|v projection too (kProjC below).
 //
-// Roofline: HBM/L2-bound on the cache reads (2 * L * D * 2 bytes per query head, shared by the 2 heads of a group
-// through L2); the decode step reads every cached key and value once per layer.
+// Roofline: latency-bound in decode (a chain of dependent L2 round trips, block and cluster barriers); the bytes are
+// 2 * L * D * 2 per query head (shared by the heads of a group through L2) plus, with the fused projection, this
+// head's slice of the q|k|v weights.
 #include <cooperative_groups.h>
 
 #include "common.cuh"
