@@ -14,7 +14,7 @@
 //    so the producer can refill it once the tensor cores have read it; a last commit marks the accumulator done;
 //  - all 4 warps: epilogue. Warp w reads tensor-memory lanes 32w .. 32w + 31 (= tile rows) with tcgen05.ld, 32
 //    columns at a time, and applies the decoder's epilogue in registers (bf16 store into the q|k|v segments, residual
-//    add, or SiLU(gate) * up), the same formulas as linear.cu.
+//    add, or SiLU(gate) * up -- the latter with the hardware exponential, this path being held to tolerance).
 // Every mbarrier wait polls a bounded number of times; a wait that runs out sets *error (when given), the kernel
 // carries on with meaningless data so every barrier still completes, and it waits again with the default limit for
 // the tensor cores before freeing tensor memory.
@@ -28,7 +28,6 @@
 
 #include "common.cuh"
 #include "decoder.h"
-#include "pexp.cuh"
 #include "runtime.h"
 #include "tcgen05.cuh"
 
@@ -38,6 +37,14 @@ namespace {
 using namespace tc;
 
 constexpr int kTcThreads = 128;
+
+// SiLU for this tolerance-held path: the hardware exponential and a fast division (the portable exponential and the
+// IEEE division of the bit-exact kernels cost ~40 instructions an element, which made the SiLU * up epilogue the
+// longest part of the kernel). The argument is clamped so the divisor stays below 2^126, where __fdividef is
+// accurate; below -80 SiLU is ~0 either way.
+__device__ __forceinline__ float silu_fast(float x) {
+    return __fdividef(x, 1.0f + __expf(fminf(-x, 80.0f)));
+}
 
 template <int kBN, int kMats>
 struct TcShape {
@@ -209,8 +216,8 @@ __global__ void __launch_bounds__(kTcThreads, 1)
                 for (int j = 0; j < 16; ++j) {
                     const float g0 = round_to_bf16(acc[2 * j]);
                     const float g1 = round_to_bf16(acc[2 * j + 1]);
-                    packed[j] = pack_bf16x2(round_to_bf16(silu_pexp(g0)) * round_to_bf16(up[2 * j]),
-                                            round_to_bf16(silu_pexp(g1)) * round_to_bf16(up[2 * j + 1]));
+                    packed[j] = pack_bf16x2(round_to_bf16(silu_fast(g0)) * round_to_bf16(up[2 * j]),
+                                            round_to_bf16(silu_fast(g1)) * round_to_bf16(up[2 * j + 1]));
                 }
             }
             if (m < p.M && n < p.N) {
