@@ -10,16 +10,21 @@
 // (after folding -0 into +0): max(key) is the lowest index of the largest value. A row whose element 0 is NaN
 // yields 0.
 //
-// Layout: a row is split across a thread-block cluster of up to 8 CTAs of 512 threads, each CTA scanning a
-// contiguous column range (scalar loads when the rows are not aligned for 16-byte vectors). The range streams through
-// shared memory by per-thread asynchronous copies, all of a chunk requested before any is read; each 16-byte vector
-// is first reduced with packed max instructions; a vector that would replace the thread's running maximum is kept
-// whole and searched for its index once, after the last vector. Measured on B200 against register loads in batches
-// of 5, 32-byte loads, clusters of 16, and bulk copies (TMA) of 2-8 KB chunks per CTA on mbarriers (8.5-12.6 us
-// against 6.9: the single issuing thread and the spinning waiters cost more than per-thread copies): slower. CTA
-// partials are combined through distributed shared memory: each CTA stores its key into cluster rank 0's shared
-// array, one cluster barrier makes them visible, rank 0 combines them. No global scratch and no second launch are
-// needed, and no thread waits on a flag (the copy-group waits are hardware waits).
+// Layout: a row is split across a thread-block cluster of up to 8 CTAs of 256 threads, each CTA scanning a
+// contiguous column range (scalar loads when the rows are not aligned for 16-byte vectors). Before its dependency
+// wait each CTA asks L2 for its range (`cp.async.bulk.prefetch.L2`): back-to-back launches then overlap, the next
+// launch's CTAs (20 KB of shared memory each, so a whole second grid fits beside the running one) pulling their
+// rows from HBM while the previous launch finishes. The range then streams through shared memory by per-thread
+// asynchronous copies, all of a chunk requested before any is read; each 16-byte vector is first reduced with packed
+// max instructions; a vector that would replace the thread's running maximum is kept whole and searched for its
+// index once, after the last vector. Measured on B200 ([64, 151936] bf16, graph-replayed launches over buffers
+// larger than L2): 6.19 us before the prefetch, 5.56-5.69 with it at 512 threads x 5 vectors, 5.23-5.26 at 256 x 5;
+// 256 x 3, 256 x 4, 192 x 5 (more chunks per thread), 256 x 10 and 128 x 10 (fewer CTAs beside the running grid)
+// 5.42-6.47; before the prefetch, register loads in batches of 5, 32-byte loads, clusters of 16 and bulk copies
+// (TMA) of 2-8 KB chunks per CTA on mbarriers were slower too. CTA partials are combined through distributed shared
+// memory: each CTA stores its key into cluster rank 0's shared array, one cluster barrier makes them visible, rank 0
+// combines them. No global scratch and no second launch are needed, and no thread waits on a flag (the copy-group
+// waits are hardware waits).
 //
 // Roofline: HBM-bound. Algorithmic bytes per row: cols * size read + 8 bytes written.
 #include <cooperative_groups.h>
@@ -32,10 +37,12 @@ namespace cg = cooperative_groups;
 namespace cppinf::device {
 namespace {
 
-constexpr int kThreads = 512;  // measured on [64, 151936] bf16: 7.90 us against 8.37 with 256 and 10.98 with 128
+constexpr int kThreads = 256;
 constexpr int kWarps = kThreads / 32;
-constexpr int kStaged = 5;  // 16-byte vectors per thread per shared-memory chunk (40 KB per CTA)
+constexpr int kStaged = 5;  // 16-byte vectors per thread per shared-memory chunk (20 KB per CTA)
 constexpr int kMaxCluster = 8;
+constexpr int64_t kPrefetchBytes = 64 * 1024;  // per CTA, issued before the dependency wait
+constexpr int kCtasPerSm = 4;                  // grid target: rows * cluster CTAs up to this many per SM
 
 __device__ __forceinline__ unsigned long long argmax_key(float v, uint32_t index) {
     uint32_t u = __float_as_uint(v);
@@ -131,7 +138,6 @@ struct Running {
 template <typename T, int kBytes>
 __global__ void __launch_bounds__(kThreads) row_argmax_kernel(const void* __restrict__ x, int64_t cols,
                                                               int64_t row_stride, int64_t* __restrict__ out) {
-    grid_dependency_begin();
     // Every CTA of the cluster has started once this barrier phase completes; it is waited on right before the one
     // DSMEM store below, long after every CTA has arrived.
     asm volatile("barrier.cluster.arrive.relaxed.aligned;" ::: "memory");
@@ -152,6 +158,22 @@ __global__ void __launch_bounds__(kThreads) row_argmax_kernel(const void* __rest
     const int per_cta = ((((ncols - 1) >> cshift) + 1 + kVec - 1) / kVec) * kVec;
     const int lo = per_cta * static_cast<int>(rank) < ncols ? per_cta * static_cast<int>(rank) : ncols;
     const int hi = lo + per_cta < ncols ? lo + per_cta : ncols;
+
+    // Before the dependency wait (while the previous kernel still runs): ask L2 for the first kPrefetchBytes of this
+    // CTA's whole vectors. A prefetch returns no data and L2 is the point of coherence, so values the previous kernel
+    // writes after it are still the ones read below.
+    if constexpr (kBytes > 0) {
+        if (threadIdx.x == 0) {
+            const int64_t whole = static_cast<int64_t>((hi - lo) / kVec) * kBytes;
+            const uint32_t bytes = static_cast<uint32_t>(whole < kPrefetchBytes ? whole : kPrefetchBytes);
+            if (bytes > 0) {
+                bulk_prefetch_l2(xr + static_cast<int64_t>(lo) * static_cast<int64_t>(sizeof(T)), bytes);
+            }
+        }
+    }
+    grid_dependency_begin();
+    // Element 0 of the row decides the NaN-at-index-0 case; its load is issued now and lands during the scan.
+    const float first = rank == 0 && threadIdx.x == 0 ? Vec16<T>::load1(xr, 0) : 0.0f;
 
     // Each thread visits its elements in increasing index order (vectors v, v + kThreads, ...; then the tail).
     Running run;
@@ -220,7 +242,6 @@ __global__ void __launch_bounds__(kThreads) row_argmax_kernel(const void* __rest
         for (unsigned r = 1; r < csize; ++r) {
             b = umax64(b, cluster_best[r]);
         }
-        const float first = Vec16<T>::load1(xr, 0);
         int64_t index = 0;
         if (first == first && b != 0ull) {
             index = static_cast<int64_t>(0xffffffffu - static_cast<uint32_t>(b & 0xffffffffull));
@@ -265,7 +286,7 @@ int cppinf_row_argmax(cppinf_dtype dtype, const void* x, int64_t rows, int64_t c
     CPPINF_REQUIRE(rows <= (int64_t{1} << 27), CPPINF_ERR_UNSUPPORTED, "row_argmax supports at most 2^27 rows.");
 
     // Enough CTAs to cover the SMs a few times, but no CTA with fewer than ~4K columns.
-    const int64_t target_ctas = static_cast<int64_t>(rt::sm_count()) * 4;
+    const int64_t target_ctas = static_cast<int64_t>(rt::sm_count()) * kCtasPerSm;
     int64_t cluster = 1;
     while (cluster < kMaxCluster && rows * cluster < target_ctas && cols / (cluster * 2) >= 4096) {
         cluster *= 2;

@@ -48,7 +48,7 @@ __device__ __forceinline__ float silu_fast(float x) {
 
 template <int kBN, int kMats>
 struct TcShape {
-    static constexpr int kStages = kMats == 2 && kBN == 128 ? 3 : 4;
+    static constexpr int kStages = kMats == 2 && kBN >= 64 ? 3 : 4;
     static constexpr uint32_t kABytes = kBM * kBK * 2;   // 16 KB
     static constexpr uint32_t kBBytes = kBN * kBK * 2;   // 4, 8 or 16 KB
     static constexpr uint32_t kStageBytes = kABytes + kMats * kBBytes;

@@ -38,13 +38,26 @@ struct RmsParams {
 // Register-resident variant: each lane holds kChunks 16-byte vectors of its row.
 template <typename T, int kChunks, bool kAdd>
 __global__ void __launch_bounds__(kThreads) rms_norm_regs_kernel(RmsParams p) {
-    grid_dependency_begin();
     using V = Vec16<T>;
     constexpr int kVec = V::kVec;
     const int lane = threadIdx.x & 31;
     const int nchunks = p.width / kVec;
     const float width_f = static_cast<float>(p.width);
     const int64_t warp_stride = static_cast<int64_t>(gridDim.x) * kWarps;
+    // Before the dependency wait (while the previous kernel still runs), lane 0 asks L2 for the warp's first row
+    // (and its addend row). A prefetch returns no data and L2 is the point of coherence, so the loads after the wait
+    // still see what the previous kernel writes.
+    const int64_t first_row = static_cast<int64_t>(blockIdx.x) * kWarps + threadIdx.x / 32;
+    if (lane == 0 && first_row < p.rows) {
+        const auto row_bytes = static_cast<uint32_t>(p.width * static_cast<int>(sizeof(T)));
+        bulk_prefetch_l2(static_cast<const char*>(p.x) + first_row * p.x_stride * static_cast<int64_t>(sizeof(T)),
+                         row_bytes);
+        if constexpr (kAdd) {
+            bulk_prefetch_l2(static_cast<const char*>(p.b) + first_row * p.width * static_cast<int64_t>(sizeof(T)),
+                             row_bytes);
+        }
+    }
+    grid_dependency_begin();
 
     for (int64_t row = static_cast<int64_t>(blockIdx.x) * kWarps + threadIdx.x / 32; row < p.rows;
          row += warp_stride) {
