@@ -20,7 +20,8 @@
 // index once, after the last vector. Measured on B200 ([64, 151936] bf16, graph-replayed launches over buffers
 // larger than L2): 6.19 us before the prefetch, 5.56-5.69 with it at 512 threads x 5 vectors, 5.23-5.26 at 256 x 5;
 // 256 x 3, 256 x 4, 192 x 5 (more chunks per thread), 256 x 10 and 128 x 10 (fewer CTAs beside the running grid)
-// 5.42-6.47; before the prefetch, register loads in batches of 5, 32-byte loads, clusters of 16 and bulk copies
+// 5.42-6.47. Each CTA also prefetching the range of the CTA half a grid away (the first CTAs to become resident
+// then cover the rest): 6.03 -> 5.35 and 5.79-5.90 -> 5.47 us on two further boxes (four partners: 6.69); before the prefetch, register loads in batches of 5, 32-byte loads, clusters of 16 and bulk copies
 // (TMA) of 2-8 KB chunks per CTA on mbarriers were slower too. CTA partials are combined through distributed shared
 // memory: each CTA stores its key into cluster rank 0's shared array, one cluster barrier makes them visible, rank 0
 // combines them. No global scratch and no second launch are needed, and no thread waits on a flag (the copy-group
@@ -41,7 +42,8 @@ constexpr int kThreads = 256;
 constexpr int kWarps = kThreads / 32;
 constexpr int kStaged = 5;  // 16-byte vectors per thread per shared-memory chunk (20 KB per CTA)
 constexpr int kMaxCluster = 8;
-constexpr int64_t kPrefetchBytes = 64 * 1024;  // per CTA, issued before the dependency wait
+constexpr int64_t kPrefetchBytes = 64 * 1024;  // per CTA range, issued before the dependency wait
+constexpr int kPrefetchSlices = 2;             // CTA ranges each CTA prefetches (4: slower)
 constexpr int kCtasPerSm = 4;                  // grid target: rows * cluster CTAs up to this many per SM
 
 __device__ __forceinline__ unsigned long long argmax_key(float v, uint32_t index) {
@@ -159,15 +161,24 @@ __global__ void __launch_bounds__(kThreads) row_argmax_kernel(const void* __rest
     const int lo = per_cta * static_cast<int>(rank) < ncols ? per_cta * static_cast<int>(rank) : ncols;
     const int hi = lo + per_cta < ncols ? lo + per_cta : ncols;
 
-    // Before the dependency wait (while the previous kernel still runs): ask L2 for the first kPrefetchBytes of this
-    // CTA's whole vectors. A prefetch returns no data and L2 is the point of coherence, so values the previous kernel
-    // writes after it are still the ones read below.
+    // Before the dependency wait (while the previous kernel still runs): ask L2 for the first kPrefetchBytes of the
+    // whole vectors of kPrefetchSlices CTAs' ranges, this CTA's and those of kPrefetchSlices - 1 partners spread over
+    // the grid (the CTAs that become resident first then also cover those that cannot yet). A prefetch returns no
+    // data and L2 is the point of coherence, so values the previous kernel writes after it are still the ones read
+    // below.
     if constexpr (kBytes > 0) {
-        if (threadIdx.x == 0) {
-            const int64_t whole = static_cast<int64_t>((hi - lo) / kVec) * kBytes;
+        if (threadIdx.x < kPrefetchSlices) {
+            const unsigned step = (gridDim.x + kPrefetchSlices - 1) / kPrefetchSlices;
+            const unsigned c = (blockIdx.x + threadIdx.x * step) % gridDim.x;
+            const int c_rank = static_cast<int>(c & (csize - 1));
+            const int c_lo = per_cta * c_rank < ncols ? per_cta * c_rank : ncols;
+            const int c_hi = c_lo + per_cta < ncols ? c_lo + per_cta : ncols;
+            const int64_t whole = static_cast<int64_t>((c_hi - c_lo) / kVec) * kBytes;
             const uint32_t bytes = static_cast<uint32_t>(whole < kPrefetchBytes ? whole : kPrefetchBytes);
             if (bytes > 0) {
-                bulk_prefetch_l2(xr + static_cast<int64_t>(lo) * static_cast<int64_t>(sizeof(T)), bytes);
+                const char* c_row = static_cast<const char*>(x) +
+                                    static_cast<int64_t>(c >> cshift) * row_stride * static_cast<int64_t>(sizeof(T));
+                bulk_prefetch_l2(c_row + static_cast<int64_t>(c_lo) * static_cast<int64_t>(sizeof(T)), bytes);
             }
         }
     }
