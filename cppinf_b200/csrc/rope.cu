@@ -20,7 +20,8 @@
 // and staged the angles and weights in shared memory: 6.43 -> 5.99 us; holding the weights as f32 (more registers,
 // fewer CTAs per SM) 6.36 us. Later, with the packed products below, packed fused multiply-adds for the bf16 sum
 // of squares: 5.92 -> 5.82 us; each unit's rows asked of L2 before the dependency wait, so that back-to-back
-// launches overlap: 5.82 -> 5.23 us.
+// launches overlap: 5.82 -> 5.23 us; each warp also prefetching the unit half a grid away: 5.41 -> 5.19 us
+// (three or four partners: 5.27 / 5.54 us; the same for the residual add + RMSNorm rows was slower).
 //
 // Reduction order: the sum of squares of a head equals the library's canonical order (lane c sums chunk c, then a
 // butterfly over lane distances 16, 8, ..., 1 over the D/kVec chunks): here a lane adds its first-half partial to its
@@ -44,6 +45,7 @@ namespace {
 constexpr int kThreads = 256;
 constexpr int kQkThreads = 64;  // two warp units per CTA
 constexpr int kQkWarps = kQkThreads / 32;
+constexpr int kPrefetchUnits = 2;  // warp units whose rows each warp prefetches before the dependency wait
 
 struct QkParams {
     const void* q;
@@ -99,13 +101,23 @@ __global__ void __launch_bounds__(kQkThreads, 16) qk_norm_rope_kernel(const QkPa
     const char* wsrc = static_cast<const char*>(is_q ? p.qw : p.kw) + hl * 16;
     const float* trow = p.table + (p.position_offset + t) * kDim + hl * kVec;
 
-    // Before the dependency wait (while the previous kernel still runs), lane 0 asks L2 for the unit's head rows
-    // (contiguous). A prefetch returns no data and L2 is the point of coherence, so the loads below still see what
-    // the previous kernel writes; everything that reads memory follows the wait, since the op does not know which
-    // of its inputs the previous kernel of the stream wrote.
-    if (lane == 0) {
-        const int unit_heads = kFull ? kHeadsPerUnit : min(kHeadsPerUnit, heads - h0);
-        bulk_prefetch_l2(src, static_cast<uint32_t>(unit_heads * kHeadBytes));
+    // Before the dependency wait (while the previous kernel still runs), lanes 0 .. kPrefetchUnits - 1 ask L2 for the
+    // head rows (contiguous) of this unit and of kPrefetchUnits - 1 partner units spread over the grid, so the warps
+    // that become resident first also cover those that cannot yet. A prefetch returns no data and L2 is the point of
+    // coherence, so the loads below still see what the previous kernel writes; everything that reads memory follows
+    // the wait, since the op does not know which of its inputs the previous kernel of the stream wrote.
+    if (lane < kPrefetchUnits) {
+        const uint32_t step = (p.units + kPrefetchUnits - 1) / kPrefetchUnits;
+        const uint32_t pu = (unit + static_cast<uint32_t>(lane) * step) % p.units;
+        const uint32_t pt = p.per_token.quot(pu);
+        const int pk = static_cast<int>(pu - pt * p.per_token.d);
+        const bool pq = pk < p.q_units;
+        const int pheads = pq ? p.q_heads : p.k_heads;
+        const int ph0 = (pq ? pk : pk - p.q_units) * kHeadsPerUnit;
+        const int unit_heads = kFull ? kHeadsPerUnit : min(kHeadsPerUnit, pheads - ph0);
+        const char* psrc = static_cast<const char*>(pq ? p.q : p.k) +
+                           (static_cast<int64_t>(pt) * pheads + ph0) * kHeadBytes;
+        bulk_prefetch_l2(psrc, static_cast<uint32_t>(unit_heads * kHeadBytes));
     }
     grid_dependency_begin();
 #pragma unroll
