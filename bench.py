@@ -844,11 +844,12 @@ def measure_decode(device, runs: int) -> dict:
         if i > 0:  # the first run is a warm-up
             tc_ms.append(e0.elapsed_time(e1))
     model.set_prefill("cuda_cores")
+    step_launches = model.step_launches()
     model.close()
     dec = statistics.median(decode_ms)
     return {"decode_ms": dec, "prefill_ms": statistics.median(prefill_ms), "e2e_s": e2e_s,
             "prefill_tc_ms": statistics.median(tc_ms), "prefill_tc_first_token_same": tc_first == tokens[0],
-            "launches_per_run": launches, "step_launches": 5 * cfg.num_hidden_layers + 1, "tokens": tokens,
+            "launches_per_run": launches, "step_launches": step_launches, "tokens": tokens,
             "deterministic": again == tokens, "cfg": cfg}
 
 

@@ -17,8 +17,10 @@
 // the post-attention norm and SiLU * up; down_proj + residual; final norm + LM head + argmax), captured once as a
 // CUDA graph. Sizes the fused attention does not take (decode_projection_fused) run the projection as a fifth kernel
 // per layer. Every kernel reads the sequence length from device memory, and the last one advances it, so the same
-// graph is replayed for every step.
+// graphs are replayed for every step: one of eight consecutive steps (no graph-launch gap between them) and one of a
+// single step for the remainder.
 #include <cstring>
+#include <optional>
 #include <string>
 #include <vector>
 
@@ -87,6 +89,8 @@ struct cppinf_qwen3 {
     int64_t len = 0;
     cudaGraphExec_t step = nullptr;
     int64_t step_launches = 0;
+    cudaGraphExec_t step_block = nullptr;  // kBlockSteps steps in one graph
+    int64_t step_block_launches = 0;
     uint32_t step_poll_limit = 0;  // the wait poll limit the decode-step graph was captured with
     int prefill_mode = 0;          // 0: CUDA-core projections (restated order), 1: tensor cores (tolerance parity)
     bool failed = false;           // a decode step reported a device error; cleared by cppinf_qwen3_reset
@@ -165,8 +169,11 @@ bool projection_fused(const cppinf_qwen3* m) {
     return cppinf::device::decode_projection_fused(m->c.head_dim, m->c.hidden_size, m->cap);
 }
 
-// One decode step at the device-side position (see the file comment). Returns the number of launches.
-int enqueue_step(cppinf_qwen3* m, cudaStream_t s, int64_t* launches) {
+// One decode step at the device-side position (see the file comment). Returns the number of launches. With
+// `after_step` (a step enqueued right behind another in one graph) the step's first kernel starts only once the
+// previous step's last kernel has completed: the attention kernel reads the sequence length before its dependency
+// wait, and the LM head before it advances that length.
+int enqueue_step(cppinf_qwen3* m, cudaStream_t s, int64_t* launches, bool after_step = false) {
     const auto& c = m->c;
     const int64_t H = c.hidden_size;
     const bool fused = projection_fused(m);
@@ -185,7 +192,11 @@ int enqueue_step(cppinf_qwen3* m, cudaStream_t s, int64_t* launches) {
             qkv.eps = c.rms_norm_eps;
             set_qkv_outputs(m, l, qkv, 0, m->d_len);
             qkv.error = m->d_error;
-            QWEN3_TRY(cppinf::device::launch_gemv(qkv, s), "qwen3_qkv");
+            {
+                const std::optional<rt::SerialLaunch> serial =
+                    after_step && i == 0 ? std::optional<rt::SerialLaunch>(std::in_place) : std::nullopt;
+                QWEN3_TRY(cppinf::device::launch_gemv(qkv, s), "qwen3_qkv");
+            }
             ++n;
         }
         // q/k-norm + RoPE and the new key's cache row are fused into the attention kernel, and with `fused` the
@@ -204,7 +215,11 @@ int enqueue_step(cppinf_qwen3* m, cudaStream_t s, int64_t* launches) {
             ap.wqkv = l.wqkv;
             ap.hidden = static_cast<int>(H);
         }
-        QWEN3_TRY(cppinf::device::launch_decoder_attention(ap, m->cap, s), "qwen3_attention");
+        {
+            const std::optional<rt::SerialLaunch> serial =
+                after_step && i == 0 && fused ? std::optional<rt::SerialLaunch>(std::in_place) : std::nullopt;
+            QWEN3_TRY(cppinf::device::launch_decoder_attention(ap, m->cap, s), "qwen3_attention");
+        }
         LinearParams o = params_for(LinearEpilogue::kResidual, m->ctx, m->q_dim, l.wo, nullptr, 1, H, m->q_dim);
         o.residual = m->h;
         o.res_ld = H;
@@ -231,6 +246,45 @@ int enqueue_step(cppinf_qwen3* m, cudaStream_t s, int64_t* launches) {
     }
     QWEN3_TRY(cppinf::device::launch_gemv(lm_head_params(m, m->h, 1, nullptr), s), "qwen3_lm_head_argmax");
     *launches = n + 1;
+    return CPPINF_OK;
+}
+
+// Decode steps replayed per graph launch when a call asks for at least this many: consecutive steps in one graph
+// leave out the graph-launch gap between them.
+constexpr int64_t kBlockSteps = 8;
+
+// Captures `count` consecutive decode steps into one executable graph.
+int capture_steps(cppinf_qwen3* m, int64_t count, cudaGraphExec_t* exec, int64_t* launches) {
+    cudaStream_t cap_stream = nullptr;
+    CPPINF_CUDA_TRY(cudaStreamCreateWithFlags(&cap_stream, cudaStreamNonBlocking));
+    cudaGraph_t graph = nullptr;
+    cudaError_t err = cudaStreamBeginCapture(cap_stream, cudaStreamCaptureModeThreadLocal);
+    int64_t total = 0;
+    int st = CPPINF_OK;
+    if (err == cudaSuccess) {
+        for (int64_t k = 0; k < count && st == CPPINF_OK; ++k) {
+            int64_t n = 0;
+            st = enqueue_step(m, cap_stream, &n, k > 0);
+            total += n;
+        }
+        err = cudaStreamEndCapture(cap_stream, &graph);
+    }
+    if (err == cudaSuccess && st == CPPINF_OK) {
+        err = cudaGraphInstantiate(exec, graph, 0);
+    }
+    if (graph != nullptr) {
+        cudaGraphDestroy(graph);
+    }
+    cudaStreamDestroy(cap_stream);
+    if (st != CPPINF_OK) {
+        return st;
+    }
+    if (err != cudaSuccess) {
+        *exec = nullptr;
+        return rt::cuda_fail(err, "qwen3_decode graph capture");
+    }
+    *launches = total;
+    rt::count_launches(-total);  // captured, not executed: each replay counts them
     return CPPINF_OK;
 }
 
@@ -517,6 +571,9 @@ int find_weight(cppinf_qwen3* m, const std::string& name, WeightSlot* slot) {
 void release(cppinf_qwen3* m) {
     if (m->step != nullptr) {
         cudaGraphExecDestroy(m->step);
+    }
+    if (m->step_block != nullptr) {
+        cudaGraphExecDestroy(m->step_block);
     }
     cudaFree(m->weights);
     cudaFree(m->cache);
@@ -934,41 +991,33 @@ int cppinf_qwen3_decode(cppinf_qwen3* model, int64_t steps, int64_t* tokens, voi
                    "qwen_attention cache is too small for the new tokens.");
     const auto s = rt::as_stream(stream);
     if (model->step != nullptr && model->step_poll_limit != rt::wait_poll_limit()) {
-        // The wait poll limit changed since the step was captured: capture it again with the current one (an
+        // The wait poll limit changed since the steps were captured: capture them again with the current one (an
         // executable graph still in flight is freed when it completes).
         cudaGraphExecDestroy(model->step);
         model->step = nullptr;
+        if (model->step_block != nullptr) {
+            cudaGraphExecDestroy(model->step_block);
+            model->step_block = nullptr;
+        }
     }
     if (model->step == nullptr) {
         model->step_poll_limit = rt::wait_poll_limit();
-        cudaStream_t cap_stream = nullptr;
-        CPPINF_CUDA_TRY(cudaStreamCreateWithFlags(&cap_stream, cudaStreamNonBlocking));
-        cudaGraph_t graph = nullptr;
-        cudaError_t err = cudaStreamBeginCapture(cap_stream, cudaStreamCaptureModeThreadLocal);
-        int64_t launches = 0;
-        int st = CPPINF_OK;
-        if (err == cudaSuccess) {
-            st = enqueue_step(model, cap_stream, &launches);
-            err = cudaStreamEndCapture(cap_stream, &graph);
-        }
-        if (err == cudaSuccess && st == CPPINF_OK) {
-            err = cudaGraphInstantiate(&model->step, graph, 0);
-        }
-        if (graph != nullptr) {
-            cudaGraphDestroy(graph);
-        }
-        cudaStreamDestroy(cap_stream);
-        if (st != CPPINF_OK) {
+        if (const int st = capture_steps(model, 1, &model->step, &model->step_launches); st != CPPINF_OK) {
             return st;
         }
-        if (err != cudaSuccess) {
-            model->step = nullptr;
-            return rt::cuda_fail(err, "qwen3_decode graph capture");
-        }
-        model->step_launches = launches;
-        rt::count_launches(-launches);  // captured, not executed: each replay below counts them
     }
-    for (int64_t i = 0; i < steps; ++i) {
+    if (steps >= kBlockSteps && model->step_block == nullptr) {
+        if (const int st = capture_steps(model, kBlockSteps, &model->step_block, &model->step_block_launches);
+            st != CPPINF_OK) {
+            return st;
+        }
+    }
+    int64_t i = 0;
+    for (; i + kBlockSteps <= steps; i += kBlockSteps) {
+        CPPINF_CUDA_TRY(cudaGraphLaunch(model->step_block, s));
+        rt::count_launches(model->step_block_launches);
+    }
+    for (; i < steps; ++i) {
         CPPINF_CUDA_TRY(cudaGraphLaunch(model->step, s));
         rt::count_launches(model->step_launches);
     }

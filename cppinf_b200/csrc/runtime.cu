@@ -9,6 +9,7 @@ namespace cppinf::runtime {
 namespace {
 
 thread_local std::string g_last_error;
+thread_local bool g_serial_launch = false;  // a SerialLaunch is alive on this thread
 std::atomic<uint64_t> g_launches{0};
 std::atomic<uint32_t> g_poll_limit{1u << 24};
 
@@ -89,6 +90,18 @@ int sm_count() {
 
 int max_threads_per_sm() {
     return props_for_current_device().max_threads_per_sm;
+}
+
+bool pdl_enabled() {
+    return !g_serial_launch;
+}
+
+SerialLaunch::SerialLaunch() : previous_(g_serial_launch) {
+    g_serial_launch = true;
+}
+
+SerialLaunch::~SerialLaunch() {
+    g_serial_launch = previous_;
 }
 
 uint32_t wait_poll_limit() {

@@ -55,11 +55,27 @@ inline bool valid_dtype(cppinf_dtype dtype) {
     return dtype == CPPINF_DTYPE_BF16 || dtype == CPPINF_DTYPE_F32;
 }
 
-// Launches `kernel` with `smem_bytes` of dynamic shared memory and programmatic dependent launch allowed: the grid
+// Launches `kernel` with `smem_bytes` of dynamic shared memory and (see pdl_enabled) programmatic dependent launch
+// allowed: the grid
 // may be scheduled while the previous kernel in the stream is still finishing. Every kernel of this library executes
 // griddepcontrol.wait before it reads memory another kernel writes, which waits for the previous grid to complete
 // and its writes to become visible, so results are the same as with plain stream order; only launch latency and the
 // previous grid's tail overlap. `cluster_x` > 1 adds a thread-block cluster dimension.
+// Programmatic dependent launch is on for every launch of this thread unless a SerialLaunch is alive on it: then the
+// grid starts only after the previous kernel of the stream has completed. For a kernel that reads, before its
+// dependency wait, data that the kernel before it writes.
+bool pdl_enabled();
+class SerialLaunch {
+public:
+    SerialLaunch();
+    ~SerialLaunch();
+    SerialLaunch(const SerialLaunch&) = delete;
+    SerialLaunch& operator=(const SerialLaunch&) = delete;
+
+private:
+    bool previous_;
+};
+
 template <typename... KernelArgs, typename... Args>
 cudaError_t launch_smem(void (*kernel)(KernelArgs...), dim3 grid, dim3 block, std::size_t smem_bytes,
                         cudaStream_t stream, unsigned cluster_x, Args&&... args) {
@@ -69,15 +85,18 @@ cudaError_t launch_smem(void (*kernel)(KernelArgs...), dim3 grid, dim3 block, st
     cfg.dynamicSmemBytes = smem_bytes;
     cfg.stream = stream;
     cudaLaunchAttribute attrs[2];
-    attrs[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-    attrs[0].val.programmaticStreamSerializationAllowed = 1;
-    unsigned n = 1;
+    unsigned n = 0;
+    if (pdl_enabled()) {
+        attrs[n].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+        attrs[n].val.programmaticStreamSerializationAllowed = 1;
+        ++n;
+    }
     if (cluster_x > 1) {
-        attrs[1].id = cudaLaunchAttributeClusterDimension;
-        attrs[1].val.clusterDim.x = cluster_x;
-        attrs[1].val.clusterDim.y = 1;
-        attrs[1].val.clusterDim.z = 1;
-        n = 2;
+        attrs[n].id = cudaLaunchAttributeClusterDimension;
+        attrs[n].val.clusterDim.x = cluster_x;
+        attrs[n].val.clusterDim.y = 1;
+        attrs[n].val.clusterDim.z = 1;
+        ++n;
     }
     cfg.attrs = attrs;
     cfg.numAttrs = n;
