@@ -844,7 +844,7 @@ def measure_decode(device, runs: int) -> dict:
         if i > 0:  # the first run is a warm-up
             tc_ms.append(e0.elapsed_time(e1))
     model.set_prefill("cuda_cores")
-    step_launches = model.step_launches()
+    step_launches = model.step_launches
     model.close()
     dec = statistics.median(decode_ms)
     return {"decode_ms": dec, "prefill_ms": statistics.median(prefill_ms), "e2e_s": e2e_s,

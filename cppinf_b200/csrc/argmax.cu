@@ -10,22 +10,25 @@
 // (after folding -0 into +0): max(key) is the lowest index of the largest value. A row whose element 0 is NaN
 // yields 0.
 //
-// Layout: a row is split across a thread-block cluster of up to 8 CTAs of 256 threads, each CTA scanning a
-// contiguous column range (scalar loads when the rows are not aligned for 16-byte vectors). Before its dependency
-// wait each CTA asks L2 for its range (`cp.async.bulk.prefetch.L2`): back-to-back launches then overlap, the next
-// launch's CTAs (20 KB of shared memory each, so a whole second grid fits beside the running one) pulling their
-// rows from HBM while the previous launch finishes. The range then streams through shared memory by per-thread
-// asynchronous copies, all of a chunk requested before any is read; each 16-byte vector is first reduced with packed
-// max instructions; a vector that would replace the thread's running maximum is kept whole and searched for its
-// index once, after the last vector. Measured on B200 ([64, 151936] bf16, graph-replayed launches over buffers
-// larger than L2): 6.19 us before the prefetch, 5.56-5.69 with it at 512 threads x 5 vectors, 5.23-5.26 at 256 x 5;
-// 256 x 3, 256 x 4, 192 x 5 (more chunks per thread), 256 x 10 and 128 x 10 (fewer CTAs beside the running grid)
-// 5.42-6.47. Each CTA also prefetching the range of the CTA half a grid away (the first CTAs to become resident
-// then cover the rest): 6.03 -> 5.35 and 5.79-5.90 -> 5.47 us on two further boxes (four partners: 6.69); before the prefetch, register loads in batches of 5, 32-byte loads, clusters of 16 and bulk copies
-// (TMA) of 2-8 KB chunks per CTA on mbarriers were slower too. CTA partials are combined through distributed shared
-// memory: each CTA stores its key into cluster rank 0's shared array, one cluster barrier makes them visible, rank 0
-// combines them. No global scratch and no second launch are needed, and no thread waits on a flag (the copy-group
-// waits are hardware waits).
+// Layout: a row is split across a thread-block cluster of up to 8 CTAs of 256 threads, each CTA scanning a contiguous
+// column range (scalar loads when the rows are not aligned for 16-byte vectors). Before its dependency wait each CTA
+// asks L2 for its range (`cp.async.bulk.prefetch.L2`): back-to-back launches then overlap, the next launch's CTAs (20
+// KB of shared memory each, so a whole second grid fits beside the running one) pulling their rows from HBM while the
+// previous launch finishes. The range then streams through shared memory by per-thread asynchronous copies and through
+// registers, all of a chunk requested before any is read; each 16-byte vector is first reduced with packed max
+// instructions; a vector that would replace the thread's running maximum is kept whole and searched for its index once,
+// after the last vector. Measured on B200 ([64, 151936] bf16, graph-replayed launches over buffers larger than L2):
+// 6.19 us before the prefetch, 5.56-5.69 with it at 512 threads x 5 vectors, 5.23-5.26 at 256 x 5; 256 x 3, 256 x 4,
+// 192 x 5 (more chunks per thread), 256 x 10 and 128 x 10 (fewer CTAs beside the running grid) 5.42-6.47. Each CTA also
+// prefetching the range of the CTA half a grid away (the first CTAs to become resident then cover the rest): 6.03 ->
+// 5.35 and 5.79-5.90 -> 5.47 us on two further boxes (four partners: 6.69). Five of each thread's ten vectors loaded
+// into registers beside the five copied to shared memory, so a thread's whole range is one round trip: 5.33-5.42 ->
+// 5.10-5.12 us on two boxes (7 + 3, 6 + 4: 6.3-6.4 us; 4 + 6 and more in registers, past 64 registers and so two waves:
+// 8.5-9.0 us); before the prefetch, register loads in batches of 5, 32-byte loads, clusters of 16 and bulk copies (TMA)
+// of 2-8 KB chunks per CTA on mbarriers were slower too. CTA partials are combined through distributed shared memory:
+// each CTA stores its key into cluster rank 0's shared array, one cluster barrier makes them visible, rank 0 combines
+// them. No global scratch and no second launch are needed, and no thread waits on a flag (the copy-group waits are
+// hardware waits).
 //
 // Roofline: HBM-bound. Algorithmic bytes per row: cols * size read + 8 bytes written.
 #include <cooperative_groups.h>
@@ -41,6 +44,8 @@ namespace {
 constexpr int kThreads = 256;
 constexpr int kWarps = kThreads / 32;
 constexpr int kStaged = 5;  // 16-byte vectors per thread per shared-memory chunk (20 KB per CTA)
+constexpr int kHeld = 5;    // 16-byte vectors per thread per chunk loaded into registers
+constexpr int kCtasPerSmMin = 4;  // register cap of 64: one wave of 4 CTAs per SM (more registers: two waves)
 constexpr int kMaxCluster = 8;
 constexpr int64_t kPrefetchBytes = 64 * 1024;  // per CTA range, issued before the dependency wait
 constexpr int kPrefetchSlices = 2;             // CTA ranges each CTA prefetches (4: slower)
@@ -138,7 +143,7 @@ struct Running {
 
 // kBytes: 32 or 16 for vector loads of the row, 0 for element loads.
 template <typename T, int kBytes>
-__global__ void __launch_bounds__(kThreads) row_argmax_kernel(const void* __restrict__ x, int64_t cols,
+__global__ void __launch_bounds__(kThreads, kCtasPerSmMin) row_argmax_kernel(const void* __restrict__ x, int64_t cols,
                                                               int64_t row_stride, int64_t* __restrict__ out) {
     // Every CTA of the cluster has started once this barrier phase completes; it is waited on right before the one
     // DSMEM store below, long after every CTA has arrived.
@@ -191,12 +196,13 @@ __global__ void __launch_bounds__(kThreads) row_argmax_kernel(const void* __rest
     if constexpr (kBytes > 0) {
         const int nvec = (hi - lo) / kVec;
         const char* base = xr + static_cast<int64_t>(lo) * static_cast<int64_t>(sizeof(T));
-        // The slice streams through shared memory in chunks of kStaged vectors per thread: every vector of a chunk
-        // is requested by an asynchronous copy before the thread waits for any of them, so a whole chunk (the whole
-        // slice, for the 151936-column vocabulary) is in flight at once without holding registers. Each thread
-        // reads back only the slots it filled, so no block barrier is needed.
+        // The slice streams in chunks of kStaged + kHeld vectors per thread: the first kStaged by asynchronous copies
+        // into shared memory, the next kHeld by loads into registers, all of a chunk requested before the thread
+        // waits for any of them, so a whole chunk (the whole slice, for the 151936-column vocabulary) is one round
+        // trip. Each thread reads back only the shared-memory slots it filled, so no block barrier is needed; the
+        // vectors are visited in increasing index order (shared-memory ones first).
         __shared__ uint4 staged[kStaged][kThreads];
-        for (int c0 = 0; c0 < nvec; c0 += kStaged * kThreads) {
+        for (int c0 = 0; c0 < nvec; c0 += (kStaged + kHeld) * kThreads) {
 #pragma unroll
             for (int u = 0; u < kStaged; ++u) {
                 const int v = c0 + u * kThreads + static_cast<int>(threadIdx.x);
@@ -205,6 +211,14 @@ __global__ void __launch_bounds__(kThreads) row_argmax_kernel(const void* __rest
                 }
                 cp_async_commit();
             }
+            uint4 held[kHeld];
+#pragma unroll
+            for (int u = 0; u < kHeld; ++u) {
+                const int v = c0 + (kStaged + u) * kThreads + static_cast<int>(threadIdx.x);
+                if (v < nvec) {
+                    held[u] = ld_stream(base + static_cast<int64_t>(v) * kBytes);
+                }
+            }
             // Vector u is visited as soon as its own copy group has landed (the later ones keep arriving).
 #pragma unroll
             for (int u = 0; u < kStaged; ++u) {
@@ -212,6 +226,13 @@ __global__ void __launch_bounds__(kThreads) row_argmax_kernel(const void* __rest
                 const int v = c0 + u * kThreads + static_cast<int>(threadIdx.x);
                 if (v < nvec) {
                     run.visit_vector<T>(staged[u][threadIdx.x], lo + v * kVec);
+                }
+            }
+#pragma unroll
+            for (int u = 0; u < kHeld; ++u) {
+                const int v = c0 + (kStaged + u) * kThreads + static_cast<int>(threadIdx.x);
+                if (v < nvec) {
+                    run.visit_vector<T>(held[u], lo + v * kVec);
                 }
             }
         }
