@@ -24,7 +24,8 @@
 // 5.35 and 5.79-5.90 -> 5.47 us on two further boxes (four partners: 6.69). Five of each thread's ten vectors loaded
 // into registers beside the five copied to shared memory, so a thread's whole range is one round trip: 5.33-5.42 ->
 // 5.10-5.12 us on two boxes (7 + 3, 6 + 4: 6.3-6.4 us; 4 + 6 and more in registers, past 64 registers and so two waves:
-// 8.5-9.0 us); before the prefetch, register loads in batches of 5, 32-byte loads, clusters of 16 and bulk copies (TMA)
+// 8.5-9.0 us). With one round trip the partner prefetch no longer pays: one range per CTA 5.07 us against 5.60 with the
+// partner's. Before the prefetch, register loads in batches of 5, 32-byte loads, clusters of 16 and bulk copies (TMA)
 // of 2-8 KB chunks per CTA on mbarriers were slower too. CTA partials are combined through distributed shared memory:
 // each CTA stores its key into cluster rank 0's shared array, one cluster barrier makes them visible, rank 0 combines
 // them. No global scratch and no second launch are needed, and no thread waits on a flag (the copy-group waits are
@@ -48,7 +49,7 @@ constexpr int kHeld = 5;    // 16-byte vectors per thread per chunk loaded into 
 constexpr int kCtasPerSmMin = 4;  // register cap of 64: one wave of 4 CTAs per SM (more registers: two waves)
 constexpr int kMaxCluster = 8;
 constexpr int64_t kPrefetchBytes = 64 * 1024;  // per CTA range, issued before the dependency wait
-constexpr int kPrefetchSlices = 2;             // CTA ranges each CTA prefetches (4: slower)
+constexpr int kPrefetchSlices = 1;             // CTA ranges each CTA prefetches (see the file comment)
 constexpr int kCtasPerSm = 4;                  // grid target: rows * cluster CTAs up to this many per SM
 
 __device__ __forceinline__ unsigned long long argmax_key(float v, uint32_t index) {
