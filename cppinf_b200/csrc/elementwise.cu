@@ -6,6 +6,8 @@
 // and stores, when every operand is 32-byte aligned), else 16 bytes, else single elements; the result is the same on
 // every path because each element is computed alone. The grid is two waves of resident blocks striding over the
 // packs, kUnroll independent packs per thread per iteration, so each thread keeps several loads in flight.
+#include <type_traits>
+
 #include "common.cuh"
 #include "runtime.h"
 
@@ -113,11 +115,38 @@ __device__ __forceinline__ uint32_t mul_bf16x2(uint32_t a, uint32_t b) {
     return d;
 }
 
+// Whether a functor asks L2 for its operands before the dependency wait (`prefetch<kBytes>(pack, bytes)`).
+template <typename F, typename = void>
+struct HasPrefetch : std::false_type {};
+template <typename F>
+struct HasPrefetch<F, std::void_t<decltype(&F::template prefetch<32>)>> : std::true_type {};
+
+// Grid-stride rounds of packs prefetched per warp. SiLU * up on [4096, 3072] bf16, measured on B200: none 13.40 us,
+// one round 12.93, two 13.45.
+constexpr int kPrefetchRounds = 1;
+
 // Generic grid-stride driver. `Functor::load<kBytes>(i)` / `compute_store<kBytes>(i, loaded)` handle pack i,
 // `Functor::scalar(e)` element e.
 template <typename Functor, int kBytes>
 __global__ void __launch_bounds__(kThreads) elementwise_kernel(Functor f, int64_t n_vec, int64_t vec_elems,
                                                                int64_t count) {
+    if constexpr (HasPrefetch<Functor>::value && kPrefetchRounds > 0) {
+        // Before the dependency wait (while the previous kernel still runs), lane 0 of each warp asks L2 for the
+        // warp's first kPrefetchRounds groups of 32 consecutive packs. A prefetch returns no data and L2 is the
+        // point of coherence, so the loads after the wait still see what the previous kernel writes.
+        if ((threadIdx.x & 31) == 0) {
+            const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
+            const int64_t first = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+#pragma unroll
+            for (int r = 0; r < kPrefetchRounds; ++r) {
+                const int64_t i = first + r * stride;
+                if (i < n_vec) {
+                    const int64_t packs = n_vec - i < 32 ? n_vec - i : 32;
+                    f.template prefetch<kBytes>(i, static_cast<uint32_t>(packs * kBytes));
+                }
+            }
+        }
+    }
     grid_dependency_begin();
     using Loaded = typename Functor::template Loaded<kBytes>;
     const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
@@ -213,6 +242,11 @@ struct SiluMulFunctor {
     template <int kBytes>
     __device__ __forceinline__ Loaded<kBytes> load(int64_t i) const {
         return {Words<kBytes>::load(gate + i * kBytes), Words<kBytes>::load(up + i * kBytes)};
+    }
+    template <int kBytes>
+    __device__ __forceinline__ void prefetch(int64_t i, uint32_t bytes) const {
+        bulk_prefetch_l2(gate + i * kBytes, bytes);
+        bulk_prefetch_l2(up + i * kBytes, bytes);
     }
     template <int kBytes>
     __device__ __forceinline__ void compute_store(int64_t i, const Loaded<kBytes>& l) const {
