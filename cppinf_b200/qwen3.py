@@ -6,8 +6,8 @@ bf16 logits [T, vocab]; ``forward_cached(token_ids)`` appends to the model's cac
 batches of cached sequences; ``generate`` is the greedy loop of src/cli/cli_app.cpp (temperature 0: argmax of the
 last logits row).
 The model itself lives in libcppinf_b200.so (cppinf_qwen3_* in include/cppinf_b200.h): weights, KV cache and
-activations stay in HBM, and one decode step is a captured CUDA graph whose kernels read the position and the
-previous token from device memory.
+activations stay in HBM, and decode steps are replayed from captured CUDA graphs (of eight steps, and of one step
+for the remainder) whose kernels read the position and the previous token from device memory.
 """
 
 from __future__ import annotations
@@ -282,7 +282,7 @@ class Qwen3Model:
         return self.forward_cached(token_ids, logits="all")[1]
 
     def decode(self, steps: int) -> list[int]:
-        """`steps` greedy decode steps from the cached state (one captured CUDA graph per step)."""
+        """`steps` greedy decode steps from the cached state (captured CUDA graphs of eight steps, then single steps)."""
         import torch
 
         if steps <= 0:
