@@ -282,7 +282,7 @@ class Qwen3Model:
         return self.forward_cached(token_ids, logits="all")[1]
 
     def decode(self, steps: int) -> list[int]:
-        """`steps` greedy decode steps from the cached state (captured CUDA graphs of eight steps, then single steps)."""
+        """`steps` greedy decode steps from the cached state (graphs of eight steps, then single steps)."""
         import torch
 
         if steps <= 0:
